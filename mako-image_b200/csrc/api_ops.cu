@@ -1,0 +1,184 @@
+// The runtime-operation layer of the C ABI (include/mkb_image.h, part 1): argument checks, then one prepared
+// kernel launch each.
+#include "common.cuh"
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace mkb {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_status_mu;
+std::vector<uint32_t*> g_status_words;  // per device
+}  // namespace
+
+mkb_status fail(mkb_status code, const std::string& msg)
+{
+    g_last_error = msg;
+    return code;
+}
+
+mkb_status cuda_status(cudaError_t e, const char* what)
+{
+    if (e == cudaSuccess)
+        return MKB_OK;
+    return fail(e == cudaErrorMemoryAllocation ? MKB_ERR_ALLOC : MKB_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+uint32_t* device_status_word()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return nullptr;
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    if (int(g_status_words.size()) <= dev)
+        g_status_words.resize(dev + 1, nullptr);
+    if (!g_status_words[dev]) {
+        uint32_t* p = nullptr;
+        if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess)
+            return nullptr;
+        cudaMemset(p, 0, sizeof(uint32_t));
+        g_status_words[dev] = p;
+    }
+    return g_status_words[dev];
+}
+
+namespace {
+
+mkb_status run_gemm(Epi epi, const void* x, long ldx, const void* w, long ldw, GemmArgs a, int bn, void* stream)
+{
+    if (!x || !w)
+        return fail(MKB_ERR_INVALID, "proj: null operand");
+    a.status = device_status_word();
+    GemmOp op;
+    const char* err = nullptr;
+    if (!gemm_prepare(op, epi, x, ldx, w, ldw, a, bn, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "proj: unsupported arguments");
+    return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "proj launch");
+}
+
+int pick_bn(int M, int N)
+{
+    // Wide tiles halve the X re-reads; narrow ones fill the SMs when there are few tiles.
+    if (N % 256 == 0 && long((M + 127) / 128) * (N / 256) >= num_sms() / 2)
+        return 256;
+    if (N % 128 == 0)
+        return 128;
+    return 64;
+}
+
+}  // namespace
+
+}  // namespace mkb
+
+using namespace mkb;
+
+extern "C" {
+
+const char* mkb_last_error(void) { return g_last_error.c_str(); }
+
+mkb_status mkb_proj(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy, int M,
+                    int N, int K, int act, int out_f32, void* stream)
+{
+    if (act < MKB_ACT_NONE || act > MKB_ACT_SILU)
+        return fail(MKB_ERR_INVALID, "proj: unknown activation");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.act = act;
+    a.out = y;
+    a.ldo = ldy;
+    return run_gemm(out_f32 ? Epi::kF32 : Epi::kBF16, x, ldx, w, ldw, a, pick_bn(M, N), stream);
+}
+
+mkb_status mkb_proj_gate_add(const void* x, long ldx, const void* w, long ldw, const float* bias, float* resid,
+                             long ldr, const float* gate, long gate_stride, int rows_per_sample, int tanh_gate, int M,
+                             int N, int K, void* stream)
+{
+    if (rows_per_sample <= 0)
+        return fail(MKB_ERR_INVALID, "proj_gate_add: rows_per_sample must be positive");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.resid = resid;
+    a.ldr = ldr;
+    a.gate = gate;
+    a.gate_bstride = gate_stride;
+    a.seg_rows = rows_per_sample;
+    a.tanh_gate = tanh_gate;
+    return run_gemm(Epi::kResid, x, ldx, w, ldw, a, pick_bn(M, N), stream);
+}
+
+mkb_status mkb_proj_qkv_heads(const void* x, long ldx, const void* w, long ldw, const float* bias,
+                              const float* norm_q, const float* norm_k, const float* rope, void* qh, void* kh,
+                              void* vh, int heads, int L, int rows_per_sample, int pos_offset, float eps, int M, int K,
+                              void* stream)
+{
+    if (heads <= 0 || L <= 0 || rows_per_sample <= 0 || pos_offset < 0 || pos_offset + rows_per_sample > L)
+        return fail(MKB_ERR_INVALID, "proj_qkv_heads: need heads > 0 and pos_offset + rows_per_sample <= L");
+    if (!norm_q || !norm_k)
+        return fail(MKB_ERR_INVALID, "proj_qkv_heads: null norm weights");
+    GemmArgs a;
+    a.M = M;
+    a.D = heads * 128;
+    a.N = 3 * a.D;
+    a.K = K;
+    a.bias = bias;
+    a.qh = static_cast<__nv_bfloat16*>(qh);
+    a.kh = static_cast<__nv_bfloat16*>(kh);
+    a.vh = static_cast<__nv_bfloat16*>(vh);
+    a.norm_q = norm_q;
+    a.norm_k = norm_k;
+    a.rope = rope;
+    a.L = L;
+    a.seg_rows = rows_per_sample;
+    a.seg_off = pos_offset;
+    a.eps = eps;
+    const int bn = (a.D % 256 == 0) ? 256 : 128;
+    return run_gemm(Epi::kQkv, x, ldx, w, ldw, a, bn, stream);
+}
+
+int mkb_swiglu_interleave(void) { return 128; }
+
+mkb_status mkb_proj_swiglu(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy,
+                           int M, int N, int K, void* stream)
+{
+    if (N % 256)
+        return fail(MKB_ERR_INVALID, "proj_swiglu: N (gate + up rows) must be a multiple of 256");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.out = y;
+    a.ldo = ldy;
+    return run_gemm(Epi::kSwiGLU, x, ldx, w, ldw, a, 256, stream);
+}
+
+mkb_status mkb_check_kernels(uint32_t* bits)
+{
+    uint32_t* st = device_status_word();
+    if (!st)
+        return fail(MKB_ERR_CUDA, "status word unavailable");
+    MKB_TRY_CUDA(cudaDeviceSynchronize(), "synchronize");
+    uint32_t v = 0;
+    MKB_TRY_CUDA(cudaMemcpy(&v, st, sizeof(v), cudaMemcpyDeviceToHost), "read status");
+    if (bits)
+        *bits = v;
+    if (v) {
+        cudaMemset(st, 0, sizeof(uint32_t));
+        return fail(MKB_ERR_KERNEL, "kernel status bits 0x" + std::to_string(v));
+    }
+    return MKB_OK;
+}
+
+}  // extern "C"

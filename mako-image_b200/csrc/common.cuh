@@ -1,0 +1,27 @@
+// Host-side helpers shared by the C-ABI translation units: the per-thread error message, status conversion and the
+// per-device kernel status word.
+#pragma once
+
+#include "../../include/mkb_image.h"
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+
+namespace mkb {
+
+// Sets the calling thread's error message and returns `code`.
+mkb_status fail(mkb_status code, const std::string& msg);
+// MKB_OK for cudaSuccess, else MKB_ERR_CUDA with "<what>: <cuda error string>".
+mkb_status cuda_status(cudaError_t e, const char* what);
+// The current device's kernel status word (allocated on first use; lives until process exit).
+uint32_t* device_status_word();
+
+#define MKB_TRY_CUDA(expr, what)                                                                                       \
+    do {                                                                                                               \
+        cudaError_t e_ = (expr);                                                                                       \
+        if (e_ != cudaSuccess)                                                                                         \
+            return ::mkb::cuda_status(e_, what);                                                                       \
+    } while (0)
+
+}  // namespace mkb

@@ -1,0 +1,506 @@
+// Persistent warp-specialised tcgen05 GEMM (see gemm.cuh for what it replaces in the reference).
+//
+// One CTA per SM walks a grouped tile order. Warp 0 streams 128x64 X tiles and BNx64 W tiles into a ring of
+// shared-memory stages with TMA (128-byte swizzle); warp 1 issues tcgen05.mma 128xBNx16 into one of two tensor-memory
+// accumulators; warps 2-5 drain the other accumulator through the fused epilogue while the next tile accumulates.
+// tcgen05.ld's 32x32b shape gives each epilogue thread one output row, so row-wise epilogue maths (per-head RMSNorm,
+// RoPE pairs, SwiGLU pairs) needs no shuffles.
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+
+namespace mkb {
+
+namespace {
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int kBarBytes = 256;
+    static constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb)
+{
+    constexpr int G = 8;
+    const int per_group = G * num_n;
+    const int group = tile / per_group;
+    const int first_m = group * G;
+    const int gsize = min(num_m - first_m, G);
+    const int t = tile - group * per_group;
+    mb = first_m + t % gsize;
+    nb = t / gsize;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x)
+{
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float apply_act(float v, int act)
+{
+    if (act == kActGeluTanh)
+        return gelu_tanh(v);
+    if (act == kActSilu)
+        return silu(v);
+    return v;
+}
+
+__device__ __forceinline__ void load_bias32(const float* bias, int col0, float (&b)[32])
+{
+    if (bias) {
+        const float4* p = reinterpret_cast<const float4*>(bias + col0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 v = __ldg(p + j);
+            b[4 * j] = v.x;
+            b[4 * j + 1] = v.y;
+            b[4 * j + 2] = v.z;
+            b[4 * j + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            b[j] = 0.0f;
+    }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32])
+{
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        d[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                          pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+// The epilogue of one tile for one thread (one row). t_row: TMEM address of this row's accumulator, column 0.
+template <int BN, Epi EPI>
+__device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int row, int n0)
+{
+    const bool row_ok = row < a.M;
+    if constexpr (EPI == Epi::kBF16 || EPI == Epi::kF32 || EPI == Epi::kResid) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+            tmem_wait_ld();
+            const int col0 = n0 + c;
+            if (!row_ok || col0 >= a.N)
+                continue;
+            float b[32];
+            load_bias32(a.bias, col0, b);
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                v[j] = __uint_as_float(r[j]) + b[j];
+            if constexpr (EPI == Epi::kBF16) {
+                if (a.act != kActNone)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = apply_act(v[j], a.act);
+                store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + col0, v);
+            } else if constexpr (EPI == Epi::kF32) {
+                if (a.act != kActNone)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = apply_act(v[j], a.act);
+                float4* d = reinterpret_cast<float4*>(static_cast<float*>(a.out) + long(row) * a.ldo + col0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+                const int bsample = row / a.seg_rows;
+                const float4* g4 = reinterpret_cast<const float4*>(a.gate + long(bsample) * a.gate_bstride + col0);
+                float4* x4 = reinterpret_cast<float4*>(a.resid + long(row) * a.ldr + col0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float4 g = __ldg(g4 + j);
+                    if (a.tanh_gate) {
+                        g.x = tanhf(g.x);
+                        g.y = tanhf(g.y);
+                        g.z = tanhf(g.z);
+                        g.w = tanhf(g.w);
+                    }
+                    float4 x = x4[j];
+                    x.x += g.x * v[4 * j];
+                    x.y += g.y * v[4 * j + 1];
+                    x.z += g.z * v[4 * j + 2];
+                    x.w += g.w * v[4 * j + 3];
+                    x4[j] = x;
+                }
+            }
+        }
+    } else if constexpr (EPI == Epi::kSwiGLU) {
+        // Tile columns [0, BN/2) are gates, [BN/2, BN) the matching ups; output column n0/2 + j.
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+            uint32_t rg[32], ru[32];
+            tmem_ld32(t_row + c, rg);
+            tmem_ld32(t_row + BN / 2 + c, ru);
+            tmem_wait_ld();
+            if (!row_ok || n0 + c >= a.N)
+                continue;
+            float bg[32], bu[32], v[32];
+            load_bias32(a.bias, n0 + c, bg);
+            load_bias32(a.bias, n0 + BN / 2 + c, bu);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                v[j] = silu(__uint_as_float(rg[j]) + bg[j]) * (__uint_as_float(ru[j]) + bu[j]);
+            store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + n0 / 2 + c, v);
+        }
+    } else {  // kQkv
+        const int bsample = row / a.seg_rows;
+        const int pos = a.seg_off + row % a.seg_rows;
+        const int heads = a.D / 128;
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) {
+            const int colh = n0 + hh * 128;
+            const int which = colh / a.D;  // 0 q, 1 k, 2 v
+            const int head = (colh % a.D) / 128;
+            float rinv = 1.0f;
+            if (which < 2) {
+                float ss = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + hh * 128 + c, r);
+                    tmem_wait_ld();
+                    float b[32];
+                    load_bias32(a.bias, colh + c, b);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float v = __uint_as_float(r[j]) + b[j];
+                        ss += v * v;
+                    }
+                }
+                rinv = rsqrtf(ss * (1.0f / 128.0f) + a.eps);
+            }
+            __nv_bfloat16* base = which == 0 ? a.qh : which == 1 ? a.kh : a.vh;
+            __nv_bfloat16* dst = base + ((long(bsample) * heads + head) * a.L + pos) * 128;
+            const float* w = which == 0 ? a.norm_q : a.norm_k;
+#pragma unroll 1
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(t_row + hh * 128 + c, r);
+                tmem_wait_ld();
+                if (!row_ok)
+                    continue;
+                float b[32], v[32];
+                load_bias32(a.bias, colh + c, b);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    v[j] = __uint_as_float(r[j]) + b[j];
+                if (which < 2) {
+                    const float4* w4 = reinterpret_cast<const float4*>(w + c);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 ww = __ldg(w4 + j);
+                        v[4 * j] *= rinv * ww.x;
+                        v[4 * j + 1] *= rinv * ww.y;
+                        v[4 * j + 2] *= rinv * ww.z;
+                        v[4 * j + 3] *= rinv * ww.w;
+                    }
+                    if (a.rope) {
+                        const float4* cs = reinterpret_cast<const float4*>(a.rope + (long(pos) * 64 + c / 2) * 2);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {  // two (cos, sin) pairs per float4
+                            const float4 t = __ldg(cs + j);
+                            const float x0 = v[4 * j], x1 = v[4 * j + 1], x2 = v[4 * j + 2], x3 = v[4 * j + 3];
+                            v[4 * j] = x0 * t.x - x1 * t.y;
+                            v[4 * j + 1] = x0 * t.y + x1 * t.x;
+                            v[4 * j + 2] = x2 * t.z - x3 * t.w;
+                            v[4 * j + 3] = x2 * t.w + x3 * t.z;
+                        }
+                    }
+                }
+                store_bf16x32(dst + c, v);
+            }
+        }
+    }
+}
+
+template <int BN, Epi EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs args)
+{
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* acc_full = empty + C::kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int num_m = (args.M + kBM - 1) / kBM, num_n = (args.N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n, num_k = (args.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tma);
+        prefetch_tmap(&tmb);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                int mb, nb;
+                tile_coords(tile, num_m, num_n, mb, nb);
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t ph = (it / C::kStages) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, args.status, kErrWaitEmpty, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * C::kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+                    tma_load_2d(sa, &tma, &full[s], kb * kBK, mb * kBM);
+                    tma_load_2d(sa + C::kABytes, &tmb, &full[s], kb * kBK, nb * BN);
+                }
+            }
+            if (!ok) {  // let the loads already issued land before the CTA can exit
+                const uint32_t first = it > uint32_t(C::kStages) ? it - C::kStages : 0;
+                for (uint32_t j = first; j < it; ++j)
+                    mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, args.status, kErrWaitDrain, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+            uint32_t it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+                const uint32_t acc = local & 1, acc_ph = (local >> 1) & 1;
+                if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, args.status, kErrWaitAccEmpty, abort_flag))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t ph = (it / C::kStages) & 1;
+                    if (!mbar_wait(&full[s], ph, args.status, kErrWaitFull, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        mma_bf16_ss(d_tmem, desc_kmajor_sw128(a_addr + k * 32), desc_kmajor_sw128(b_addr + k * 32),
+                                    idesc, (kb | k) != 0);
+                    mma_commit(&empty[s]);
+                }
+                if (ok)
+                    mma_commit(&acc_full[acc]);
+            }
+            // Every MMA must be complete before tensor memory is released.
+            mma_commit(drain);
+            mbar_wait(drain, 0, args.status, kErrWaitDrain, nullptr);
+        }
+    } else {
+        const int q = warp & 3;  // the TMEM lane quarter this warp may access
+        uint32_t local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            int mb, nb;
+            tile_coords(tile, num_m, num_n, mb, nb);
+            const uint32_t acc = local & 1, acc_ph = (local >> 1) & 1;
+            if (!mbar_wait(&acc_full[acc], acc_ph, args.status, kErrWaitAccFull, abort_flag))
+                break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+            epilogue<BN, EPI>(args, t_row, mb * kBM + q * 32 + lane, nb * BN);
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+template <int BN, Epi EPI>
+cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
+{
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+        if (e != cudaSuccess)
+            return e;
+        attr_set = true;
+    }
+    k_gemm<BN, EPI><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.ta, op.tb, op.args);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_bn(const GemmOp& op, cudaStream_t st)
+{
+    switch (op.epi) {
+    case Epi::kBF16: return launch_t<BN, Epi::kBF16>(op, st);
+    case Epi::kF32: return launch_t<BN, Epi::kF32>(op, st);
+    case Epi::kResid: return launch_t<BN, Epi::kResid>(op, st);
+    case Epi::kQkv: return launch_t<BN, Epi::kQkv>(op, st);
+    case Epi::kSwiGLU: return launch_t<BN, Epi::kSwiGLU>(op, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int num_sms()
+{
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0)
+            n = 148;
+    }
+    return n;
+}
+
+bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer, const char** err)
+{
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_bytes & 15)) {
+        *err = "tensor map: base or row stride not 16-byte aligned";
+        return false;
+    }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *err = "cuTensorMapEncodeTiled failed";
+        return false;
+    }
+    return true;
+}
+
+bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
+                  int bn, const char** err)
+{
+    op.ready = false;
+    if (bn != 64 && bn != 128 && bn != 256) {
+        *err = "gemm: tile width must be 64, 128 or 256";
+        return false;
+    }
+    if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
+        *err = "gemm: M, N, K must be positive, N a multiple of 32, K a multiple of 8";
+        return false;
+    }
+    if (epi == Epi::kQkv && (bn < 128 || args.D % bn || args.N != 3 * args.D || !args.qh || !args.kh || !args.vh)) {
+        *err = "gemm: qkv epilogue needs N = 3 D, D a multiple of the tile width, and q/k/v outputs";
+        return false;
+    }
+    if (epi == Epi::kSwiGLU && args.N % bn) {
+        *err = "gemm: swiglu epilogue needs N a multiple of the tile width";
+        return false;
+    }
+    if (epi == Epi::kResid && (!args.resid || !args.gate || (args.ldr & 3))) {
+        *err = "gemm: residual epilogue needs resid, gate, and ldr a multiple of 4";
+        return false;
+    }
+    if ((epi == Epi::kBF16 || epi == Epi::kSwiGLU) && (!args.out || (args.ldo & 7))) {
+        *err = "gemm: bf16 output needs out and ldo a multiple of 8";
+        return false;
+    }
+    if (epi == Epi::kF32 && (!args.out || (args.ldo & 3))) {
+        *err = "gemm: f32 output needs out and ldo a multiple of 4";
+        return false;
+    }
+    if (!make_tmap_bf16_2d(&op.ta, X, uint64_t(args.K), uint64_t(args.M), uint64_t(ldx) * 2, kBK, kBM, err))
+        return false;
+    if (!make_tmap_bf16_2d(&op.tb, W, uint64_t(args.K), uint64_t(args.N), uint64_t(ldw) * 2, kBK, uint32_t(bn), err))
+        return false;
+    op.args = args;
+    op.epi = epi;
+    op.bn = bn;
+    const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + bn - 1) / bn);
+    op.grid = tiles < num_sms() ? tiles : num_sms();
+    op.ready = true;
+    return true;
+}
+
+cudaError_t gemm_launch(const GemmOp& op, cudaStream_t st)
+{
+    if (!op.ready)
+        return cudaErrorInvalidValue;
+    switch (op.bn) {
+    case 64: return launch_bn<64>(op, st);
+    case 128: return launch_bn<128>(op, st);
+    case 256: return launch_bn<256>(op, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mkb

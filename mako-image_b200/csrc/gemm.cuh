@@ -1,0 +1,79 @@
+// Persistent tcgen05 GEMM for sm_100a: Y[M][N] = X[M][K] * W[N][K]^T with bf16 operands, fp32 accumulation in
+// tensor memory and fused epilogues. This replaces the runtime's `proj()` matrix product that the reference calls
+// for every projection of the denoiser (src/image/qwen_image.cpp:196-288 and src/image/sdxl.cpp:763-794), together
+// with the element-wise kernels that follow it there: bias, activation (`gelu_tanh`, `silu`, `swiglu_rows`), the
+// gated residual add (`gate_add`, src/kernels/image.metal:56-65) and the per-head RMSNorm + RoPE into the attention
+// layout (`heads_norm_half` / `heads_half`, src/image/qwen_image.cpp:226-250).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace mkb {
+
+enum class Epi : int {
+    kBF16 = 0,    // out_bf16[row][col] = act(acc + bias)
+    kF32 = 1,     // out_f32[row][col]  = act(acc + bias)
+    kResid = 2,   // resid[row][col] += g(gate[b][col]) * (acc + bias), fp32 residual stream
+    kQkv = 3,     // q/k: RMSNorm per 128-wide head, weight, RoPE; v: as is; bf16 into [B][H][L][128]
+    kSwiGLU = 4,  // columns come in 128-wide (gate | up) pairs: out_bf16[row][col/2] = silu(gate) * up
+};
+
+enum Act : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };
+
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;
+    const float* bias = nullptr;  // [N] or null
+    int act = kActNone;
+    // kBF16 / kF32 / kSwiGLU output
+    void* out = nullptr;
+    long ldo = 0;
+    // kResid
+    float* resid = nullptr;
+    long ldr = 0;
+    const float* gate = nullptr;  // gate of sample b at gate + b * gate_bstride
+    long gate_bstride = 0;
+    int tanh_gate = 0;            // x += tanh(g) * y (the reference's gate_add) instead of x += g * y
+    // rows -> (sample, position): sample = row / seg_rows, position = seg_off + row % seg_rows
+    int seg_rows = 1 << 30;
+    int seg_off = 0;
+    // kQkv
+    __nv_bfloat16* qh = nullptr;
+    __nv_bfloat16* kh = nullptr;
+    __nv_bfloat16* vh = nullptr;
+    const float* norm_q = nullptr;  // [128]
+    const float* norm_k = nullptr;  // [128]
+    const float* rope = nullptr;    // [L][64][2] (cos, sin) per joint position, or null for no rotation
+    int D = 0;                      // width of each of q, k, v (heads * 128)
+    int L = 0;                      // joint sequence length of the head layout
+    float eps = 1e-6f;
+    uint32_t* status = nullptr;     // error bits (kErr*), may be null
+};
+
+// A prepared launch: tensor maps and arguments are built once (buffers are fixed), then launched any number of
+// times, also inside CUDA graph capture.
+struct GemmOp {
+    CUtensorMap ta, tb;
+    GemmArgs args;
+    Epi epi = Epi::kBF16;
+    int bn = 256;
+    int grid = 0;
+    bool ready = false;
+};
+
+// Builds a GemmOp. X: [M][K] bf16 rows `ldx` elements apart; W: [N][K] bf16 rows `ldw` apart. Returns false with a
+// message in *err on unsupported shapes or misaligned pointers.
+bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
+                  int bn, const char** err);
+cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+int num_sms();
+
+// Encodes a 2-D bf16 tensor map with the 128-byte swizzle: inner (contiguous) extent `inner`, `outer` rows
+// `row_bytes` apart, box `box_inner` x `box_outer`.
+bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer, const char** err);
+
+}  // namespace mkb

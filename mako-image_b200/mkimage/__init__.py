@@ -1,0 +1,7 @@
+"""Python binding of libmkb_image.so (the C ABI in include/mkb_image.h), for the tests and the bench.
+
+The library is the product; this module only loads it with ctypes and turns error codes into exceptions. Device
+buffers are passed as raw pointers (for example ``tensor.data_ptr()`` of a torch CUDA tensor)."""
+
+from ._lib import lib, MkbError, check, LIB_PATH, stream_ptr  # noqa: F401
+from . import ops  # noqa: F401

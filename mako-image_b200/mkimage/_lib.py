@@ -1,0 +1,59 @@
+"""ctypes loader for libmkb_image.so. Importing fails loudly when the library has not been built: there is no
+fallback implementation."""
+
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "lib", "libmkb_image.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C mako-image_b200` (or __graft_entry__.build())")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_vp, _i, _l, _f, _u64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_float, ctypes.c_uint64
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+_SIGS = {
+    "mkb_last_error": (ctypes.c_char_p, []),
+    "mkb_proj": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _i, _i, _vp]),
+    "mkb_proj_gate_add": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _vp, _l, _i, _i, _i, _i, _i, _vp]),
+    "mkb_proj_qkv_heads": (_i, [_vp, _l, _vp, _l, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _i, _vp]),
+    "mkb_proj_swiglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
+    "mkb_swiglu_interleave": (_i, []),
+    "mkb_check_kernels": (_i, [_u32p]),
+}
+
+
+def _bind(name, restype, argtypes):
+    fn = getattr(lib, name, None)
+    if fn is None:
+        return None
+    fn.restype = restype
+    fn.argtypes = argtypes
+    return fn
+
+
+for _name, (_res, _args) in _SIGS.items():
+    _bind(_name, _res, _args)
+
+
+class MkbError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"mkb error {code}: {msg}")
+        self.code = code
+
+
+def check(code):
+    """Raise MkbError for a non-zero mkb_status."""
+    if code != 0:
+        raise MkbError(code, lib.mkb_last_error().decode())
+    return code
+
+
+def stream_ptr(stream=None):
+    """The raw cudaStream_t of a torch stream (None: torch's current stream)."""
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)

@@ -1,0 +1,91 @@
+"""Row and matrix operations of the reference's denoiser, restated in numpy (fp32 unless noted).
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py). Each function cites the reference call site it follows."""
+
+import numpy as np
+
+
+def bf16_round(a):
+    """Round fp32 values to the nearest bf16 (ties to even), returned as fp32."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(a.shape)
+
+
+def linear(x, w, b=None):
+    """y = x w^T + b: the runtime's proj() with W stored [out][in] (qwen_image.cpp:99-105 stacks rows that way)."""
+    y = np.asarray(x, np.float32) @ np.asarray(w, np.float32).T
+    if b is not None:
+        y = y + np.asarray(b, np.float32)
+    return y.astype(np.float32)
+
+
+def gelu_tanh(x):
+    """GELU, tanh approximation (the `gelu_tanh` kernel applied at qwen_image.cpp:211)."""
+    x = np.asarray(x, np.float32)
+    return (0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x * x * x)))).astype(np.float32)
+
+
+def silu(x):
+    """x * sigmoid(x) (the `silu` kernel, qwen_image.cpp:198,202)."""
+    x = np.asarray(x, np.float32)
+    return (x / (1.0 + np.exp(-x))).astype(np.float32)
+
+
+def rms_norm(x, w, eps=1e-6):
+    """x / rms(x) * w over the last axis (runtime norm(), qwen_image.cpp:208; per-head norms :226-242)."""
+    x = np.asarray(x, np.float32)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    return (x / np.sqrt(ms + eps).astype(np.float32) * np.asarray(w, np.float32)).astype(np.float32)
+
+
+def ln_modulate(x, scale, shift=None, eps=1e-6):
+    """LayerNorm without affine, times (1 + scale), plus shift (`ln_modulate`, src/kernels/image.metal:33-53; the
+    reference has no shift, Qwen-Image-1's AdaLN adds one)."""
+    x = np.asarray(x, np.float32)
+    x64 = x.astype(np.float64)
+    mean = x64.mean(axis=-1, keepdims=True)
+    var = ((x64 - mean) ** 2).mean(axis=-1, keepdims=True)
+    y = ((x64 - mean) / np.sqrt(var + eps)).astype(np.float32) * (1.0 + np.asarray(scale, np.float32))
+    if shift is not None:
+        y = y + np.asarray(shift, np.float32)
+    return y.astype(np.float32)
+
+
+def rope_pairs(x, cs):
+    """Rotate interleaved pairs (x[2i], x[2i+1]) by the table cs[..., i, (cos, sin)] (RoPE mode 2 of
+    heads_norm_half, qwen_image.cpp:226-242; table built by rope3, :31-45). x [..., L, 128], cs [L, 64, 2]."""
+    x = np.asarray(x, np.float32)
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    c, s = cs[..., 0], cs[..., 1]
+    out = np.empty_like(x)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x0 * s + x1 * c
+    return out
+
+
+def attention(q, k, v, mask=None):
+    """softmax(q k^T / sqrt(d)) v per head (runtime attention(), qwen_image.cpp:271). q [H][Lq][d], k/v [H][Lk][d];
+    mask [Lq][Lk] boolean (True = may attend) or None."""
+    q = np.asarray(q, np.float32)
+    d = q.shape[-1]
+    out = np.empty(q.shape, np.float32)
+    for h in range(q.shape[0]):
+        s = (q[h] @ np.asarray(k[h], np.float32).T) * np.float32(1.0 / np.sqrt(d))
+        if mask is not None:
+            s = np.where(mask, s, -np.inf)
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=-1, keepdims=True)
+        out[h] = p @ np.asarray(v[h], np.float32)
+    return out
+
+
+def timestep_sinusoid(sigma, dim=256):
+    """Cos-first sinusoid of 1000 * sigma (qwen_image.cpp:179-187): freq_i = exp(-ln(10000) i / (dim/2))."""
+    half = dim // 2
+    i = np.arange(half, dtype=np.float32)
+    freq = np.exp(-np.log(np.float32(10000.0)) * i / np.float32(half)).astype(np.float32)
+    arg = np.float32(1000.0 * sigma) * freq
+    return np.concatenate([np.cos(arg), np.sin(arg)]).astype(np.float32)
