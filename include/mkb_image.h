@@ -74,6 +74,20 @@ mkb_status mkb_proj_swiglu(const void* x, long ldx, const void* w, long ldw, con
  * matrix are gate rows [j*B, (j+1)*B), the next B rows the matching up rows. */
 int mkb_swiglu_interleave(void);
 
+/* Attention masks. */
+enum { MKB_MASK_NONE = 0, MKB_MASK_COND_CAUSAL = 1 };
+
+/* Flash attention, head dim 128: out = softmax(q k^T / sqrt(128)) v per (sample, head). q is [B][H][Lq_rows][128],
+ * k and v [B][H][Lk_rows][128] (bf16, head-major, as mkb_proj_qkv_heads writes them); the first Lq query rows and Lk
+ * keys are used. Query row i sits at joint position q_pos0 + i; keys at positions 0..Lk-1. MKB_MASK_COND_CAUSAL: a
+ * query at position < cond_len sees keys < cond_len only (the reference's text rows, which is what lets it cache the
+ * text K/V; qwen_image.cpp:251-271). Output rows are bf16 [.][H*128]: position p < split goes to row
+ * (b * rows0 + p) of out0, otherwise row (b * rows1 + p - split) of out1 (the text and image streams' inputs of the
+ * output projection). Replaces TransformerRuntime::attention() (qwen_image.cpp:271). */
+mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk, int Lk_rows, int B,
+                         int H, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0, int rows0,
+                         void* out1, long ld1, int rows1, void* stream);
+
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */
 mkb_status mkb_check_kernels(uint32_t* bits);

@@ -1,6 +1,7 @@
 // The runtime-operation layer of the C ABI (include/mkb_image.h, part 1): argument checks, then one prepared
 // kernel launch each.
 #include "common.cuh"
+#include "attention.cuh"
 #include "gemm.cuh"
 #include "sm100.cuh"
 
@@ -162,6 +163,38 @@ mkb_status mkb_proj_swiglu(const void* x, long ldx, const void* w, long ldw, con
     a.out = y;
     a.ldo = ldy;
     return run_gemm(Epi::kSwiGLU, x, ldx, w, ldw, a, 256, stream);
+}
+
+mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk, int Lk_rows, int B,
+                         int H, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0, int rows0,
+                         void* out1, long ld1, int rows1, void* stream)
+{
+    if (!q || !k || !v)
+        return fail(MKB_ERR_INVALID, "attention: null q/k/v");
+    if (mask != MKB_MASK_NONE && mask != MKB_MASK_COND_CAUSAL)
+        return fail(MKB_ERR_INVALID, "attention: unknown mask");
+    AttnArgs a;
+    a.B = B;
+    a.H = H;
+    a.Lq = Lq;
+    a.Lk = Lk;
+    a.q_pos0 = q_pos0;
+    a.mask = mask;
+    a.cond_len = cond_len;
+    a.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
+    a.split = split;
+    a.out0 = static_cast<__nv_bfloat16*>(out0);
+    a.ld0 = ld0;
+    a.rows0 = rows0;
+    a.out1 = static_cast<__nv_bfloat16*>(out1);
+    a.ld1 = ld1;
+    a.rows1 = rows1;
+    a.status = device_status_word();
+    AttnOp op;
+    const char* err = nullptr;
+    if (!attn_prepare(op, q, Lq_rows, k, v, Lk_rows, a, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "attention: unsupported arguments");
+    return cuda_status(attn_launch(op, static_cast<cudaStream_t>(stream)), "attention launch");
 }
 
 mkb_status mkb_check_kernels(uint32_t* bits)

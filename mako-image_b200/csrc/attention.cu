@@ -1,0 +1,371 @@
+// Flash attention forward, head dim 128, on tcgen05 (see attention.cuh).
+//
+// One CTA per (128-row query tile, head, sample); two CTAs share an SM so one's softmax overlaps the other's MMAs.
+//   warp 0     TMA: the Q tile once, then K and V tiles of 128 keys (128-byte swizzle, two 64-wide panels each)
+//   warp 1     MMA: S = Q K^T into tensor memory (128 x 128 fp32), then O += P V with P read from tensor memory
+//   warps 2-5  softmax, one thread per query row: S row from TMEM, online max with lazy rescaling (O is rescaled
+//              only when a row's max grows by more than 2^8), P = exp2(S - m) as bf16 written back over S, and at
+//              the end O / l into the output projection's input rows.
+// TMEM columns: [0, 128) S (P aliases [0, 64)), [128, 256) O.
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <cmath>
+#include <mutex>
+
+namespace mkb {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kTile = 128;                 // query rows per CTA, keys per KV tile
+constexpr int kPanel = kTile * 64 * 2;     // one 64-wide bf16 panel of 128 rows: 16 KB
+constexpr int kTileBytes = 2 * kPanel;     // 32 KB
+constexpr int kSmem = 1024 + 3 * kTileBytes + 256;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 128;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+__device__ __forceinline__ float ex2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
+{
+    uint32_t a[16], b[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        a[i] = r[i];
+        b[i] = r[16 + i];
+    }
+    tmem_st16(taddr, a);
+    tmem_st16(taddr + 16, b);
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    k_attn(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+           const __grid_constant__ CUtensorMap tv, const AttnArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kTileBytes;
+    uint8_t* sV = smem + 2 * kTileBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * kTileBytes);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = bars + 2;
+    uint64_t* v_full = bars + 3;
+    uint64_t* v_empty = bars + 4;
+    uint64_t* s_full = bars + 5;
+    uint64_t* p_full = bars + 6;
+    uint64_t* o_done = bars + 7;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int q0 = blockIdx.x * kTile, h = blockIdx.y, b = blockIdx.z;
+    const int bh = b * a.H + h;
+
+    // Keys this tile needs: a tile of text rows only (condition-causal) stops at the text boundary.
+    int n_keys = a.Lk;
+    if (a.mask == kMaskCondCausal) {
+        const int last_pos = a.q_pos0 + min(q0 + kTile, a.Lq) - 1;
+        if (last_pos < a.cond_len)
+            n_keys = min(a.Lk, a.cond_len);
+    }
+    const int nkv = (n_keys + kTile - 1) / kTile;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(k_full, 1);
+        mbar_init(k_empty, 1);
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        prefetch_tmap(&tv);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued_k = 0, issued_v = 0;
+            bool ok = true;
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            tma_load_3d(sQ, &tq, q_full, 0, q0, bh);
+            tma_load_3d(sQ + kPanel, &tq, q_full, 64, q0, bh);
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (!mbar_wait(k_empty, (j & 1) ^ 1, a.status, kErrAttnWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(k_full, kTileBytes);
+                tma_load_3d(sK, &tk, k_full, 0, j * kTile, bh);
+                tma_load_3d(sK + kPanel, &tk, k_full, 64, j * kTile, bh);
+                ++issued_k;
+                if (!mbar_wait(v_empty, (j & 1) ^ 1, a.status, kErrAttnWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(v_full, kTileBytes);
+                tma_load_3d(sV, &tv, v_full, 0, j * kTile, bh);
+                tma_load_3d(sV + kPanel, &tv, v_full, 64, j * kTile, bh);
+                ++issued_v;
+            }
+            if (!ok) {  // let issued loads land before exit
+                mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
+                if (issued_k)
+                    mbar_wait(k_full, (issued_k - 1) & 1, a.status, kErrWaitDrain, nullptr);
+                if (issued_v)
+                    mbar_wait(v_full, (issued_v - 1) & 1, a.status, kErrWaitDrain, nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, 0, 1);  // V is MN-major (head dim contiguous)
+            const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+            bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (!mbar_wait(k_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                    break;
+                if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, a.status, kErrAttnWait, abort_flag))
+                    break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
+                    mma_bf16_ss(tmem + kColS, desc_kmajor_sw128(q_addr + off), desc_kmajor_sw128(k_addr + off),
+                                idesc_s, k > 0);
+                }
+                mma_commit(k_empty);
+                mma_commit(s_full);
+                if (!mbar_wait(p_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                    break;
+                if (!mbar_wait(v_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                    break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms)
+                    mma_bf16_ts(tmem + kColO, tmem + kColS + 8 * k,
+                                desc_mnmajor_sw128(v_addr + k * 2048, kPanel, 1024), idesc_o, (j > 0) || (k > 0));
+                mma_commit(v_empty);
+                mma_commit(o_done);
+            }
+            mma_commit(k_empty);  // drain: arrives once every MMA issued above has completed
+            mbar_wait(k_empty, nkv & 1, a.status, kErrWaitDrain, nullptr);
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t t_lane = tmem + (uint32_t(quarter * 32) << 16);
+        const int qrow = q0 + r;
+        const int qpos = a.q_pos0 + qrow;
+        const bool text_query = a.mask == kMaskCondCausal && qpos < a.cond_len;
+        const int key_limit = text_query ? min(a.Lk, a.cond_len) : a.Lk;
+        float m_used = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!mbar_wait(s_full, j & 1, a.status, kErrAttnWait, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int key0 = j * kTile;
+            const int valid = min(kTile, key_limit - key0);  // keys [0, valid) of this tile are visible
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t s[32];
+                tmem_ld32(t_lane + kColS + c * 32, s);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (c * 32 + i < valid)
+                        mx = fmaxf(mx, __uint_as_float(s[i]) * a.scale_log2);
+            }
+            const bool need = mx > m_used + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, need)) {
+                const float m_new = need ? mx : m_used;
+                const float f = ex2(m_used - m_new);  // 0 on the first tile
+                l *= f;
+                if (j > 0) {
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(t_lane + kColO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+                        tmem_st32(t_lane + kColO + c * 32, o);
+                    }
+                }
+                m_used = m_new;
+            }
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t s[32], p[16];
+                tmem_ld32(t_lane + kColS + c * 32, s);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int k0 = c * 32 + 2 * i;
+                    const float p0 = k0 < valid ? ex2(__uint_as_float(s[2 * i]) * a.scale_log2 - m_used) : 0.0f;
+                    const float p1 = k0 + 1 < valid ? ex2(__uint_as_float(s[2 * i + 1]) * a.scale_log2 - m_used) : 0.0f;
+                    l += p0 + p1;
+                    p[i] = pack_bf16x2(p0, p1);
+                }
+                tmem_st16(t_lane + kColS + c * 16, p);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(o_done, (nkv - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const bool row_ok = qrow < a.Lq;
+            __nv_bfloat16* dst = nullptr;
+            if (row_ok) {
+                dst = qpos < a.split ? a.out0 + (long(b) * a.rows0 + qpos) * a.ld0
+                                     : a.out1 + (long(b) * a.rows1 + (qpos - a.split)) * a.ld1;
+                dst += h * 128;
+            }
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld32(t_lane + kColO + c * 32, o);
+                tmem_wait_ld();
+                if (row_ok) {
+                    uint4* d = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                          pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Head-major [BH][rows][128] bf16 as a 3-D map, box 64 x 128 x 1 with the 128-byte swizzle; rows past `rows` of a
+// head read as zeros.
+bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, const char** err)
+{
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    if (reinterpret_cast<uintptr_t>(p) & 15) {
+        *err = "attention: q/k/v must be 16-byte aligned";
+        return false;
+    }
+    cuuint64_t dims[3] = {128, cuuint64_t(rows), cuuint64_t(bh)};
+    cuuint64_t strides[2] = {128 * 2, cuuint64_t(rows) * 128 * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        *err = "attention: tensor map encoding failed";
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const void* v, int Lk_rows,
+                  const AttnArgs& args, const char** err)
+{
+    op.ready = false;
+    if (args.B <= 0 || args.H <= 0 || args.Lq <= 0 || args.Lk <= 0 || Lq_rows < args.Lq || Lk_rows < args.Lk) {
+        *err = "attention: bad sizes";
+        return false;
+    }
+    const bool text_rows = args.q_pos0 < args.split;  // some query rows route to out0
+    if (!args.out1 || (text_rows && !args.out0) || (args.ld0 & 7) || (args.ld1 & 7)) {
+        *err = "attention: outputs missing or leading dimensions not multiples of 8";
+        return false;
+    }
+    if ((text_rows && args.rows0 < args.split) || args.q_pos0 < 0 ||
+        args.q_pos0 + args.Lq - args.split > args.rows1) {
+        *err = "attention: output rows do not cover the query positions";
+        return false;
+    }
+    if (args.mask == kMaskCondCausal && args.cond_len <= 0) {
+        *err = "attention: condition-causal mask needs cond_len > 0";
+        return false;
+    }
+    const int bh = args.B * args.H;
+    if (!make_heads_map(&op.tq, q, Lq_rows, bh, err) || !make_heads_map(&op.tk, k, Lk_rows, bh, err) ||
+        !make_heads_map(&op.tv, v, Lk_rows, bh, err))
+        return false;
+    op.args = args;
+    op.grid = dim3((args.Lq + kTile - 1) / kTile, args.H, args.B);
+    op.ready = true;
+    return true;
+}
+
+cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
+{
+    if (!op.ready)
+        return cudaErrorInvalidValue;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+        if (e != cudaSuccess)
+            return e;
+        attr = true;
+    }
+    k_attn<<<op.grid, kThreads, kSmem, st>>>(op.tq, op.tk, op.tv, op.args);
+    return cudaGetLastError();
+}
+
+}  // namespace mkb

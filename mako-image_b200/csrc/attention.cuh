@@ -1,0 +1,51 @@
+// Fused flash attention on tcgen05 for head dim 128: softmax(q k^T / sqrt(128)) v over head-major bf16 q/k/v.
+// Replaces the runtime's attention() the reference calls per block (src/image/qwen_image.cpp:271), including its
+// mask modes, and writes each query row straight into the token-major input of the output projection of its
+// stream (text rows and image rows go to separate buffers).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace mkb {
+
+enum AttnMask : int {
+    kMaskNone = 0,      // every query sees every key (Qwen-Image-1 joint attention)
+    kMaskCondCausal = 1 // queries at joint positions < cond_len see only keys < cond_len (the reference's text rows)
+};
+
+struct AttnArgs {
+    int B = 0, H = 0;
+    int Lq = 0;          // query rows per (sample, head) in q
+    int Lk = 0;          // key rows per (sample, head) in k / v
+    int q_pos0 = 0;      // joint position of query row 0 (keys start at joint position 0)
+    int mask = kMaskNone;
+    int cond_len = 0;    // kMaskCondCausal boundary
+    float scale_log2 = 0.f;  // softmax scale * log2(e)
+    // Output routing by joint position p of a query row: p < split -> out0 row (b * rows0 + p),
+    // else out1 row (b * rows1 + p - split); columns [h * 128, h * 128 + 128).
+    int split = 0;
+    __nv_bfloat16* out0 = nullptr;
+    long ld0 = 0;
+    int rows0 = 0;
+    __nv_bfloat16* out1 = nullptr;
+    long ld1 = 0;
+    int rows1 = 0;
+    uint32_t* status = nullptr;
+};
+
+struct AttnOp {
+    CUtensorMap tq, tk, tv;
+    AttnArgs args;
+    dim3 grid;
+    bool ready = false;
+};
+
+// q: [B][H][Lq_rows][128], k/v: [B][H][Lk_rows][128] (bf16, contiguous); Lq_rows >= args.Lq, Lk_rows >= args.Lk.
+bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const void* v, int Lk_rows,
+                  const AttnArgs& args, const char** err);
+cudaError_t attn_launch(const AttnOp& op, cudaStream_t stream);
+
+}  // namespace mkb

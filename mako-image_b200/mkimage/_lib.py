@@ -22,6 +22,7 @@ _SIGS = {
     "mkb_proj_swiglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
     "mkb_swiglu_interleave": (_i, []),
     "mkb_check_kernels": (_i, [_u32p]),
+    "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
 }
 
 

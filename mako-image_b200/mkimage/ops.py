@@ -65,3 +65,20 @@ def check_kernels():
     bits = ctypes.c_uint32(0)
     check(lib.mkb_check_kernels(ctypes.byref(bits)))
     return bits.value
+
+
+MASK_NONE, MASK_COND_CAUSAL = 0, 1
+
+
+def attention(q, k, v, out0, out1, split, Lq=None, Lk=None, q_pos0=0, mask=MASK_NONE, cond_len=0):
+    """Flash attention over head-major q [B][H][Lq_rows][128], k/v [B][H][Lk_rows][128]; rows routed into out0
+    (joint positions < split) and out1 (see mkb_attention)."""
+    B, H, Lq_rows, _ = q.shape
+    Lk_rows = k.shape[2]
+    Lq = Lq or Lq_rows
+    Lk = Lk or Lk_rows
+    rows0 = out0.shape[0] // B if out0 is not None else 0
+    rows1 = out1.shape[0] // B
+    check(lib.mkb_attention(_p(q), Lq, Lq_rows, _p(k), _p(v), Lk, Lk_rows, B, H, q_pos0, mask, cond_len, split,
+                            _p(out0), out0.stride(0) if out0 is not None else 0, rows0, _p(out1), out1.stride(0),
+                            rows1, stream_ptr()))

@@ -1,0 +1,76 @@
+"""Parity of the tcgen05 flash-attention kernel (mkb_attention) against the numpy oracle.
+
+Tolerance: P is rounded to bf16 before the P.V product and outputs are bf16, so max-abs <= 2e-2 (outputs are
+O(1) averages of unit-variance values) and cosine >= 0.999 per row block."""
+
+import numpy as np
+import pytest
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _heads(shape, seed, cuda):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(torch.bfloat16).to(cuda)
+
+
+def _run(cuda, B, H, S, N, mask, later=False):
+    import torch
+    import mkimage
+
+    L = S + N
+    q = _heads((B, H, L, 128), 1, cuda)
+    k = _heads((B, H, L, 128), 2, cuda)
+    v = _heads((B, H, L, 128), 3, cuda)
+    out0 = torch.zeros(B * S, H * 128, dtype=torch.bfloat16, device=cuda)
+    out1 = torch.zeros(B * N, H * 128, dtype=torch.bfloat16, device=cuda)
+    if later:  # queries: the image rows only, at joint positions S..L-1
+        qi = q[:, :, S:].contiguous()
+        mkimage.ops.attention(qi, k, v, None, out1, split=S, q_pos0=S, mask=mask, cond_len=S)
+    else:
+        mkimage.ops.attention(q, k, v, out0, out1, split=S, mask=mask, cond_len=S)
+    assert mkimage.ops.check_kernels() == 0
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    pos = np.arange(L)
+    m = None
+    if mask == mkimage.ops.MASK_COND_CAUSAL:
+        m = (pos[:, None] >= S) | (pos[None, :] < S)
+    for b in range(B):
+        ref = O.attention(qn[b], kn[b], vn[b], m)  # [H][L][128]
+        ref = ref.transpose(1, 0, 2).reshape(L, H * 128)
+        got_img = out1[b * N:(b + 1) * N].float().cpu().numpy()
+        err = np.abs(got_img - ref[S:]).max()
+        assert err < 2e-2, err
+        cos = (got_img * ref[S:]).sum() / np.sqrt((got_img ** 2).sum() * (ref[S:] ** 2).sum())
+        assert cos > 0.999
+        if not later:
+            got_txt = out0[b * S:(b + 1) * S].float().cpu().numpy()
+            assert np.abs(got_txt - ref[:S]).max() < 2e-2
+
+
+@pytest.mark.parametrize("B,H,S,N", [(1, 1, 128, 128), (2, 3, 44, 256), (1, 2, 77, 1000)])
+def test_attention_joint(cuda, B, H, S, N):
+    _run(cuda, B, H, S, N, 0)
+
+
+@pytest.mark.parametrize("B,H,S,N", [(2, 3, 44, 256), (1, 2, 200, 300)])
+def test_attention_cond_causal(cuda, B, H, S, N):
+    _run(cuda, B, H, S, N, 1)
+
+
+def test_attention_cond_causal_cached_text(cuda):
+    _run(cuda, 2, 2, 130, 260, 1, later=True)
+
+
+def test_attention_rejects_bad_routing(cuda):
+    import torch
+    import mkimage
+
+    q = torch.zeros(1, 1, 256, 128, dtype=torch.bfloat16, device=cuda)
+    out1 = torch.zeros(100, 128, dtype=torch.bfloat16, device=cuda)  # too few rows for 256 queries
+    with pytest.raises(mkimage.MkbError):
+        mkimage.ops.attention(q, q, q, None, out1, split=0)
