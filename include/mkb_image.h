@@ -88,6 +88,85 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
                          int H, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0, int rows0,
                          void* out1, long ld1, int rows1, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * The denoiser (image::Engine's model interface, src/image/engine.hpp:158-166, on the Qwen-Image-style MMDiT).
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* Variants: MKB_VARIANT_QWEN1 is the Qwen-Image(-1) MMDiT shape (separate text/image weights with biases, per-block
+ * AdaLN shift/scale/gate, GELU-tanh FFN, joint attention); MKB_VARIANT_REF21 is the reference's own block math
+ * (src/image/qwen_image.cpp:144-293: shared weights, one shared modulation, tanh gates, SwiGLU, condition-causal
+ * attention with the text K/V cached after a slot's first step). */
+enum { MKB_VARIANT_QWEN1 = 0, MKB_VARIANT_REF21 = 1 };
+
+typedef struct mkb_dit_config {
+    int variant;
+    int hidden;           /* D = heads * 128 */
+    int heads;
+    int ffn;              /* F (qwen1: GELU width; ref21: SwiGLU width) */
+    int blocks;
+    int text_dim;         /* width of the prompt embeddings, a multiple of 128 */
+    int max_batch;        /* samples per step call, 1..8 */
+    int max_text_tokens;  /* S */
+    int max_image_tokens; /* N = h * w */
+    int slots;            /* text conditionings kept (the reference's slot argument; 2 = cond / uncond) */
+} mkb_dit_config;
+
+typedef struct mkb_dit mkb_dit;
+
+/* Creates a denoiser on the current CUDA device: allocates weights and step buffers for the configured maxima.
+ * Weights start at zero; fill them with mkb_dit_init_random or mkb_dit_weight_write. */
+mkb_status mkb_dit_create(const mkb_dit_config* cfg, mkb_dit** out);
+void mkb_dit_destroy(mkb_dit* d);
+
+/* Synthetic weights from a seed: weight i is filled from the normal stream tensor_key(seed, i) (splitmix64 based,
+ * the generator of oracle/rng.py) with std `std` (norm scales: 1 + 0.1 N(0,1)). */
+mkb_status mkb_dit_init_random(mkb_dit* d, uint64_t seed, float std);
+
+/* Weight table: count, and name / shape (rows, cols; cols = 0 for vectors) of entry i. Names follow the reference's
+ * module names in short form ("blk3.img.qkv.w", "time.lin1.w", ...); matrices are stored bf16, vectors fp32. */
+int mkb_dit_weight_count(const mkb_dit* d);
+mkb_status mkb_dit_weight_info(const mkb_dit* d, int i, const char** name, long* rows, long* cols);
+/* Copies a weight to / from host fp32 (matrices are rounded to bf16 on write). The reference's row order is kept:
+ * a SwiGLU gate_up matrix is [gate rows; up rows] here even though the device interleaves it. */
+mkb_status mkb_dit_weight_read(mkb_dit* d, const char* name, float* host);
+mkb_status mkb_dit_weight_write(mkb_dit* d, const char* name, const float* host);
+
+/* Engine::begin (engine.hpp:165): prompt embeddings [S][text_dim] (host fp32) for `slot` on an h x w token grid.
+ * Slots share the grid (the last begin sets it). Resets the slot's step count (ref21: its text K/V cache). */
+mkb_status mkb_dit_begin(mkb_dit* d, const float* prompt, int S, int h, int w, int slot);
+
+/* Engine::step (engine.hpp:166): the velocity out[N][64] for latents[N][64] at noise level sigma, for one slot
+ * (host buffers; blocks until done). */
+mkb_status mkb_dit_step(mkb_dit* d, const float* latents, float sigma, float* out, int slot);
+
+/* n samples in one pass (batch): sample i uses slots[i], latents + i*N*64 and sigmas[i]; velocities to out + i*N*64.
+ * All slots need the same prompt length; ref21 also needs them at the same step count. Host buffers. */
+mkb_status mkb_dit_step_batch(mkb_dit* d, int n, const int* slots, const float* latents, const float* sigmas,
+                              float* out);
+
+/* The same on device buffers (latents_dev / out_dev [n][N][64] fp32), enqueued on `stream` without a host sync. */
+mkb_status mkb_dit_step_batch_dev(mkb_dit* d, int n, const int* slots, const float* latents_dev, const float* sigmas,
+                                  float* out_dev, void* stream);
+
+/* One guided Euler step of a generation (Engine::generate's loop body, engine.cpp:471-506): the cond (slot 0) and
+ * uncond (slot 1) predictions in one batched pass, v = v_u + guidance (v_c - v_u), latents += (sigma_next - sigma) v.
+ * latents [N][64] host fp32, updated in place. */
+mkb_status mkb_dit_step_cfg(mkb_dit* d, float* latents, float sigma, float sigma_next, float guidance);
+
+/* The device-buffer form of mkb_dit_step_cfg for n_images images at once (2 * n_images samples; image i uses slots
+ * 2i and 2i+1): latents_dev [n_images][N][64] updated in place on `stream`. */
+mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, float sigma, float sigma_next,
+                                float guidance, void* stream);
+
+/* Stage probe, as the reference's probe() hooks (qwen_image.cpp:200-287): when set, step calls fn(name, layer,
+ * data, count, user) with host fp32 copies of named stages ("temb", "txt_in", "img_in", "block" with the block index,
+ * "norm_out"; qwen1 blocks report "block.txt" and "block.img"). NULL turns it off. Probing synchronises. */
+typedef void (*mkb_probe_fn)(const char* name, int layer, const float* data, long count, void* user);
+mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user);
+
+/* Algorithmic FLOPs of one step over n samples at the current grid and prompt length (GEMMs + attention). */
+double mkb_dit_step_flops(const mkb_dit* d, int n, int first_step);
+
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */
 mkb_status mkb_check_kernels(uint32_t* bits);

@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             int issued_k = 0, issued_v = 0;
             bool ok = true;
             mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_3d(sQ, &tq, q_full, 0, q0, bh);
-            tma_load_3d(sQ + kPanel, &tq, q_full, 64, q0, bh);
+            tma_load_3d(sQ, &tq, q_full, 0, a.q_row0 + q0, bh);
+            tma_load_3d(sQ + kPanel, &tq, q_full, 64, a.q_row0 + q0, bh);
             for (int j = 0; j < nkv && ok; ++j) {
                 if (!mbar_wait(k_empty, (j & 1) ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
@@ -325,7 +325,8 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
                   const AttnArgs& args, const char** err)
 {
     op.ready = false;
-    if (args.B <= 0 || args.H <= 0 || args.Lq <= 0 || args.Lk <= 0 || Lq_rows < args.Lq || Lk_rows < args.Lk) {
+    if (args.B <= 0 || args.H <= 0 || args.Lq <= 0 || args.Lk <= 0 || args.q_row0 < 0 ||
+        Lq_rows < args.q_row0 + args.Lq || Lk_rows < args.Lk) {
         *err = "attention: bad sizes";
         return false;
     }

@@ -21,6 +21,7 @@ struct AttnArgs {
     int Lq = 0;          // query rows per (sample, head) in q
     int Lk = 0;          // key rows per (sample, head) in k / v
     int q_pos0 = 0;      // joint position of query row 0 (keys start at joint position 0)
+    int q_row0 = 0;      // row of q (within each head) holding query row 0
     int mask = kMaskNone;
     int cond_len = 0;    // kMaskCondCausal boundary
     float scale_log2 = 0.f;  // softmax scale * log2(e)

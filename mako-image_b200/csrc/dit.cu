@@ -1,0 +1,1108 @@
+// The denoiser handle behind include/mkb_image.h part 2: weights, step buffers and the per-step executor of the
+// Qwen-Image-style MMDiT, in the reference's two block variants.
+//
+// The executor follows QwenImage::step (src/image/qwen_image.cpp:144-293) stage by stage, but every stage is one of
+// this library's fused kernels: the time path runs as fp32-activation GEMVs, each projection is one tcgen05 GEMM
+// whose epilogue applies bias / activation / gated residual / per-head RMSNorm + RoPE, LayerNorm-modulate is one
+// warp-per-row pass, and attention is one flash kernel writing straight into the output projection's input.
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "rowops.cuh"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace mkb {
+
+namespace {
+
+constexpr int kHeadDim = 128, kLatent = 64, kTimeDim = 256;
+constexpr float kEps = 1e-6f;
+constexpr int kSwigluBlock = 128;  // gate/up interleave of the SwiGLU GEMM (one 256-wide tile = 128 gate + 128 up)
+
+uint64_t splitmix64_host(uint64_t x)
+{
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+struct Weight {
+    std::string name;
+    long rows = 0, cols = 0;  // cols == 0: vector
+    size_t off = 0;           // element offset in its arena (bf16 matrices / fp32 vectors)
+    bool swiglu = false;      // stored gate/up-interleaved
+    bool norm = false;        // a norm scale (random init around 1)
+    size_t count() const { return size_t(rows) * (cols ? cols : 1); }
+};
+
+// rope3 of the reference (qwen_image.cpp:31-45): 8 pairs on the frame axis, 28 each on height and width, theta 1e4.
+void rope3(float* cs, long f, long hp, long wp)
+{
+    const int dims[3] = {16, 56, 56};
+    const long pos[3] = {f, hp, wp};
+    int i = 0;
+    for (int a = 0; a < 3; ++a)
+        for (int j = 0; j < dims[a] / 2; ++j, ++i) {
+            const float inv = 1.0f / std::pow(10000.0f, float(2 * j) / float(dims[a]));
+            const float ang = float(pos[a]) * inv;
+            cs[2 * i] = std::cos(ang);
+            cs[2 * i + 1] = std::sin(ang);
+        }
+}
+
+}  // namespace
+
+struct DitImpl {
+    mkb_dit_config cfg{};
+    int D = 0, H = 0, F = 0, NB = 0, TD = 0;
+    int Bmax = 0, Smax = 0, Nmax = 0, Lmax = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t* status = nullptr;
+
+    std::vector<Weight> weights;
+    std::map<std::string, int> windex;
+    __nv_bfloat16* wmat = nullptr;
+    float* wvec = nullptr;
+    size_t wmat_n = 0, wvec_n = 0;
+
+    // step buffers
+    float *x_txt = nullptr, *x_img = nullptr, *vel = nullptr, *lat = nullptr;
+    __nv_bfloat16 *xn = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr, *attn = nullptr, *hid = nullptr;
+    __nv_bfloat16 *lat_bf = nullptr, *txt_bf = nullptr, *txt_mid = nullptr;
+    float *tp = nullptr, *h1 = nullptr, *temb = nullptr, *st = nullptr, *mod = nullptr, *omod = nullptr;
+    float *sig = nullptr, *rope = nullptr;
+    float* cfg_lat = nullptr;  // device copy of one image's latents for the host-buffer guided step
+
+    struct Slot {
+        bool begun = false;
+        int S = 0, steps = 0;
+        float* prompt = nullptr;                    // device [Smax][TD]
+        std::vector<__nv_bfloat16*> kc, vc;         // ref21 text K/V per block, [H][S][128]
+    };
+    std::vector<Slot> slots;
+    int gh = 0, gw = 0;
+    long rope_key[3] = {-1, -1, -1};
+
+    mkb_probe_fn probe = nullptr;
+    void* probe_user = nullptr;
+
+    // Prepared launches per geometry (batch, text rows, image rows, first step of ref21).
+    struct Plan {
+        std::vector<GemmOp> ops;  // indexed by the builder
+        AttnOp att;
+        std::vector<GemmOp> per_sample;  // ref21 txt_in2 / img_in per sample
+    };
+    std::map<std::tuple<int, int, int, int>, std::unique_ptr<Plan>> plans;
+
+    ~DitImpl();
+    mkb_status create(const mkb_dit_config& c);
+    void add_weight(const std::string& name, long rows, long cols, bool norm = false, bool swiglu = false);
+    const Weight* find(const std::string& n) const
+    {
+        auto it = windex.find(n);
+        return it == windex.end() ? nullptr : &weights[it->second];
+    }
+    const __nv_bfloat16* M(const std::string& n) const { return wmat + find(n)->off; }
+    const float* V(const std::string& n) const
+    {
+        const Weight* w = find(n);
+        return w ? wvec + w->off : nullptr;
+    }
+    mkb_status build_plan(int B, int S, int N, int first, Plan** out);
+    mkb_status run(int B, const int* slot_ids, const float* sigmas, cudaStream_t s, bool* first_out);
+    mkb_status upload_rope(int S, cudaStream_t s);
+    mkb_status emit(const char* name, int layer, const float* dev, long count, cudaStream_t s);
+    mkb_status check_status();
+};
+
+DitImpl::~DitImpl()
+{
+    void* bufs[] = {wmat, wvec, x_txt, x_img, vel, lat, xn, qh, kh, vh, attn, hid, lat_bf, txt_bf, txt_mid,
+                    tp, h1, temb, st, mod, omod, sig, rope, cfg_lat};
+    for (void* p : bufs)
+        if (p)
+            cudaFree(p);
+    for (auto& s : slots) {
+        if (s.prompt)
+            cudaFree(s.prompt);
+        for (auto* p : s.kc)
+            cudaFree(p);
+        for (auto* p : s.vc)
+            cudaFree(p);
+    }
+    if (stream)
+        cudaStreamDestroy(stream);
+}
+
+void DitImpl::add_weight(const std::string& name, long rows, long cols, bool norm, bool swiglu)
+{
+    Weight w;
+    w.name = name;
+    w.rows = rows;
+    w.cols = cols;
+    w.norm = norm;
+    w.swiglu = swiglu;
+    if (cols) {
+        w.off = wmat_n;
+        wmat_n += size_t(rows) * cols;
+    } else {
+        w.off = wvec_n;
+        wvec_n += size_t(rows);
+        wvec_n = (wvec_n + 3) & ~size_t(3);  // keep every vector 16-byte aligned
+    }
+    windex[name] = int(weights.size());
+    weights.push_back(w);
+}
+
+mkb_status DitImpl::create(const mkb_dit_config& c)
+{
+    cfg = c;
+    D = c.hidden;
+    H = c.heads;
+    F = c.ffn;
+    NB = c.blocks;
+    TD = c.text_dim;
+    Bmax = c.max_batch;
+    Smax = c.max_text_tokens;
+    Nmax = c.max_image_tokens;
+    Lmax = Smax + Nmax;
+    if (c.variant != MKB_VARIANT_QWEN1 && c.variant != MKB_VARIANT_REF21)
+        return fail(MKB_ERR_INVALID, "dit: unknown variant");
+    if (H <= 0 || D != H * kHeadDim || D % 256 || F <= 0 || F % 256 || NB <= 0 || TD <= 0 || TD % 128 ||
+        TD > 4096 || D > 4096)
+        return fail(MKB_ERR_INVALID, "dit: need hidden = heads * 128 (a multiple of 256, <= 4096), ffn a multiple "
+                                     "of 256, text_dim a multiple of 128 (<= 4096), blocks > 0");
+    if (Bmax < 1 || Bmax > 8 || Smax < 1 || Nmax < 1 || c.slots < 1)
+        return fail(MKB_ERR_INVALID, "dit: need 1 <= max_batch <= 8, max tokens >= 1, slots >= 1");
+    const bool q1 = c.variant == MKB_VARIANT_QWEN1;
+
+    // Weight table. The per-block modulation matrices come first so all of them form one stacked GEMV operand.
+    if (q1) {
+        for (int i = 0; i < NB; ++i)
+            for (const char* s : {"img", "txt"}) {
+                const std::string p = "blk" + std::to_string(i) + "." + s + ".";
+                add_weight(p + "mod.w", 6L * D, D);
+                add_weight(p + "mod.b", 6L * D, 0);
+            }
+        add_weight("time.lin1.w", D, kTimeDim);
+        add_weight("time.lin1.b", D, 0);
+        add_weight("time.lin2.w", D, D);
+        add_weight("time.lin2.b", D, 0);
+        add_weight("img_in.w", D, kLatent);
+        add_weight("img_in.b", D, 0);
+        add_weight("txt_norm.w", TD, 0, true);
+        add_weight("txt_in.w", D, TD);
+        add_weight("txt_in.b", D, 0);
+        add_weight("norm_out.w", 2L * D, D);
+        add_weight("norm_out.b", 2L * D, 0);
+        add_weight("proj_out.w", kLatent, D);
+        add_weight("proj_out.b", kLatent, 0);
+        for (int i = 0; i < NB; ++i)
+            for (const char* s : {"img", "txt"}) {
+                const std::string p = "blk" + std::to_string(i) + "." + s + ".";
+                add_weight(p + "qkv.w", 3L * D, D);
+                add_weight(p + "qkv.b", 3L * D, 0);
+                add_weight(p + "norm_q", kHeadDim, 0, true);
+                add_weight(p + "norm_k", kHeadDim, 0, true);
+                add_weight(p + "o.w", D, D);
+                add_weight(p + "o.b", D, 0);
+                add_weight(p + "ff1.w", F, D);
+                add_weight(p + "ff1.b", F, 0);
+                add_weight(p + "ff2.w", D, F);
+                add_weight(p + "ff2.b", D, 0);
+            }
+    } else {
+        add_weight("time.lin1.w", D, kTimeDim);
+        add_weight("time.lin2.w", D, D);
+        add_weight("mod.w", 4L * D, D);
+        add_weight("img_in.w", D, kLatent);
+        add_weight("txt_norm.w", TD, 0, true);
+        add_weight("txt_in1.w", D, TD);
+        add_weight("txt_in2.w", D, D);
+        add_weight("norm_out.w", D, D);
+        add_weight("proj_out.w", kLatent, D);
+        for (int i = 0; i < NB; ++i) {
+            const std::string p = "blk" + std::to_string(i) + ".";
+            add_weight(p + "qkv.w", 3L * D, D);
+            add_weight(p + "norm_q", kHeadDim, 0, true);
+            add_weight(p + "norm_k", kHeadDim, 0, true);
+            add_weight(p + "o.w", D, D);
+            add_weight(p + "gate_up.w", 2L * F, D, false, true);
+            add_weight(p + "down.w", D, F);
+        }
+    }
+
+    MKB_TRY_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    status = device_status_word();
+    if (!status)
+        return fail(MKB_ERR_CUDA, "status word");
+    auto alloc = [&](void** p, size_t bytes, const char* what) -> mkb_status {
+        cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+        if (e != cudaSuccess)
+            return fail(MKB_ERR_ALLOC, std::string("dit: allocating ") + what + ": " + cudaGetErrorString(e));
+        return MKB_OK;
+    };
+#define MKB_ALLOC(ptr, bytes)                                                                                          \
+    do {                                                                                                               \
+        mkb_status s_ = alloc(reinterpret_cast<void**>(&ptr), (bytes), #ptr);                                          \
+        if (s_ != MKB_OK)                                                                                              \
+            return s_;                                                                                                 \
+    } while (0)
+    MKB_ALLOC(wmat, wmat_n * 2);
+    MKB_ALLOC(wvec, wvec_n * 4);
+    MKB_TRY_CUDA(cudaMemset(wmat, 0, wmat_n * 2), "zero weights");
+    MKB_TRY_CUDA(cudaMemset(wvec, 0, wvec_n * 4), "zero weights");
+    const size_t B = Bmax, L = Lmax;
+    MKB_ALLOC(x_txt, B * Smax * D * 4);
+    MKB_ALLOC(x_img, B * L * D * 4);
+    MKB_ALLOC(xn, B * L * D * 2);
+    MKB_ALLOC(qh, B * H * L * kHeadDim * 2);
+    MKB_ALLOC(kh, B * H * L * kHeadDim * 2);
+    MKB_ALLOC(vh, B * H * L * kHeadDim * 2);
+    MKB_ALLOC(attn, B * L * D * 2);
+    MKB_ALLOC(hid, B * L * F * 2);
+    MKB_ALLOC(vel, B * L * kLatent * 4);
+    MKB_ALLOC(lat, B * Nmax * kLatent * 4);
+    MKB_ALLOC(lat_bf, B * Nmax * kLatent * 2);
+    MKB_ALLOC(txt_bf, B * Smax * TD * 2);
+    MKB_ALLOC(txt_mid, B * Smax * D * 2);
+    MKB_ALLOC(tp, 2 * B * kTimeDim * 4);
+    MKB_ALLOC(h1, 2 * B * D * 4);
+    MKB_ALLOC(temb, 2 * B * D * 4);
+    MKB_ALLOC(st, 2 * B * D * 4);
+    MKB_ALLOC(mod, q1 ? B * NB * 12 * D * 4 : 2 * B * 4 * D * 4);
+    MKB_ALLOC(omod, 2 * B * 2 * D * 4);
+    MKB_ALLOC(sig, 2 * B * 4);
+    MKB_ALLOC(rope, L * 64 * 2 * 4);
+    MKB_ALLOC(cfg_lat, size_t(Nmax) * kLatent * 4);
+    slots.resize(c.slots);
+    for (auto& s : slots) {
+        MKB_ALLOC(s.prompt, size_t(Smax) * TD * 4);
+        if (!q1) {
+            s.kc.resize(NB, nullptr);
+            s.vc.resize(NB, nullptr);
+            for (int i = 0; i < NB; ++i) {
+                MKB_ALLOC(s.kc[i], size_t(H) * Smax * kHeadDim * 2);
+                MKB_ALLOC(s.vc[i], size_t(H) * Smax * kHeadDim * 2);
+            }
+        }
+    }
+#undef MKB_ALLOC
+    return MKB_OK;
+}
+
+mkb_status DitImpl::upload_rope(int S, cudaStream_t s)
+{
+    if (rope_key[0] == S && rope_key[1] == gh && rope_key[2] == gw)
+        return MKB_OK;
+    const long L = S + long(gh) * gw;
+    std::vector<float> t(size_t(L) * kHeadDim);
+    const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
+    // Text positions: (t, t, t) in the reference (qwen_image.cpp:136-137); Qwen-Image-1 starts them after the
+    // image's centred grid, at max(h/2, w/2). The image takes the frame position S (reference) or 0.
+    const long m = q1 ? std::max(gh / 2, gw / 2) : 0;
+    for (long i = 0; i < S; ++i)
+        rope3(t.data() + i * kHeadDim, m + i, m + i, m + i);
+    for (long y = 0; y < gh; ++y)
+        for (long x = 0; x < gw; ++x)
+            rope3(t.data() + (S + y * gw + x) * kHeadDim, q1 ? 0 : S, y - (gh - gh / 2), x - (gw - gw / 2));
+    MKB_TRY_CUDA(cudaMemcpyAsync(rope, t.data(), t.size() * 4, cudaMemcpyHostToDevice, s), "rope upload");
+    MKB_TRY_CUDA(cudaStreamSynchronize(s), "rope upload");
+    rope_key[0] = S;
+    rope_key[1] = gh;
+    rope_key[2] = gw;
+    return MKB_OK;
+}
+
+mkb_status DitImpl::emit(const char* name, int layer, const float* dev, long count, cudaStream_t s)
+{
+    if (!probe)
+        return MKB_OK;
+    std::vector<float> h(count);
+    MKB_TRY_CUDA(cudaStreamSynchronize(s), "probe sync");
+    MKB_TRY_CUDA(cudaMemcpy(h.data(), dev, size_t(count) * 4, cudaMemcpyDeviceToHost), "probe copy");
+    probe(name, layer, h.data(), count, probe_user);
+    return MKB_OK;
+}
+
+mkb_status DitImpl::check_status()
+{
+    uint32_t v = 0;
+    MKB_TRY_CUDA(cudaMemcpy(&v, status, 4, cudaMemcpyDeviceToHost), "status read");
+    if (v) {
+        cudaMemset(status, 0, 4);
+        return fail(MKB_ERR_KERNEL, "dit: kernel status bits 0x" + std::to_string(v));
+    }
+    return MKB_OK;
+}
+
+// Op indices of a plan.
+namespace op {
+// qwen1: per block 8 ops: [qkv_txt, qkv_img, o_txt, o_img, ff1_txt, ff1_img, ff2_txt, ff2_img]; then globals.
+// ref21: per block 4 ops: [qkv, o, gate_up, down]; then globals.
+constexpr int kQ1PerBlock = 8, kR21PerBlock = 4;
+enum Global { kTxtIn = 0, kImgIn = 1, kProjOut = 2, kTxtIn1 = 3, kCount = 4 };
+}  // namespace op
+
+mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
+{
+    const auto key = std::make_tuple(B, S, N, first);
+    auto it = plans.find(key);
+    if (it != plans.end()) {
+        *out = it->second.get();
+        return MKB_OK;
+    }
+    auto plan = std::make_unique<Plan>();
+    const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
+    const int L = S + N;
+    const char* err = nullptr;
+    auto prep = [&](GemmOp& o, Epi epi, const void* X, long ldx, const void* W, long ldw, GemmArgs a,
+                    int bn) -> bool {
+        a.status = status;
+        return gemm_prepare(o, epi, X, ldx, W, ldw, a, bn, &err);
+    };
+    auto bn_for = [&](int M, int Nc) {
+        if (Nc % 256 == 0 && long((M + 127) / 128) * (Nc / 256) >= 74)
+            return 256;
+        return Nc % 128 == 0 ? 128 : 64;
+    };
+    const int per = q1 ? op::kQ1PerBlock : op::kR21PerBlock;
+    plan->ops.resize(size_t(NB) * per + op::kCount);
+    GemmOp* g = plan->ops.data() + size_t(NB) * per;
+    if (q1) {
+        const int Mt = B * S, Mi = B * N;
+        const long mstride = long(NB) * 12 * D;  // per-sample stride of the stacked modulation
+        __nv_bfloat16* xn_s[2] = {xn, xn + size_t(Mt) * D};
+        __nv_bfloat16* at_s[2] = {attn, attn + size_t(Mt) * D};
+        __nv_bfloat16* hd_s[2] = {hid, hid + size_t(Mt) * F};
+        float* x_s[2] = {x_txt, x_img};
+        const int M_s[2] = {Mt, Mi}, rps[2] = {S, N}, off[2] = {0, S};
+        const char* nm[2] = {"txt", "img"};
+        for (int i = 0; i < NB; ++i) {
+            GemmOp* o = plan->ops.data() + size_t(i) * per;
+            for (int s = 0; s < 2; ++s) {
+                const std::string p = "blk" + std::to_string(i) + "." + nm[s] + ".";
+                const int stream_idx = s == 0 ? 1 : 0;  // mod order: img then txt per block
+                const float* mb = mod + (size_t(i) * 2 + stream_idx) * 6 * D;
+                GemmArgs a;
+                a.M = M_s[s];
+                a.N = 3 * D;
+                a.K = D;
+                a.bias = V(p + "qkv.b");
+                a.qh = qh;
+                a.kh = kh;
+                a.vh = vh;
+                a.norm_q = V(p + "norm_q");
+                a.norm_k = V(p + "norm_k");
+                a.rope = rope;
+                a.D = D;
+                a.L = L;
+                a.seg_rows = rps[s];
+                a.seg_off = off[s];
+                a.eps = kEps;
+                if (!prep(o[0 + s], Epi::kQkv, xn_s[s], D, M(p + "qkv.w"), D, a, 256))
+                    return fail(MKB_ERR_INVALID, err);
+                GemmArgs r;
+                r.M = M_s[s];
+                r.N = D;
+                r.K = D;
+                r.bias = V(p + "o.b");
+                r.resid = x_s[s];
+                r.ldr = D;
+                r.gate = mb + 2 * D;
+                r.gate_bstride = mstride;
+                r.seg_rows = rps[s];
+                if (!prep(o[2 + s], Epi::kResid, at_s[s], D, M(p + "o.w"), D, r, bn_for(r.M, D)))
+                    return fail(MKB_ERR_INVALID, err);
+                GemmArgs f1;
+                f1.M = M_s[s];
+                f1.N = F;
+                f1.K = D;
+                f1.bias = V(p + "ff1.b");
+                f1.act = kActGeluTanh;
+                f1.out = hd_s[s];
+                f1.ldo = F;
+                if (!prep(o[4 + s], Epi::kBF16, xn_s[s], D, M(p + "ff1.w"), D, f1, bn_for(f1.M, F)))
+                    return fail(MKB_ERR_INVALID, err);
+                GemmArgs f2 = r;
+                f2.K = F;
+                f2.bias = V(p + "ff2.b");
+                f2.gate = mb + 5 * D;
+                if (!prep(o[6 + s], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_for(f2.M, D)))
+                    return fail(MKB_ERR_INVALID, err);
+            }
+        }
+        GemmArgs a;
+        a.M = Mt;
+        a.N = D;
+        a.K = TD;
+        a.bias = V("txt_in.b");
+        a.out = x_txt;
+        a.ldo = D;
+        if (!prep(g[op::kTxtIn], Epi::kF32, txt_bf, TD, M("txt_in.w"), TD, a, bn_for(Mt, D)))
+            return fail(MKB_ERR_INVALID, err);
+        a.M = Mi;
+        a.K = kLatent;
+        a.bias = V("img_in.b");
+        a.out = x_img;
+        if (!prep(g[op::kImgIn], Epi::kF32, lat_bf, kLatent, M("img_in.w"), kLatent, a, bn_for(Mi, D)))
+            return fail(MKB_ERR_INVALID, err);
+        a.N = kLatent;
+        a.K = D;
+        a.bias = V("proj_out.b");
+        a.out = vel;
+        a.ldo = kLatent;
+        if (!prep(g[op::kProjOut], Epi::kF32, xn + size_t(Mt) * D, D, M("proj_out.w"), D, a, 64))
+            return fail(MKB_ERR_INVALID, err);
+        AttnArgs at;
+        at.B = B;
+        at.H = H;
+        at.Lq = L;
+        at.Lk = L;
+        at.mask = kMaskNone;
+        at.scale_log2 = 1.4426950408889634f / std::sqrt(float(kHeadDim));
+        at.split = S;
+        at.out0 = attn;
+        at.ld0 = D;
+        at.rows0 = S;
+        at.out1 = attn + size_t(Mt) * D;
+        at.ld1 = D;
+        at.rows1 = N;
+        at.status = status;
+        if (!attn_prepare(plan->att, qh, L, kh, vh, L, at, &err))
+            return fail(MKB_ERR_INVALID, err);
+    } else {
+        const int T = first ? L : N, split = first ? S : 0, Mr = B * T;
+        const long mstride = 8L * D;  // two modulation rows of 4D per sample
+        for (int i = 0; i < NB; ++i) {
+            GemmOp* o = plan->ops.data() + size_t(i) * per;
+            const std::string p = "blk" + std::to_string(i) + ".";
+            GemmArgs a;
+            a.M = Mr;
+            a.N = 3 * D;
+            a.K = D;
+            a.qh = qh;
+            a.kh = kh;
+            a.vh = vh;
+            a.norm_q = V(p + "norm_q");
+            a.norm_k = V(p + "norm_k");
+            a.rope = rope;
+            a.D = D;
+            a.L = L;
+            a.seg_rows = T;
+            a.seg_off = first ? 0 : S;
+            a.eps = kEps;
+            if (!prep(o[0], Epi::kQkv, xn, D, M(p + "qkv.w"), D, a, 256))
+                return fail(MKB_ERR_INVALID, err);
+            GemmArgs r;
+            r.M = Mr;
+            r.N = D;
+            r.K = D;
+            r.resid = x_img;
+            r.ldr = D;
+            r.gate = mod + D;
+            r.gate_bstride = mstride;
+            r.seg_rows = T;
+            r.tanh_gate = 1;
+            r.gate_split = split;
+            r.gate_alt_off = 4L * D;
+            if (!prep(o[1], Epi::kResid, attn, D, M(p + "o.w"), D, r, bn_for(Mr, D)))
+                return fail(MKB_ERR_INVALID, err);
+            GemmArgs sg;
+            sg.M = Mr;
+            sg.N = 2 * F;
+            sg.K = D;
+            sg.out = hid;
+            sg.ldo = F;
+            if (!prep(o[2], Epi::kSwiGLU, xn, D, M(p + "gate_up.w"), D, sg, 256))
+                return fail(MKB_ERR_INVALID, err);
+            GemmArgs r2 = r;
+            r2.K = F;
+            r2.gate = mod + 3 * D;
+            if (!prep(o[3], Epi::kResid, hid, F, M(p + "down.w"), F, r2, bn_for(Mr, D)))
+                return fail(MKB_ERR_INVALID, err);
+        }
+        GemmArgs a;
+        a.M = B * S;
+        a.N = D;
+        a.K = TD;
+        a.act = kActGeluTanh;
+        a.out = txt_mid;
+        a.ldo = D;
+        if (!prep(g[op::kTxtIn1], Epi::kBF16, txt_bf, TD, M("txt_in1.w"), TD, a, bn_for(B * S, D)))
+            return fail(MKB_ERR_INVALID, err);
+        a.M = Mr;
+        a.N = kLatent;
+        a.K = D;
+        a.act = kActNone;
+        a.out = vel;
+        a.ldo = kLatent;
+        if (!prep(g[op::kProjOut], Epi::kF32, xn, D, M("proj_out.w"), D, a, 64))
+            return fail(MKB_ERR_INVALID, err);
+        // Per sample: the text input (first step) and the image input into the sample's rows of the joint x.
+        plan->per_sample.resize(size_t(B) * 2);
+        for (int b = 0; b < B; ++b) {
+            GemmArgs t;
+            t.M = S;
+            t.N = D;
+            t.K = D;
+            t.out = x_img + size_t(b) * T * D;
+            t.ldo = D;
+            if (first && !prep(plan->per_sample[2 * b], Epi::kF32, txt_mid + size_t(b) * S * D, D, M("txt_in2.w"), D,
+                               t, bn_for(S, D)))
+                return fail(MKB_ERR_INVALID, err);
+            GemmArgs im;
+            im.M = N;
+            im.N = D;
+            im.K = kLatent;
+            im.out = x_img + (size_t(b) * T + split) * D;
+            im.ldo = D;
+            if (!prep(plan->per_sample[2 * b + 1], Epi::kF32, lat_bf + size_t(b) * N * kLatent, kLatent, M("img_in.w"),
+                      kLatent, im, bn_for(N, D)))
+                return fail(MKB_ERR_INVALID, err);
+        }
+        AttnArgs at;
+        at.B = B;
+        at.H = H;
+        at.Lq = T;
+        at.Lk = L;
+        at.q_pos0 = first ? 0 : S;
+        at.q_row0 = first ? 0 : S;
+        at.mask = kMaskCondCausal;
+        at.cond_len = S;
+        at.scale_log2 = 1.4426950408889634f / std::sqrt(float(kHeadDim));
+        at.split = S;
+        at.out0 = attn;
+        at.ld0 = D;
+        at.rows0 = T;
+        at.out1 = first ? attn + size_t(S) * D : attn;
+        at.ld1 = D;
+        at.rows1 = T;
+        at.status = status;
+        if (!attn_prepare(plan->att, qh, L, kh, vh, L, at, &err))
+            return fail(MKB_ERR_INVALID, err);
+    }
+    *out = plan.get();
+    plans[key] = std::move(plan);
+    return MKB_OK;
+}
+
+#define MKB_TRY(expr)                                                                                                  \
+    do {                                                                                                               \
+        mkb_status s_ = (expr);                                                                                        \
+        if (s_ != MKB_OK)                                                                                              \
+            return s_;                                                                                                 \
+    } while (0)
+#define MKB_K(expr, what) MKB_TRY_CUDA((expr), what)
+
+// Runs one step for B samples whose latents are in `lat` (device, [B][N][64]) with host noise levels `sigmas`.
+// Velocities of sample b's image rows end in vel at rows (b * T + split) (see `first_out` for ref21's layout).
+mkb_status DitImpl::run(int B, const int* slot_ids, const float* sigmas, cudaStream_t s, bool* first_out)
+{
+    if (B < 1 || B > Bmax)
+        return fail(MKB_ERR_INVALID, "dit: batch out of range");
+    int S = -1, steps = -1;
+    for (int b = 0; b < B; ++b) {
+        const int id = slot_ids[b];
+        if (id < 0 || id >= int(slots.size()) || !slots[id].begun)
+            return fail(MKB_ERR_STATE, "dit: step on a slot without begin");
+        if (S >= 0 && slots[id].S != S)
+            return fail(MKB_ERR_INVALID, "dit: batched slots need the same prompt length");
+        if (cfg.variant == MKB_VARIANT_REF21 && steps >= 0 && slots[id].steps != steps)
+            return fail(MKB_ERR_INVALID, "dit: batched ref21 slots must be at the same step");
+        S = slots[id].S;
+        steps = slots[id].steps;
+    }
+    const int N = gh * gw;
+    const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
+    const int first = q1 ? 1 : (steps == 0);
+    const int L = S + N, T = q1 ? L : (first ? L : N), split = q1 ? S : (first ? S : 0);
+    Plan* plan = nullptr;
+    MKB_TRY(upload_rope(S, s));
+    MKB_TRY(build_plan(B, S, N, first, &plan));
+    const int per = q1 ? op::kQ1PerBlock : op::kR21PerBlock;
+    GemmOp* g = plan->ops.data() + size_t(NB) * per;
+
+    // Time path: sinusoid -> lin1 -> silu -> lin2 (temb) -> silu -> modulations (qwen_image.cpp:179-205).
+    const int R = q1 ? B : 2 * B;  // ref21: rows (sigma, 0) per sample
+    std::vector<float> sv(R);
+    for (int b = 0; b < B; ++b) {
+        if (q1)
+            sv[b] = sigmas[b];
+        else {
+            sv[2 * b] = sigmas[b];
+            sv[2 * b + 1] = 0.0f;
+        }
+    }
+    MKB_K(cudaMemcpyAsync(sig, sv.data(), R * 4, cudaMemcpyHostToDevice, s), "sigma upload");
+    MKB_K(timestep_sinusoid(sig, tp, R, s), "sinusoid");
+    MKB_K(gemv(M("time.lin1.w"), tp, kTimeDim, V("time.lin1.b"), h1, D, R, D, kTimeDim, kActSilu, s), "time lin1");
+    MKB_K(gemv(M("time.lin2.w"), h1, D, V("time.lin2.b"), temb, D, R, D, D, kActNone, s), "time lin2");
+    MKB_TRY(emit("temb", -1, temb, long(R) * D, s));
+    MKB_K(silu_f32(temb, st, size_t(R) * D, s), "silu");
+    if (q1) {
+        const int Nm = NB * 12 * D;
+        MKB_K(gemv(wmat, st, D, wvec, mod, Nm, B, Nm, D, kActNone, s), "modulation");
+        MKB_K(gemv(M("norm_out.w"), st, D, V("norm_out.b"), omod, 2 * D, B, 2 * D, D, kActNone, s), "norm_out mod");
+    } else {
+        MKB_K(gemv(M("mod.w"), st, D, nullptr, mod, 4 * D, R, 4 * D, D, kActNone, s), "modulation");
+        MKB_TRY(emit("modulation", -1, mod, long(R) * 4 * D, s));
+        MKB_K(gemv(M("norm_out.w"), st, D, nullptr, omod, D, R, D, D, kActNone, s), "norm_out mod");
+    }
+
+    // Inputs: text rows (every step for qwen1, the first for ref21) and image rows.
+    if (first) {
+        RmsArgs ra{};
+        for (int b = 0; b < B; ++b)
+            ra.src[b] = slots[slot_ids[b]].prompt;
+        ra.y = txt_bf;
+        ra.w = V("txt_norm.w");
+        ra.samples = B;
+        ra.rows_per_sample = S;
+        ra.C = TD;
+        ra.eps = kEps;
+        MKB_K(rms_norm_rows(ra, s), "txt_norm");
+        if (q1) {
+            MKB_K(gemm_launch(g[op::kTxtIn], s), "txt_in");
+            MKB_TRY(emit("txt_in", -1, x_txt, long(B) * S * D, s));
+        } else {
+            MKB_K(gemm_launch(g[op::kTxtIn1], s), "txt_in1");
+            for (int b = 0; b < B; ++b)
+                MKB_K(gemm_launch(plan->per_sample[2 * b], s), "txt_in2");
+        }
+    }
+    MKB_K(cast_f32_bf16(lat, lat_bf, size_t(B) * N * kLatent, s), "latents cast");
+    if (q1) {
+        MKB_K(gemm_launch(g[op::kImgIn], s), "img_in");
+        MKB_TRY(emit("img_in", -1, x_img, long(B) * N * D, s));
+    } else {
+        for (int b = 0; b < B; ++b)
+            MKB_K(gemm_launch(plan->per_sample[2 * b + 1], s), "img_in");
+        MKB_TRY(emit("x_in", -1, x_img, long(B) * T * D, s));
+    }
+
+    for (int i = 0; i < NB; ++i) {
+        GemmOp* o = plan->ops.data() + size_t(i) * per;
+        if (q1) {
+            const int Mt = B * S, Mi = B * N;
+            const long mstride = long(NB) * 12 * D;
+            for (int sidx = 0; sidx < 2; ++sidx) {  // 0 txt, 1 img
+                const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
+                LnModArgs la{};
+                la.x = sidx == 0 ? x_txt : x_img;
+                la.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
+                la.scale = mb + D;
+                la.shift = mb;
+                la.mod_stride = mstride;
+                la.rows = sidx == 0 ? Mt : Mi;
+                la.D = D;
+                la.rows_per_sample = sidx == 0 ? S : N;
+                la.eps = kEps;
+                MKB_K(ln_modulate(la, s), "ln_modulate 1");
+                MKB_K(gemm_launch(o[0 + sidx], s), "qkv");
+            }
+            MKB_K(attn_launch(plan->att, s), "attention");
+            for (int sidx = 0; sidx < 2; ++sidx) {
+                const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
+                MKB_K(gemm_launch(o[2 + sidx], s), "o proj");
+                LnModArgs la{};
+                la.x = sidx == 0 ? x_txt : x_img;
+                la.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
+                la.scale = mb + 4 * D;
+                la.shift = mb + 3 * D;
+                la.mod_stride = mstride;
+                la.rows = sidx == 0 ? Mt : Mi;
+                la.D = D;
+                la.rows_per_sample = sidx == 0 ? S : N;
+                la.eps = kEps;
+                MKB_K(ln_modulate(la, s), "ln_modulate 2");
+                MKB_K(gemm_launch(o[4 + sidx], s), "ff1");
+                MKB_K(gemm_launch(o[6 + sidx], s), "ff2");
+            }
+            if (probe) {
+                MKB_TRY(emit("block.txt", i, x_txt, long(Mt) * D, s));
+                MKB_TRY(emit("block.img", i, x_img, long(Mi) * D, s));
+            }
+        } else {
+            const int Mr = B * T;
+            LnModArgs la{};
+            la.x = x_img;
+            la.y = xn;
+            la.scale = mod;
+            la.shift = nullptr;
+            la.mod_stride = 8L * D;
+            la.alt_off = 4L * D;
+            la.split = split;
+            la.rows = Mr;
+            la.D = D;
+            la.rows_per_sample = T;
+            la.eps = kEps;
+            MKB_K(ln_modulate(la, s), "ln_modulate 1");
+            MKB_K(gemm_launch(o[0], s), "qkv");
+            for (int b = 0; b < B; ++b) {
+                auto& sl = slots[slot_ids[b]];
+                const size_t hoff = size_t(b) * H * L * kHeadDim;
+                if (first) {  // keep the text's keys and values (qwen_image.cpp:251-257)
+                    MKB_K(copy_head_rows(kh + hoff, L, 0, sl.kc[i], S, 0, H, S, s), "kv save");
+                    MKB_K(copy_head_rows(vh + hoff, L, 0, sl.vc[i], S, 0, H, S, s), "kv save");
+                } else {  // restore them (qwen_image.cpp:258-262)
+                    MKB_K(copy_head_rows(sl.kc[i], S, 0, kh + hoff, L, 0, H, S, s), "kv restore");
+                    MKB_K(copy_head_rows(sl.vc[i], S, 0, vh + hoff, L, 0, H, S, s), "kv restore");
+                }
+            }
+            MKB_K(attn_launch(plan->att, s), "attention");
+            MKB_K(gemm_launch(o[1], s), "o proj");
+            la.scale = mod + 2 * D;
+            MKB_K(ln_modulate(la, s), "ln_modulate 2");
+            MKB_K(gemm_launch(o[2], s), "gate_up");
+            MKB_K(gemm_launch(o[3], s), "down");
+            MKB_TRY(emit("block", i, x_img, long(Mr) * D, s));
+        }
+    }
+
+    // norm_out + proj_out (qwen_image.cpp:285-288).
+    LnModArgs la{};
+    la.D = D;
+    la.eps = kEps;
+    if (q1) {
+        la.x = x_img;
+        la.y = xn + size_t(B) * S * D;
+        la.scale = omod;
+        la.shift = omod + D;
+        la.mod_stride = 2L * D;
+        la.rows = B * N;
+        la.rows_per_sample = N;
+        MKB_K(ln_modulate(la, s), "norm_out");
+    } else {
+        la.x = x_img;
+        la.y = xn;
+        la.scale = omod;
+        la.mod_stride = 2L * D;
+        la.alt_off = D;
+        la.split = split;
+        la.rows = B * T;
+        la.rows_per_sample = T;
+        MKB_K(ln_modulate(la, s), "norm_out");
+    }
+    MKB_K(gemm_launch(g[op::kProjOut], s), "proj_out");
+    if (!q1)
+        for (int b = 0; b < B; ++b)
+            slots[slot_ids[b]].steps++;
+    if (first_out)
+        *first_out = first;
+    return MKB_OK;
+}
+
+}  // namespace mkb
+
+struct mkb_dit {
+    mkb::DitImpl impl;
+};
+
+using namespace mkb;
+
+namespace {
+
+mkb_status check_handle(const mkb_dit* d)
+{
+    return d ? MKB_OK : fail(MKB_ERR_INVALID, "dit: null handle");
+}
+
+// Copies the image rows' velocities of B samples from vel to out_dev (device) on stream s.
+mkb_status gather_velocity(DitImpl& m, int B, int S, bool first, float* out, cudaMemcpyKind kind, cudaStream_t s)
+{
+    const int N = m.gh * m.gw;
+    const bool q1 = m.cfg.variant == MKB_VARIANT_QWEN1;
+    const int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
+    MKB_TRY_CUDA(cudaMemcpy2DAsync(out, size_t(N) * kLatent * 4, m.vel + size_t(split) * kLatent,
+                                   size_t(T) * kLatent * 4, size_t(N) * kLatent * 4, B, kind, s),
+                 "velocity copy");
+    return MKB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mkb_status mkb_dit_create(const mkb_dit_config* cfg, mkb_dit** out)
+{
+    if (!cfg || !out)
+        return fail(MKB_ERR_INVALID, "dit_create: null argument");
+    auto* d = new (std::nothrow) mkb_dit;
+    if (!d)
+        return fail(MKB_ERR_ALLOC, "dit_create: host allocation");
+    mkb_status s = d->impl.create(*cfg);
+    if (s != MKB_OK) {
+        delete d;
+        return s;
+    }
+    *out = d;
+    return MKB_OK;
+}
+
+void mkb_dit_destroy(mkb_dit* d)
+{
+    if (d) {
+        cudaStreamSynchronize(d->impl.stream);
+        delete d;
+    }
+}
+
+mkb_status mkb_dit_init_random(mkb_dit* d, uint64_t seed, float std)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    for (size_t i = 0; i < m.weights.size(); ++i) {
+        const Weight& w = m.weights[i];
+        const uint64_t key = splitmix64_host(seed * 0x100000001B3ull + i);
+        const float sd = w.norm ? 0.1f : std, mean = w.norm ? 1.0f : 0.0f;
+        if (w.cols)
+            MKB_TRY_CUDA(fill_normal(m.wmat + w.off, true, w.count(), key, 0, sd, mean, m.stream), "init");
+        else
+            MKB_TRY_CUDA(fill_normal(m.wvec + w.off, false, w.count(), key, 0, sd, mean, m.stream), "init");
+    }
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "init sync");
+    return MKB_OK;
+}
+
+int mkb_dit_weight_count(const mkb_dit* d) { return d ? int(d->impl.weights.size()) : 0; }
+
+mkb_status mkb_dit_weight_info(const mkb_dit* d, int i, const char** name, long* rows, long* cols)
+{
+    MKB_TRY(check_handle(d));
+    if (i < 0 || i >= int(d->impl.weights.size()))
+        return fail(MKB_ERR_INVALID, "weight_info: index out of range");
+    const Weight& w = d->impl.weights[i];
+    if (name)
+        *name = w.name.c_str();
+    if (rows)
+        *rows = w.rows;
+    if (cols)
+        *cols = w.cols;
+    return MKB_OK;
+}
+
+namespace {
+
+// Device row of reference row r of a gate/up matrix [gate F rows; up F rows], interleaved in blocks of kSwigluBlock.
+long swiglu_row(long r, long F)
+{
+    const bool up = r >= F;
+    const long j = up ? r - F : r;
+    return (j / kSwigluBlock) * 2 * kSwigluBlock + (up ? kSwigluBlock : 0) + j % kSwigluBlock;
+}
+
+}  // namespace
+
+mkb_status mkb_dit_weight_read(mkb_dit* d, const char* name, float* host)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    const Weight* w = name ? m.find(name) : nullptr;
+    if (!w || !host)
+        return fail(MKB_ERR_INVALID, std::string("weight_read: unknown weight ") + (name ? name : "(null)"));
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "sync");
+    if (!w->cols) {
+        MKB_TRY_CUDA(cudaMemcpy(host, m.wvec + w->off, w->count() * 4, cudaMemcpyDeviceToHost), "weight read");
+        return MKB_OK;
+    }
+    std::vector<__nv_bfloat16> tmp(w->count());
+    MKB_TRY_CUDA(cudaMemcpy(tmp.data(), m.wmat + w->off, w->count() * 2, cudaMemcpyDeviceToHost), "weight read");
+    for (long r = 0; r < w->rows; ++r) {
+        const long dr = w->swiglu ? swiglu_row(r, w->rows / 2) : r;
+        for (long c = 0; c < w->cols; ++c)
+            host[r * w->cols + c] = __bfloat162float(tmp[size_t(dr) * w->cols + c]);
+    }
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_weight_write(mkb_dit* d, const char* name, const float* host)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    const Weight* w = name ? m.find(name) : nullptr;
+    if (!w || !host)
+        return fail(MKB_ERR_INVALID, std::string("weight_write: unknown weight ") + (name ? name : "(null)"));
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "sync");
+    if (!w->cols) {
+        MKB_TRY_CUDA(cudaMemcpy(m.wvec + w->off, host, w->count() * 4, cudaMemcpyHostToDevice), "weight write");
+        return MKB_OK;
+    }
+    std::vector<__nv_bfloat16> tmp(w->count());
+    for (long r = 0; r < w->rows; ++r) {
+        const long dr = w->swiglu ? swiglu_row(r, w->rows / 2) : r;
+        for (long c = 0; c < w->cols; ++c)
+            tmp[size_t(dr) * w->cols + c] = __float2bfloat16_rn(host[r * w->cols + c]);
+    }
+    MKB_TRY_CUDA(cudaMemcpy(m.wmat + w->off, tmp.data(), w->count() * 2, cudaMemcpyHostToDevice), "weight write");
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_begin(mkb_dit* d, const float* prompt, int S, int h, int w, int slot)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    if (slot < 0 || slot >= int(m.slots.size()))
+        return fail(MKB_ERR_INVALID, "begin: slot out of range");
+    if (!prompt || S < 1 || S > m.Smax)
+        return fail(MKB_ERR_INVALID, "begin: prompt embeddings must be 1..max_text_tokens rows");
+    if (h < 1 || w < 1 || long(h) * w > m.Nmax)
+        return fail(MKB_ERR_INVALID, "begin: h * w must be 1..max_image_tokens");
+    auto& sl = m.slots[slot];
+    MKB_TRY_CUDA(cudaMemcpyAsync(sl.prompt, prompt, size_t(S) * m.TD * 4, cudaMemcpyHostToDevice, m.stream),
+                 "prompt upload");
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "prompt upload");
+    sl.S = S;
+    sl.steps = 0;
+    sl.begun = true;
+    m.gh = h;
+    m.gw = w;
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_step_batch_dev(mkb_dit* d, int n, const int* slots, const float* latents_dev, const float* sigmas,
+                                  float* out_dev, void* stream)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    if (n < 1 || n > m.Bmax || !slots || !latents_dev || !sigmas || !out_dev)
+        return fail(MKB_ERR_INVALID, "step: bad arguments");
+    if (m.gh * m.gw == 0)
+        return fail(MKB_ERR_STATE, "step before begin");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+    const int N = m.gh * m.gw;
+    MKB_TRY_CUDA(cudaMemcpyAsync(m.lat, latents_dev, size_t(n) * N * kLatent * 4, cudaMemcpyDeviceToDevice, s),
+                 "latents");
+    bool first = false;
+    const int S = m.slots[slots[0]].S;
+    MKB_TRY(m.run(n, slots, sigmas, s, &first));
+    return gather_velocity(m, n, S, first, out_dev, cudaMemcpyDeviceToDevice, s);
+}
+
+mkb_status mkb_dit_step_batch(mkb_dit* d, int n, const int* slots, const float* latents, const float* sigmas,
+                              float* out)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    if (n < 1 || n > m.Bmax || !slots || !latents || !sigmas || !out)
+        return fail(MKB_ERR_INVALID, "step: bad arguments");
+    if (m.gh * m.gw == 0)
+        return fail(MKB_ERR_STATE, "step before begin");
+    const int N = m.gh * m.gw;
+    for (int i = 0; i < n; ++i)
+        if (slots[i] < 0 || slots[i] >= int(m.slots.size()) || !m.slots[slots[i]].begun)
+            return fail(MKB_ERR_STATE, "step on a slot without begin");
+    MKB_TRY_CUDA(cudaMemcpyAsync(m.lat, latents, size_t(n) * N * kLatent * 4, cudaMemcpyHostToDevice, m.stream),
+                 "latents upload");
+    bool first = false;
+    const int S = m.slots[slots[0]].S;
+    MKB_TRY(m.run(n, slots, sigmas, m.stream, &first));
+    MKB_TRY(gather_velocity(m, n, S, first, out, cudaMemcpyDeviceToHost, m.stream));
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "step sync");
+    return m.check_status();
+}
+
+mkb_status mkb_dit_step(mkb_dit* d, const float* latents, float sigma, float* out, int slot)
+{
+    return mkb_dit_step_batch(d, 1, &slot, latents, &sigma, out);
+}
+
+mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, float sigma, float sigma_next,
+                                float guidance, void* stream)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    const int B = 2 * n_images;
+    if (n_images < 1 || B > m.Bmax || int(m.slots.size()) < B || !latents_dev)
+        return fail(MKB_ERR_INVALID, "step_cfg: need 2 * n_images <= max_batch and as many slots");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+    const int N = m.gh * m.gw;
+    const size_t img = size_t(N) * kLatent;
+    std::vector<int> ids(B);
+    std::vector<float> sg(B, sigma);
+    for (int i = 0; i < B; ++i)
+        ids[i] = i;
+    // Both predictions of image i see the same latents.
+    for (int i = 0; i < n_images; ++i)
+        for (int k = 0; k < 2; ++k)
+            MKB_TRY_CUDA(cudaMemcpyAsync(m.lat + (2 * i + k) * img, latents_dev + i * img, img * 4,
+                                         cudaMemcpyDeviceToDevice, s),
+                         "latents");
+    bool first = false;
+    MKB_TRY(m.run(B, ids.data(), sg.data(), s, &first));
+    const int S = m.slots[0].S;
+    const bool q1 = m.cfg.variant == MKB_VARIANT_QWEN1;
+    const int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
+    for (int i = 0; i < n_images; ++i) {
+        const float* vc = m.vel + (size_t(2 * i) * T + split) * kLatent;
+        const float* vu = m.vel + (size_t(2 * i + 1) * T + split) * kLatent;
+        MKB_TRY_CUDA(cfg_euler(latents_dev + i * img, vc, vu, guidance, sigma_next - sigma, img, s), "cfg euler");
+    }
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_step_cfg(mkb_dit* d, float* latents, float sigma, float sigma_next, float guidance)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    if (!latents)
+        return fail(MKB_ERR_INVALID, "step_cfg: null latents");
+    const size_t img = size_t(m.gh) * m.gw * kLatent;
+    float* dev = m.cfg_lat;
+    mkb_status st = MKB_OK;
+    if (cudaMemcpyAsync(dev, latents, img * 4, cudaMemcpyHostToDevice, m.stream) != cudaSuccess)
+        st = fail(MKB_ERR_CUDA, "step_cfg: latents upload");
+    if (st == MKB_OK)
+        st = mkb_dit_step_cfg_dev(d, 1, dev, sigma, sigma_next, guidance, m.stream);
+    if (st == MKB_OK && cudaMemcpyAsync(latents, dev, img * 4, cudaMemcpyDeviceToHost, m.stream) != cudaSuccess)
+        st = fail(MKB_ERR_CUDA, "step_cfg: latents download");
+    if (cudaStreamSynchronize(m.stream) != cudaSuccess && st == MKB_OK)
+        st = fail(MKB_ERR_CUDA, "step_cfg: sync");
+    if (st == MKB_OK)
+        st = m.check_status();
+    return st;
+}
+
+mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user)
+{
+    MKB_TRY(check_handle(d));
+    d->impl.probe = fn;
+    d->impl.probe_user = user;
+    return MKB_OK;
+}
+
+double mkb_dit_step_flops(const mkb_dit* d, int n, int first_step)
+{
+    if (!d)
+        return 0;
+    const DitImpl& m = d->impl;
+    const double D = m.D, F = m.F, N = double(m.gh) * m.gw;
+    double S = 0;
+    for (const auto& s : m.slots)
+        if (s.begun) {
+            S = s.S;
+            break;
+        }
+    const double L = S + N;
+    double per;
+    if (m.cfg.variant == MKB_VARIANT_QWEN1) {
+        per = m.NB * (2 * L * (4 * D * D + 2 * D * F) + 4 * L * L * D);
+        per += 2 * S * m.TD * D + 2 * N * 64 * D + 2 * N * D * 64;
+    } else {
+        const double rows = first_step ? L : N;
+        const double att = first_step ? 4 * D * (S * S + N * L) : 4 * D * N * L;
+        per = m.NB * (2 * rows * (4 * D * D + 3 * D * F) + att);
+        per += (first_step ? 2 * S * (m.TD * D + D * D) : 0) + 2 * N * 64 * D + 2 * rows * D * 64;
+    }
+    return per * n;
+}
+
+}  // extern "C"

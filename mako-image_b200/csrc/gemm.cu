@@ -124,7 +124,9 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
                     d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             } else {
                 const int bsample = row / a.seg_rows;
-                const float4* g4 = reinterpret_cast<const float4*>(a.gate + long(bsample) * a.gate_bstride + col0);
+                const int within = row - bsample * a.seg_rows;
+                const float4* g4 = reinterpret_cast<const float4*>(
+                    a.gate + long(bsample) * a.gate_bstride + (within < a.gate_split ? a.gate_alt_off : 0) + col0);
                 float4* x4 = reinterpret_cast<float4*>(a.resid + long(row) * a.ldr + col0);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {

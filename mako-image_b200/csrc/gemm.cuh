@@ -36,6 +36,8 @@ struct GemmArgs {
     const float* gate = nullptr;  // gate of sample b at gate + b * gate_bstride
     long gate_bstride = 0;
     int tanh_gate = 0;            // x += tanh(g) * y (the reference's gate_add) instead of x += g * y
+    int gate_split = 0;           // rows whose index within their sample is < gate_split use gate + gate_alt_off
+    long gate_alt_off = 0;        //   (the reference's text rows take modulation row 1)
     // rows -> (sample, position): sample = row / seg_rows, position = seg_off + row % seg_rows
     int seg_rows = 1 << 30;
     int seg_off = 0;

@@ -5,3 +5,4 @@ buffers are passed as raw pointers (for example ``tensor.data_ptr()`` of a torch
 
 from ._lib import lib, MkbError, check, LIB_PATH, stream_ptr  # noqa: F401
 from . import ops  # noqa: F401
+from .dit import Dit, DitConfig, QWEN1, REF21  # noqa: F401

@@ -22,6 +22,21 @@ _SIGS = {
     "mkb_proj_swiglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
     "mkb_swiglu_interleave": (_i, []),
     "mkb_check_kernels": (_i, [_u32p]),
+    "mkb_dit_create": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "mkb_dit_destroy": (None, [_vp]),
+    "mkb_dit_init_random": (_i, [_vp, _u64, _f]),
+    "mkb_dit_weight_count": (_i, [_vp]),
+    "mkb_dit_weight_info": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_l), ctypes.POINTER(_l)]),
+    "mkb_dit_weight_read": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_dit_weight_write": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_dit_begin": (_i, [_vp, _vp, _i, _i, _i, _i]),
+    "mkb_dit_step": (_i, [_vp, _vp, _f, _vp, _i]),
+    "mkb_dit_step_batch": (_i, [_vp, _i, _vp, _vp, _vp, _vp]),
+    "mkb_dit_step_batch_dev": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp]),
+    "mkb_dit_step_cfg": (_i, [_vp, _vp, _f, _f, _f]),
+    "mkb_dit_step_cfg_dev": (_i, [_vp, _i, _vp, _f, _f, _f, _vp]),
+    "mkb_dit_set_probe": (_i, [_vp, _vp, _vp]),
+    "mkb_dit_step_flops": (ctypes.c_double, [_vp, _i, _i]),
     "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
 }
 
