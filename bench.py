@@ -1,0 +1,344 @@
+"""Benchmark of the B200 denoiser hot path: Qwen-Image-shape MMDiT denoising steps per second.
+
+Default: the full 60-block Qwen-Image-shape MMDiT (hidden 3072, 24 heads x 128, FFN 12288
+GELU, text 3584 -> 3072) at 1024^2 (4096 image + 256 text tokens), CFG batch 2 (cond / uncond in one pass), the
+Euler update fused on the device. One "step" = one guided denoising step of one image. Weights are random bf16
+N(0, 0.02) generated on the device by seed; prompt and latents are seeded synthetic normals.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl mkb|reference] [--config 1|2|5]
+
+Under torchrun (N > 1) every rank runs its own image on its own GPU (weak scaling: CFG pairs are independent, no
+collective on the data path); value = images*steps over the max-over-ranks device time.
+
+--impl reference times the reference's math on the host CPU cores instead: the oracle port (oracle/qwen_dit.py,
+numpy/BLAS) on a bounded sample (one block of one sample, scaled to the full step), since the reference's own
+implementation (Metal) cannot run here.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mako-image_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "Qwen-Image-shape DiT steps/s at 1024^2 (CFG batch 2, Euler fused)"
+UNIT = "steps/s"
+
+CONFIGS = {
+    # name: (grid h, grid w, text tokens, images, blocks)
+    1: dict(h=32, w=32, S=128, images=1, blocks=1, cfg=False,
+            workload="qwen1 MMDiT, 1 block, 1024 image + 128 text tokens, batch 1 (BASELINE configs[0])"),
+    2: dict(h=64, w=64, S=256, images=1, blocks=60, cfg=True,
+            workload="qwen1 MMDiT, 60 blocks, 1024^2 (4096 image + 256 text tokens), CFG batch 2, Euler fused "
+                     "(BASELINE configs[1])"),
+    5: dict(h=128, w=128, S=1024, images=4, blocks=60, cfg=True,
+            workload="qwen1 MMDiT, 60 blocks, 2048^2 (16384 image + 1024 text tokens), CFG batch 2 x 4 images "
+                     "(BASELINE configs[4]) on one GPU per rank"),
+}
+D, H, F, TD = 3072, 24, 12288, 3584
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+_CPU_CACHE = {}
+
+
+def cpu_baseline(cfg, reps=1):
+    """The oracle port (numpy; BLAS threads on the host cores) on a bounded sample: one qwen1 block of one sample at
+    the config's shape. Returns seconds per full step (scaled by blocks x samples) and the sample description."""
+    import numpy as np
+    from oracle import qwen_dit as QD
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    h, w, S = cfg["h"], cfg["w"], cfg["S"]
+    N = h * w
+    oc = QD.default_cfg("qwen1", D, H, F, 1, TD)
+    r = np.random.default_rng(0)
+    if "W" not in _CPU_CACHE:
+        W = {}
+        for name, shape in QD.weight_shapes(oc).items():
+            if name.endswith(("norm_q", "norm_k", "txt_norm.w")):
+                W[name] = np.ones(shape, np.float32)
+            else:
+                W[name] = (r.standard_normal(shape, dtype=np.float32) * 0.02)
+        _CPU_CACHE["W"] = W
+    W = _CPU_CACHE["W"]
+    prompt = r.standard_normal((S, TD), dtype=np.float32)
+    lat = r.standard_normal((N, 64), dtype=np.float32)
+    # time the block alone (the step's inputs prepared outside the timed region)
+    st = np.ones(D, np.float32) * 0.1
+    rope = QD.rope_table(oc, S, h, w)
+    x_txt = QD.text_in(oc, W, prompt)
+    x_img = lat @ W["img_in.w"].T
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        QD.block_qwen1(oc, W, 0, x_txt, x_img, st, rope)
+        times.append(time.perf_counter() - t0)
+    t_block = min(times)
+    samples = cfg["images"] * (2 if cfg["cfg"] else 1)
+    t_step = t_block * cfg["blocks"] * samples
+    sample = (f"one qwen1 block of one sample ({N} image + {S} text tokens), {t_block:.2f} s, scaled x "
+              f"{cfg['blocks']} blocks x {samples} samples (extrapolated from 1 block)")
+    return t_step, cores, sample
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(cfg)
+    secs = []
+    for _ in range(args.steps):
+        t, cores, sample = cpu_baseline(cfg)
+        secs.append(t)
+    t_step = statistics.mean(secs)
+    v = 1.0 / t_step
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["workload"], "impl_detail": "oracle port (numpy + BLAS) on host cores"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_mkb(args, cfg):
+    import numpy as np
+    import torch
+    import mkimage
+    from oracle import rng
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    h, w, S, n_img = cfg["h"], cfg["w"], cfg["S"], cfg["images"]
+    N = h * w
+    B = n_img * (2 if cfg["cfg"] else 1)
+    d = mkimage.Dit(mkimage.DitConfig(variant=mkimage.QWEN1, hidden=D, heads=H, ffn=F, blocks=cfg["blocks"],
+                                      text_dim=TD, max_batch=B, max_text_tokens=S, max_image_tokens=N, slots=B))
+    d.init_random(seed=1234)
+    for s in range(B):
+        prompt = rng.normal(rng.tensor_key(99, s), S * TD).reshape(S, TD)
+        d.begin(prompt, h, w, slot=s)
+    lat_host = rng.normal(rng.tensor_key(98, rank), n_img * N * 64).reshape(n_img, N, 64)
+    lat = torch.from_numpy(lat_host).to(dev)
+    sig = mkimage.sigmas(40, N)
+    i0 = int(np.argmin(np.abs(sig[:-1] - 0.5)))
+    sigma, sigma_next = float(sig[i0]), float(sig[i0 + 1])
+    stream = torch.cuda.current_stream(dev)
+    sp = mkimage.stream_ptr(stream)
+
+    def one_step():
+        if cfg["cfg"]:
+            d.step_cfg_dev(n_img, lat.data_ptr(), sigma, sigma_next, 4.0, sp)
+        else:
+            out = torch.empty_like(lat)
+            d.step_batch_dev([0], lat.data_ptr(), [sigma], out.data_ptr(), sp)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    launches0 = mkimage.lib.mkb_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            one_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = mkimage.lib.mkb_kernel_launches() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    mkimage.ops.check_kernels()
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+        torch.distributed.barrier()
+    value = n_img * ws * 1e3 / ms
+    flops_step = d.step_flops(B)
+
+    # End to end through the public host-buffer API: pinned latents in, updated latents out, every step.
+    e2e = None
+    if cfg["cfg"] and n_img == 1:
+        pinned = torch.from_numpy(lat_host[0].copy()).pin_memory()
+        guided = d.step_cfg_inplace(pinned.numpy())  # H2D from and D2H into the pinned buffer every step
+        for _ in range(2):
+            guided(sigma, sigma_next, 4.0)
+        if ws > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            guided(sigma, sigma_next, 4.0)
+        t_e2e = (time.perf_counter() - t0) / args.steps
+        if ws > 1:
+            t = torch.tensor([t_e2e], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            t_e2e = t.item()
+        e2e = {"value": n_img * ws / t_e2e, "unit": UNIT, "h2d_bytes_per_step": N * 64 * 4,
+               "d2h_bytes_per_step": N * 64 * 4}
+
+    # Roofline of the dominant kernel: the tcgen05 GEMM at the step's FFN-up shape (the largest GEMM, GELU
+    # epilogue), timed alone on the same stream with CUDA events.
+    peak_tf, peak_hbm, peak_kind = _peaks()
+    M_img = B * N
+    xa = torch.randn(M_img, D, device=dev).to(torch.bfloat16)
+    wa = (torch.randn(F, D, device=dev) * 0.02).to(torch.bfloat16)
+    ba = torch.zeros(F, device=dev)
+    ya = torch.empty(M_img, F, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        mkimage.ops.proj(xa, wa, ba, act=mkimage.ops.ACT_GELU_TANH, out=ya)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    g0.record(stream)
+    for _ in range(reps):
+        mkimage.ops.proj(xa, wa, ba, act=mkimage.ops.ACT_GELU_TANH, out=ya)
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = g0.elapsed_time(g1) / reps
+    gemm_flops = 2.0 * M_img * F * D
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemm_ffn_up_config2.md")) as f:
+            for ln in f:
+                if ln.startswith("dram_bytes_per_launch:"):
+                    traffic = float(ln.split(":")[1])
+    except Exception:
+        pass
+    roofline = {"bound": "tensor", "kernel": "k_gemm (tcgen05, FFN-up 8192x12288x3072, GELU epilogue)",
+                "achieved": achieved, "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                "frac": achieved / peak_tf, "traffic": traffic,
+                "step_tflops": flops_step / (ms * 1e-3) / 1e12 / max(1, 1),
+                "step_frac": flops_step / (ms * 1e-3) / 1e12 / peak_tf}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        t_step, cores, sample = cpu_baseline(cfg)
+        cpu = {"value": n_img / t_step, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfg["workload"], "hidden": D, "heads": H, "ffn": F, "blocks": cfg["blocks"],
+                           "image_tokens": N, "text_tokens": S, "samples_per_gpu": B,
+                           "parallelism": f"replicas x{ws} (one image per GPU, CFG pair batched)",
+                           "l2": "inputs larger than L2 (40.8 GB of weights streamed per step)",
+                           "step_tflop": flops_step / 1e12},
+                "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+                "gpu_launches": int(launches)}
+        print(json.dumps(line), flush=True)
+    d.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_mkb(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -35,6 +35,9 @@ typedef enum mkb_status {
 /* The message of the last error on this thread ("" if none). */
 const char* mkb_last_error(void);
 
+/* Kernel launches this library has made in this process (all threads, all devices). */
+uint64_t mkb_kernel_launches(void);
+
 /* Activations a projection epilogue can apply. */
 enum { MKB_ACT_NONE = 0, MKB_ACT_GELU_TANH = 1, MKB_ACT_SILU = 2 };
 
@@ -166,6 +169,46 @@ mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user);
 
 /* Algorithmic FLOPs of one step over n samples at the current grid and prompt length (GEMMs + attention). */
 double mkb_dit_step_flops(const mkb_dit* d, int n, int first_step);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Schedule and samplers of the generation loop (host code; Engine::sigmas / generate, src/image/engine.cpp:335-506,
+ * and image::ErSde, src/image/er_sde.hpp:12-27).
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* The flow-matching schedule's shift (Engine::Schedule, src/image/engine.hpp:251-256). */
+typedef struct mkb_schedule {
+    double base_seq, max_seq, base_shift, max_shift, terminal;
+    int fixed_mu; /* nonzero: use mu instead of the token-count shift (distilled models) */
+    double mu;
+} mkb_schedule;
+
+/* The reference's defaults: base 256 -> 0.5, max 4096 -> 1.15, no terminal stretch. */
+void mkb_schedule_default(mkb_schedule* s);
+
+/* Engine::sigmas (engine.cpp:347-365): steps noise levels for `tokens` latent tokens, then 0; out has steps + 1
+ * entries. sched NULL: the defaults. */
+mkb_status mkb_sigmas(const mkb_schedule* sched, uint32_t steps, uint32_t tokens, float* out);
+
+/* Engine::top_sigma (engine.cpp:341-345): where ER-SDE starts for a flow model instead of 1. */
+float mkb_top_sigma(const mkb_schedule* sched, uint32_t tokens);
+
+/* x += (sigma_next - sigma) * (v_u + guidance * (v_c - v_u)) on host arrays of n floats (v_uncond NULL: no
+ * guidance): the guided Euler update of engine.cpp:475-480, 500-503. */
+void mkb_guided_euler(float* x, const float* v_cond, const float* v_uncond, float guidance, float sigma,
+                      float sigma_next, long n);
+
+/* ER-SDE (image::ErSde): the three-stage extended reverse-time SDE solver. */
+typedef struct mkb_er_sde mkb_er_sde;
+/* sigmas: the schedule ending at 0 (n entries); flow: latents are (1 - s) image + s noise; top: a flow model's
+ * first level in place of 1 (ErSde::ErSde, er_sde.cpp:17-25). */
+mkb_status mkb_er_sde_create(const float* sigmas, int n, int flow, float top, mkb_er_sde** out);
+void mkb_er_sde_destroy(mkb_er_sde* e);
+/* The level step i runs the model at (ErSde::sigma). */
+float mkb_er_sde_sigma(const mkb_er_sde* e, int i);
+/* x (n floats) from level i to i + 1 given the model's image estimate `denoised` and unit-normal noise scaled by
+ * s_noise (ErSde::step, er_sde.cpp:27-74). */
+mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised, const float* noise, long n,
+                           float s_noise);
 
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */

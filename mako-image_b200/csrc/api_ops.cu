@@ -5,6 +5,7 @@
 #include "gemm.cuh"
 #include "sm100.cuh"
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -13,9 +14,12 @@ namespace mkb {
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<unsigned long long> g_launches{0};
 std::mutex g_status_mu;
 std::vector<uint32_t*> g_status_words;  // per device
 }  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 mkb_status fail(mkb_status code, const std::string& msg)
 {
@@ -82,6 +86,8 @@ using namespace mkb;
 extern "C" {
 
 const char* mkb_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t mkb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 mkb_status mkb_proj(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy, int M,
                     int N, int K, int act, int out_f32, void* stream)

@@ -10,6 +10,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "sm100.cuh"
+#include "common.cuh"
 
 #include <cudaTypedefs.h>
 #include <cmath>
@@ -366,6 +367,7 @@ cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
         attr = true;
     }
     k_attn<<<op.grid, kThreads, kSmem, st>>>(op.tq, op.tk, op.tv, op.args);
+    count_launch();
     return cudaGetLastError();
 }
 

@@ -7,6 +7,7 @@
 // RoPE pairs, SwiGLU pairs) needs no shuffles.
 #include "gemm.cuh"
 #include "sm100.cuh"
+#include "common.cuh"
 
 #include <cudaTypedefs.h>
 #include <cstdio>
@@ -391,6 +392,7 @@ cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
         attr_set = true;
     }
     k_gemm<BN, EPI><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.ta, op.tb, op.args);
+    count_launch();
     return cudaGetLastError();
 }
 

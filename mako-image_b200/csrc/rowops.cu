@@ -1,5 +1,6 @@
 // Row and element kernels (see rowops.cuh).
 #include "rowops.cuh"
+#include "common.cuh"
 
 #include <cstdint>
 
@@ -248,6 +249,7 @@ cudaError_t ln_modulate(const LnModArgs& a, cudaStream_t st)
         k_ln_mod<24><<<blocks, 256, 0, st>>>(a);
     else
         k_ln_mod<32><<<blocks, 256, 0, st>>>(a);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -267,6 +269,7 @@ cudaError_t rms_norm_rows(const RmsArgs& a, cudaStream_t st)
         k_rms<24><<<blocks, 256, 0, st>>>(a);
     else
         k_rms<32><<<blocks, 256, 0, st>>>(a);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -303,6 +306,7 @@ cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* 
         MKB_GEMV(8)
     }
 #undef MKB_GEMV
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -311,6 +315,7 @@ cudaError_t timestep_sinusoid(const float* t, float* tp, int rows, cudaStream_t 
     if (rows <= 0)
         return cudaSuccess;
     k_sinusoid<<<rows, 128, 0, st>>>(t, tp, rows);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -320,6 +325,7 @@ cudaError_t fill_normal(void* out, bool bf16, uint64_t n, uint64_t key, uint64_t
     if (!n)
         return cudaSuccess;
     k_fill_normal<<<grid_for(n, 256), 256, 0, st>>>(out, bf16 ? 1 : 0, n, key, offset, std, mean);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -328,6 +334,7 @@ cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStre
     if (!n)
         return cudaSuccess;
     k_cast<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -336,6 +343,7 @@ cudaError_t silu_f32(const float* x, float* y, uint64_t n, cudaStream_t st)
     if (!n)
         return cudaSuccess;
     k_silu<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -349,6 +357,7 @@ cudaError_t copy_head_rows(const __nv_bfloat16* src, int src_rows, int src_off, 
     const uint64_t n = uint64_t(heads) * rows * 16;
     k_copy_heads<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(src), src_rows, src_off,
                                                    reinterpret_cast<uint4*>(dst), dst_rows, dst_off, heads, rows);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -357,6 +366,7 @@ cudaError_t cfg_euler(float* x, const float* v_c, const float* v_u, float g, flo
     if (!n)
         return cudaSuccess;
     k_cfg_euler<<<grid_for(n, 256), 256, 0, st>>>(x, v_c, v_u, g, dt, n);
+    count_launch();
     return cudaGetLastError();
 }
 

@@ -16,6 +16,7 @@ _u32p = ctypes.POINTER(ctypes.c_uint32)
 
 _SIGS = {
     "mkb_last_error": (ctypes.c_char_p, []),
+    "mkb_kernel_launches": (_u64, []),
     "mkb_proj": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _i, _i, _vp]),
     "mkb_proj_gate_add": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _vp, _l, _i, _i, _i, _i, _i, _vp]),
     "mkb_proj_qkv_heads": (_i, [_vp, _l, _vp, _l, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _i, _vp]),
@@ -37,6 +38,14 @@ _SIGS = {
     "mkb_dit_step_cfg_dev": (_i, [_vp, _i, _vp, _f, _f, _f, _vp]),
     "mkb_dit_set_probe": (_i, [_vp, _vp, _vp]),
     "mkb_dit_step_flops": (ctypes.c_double, [_vp, _i, _i]),
+    "mkb_schedule_default": (None, [_vp]),
+    "mkb_sigmas": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp]),
+    "mkb_top_sigma": (_f, [_vp, ctypes.c_uint32]),
+    "mkb_guided_euler": (None, [_vp, _vp, _vp, _f, _f, _f, _l]),
+    "mkb_er_sde_create": (_i, [_vp, _i, _i, _f, ctypes.POINTER(_vp)]),
+    "mkb_er_sde_destroy": (None, [_vp]),
+    "mkb_er_sde_sigma": (_f, [_vp, _i]),
+    "mkb_er_sde_step": (_i, [_vp, _i, _vp, _vp, _vp, _l, _f]),
     "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
 }
 

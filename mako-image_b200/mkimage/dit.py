@@ -113,6 +113,14 @@ class Dit:
         check(lib.mkb_dit_step_cfg(self.h, _fptr(x), sigma, sigma_next, guidance))
         return x
 
+    def step_cfg_inplace(self, latents):
+        """step_cfg on a caller-owned C-contiguous float32 array (e.g. a pinned buffer), updated in place."""
+
+        def run(sigma, sigma_next, guidance):
+            check(lib.mkb_dit_step_cfg(self.h, _fptr(latents), sigma, sigma_next, guidance))
+
+        return run
+
     def step_cfg_dev(self, n_images, latents_dev, sigma, sigma_next, guidance, stream=None):
         check(lib.mkb_dit_step_cfg_dev(self.h, n_images, ctypes.c_void_p(latents_dev), sigma, sigma_next, guidance,
                                        stream))
