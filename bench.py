@@ -232,10 +232,12 @@ def run_mkb(args, cfg):
     launches0 = mkimage.lib.mkb_kernel_launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("mkb_timed")
         e0.record(stream)
         for _ in range(args.steps):
             one_step()
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     launches = mkimage.lib.mkb_kernel_launches() - launches0
     ms = e0.elapsed_time(e1) / args.steps
@@ -324,6 +326,50 @@ def run_mkb(args, cfg):
         torch.distributed.destroy_process_group()
 
 
+def run_kernel(args, cfg):
+    """One hot kernel alone at the config's shape, for profiling: 3 warm-up launches then 3 timed ones (CUDA
+    events). gemm: the FFN-up projection (GELU epilogue); attention: the joint flash attention of one block;
+    lnmod: the modulated LayerNorm of the image rows."""
+    import torch
+    import mkimage
+
+    dev = torch.device("cuda", 0)
+    h, w, S, n_img = cfg["h"], cfg["w"], cfg["S"], cfg["images"]
+    N = h * w
+    B = n_img * (2 if cfg["cfg"] else 1)
+    L = S + N
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "gemm":
+        x = torch.randn(B * N, D, device=dev, generator=g).to(torch.bfloat16)
+        wt = (torch.randn(F, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        b = torch.zeros(F, device=dev)
+        y = torch.empty(B * N, F, device=dev, dtype=torch.bfloat16)
+        fn = lambda: mkimage.ops.proj(x, wt, b, act=mkimage.ops.ACT_GELU_TANH, out=y)  # noqa: E731
+        work, unit = 2.0 * B * N * F * D, "TFLOP/s"
+    elif args.kernel == "attention":
+        q = torch.randn(B, H, L, 128, device=dev, generator=g).to(torch.bfloat16)
+        k, v = torch.randn_like(q), torch.randn_like(q)
+        o0 = torch.empty(B * S, D, device=dev, dtype=torch.bfloat16)
+        o1 = torch.empty(B * N, D, device=dev, dtype=torch.bfloat16)
+        fn = lambda: mkimage.ops.attention(q, k, v, o0, o1, split=S)  # noqa: E731
+        work, unit = 4.0 * B * L * L * D, "TFLOP/s"
+    else:
+        raise SystemExit(f"unknown kernel {args.kernel}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 3
+    mkimage.ops.check_kernels()
+    print(json.dumps({"kernel": args.kernel, "config": cfg["workload"], "ms": ms,
+                      "achieved": work / (ms * 1e-3) / 1e12, "unit": unit}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -332,9 +378,13 @@ def main():
     ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["gemm", "attention"], default=None,
+                    help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args, cfg)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_mkb(args, cfg)

@@ -1,0 +1,177 @@
+// The C++ Engine mirror over the C ABI (see engine.hpp).
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <random>
+
+namespace mkb::image {
+
+void check(mkb_status s, const char* what)
+{
+    if (s != MKB_OK)
+        throw std::runtime_error(std::string(what) + ": " + mkb_last_error());
+}
+
+std::optional<Sampler> parse_sampler(std::string_view n)
+{
+    if (n == "euler")
+        return Sampler::euler;
+    if (n == "euler_a" || n == "euler_ancestral")
+        return Sampler::euler_ancestral;
+    if (n == "er_sde")
+        return Sampler::er_sde;
+    return std::nullopt;
+}
+
+const char* sampler_name(Sampler s)
+{
+    switch (s) {
+    case Sampler::euler: return "euler";
+    case Sampler::euler_ancestral: return "euler_a";
+    case Sampler::er_sde: return "er_sde";
+    }
+    return "";
+}
+
+std::vector<float> Engine::sigmas(uint32_t steps, uint32_t tokens, std::optional<float> terminal) const
+{
+    mkb_schedule s = sched_;
+    if (s.max_seq == 0)
+        mkb_schedule_default(&s);
+    if (terminal)
+        s.terminal = *terminal;
+    std::vector<float> out(steps + 1);
+    check(mkb_sigmas(&s, steps, tokens, out.data()), "sigmas");
+    return out;
+}
+
+float Engine::top_sigma(uint32_t tokens) const
+{
+    mkb_schedule s = sched_;
+    if (s.max_seq == 0)
+        mkb_schedule_default(&s);
+    return mkb_top_sigma(&s, tokens);
+}
+
+std::vector<float> Engine::denoise(const Request& r)
+{
+    const uint32_t N = r.h * r.w, lat = latent_width();
+    const Sampler sampler = r.sampler.value_or(default_sampler());
+    if (sampler == Sampler::euler_ancestral && !predicts_noise())
+        throw std::runtime_error(std::string(name()) + ": Euler a needs a model that predicts the noise");
+    std::vector<float> x(size_t(N) * lat);
+    std::mt19937_64 rng(r.seed);
+    std::normal_distribution<float> nd;
+    if (!r.noise.empty()) {
+        if (r.noise.size() != x.size())
+            throw std::runtime_error("noise must be [h * w][64]");
+        std::copy(r.noise.begin(), r.noise.end(), x.begin());
+    } else {
+        for (float& v : x)
+            v = nd(rng);
+    }
+    const auto sig = sigmas(r.steps ? r.steps : default_steps(), N, r.terminal);
+    const uint32_t steps = uint32_t(sig.size() - 1);
+    begin(r.prompt, r.h, r.w, 0);
+    const float scale = r.guidance.value_or(default_guidance());
+    const bool guided = scale != 1.0f && !r.negative.empty();
+    if (guided)
+        begin(r.negative, r.h, r.w, 1);
+    mkb_er_sde* er = nullptr;
+    std::vector<float> noise;
+    if (sampler == Sampler::er_sde) {
+        check(mkb_er_sde_create(sig.data(), int(sig.size()), predicts_noise() ? 0 : 1, top_sigma(N), &er), "ER-SDE");
+        noise.resize(x.size());
+    }
+    struct Guard {
+        mkb_er_sde* e;
+        ~Guard() { mkb_er_sde_destroy(e); }
+    } guard{er};
+    for (uint32_t i = 0; i < steps; ++i) {
+        const float s = er ? mkb_er_sde_sigma(er, int(i)) : sig[i];
+        // Plain guided Euler runs as one batched device pass (cond + uncond, update fused).
+        if (!er && sampler == Sampler::euler && guided && guided_step(x, s, sig[i + 1], scale)) {
+            if (r.progress)
+                r.progress(i + 1, steps);
+            continue;
+        }
+        auto v = step(x, s, 0);
+        if (guided) {
+            const auto neg = step(x, s, 1);
+            for (size_t j = 0; j < v.size(); ++j)
+                v[j] = neg[j] + scale * (v[j] - neg[j]);
+        }
+        if (er) {
+            for (size_t j = 0; j < v.size(); ++j)
+                v[j] = x[j] - s * v[j];
+            if (sig[i + 1] > 0)
+                for (float& n : noise)
+                    n = nd(rng);
+            check(mkb_er_sde_step(er, int(i), x.data(), v.data(), noise.data(), long(x.size()), 1.0f), "ER-SDE step");
+        } else if (sampler == Sampler::euler_ancestral) {
+            const double from = sig[i], to = sig[i + 1];
+            const double up = std::min(to, std::sqrt(to * to * (from * from - to * to) / (from * from)));
+            const float dt = float(std::sqrt(to * to - up * up) - from);
+            for (size_t j = 0; j < x.size(); ++j)
+                x[j] += dt * v[j];
+            if (up > 0)
+                for (float& xv : x)
+                    xv += float(up) * nd(rng);
+        } else {
+            mkb_guided_euler(x.data(), v.data(), nullptr, 1.0f, sig[i], sig[i + 1], long(x.size()));
+        }
+        if (r.progress)
+            r.progress(i + 1, steps);
+    }
+    return x;
+}
+
+QwenImage::QwenImage(const mkb_dit_config& cfg) : cfg_(cfg)
+{
+    mkb_schedule_default(&sched_);
+    check(mkb_dit_create(&cfg, &d_), "create");
+}
+
+QwenImage::~QwenImage() { mkb_dit_destroy(d_); }
+
+void QwenImage::init_random(uint64_t seed, float std) { check(mkb_dit_init_random(d_, seed, std), "init_random"); }
+
+void QwenImage::load_weight(const std::string& name, std::span<const float> values)
+{
+    check(mkb_dit_weight_write(d_, name.c_str(), values.data()), "load_weight");
+}
+
+void QwenImage::begin(std::span<const float> prompt, uint32_t h, uint32_t w, uint32_t slot)
+{
+    const uint32_t td = uint32_t(cfg_.text_dim);
+    if (prompt.empty() || prompt.size() % td)
+        throw std::runtime_error("prompt embeddings must be rows of " + std::to_string(td));
+    check(mkb_dit_begin(d_, prompt.data(), int(prompt.size() / td), int(h), int(w), int(slot)), "begin");
+    gh_ = h;
+    gw_ = w;
+    if (slot < 2)
+        prompt_rows_[slot] = uint32_t(prompt.size() / td);
+}
+
+std::vector<float> QwenImage::step(std::span<const float> latents, float sigma, uint32_t slot)
+{
+    const uint64_t N = uint64_t(gh_) * gw_;
+    if (latents.size() != N * latent_width())
+        throw std::runtime_error("latents must be [h * w][64]");
+    std::vector<float> out(latents.size());
+    check(mkb_dit_step(d_, latents.data(), sigma, out.data(), int(slot)), "step");
+    return out;
+}
+
+bool QwenImage::guided_step(std::vector<float>& x, float sigma, float sigma_next, float scale)
+{
+    // Both slots batched needs equal prompt lengths (and, for the reference variant, equal step counts, which the
+    // loop keeps).
+    if (prompt_rows_[0] != prompt_rows_[1] || cfg_.max_batch < 2 || cfg_.slots < 2)
+        return false;
+    check(mkb_dit_step_cfg(d_, x.data(), sigma, sigma_next, scale), "guided step");
+    return true;
+}
+
+}  // namespace mkb::image
