@@ -213,7 +213,9 @@ def run_mkb(args, cfg):
     sig = mkimage.sigmas(40, N)
     i0 = int(np.argmin(np.abs(sig[:-1] - 0.5)))
     sigma, sigma_next = float(sig[i0]), float(sig[i0 + 1])
-    stream = torch.cuda.current_stream(dev)
+    # One explicit stream for the library's launches and the CUDA events that time them.
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     sp = mkimage.stream_ptr(stream)
 
     def one_step():

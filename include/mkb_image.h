@@ -147,7 +147,8 @@ mkb_status mkb_dit_step(mkb_dit* d, const float* latents, float sigma, float* ou
 mkb_status mkb_dit_step_batch(mkb_dit* d, int n, const int* slots, const float* latents, const float* sigmas,
                               float* out);
 
-/* The same on device buffers (latents_dev / out_dev [n][N][64] fp32), enqueued on `stream` without a host sync. */
+/* The same on device buffers (latents_dev / out_dev [n][N][64] fp32), enqueued on `stream` without a host sync
+ * (stream NULL: the handle's own non-blocking stream, which does not order with the legacy default stream). */
 mkb_status mkb_dit_step_batch_dev(mkb_dit* d, int n, const int* slots, const float* latents_dev, const float* sigmas,
                                   float* out_dev, void* stream);
 

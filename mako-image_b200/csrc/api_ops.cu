@@ -19,7 +19,7 @@ std::mutex g_status_mu;
 std::vector<uint32_t*> g_status_words;  // per device
 }  // namespace
 
-void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_launch(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 mkb_status fail(mkb_status code, const std::string& msg)
 {

@@ -15,7 +15,7 @@ mkb_status fail(mkb_status code, const std::string& msg);
 // MKB_OK for cudaSuccess, else MKB_ERR_CUDA with "<what>: <cuda error string>".
 mkb_status cuda_status(cudaError_t e, const char* what);
 // Counts kernel launches made by this library (mkb_kernel_launches).
-void count_launch();
+void count_launch(unsigned long long n = 1);
 // The current device's kernel status word (allocated on first use; lives until process exit).
 uint32_t* device_status_word();
 

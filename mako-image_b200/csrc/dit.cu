@@ -102,6 +102,16 @@ struct DitImpl {
     };
     std::map<std::tuple<int, int, int, int>, std::unique_ptr<Plan>> plans;
 
+    // The step body captured as a CUDA graph per (batch, prompt rows, image rows, first step, slots): the first call
+    // of a key runs eagerly (it sets kernel attributes and plans), the second captures, later ones replay.
+    struct Graph {
+        int seen = 0;
+        cudaGraphExec_t exec = nullptr;
+        unsigned long long launches = 0;
+    };
+    std::map<std::vector<int>, Graph> graphs;
+    bool use_graphs = true;
+
     ~DitImpl();
     mkb_status create(const mkb_dit_config& c);
     void add_weight(const std::string& name, long rows, long cols, bool norm = false, bool swiglu = false);
@@ -118,6 +128,7 @@ struct DitImpl {
     }
     mkb_status build_plan(int B, int S, int N, int first, Plan** out);
     mkb_status run(int B, const int* slot_ids, const float* sigmas, cudaStream_t s, bool* first_out);
+    mkb_status body(int B, const int* slot_ids, int S, int N, int first, Plan* plan, cudaStream_t s);
     mkb_status upload_rope(int S, cudaStream_t s);
     mkb_status emit(const char* name, int layer, const float* dev, long count, cudaStream_t s);
     mkb_status check_status();
@@ -138,6 +149,9 @@ DitImpl::~DitImpl()
         for (auto* p : s.vc)
             cudaFree(p);
     }
+    for (auto& g : graphs)
+        if (g.second.exec)
+            cudaGraphExecDestroy(g.second.exec);
     if (stream)
         cudaStreamDestroy(stream);
 }
@@ -624,15 +638,12 @@ mkb_status DitImpl::run(int B, const int* slot_ids, const float* sigmas, cudaStr
     const int N = gh * gw;
     const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
     const int first = q1 ? 1 : (steps == 0);
-    const int L = S + N, T = q1 ? L : (first ? L : N), split = q1 ? S : (first ? S : 0);
     Plan* plan = nullptr;
     MKB_TRY(upload_rope(S, s));
     MKB_TRY(build_plan(B, S, N, first, &plan));
-    const int per = q1 ? op::kQ1PerBlock : op::kR21PerBlock;
-    GemmOp* g = plan->ops.data() + size_t(NB) * per;
 
-    // Time path: sinusoid -> lin1 -> silu -> lin2 (temb) -> silu -> modulations (qwen_image.cpp:179-205).
-    const int R = q1 ? B : 2 * B;  // ref21: rows (sigma, 0) per sample
+    // Noise levels of the time path (ref21: rows (sigma, 0) per sample, the image's and the text's).
+    const int R = q1 ? B : 2 * B;
     std::vector<float> sv(R);
     for (int b = 0; b < B; ++b) {
         if (q1)
@@ -643,6 +654,53 @@ mkb_status DitImpl::run(int B, const int* slot_ids, const float* sigmas, cudaStr
         }
     }
     MKB_K(cudaMemcpyAsync(sig, sv.data(), R * 4, cudaMemcpyHostToDevice, s), "sigma upload");
+    if (probe || !use_graphs) {
+        MKB_TRY(body(B, slot_ids, S, N, first, plan, s));
+    } else {
+        std::vector<int> key = {B, S, N, first};
+        key.insert(key.end(), slot_ids, slot_ids + B);
+        Graph& g = graphs[key];
+        if (g.exec) {
+            MKB_K(cudaGraphLaunch(g.exec, s), "graph launch");
+            count_launch(g.launches);
+        } else if (g.seen++ == 0) {
+            MKB_TRY(body(B, slot_ids, S, N, first, plan, s));
+        } else {
+            cudaGraph_t graph = nullptr;
+            MKB_K(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+            const unsigned long long l0 = mkb_kernel_launches();
+            mkb_status st = body(B, slot_ids, S, N, first, plan, s);
+            cudaError_t ce = cudaStreamEndCapture(s, &graph);
+            if (st != MKB_OK) {
+                if (graph)
+                    cudaGraphDestroy(graph);
+                return st;
+            }
+            MKB_K(ce, "end capture");
+            g.launches = mkb_kernel_launches() - l0;
+            ce = cudaGraphInstantiate(&g.exec, graph, 0);
+            cudaGraphDestroy(graph);
+            MKB_K(ce, "graph instantiate");
+            MKB_K(cudaGraphLaunch(g.exec, s), "graph launch");
+        }
+    }
+    if (!q1)
+        for (int b = 0; b < B; ++b)
+            slots[slot_ids[b]].steps++;
+    if (first_out)
+        *first_out = first;
+    return MKB_OK;
+}
+
+// Everything of a step after the noise levels are on the device: kernel launches only (capturable).
+mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Plan* plan, cudaStream_t s)
+{
+    const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
+    const int L = S + N, T = q1 ? L : (first ? L : N), split = q1 ? S : (first ? S : 0);
+    const int per = q1 ? op::kQ1PerBlock : op::kR21PerBlock;
+    GemmOp* g = plan->ops.data() + size_t(NB) * per;
+    const int R = q1 ? B : 2 * B;
+    // Time path: sinusoid -> lin1 -> silu -> lin2 (temb) -> silu -> modulations (qwen_image.cpp:179-205).
     MKB_K(timestep_sinusoid(sig, tp, R, s), "sinusoid");
     MKB_K(gemv(M("time.lin1.w"), tp, kTimeDim, V("time.lin1.b"), h1, D, R, D, kTimeDim, kActSilu, s), "time lin1");
     MKB_K(gemv(M("time.lin2.w"), h1, D, V("time.lin2.b"), temb, D, R, D, D, kActNone, s), "time lin2");
@@ -793,11 +851,6 @@ mkb_status DitImpl::run(int B, const int* slot_ids, const float* sigmas, cudaStr
         MKB_K(ln_modulate(la, s), "norm_out");
     }
     MKB_K(gemm_launch(g[op::kProjOut], s), "proj_out");
-    if (!q1)
-        for (int b = 0; b < B; ++b)
-            slots[slot_ids[b]].steps++;
-    if (first_out)
-        *first_out = first;
     return MKB_OK;
 }
 

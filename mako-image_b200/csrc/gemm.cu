@@ -43,10 +43,18 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
     nb = t / gsize;
 }
 
+// tanh on the SFU (tanh.approx.f32, relative error ~2^-11): below the bf16 rounding of every output it feeds.
+__device__ __forceinline__ float tanh_fast(float x)
+{
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x)
 {
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-    return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+    return 0.5f * x * (1.0f + tanh_fast(k0 * (x + k1 * x * x * x)));
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -133,10 +141,10 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
                 for (int j = 0; j < 8; ++j) {
                     float4 g = __ldg(g4 + j);
                     if (a.tanh_gate) {
-                        g.x = tanhf(g.x);
-                        g.y = tanhf(g.y);
-                        g.z = tanhf(g.z);
-                        g.w = tanhf(g.w);
+                        g.x = tanh_fast(g.x);
+                        g.y = tanh_fast(g.y);
+                        g.z = tanh_fast(g.z);
+                        g.w = tanh_fast(g.w);
                     }
                     float4 x = x4[j];
                     x.x += g.x * v[4 * j];

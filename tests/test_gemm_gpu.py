@@ -55,7 +55,8 @@ def test_proj_act(cuda, act):
     y = mkimage.ops.proj(x, w, b, act=act, out_f32=True)
     lin = O.linear(_np(x), _np(w), _np(b))
     ref = O.gelu_tanh(lin) if act == 1 else O.silu(lin)
-    assert np.abs(_np(y) - ref).max() < 1e-4 * max(1.0, np.abs(ref).max())
+    # tanh runs on the SFU (tanh.approx, relative error ~2^-11), well below the bf16 rounding the model applies
+    assert np.abs(_np(y) - ref).max() < 1e-3 * max(1.0, np.abs(ref).max())
 
 
 @pytest.mark.parametrize("tanh_gate", [False, True])
