@@ -1,12 +1,16 @@
 // Flash attention forward, head dim 128, on tcgen05 (see attention.cuh).
 //
-// One CTA per (128-row query tile, head, sample); two CTAs share an SM so one's softmax overlaps the other's MMAs.
-//   warp 0     TMA: the Q tile once, then K and V tiles of 128 keys (128-byte swizzle, two 64-wide panels each)
-//   warp 1     MMA: S = Q K^T into tensor memory (128 x 128 fp32), then O += P V with P read from tensor memory
-//   warps 2-5  softmax, one thread per query row: S row from TMEM, online max with lazy rescaling (O is rescaled
-//              only when a row's max grows by more than 2^8), P = exp2(S - m) as bf16 written back over S, and at
-//              the end O / l into the output projection's input rows.
-// TMEM columns: [0, 128) S (P aliases [0, 64)), [128, 256) O.
+// One CTA per SM-sized work item: two 128-row query tiles (A and B) of one (sample, head) share every K/V tile.
+//   warp 0     TMA: both Q tiles once, then K and V tiles of 128 keys into 2-stage rings (128-byte swizzle,
+//              two 64-wide panels each)
+//   warp 1     MMA, per KV tile j: S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V, O_B += P_B V, with P read from
+//              tensor memory. While one tile's softmax runs, the tensor pipe works on the other tile.
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one thread per query row holds its 128 scores in registers,
+//              keeps a running max with lazy rescaling (O is rescaled only when a row's max grows by more than 2^8),
+//              writes P = 2^(S - m) as bf16 over the first 64 columns of its S, and at the end stores O / l into the
+//              output projection's input rows. Part of each row's exponentials run as a polynomial on the FMA pipe
+//              to offload the SFU.
+// TMEM columns: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512).
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "sm100.cuh"
@@ -20,20 +24,36 @@ namespace mkb {
 
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kTile = 128;                 // query rows per CTA, keys per KV tile
+constexpr int kThreads = 320;
+constexpr int kTile = 128;                 // query rows per tile, keys per KV tile
 constexpr int kPanel = kTile * 64 * 2;     // one 64-wide bf16 panel of 128 rows: 16 KB
 constexpr int kTileBytes = 2 * kPanel;     // 32 KB
-constexpr int kSmem = 1024 + 3 * kTileBytes + 256;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0, kColO = 128;
+constexpr int kSmem = 1024 + 6 * kTileBytes + 256;
+constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Elements [kEmuFrom, 128) of each score row take 2^x from the FMA-pipe polynomial instead of the SFU.
+constexpr int kEmuFrom = 96;
 
 __device__ __forceinline__ float ex2(float x)
 {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here for
+// least maximum relative error on that interval (7.5e-5, below bf16's 3.9e-3), 2^n added to the exponent bits.
+// Arguments below -126 flush to 0 like ex2.approx.ftz.
+__device__ __forceinline__ float ex2_poly(float x)
+{
+    x = fmaxf(x, -126.0f);
+    const float t = x + 12582912.0f;  // 1.5 * 2^23: the rounded integer lands in the low mantissa bits
+    const int n = __float_as_int(t) - 0x4B400000;
+    const float f = x - (t - 12582912.0f);
+    float p = fmaf(0.055171459913253784f, f, 0.2426108568906784f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999281167984009f);
+    return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
@@ -48,35 +68,36 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
     tmem_st16(taddr + 16, b);
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     k_attn(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
            const __grid_constant__ CUtensorMap tv, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = smem + kTileBytes;
-    uint8_t* sV = smem + 2 * kTileBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * kTileBytes);
+    uint8_t* sQ = smem;                   // [2 tiles][32 KB]
+    uint8_t* sK = smem + 2 * kTileBytes;  // [2 stages][32 KB]
+    uint8_t* sV = smem + 4 * kTileBytes;  // [2 stages][32 KB]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = bars + 2;
-    uint64_t* v_full = bars + 3;
-    uint64_t* v_empty = bars + 4;
-    uint64_t* s_full = bars + 5;
-    uint64_t* p_full = bars + 6;
-    uint64_t* o_done = bars + 7;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;    // [2]
+    uint64_t* v_empty = bars + 7;   // [2]
+    uint64_t* s_full = bars + 9;    // [2 tiles]
+    uint64_t* p_full = bars + 11;   // [2 tiles]
+    uint64_t* o_done = bars + 13;   // [2 tiles]
+    uint64_t* drain = bars + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int q0 = blockIdx.x * kTile, h = blockIdx.y, b = blockIdx.z;
+    const int q0 = blockIdx.x * 2 * kTile, h = blockIdx.y, b = blockIdx.z;
     const int bh = b * a.H + h;
 
-    // Keys this tile needs: a tile of text rows only (condition-causal) stops at the text boundary.
+    // Keys this CTA needs: query rows that are all text (condition-causal) stop at the text boundary.
     int n_keys = a.Lk;
     if (a.mask == kMaskCondCausal) {
-        const int last_pos = a.q_pos0 + min(q0 + kTile, a.Lq) - 1;
+        const int last_pos = a.q_pos0 + min(q0 + 2 * kTile, a.Lq) - 1;
         if (last_pos < a.cond_len)
             n_keys = min(a.Lk, a.cond_len);
     }
@@ -84,13 +105,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(k_full, 1);
-        mbar_init(k_empty, 1);
-        mbar_init(v_full, 1);
-        mbar_init(v_empty, 1);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_done[i], 1);
+        }
+        mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -112,33 +136,37 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_3d(sQ, &tq, q_full, 0, a.q_row0 + q0, bh);
-            tma_load_3d(sQ + kPanel, &tq, q_full, 64, a.q_row0 + q0, bh);
+            mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+            for (int t = 0; t < 2; ++t) {
+                tma_load_3d(sQ + t * kTileBytes, &tq, q_full, 0, a.q_row0 + q0 + t * kTile, bh);
+                tma_load_3d(sQ + t * kTileBytes + kPanel, &tq, q_full, 64, a.q_row0 + q0 + t * kTile, bh);
+            }
             for (int j = 0; j < nkv && ok; ++j) {
-                if (!mbar_wait(k_empty, (j & 1) ^ 1, a.status, kErrAttnWait, abort_flag)) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&k_empty[st], ph ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(k_full, kTileBytes);
-                tma_load_3d(sK, &tk, k_full, 0, j * kTile, bh);
-                tma_load_3d(sK + kPanel, &tk, k_full, 64, j * kTile, bh);
+                mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+                tma_load_3d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kTile, bh);
+                tma_load_3d(sK + st * kTileBytes + kPanel, &tk, &k_full[st], 64, j * kTile, bh);
                 ++issued_k;
-                if (!mbar_wait(v_empty, (j & 1) ^ 1, a.status, kErrAttnWait, abort_flag)) {
+                if (!mbar_wait(&v_empty[st], ph ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(v_full, kTileBytes);
-                tma_load_3d(sV, &tv, v_full, 0, j * kTile, bh);
-                tma_load_3d(sV + kPanel, &tv, v_full, 64, j * kTile, bh);
+                mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+                tma_load_3d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kTile, bh);
+                tma_load_3d(sV + st * kTileBytes + kPanel, &tv, &v_full[st], 64, j * kTile, bh);
                 ++issued_v;
             }
-            if (!ok) {  // let issued loads land before exit
+            if (!ok) {  // let the loads already issued land before the CTA can exit
                 mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
-                if (issued_k)
-                    mbar_wait(k_full, (issued_k - 1) & 1, a.status, kErrWaitDrain, nullptr);
-                if (issued_v)
-                    mbar_wait(v_full, (issued_v - 1) & 1, a.status, kErrWaitDrain, nullptr);
+                for (int j = issued_k > 2 ? issued_k - 2 : 0; j < issued_k; ++j)
+                    mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status, kErrWaitDrain, nullptr);
+                for (int j = issued_v > 2 ? issued_v - 2 : 0; j < issued_v; ++j)
+                    mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status, kErrWaitDrain, nullptr);
             }
         }
     } else if (warp == 1) {
@@ -148,63 +176,86 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
             bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
             for (int j = 0; j < nkv && ok; ++j) {
-                if (!mbar_wait(k_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&k_full[st], ph, a.status, kErrAttnWait, abort_flag))
                     break;
-                if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, a.status, kErrAttnWait, abort_flag))
-                    break;
-                tc_fence_after();
+                for (int t = 0; t < 2 && ok; ++t) {
+                    // S_t is overwritten only once the previous O_t += P_t V has read P_t (aliased on S_t).
+                    if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
-                    mma_bf16_ss(tmem + kColS, desc_kmajor_sw128(q_addr + off), desc_kmajor_sw128(k_addr + off),
-                                idesc_s, k > 0);
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
+                        mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * kTileBytes + off),
+                                    desc_kmajor_sw128(k_addr + st * kTileBytes + off), idesc_s, k > 0);
+                    }
+                    mma_commit(&s_full[t]);
                 }
-                mma_commit(k_empty);
-                mma_commit(s_full);
-                if (!mbar_wait(p_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                if (!ok)
                     break;
-                if (!mbar_wait(v_full, j & 1, a.status, kErrAttnWait, abort_flag))
+                mma_commit(&k_empty[st]);
+                if (!mbar_wait(&v_full[st], ph, a.status, kErrAttnWait, abort_flag))
                     break;
-                tc_fence_after();
+                for (int t = 0; t < 2 && ok; ++t) {
+                    if (!mbar_wait(&p_full[t], j & 1, a.status, kErrAttnWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms)
-                    mma_bf16_ts(tmem + kColO, tmem + kColS + 8 * k,
-                                desc_mnmajor_sw128(v_addr + k * 2048, kPanel, 1024), idesc_o, (j > 0) || (k > 0));
-                mma_commit(v_empty);
-                mma_commit(o_done);
+                    for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms)
+                        mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + 8 * k,
+                                    desc_mnmajor_sw128(v_addr + st * kTileBytes + k * 2048, kPanel, 1024), idesc_o,
+                                    (j > 0) || (k > 0));
+                    mma_commit(&o_done[t]);
+                }
+                if (ok)
+                    mma_commit(&v_empty[st]);
             }
-            mma_commit(k_empty);  // drain: arrives once every MMA issued above has completed
-            mbar_wait(k_empty, nkv & 1, a.status, kErrWaitDrain, nullptr);
+            mma_commit(drain);  // arrives once every MMA issued above has completed
+            mbar_wait(drain, 0, a.status, kErrWaitDrain, nullptr);
         }
     } else {
+        const int t = (warp - 2) >> 2;  // query tile of this softmax warp group
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         const uint32_t t_lane = tmem + (uint32_t(quarter * 32) << 16);
-        const int qrow = q0 + r;
+        const uint32_t col_s = t * 128, col_o = 256 + t * 128;
+        const int qrow = q0 + t * kTile + r;
         const int qpos = a.q_pos0 + qrow;
         const bool text_query = a.mask == kMaskCondCausal && qpos < a.cond_len;
         const int key_limit = text_query ? min(a.Lk, a.cond_len) : a.Lk;
+        const float sc = a.scale_log2;
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
-            if (!mbar_wait(s_full, j & 1, a.status, kErrAttnWait, abort_flag)) {
+            if (!mbar_wait(&s_full[t], j & 1, a.status, kErrAttnWait, abort_flag)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int key0 = j * kTile;
-            const int valid = min(kTile, key_limit - key0);  // keys [0, valid) of this tile are visible
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t s[32];
-                tmem_ld32(t_lane + kColS + c * 32, s);
-                tmem_wait_ld();
+            uint32_t s[128];
+            tmem_ld32(t_lane + col_s, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+            tmem_ld32(t_lane + col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+            tmem_ld32(t_lane + col_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+            tmem_ld32(t_lane + col_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+            tmem_wait_ld();
+            const int valid = min(kTile, key_limit - j * kTile);  // keys [0, valid) of this tile are visible
+            if (valid < kTile) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c * 32 + i < valid)
-                        mx = fmaxf(mx, __uint_as_float(s[i]) * a.scale_log2);
+                for (int i = 0; i < 128; ++i)
+                    if (i >= valid)
+                        s[i] = __float_as_uint(-INFINITY);
             }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 128; i += 2)
+                mx = fmaxf(mx, fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 1])));
+            mx *= sc;
             const bool need = mx > m_used + kRescaleThreshold;
             if (__any_sync(0xffffffffu, need)) {
                 const float m_new = need ? mx : m_used;
@@ -214,36 +265,40 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
                         uint32_t o[32];
-                        tmem_ld32(t_lane + kColO + c * 32, o);
+                        tmem_ld32(t_lane + col_o + c * 32, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-                        tmem_st32(t_lane + kColO + c * 32, o);
+                        tmem_st32(t_lane + col_o + c * 32, o);
                     }
                 }
                 m_used = m_new;
             }
-#pragma unroll 1
+            const float neg_m = -m_used;
+            float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
-                uint32_t s[32], p[16];
-                tmem_ld32(t_lane + kColS + c * 32, s);
-                tmem_wait_ld();
+                uint32_t p[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int k0 = c * 32 + 2 * i;
-                    const float p0 = k0 < valid ? ex2(__uint_as_float(s[2 * i]) * a.scale_log2 - m_used) : 0.0f;
-                    const float p1 = k0 + 1 < valid ? ex2(__uint_as_float(s[2 * i + 1]) * a.scale_log2 - m_used) : 0.0f;
-                    l += p0 + p1;
+                    const int k = c * 32 + 2 * i;
+                    const float x0 = fmaf(__uint_as_float(s[k]), sc, neg_m);
+                    const float x1 = fmaf(__uint_as_float(s[k + 1]), sc, neg_m);
+                    const float p0 = k >= kEmuFrom ? ex2_poly(x0) : ex2(x0);
+                    const float p1 = k + 1 >= kEmuFrom ? ex2_poly(x1) : ex2(x1);
+                    l0 += p0;
+                    l1 += p1;
                     p[i] = pack_bf16x2(p0, p1);
                 }
-                tmem_st16(t_lane + kColS + c * 16, p);
+                tmem_st16(t_lane + col_s + c * 16, p);
             }
+            l += l0 + l1;
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[t]);
         }
-        if (ok && mbar_wait(o_done, (nkv - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
+        if (ok && nkv > 0 && mbar_wait(&o_done[t], (nkv - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
             tc_fence_after();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             const bool row_ok = qrow < a.Lq;
@@ -256,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
                 uint32_t o[32];
-                tmem_ld32(t_lane + kColO + c * 32, o);
+                tmem_ld32(t_lane + col_o + c * 32, o);
                 tmem_wait_ld();
                 if (row_ok) {
                     uint4* d = reinterpret_cast<uint4*>(dst + c * 32);
@@ -350,7 +405,7 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         !make_heads_map(&op.tv, v, Lk_rows, bh, err))
         return false;
     op.args = args;
-    op.grid = dim3((args.Lq + kTile - 1) / kTile, args.H, args.B);
+    op.grid = dim3((args.Lq + 2 * kTile - 1) / (2 * kTile), args.H, args.B);
     op.ready = true;
     return true;
 }
