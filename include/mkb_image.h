@@ -77,19 +77,56 @@ mkb_status mkb_proj_swiglu(const void* x, long ldx, const void* w, long ldw, con
  * matrix are gate rows [j*B, (j+1)*B), the next B rows the matching up rows. */
 int mkb_swiglu_interleave(void);
 
+/* y = x * w^T + bias + addvec[row / rows_per_sample] + resid (each optional: NULL), y fp32 (out_f32 = 1) or bf16.
+ * resid is fp32 [M][N] rows ld_resid apart and may be y itself (an in-place residual add). The projections of the
+ * SDXL UNet's transformer blocks with their residual adds (sdxl.cpp:763-795). */
+mkb_status mkb_proj_add(const void* x, long ldx, const void* w, long ldw, const float* bias, const float* addvec,
+                        long addvec_stride, int rows_per_sample, const float* resid, long ld_resid, void* y, long ldy,
+                        int out_f32, int M, int N, int K, void* stream);
+
+/* y = x * w^T + bias scattered into head-major bf16 [samples][heads][L][head_dim]: columns [p*D, (p+1)*D) go to part
+ * part0 + p of (q, k, v), head h at columns h*head_dim of its part; row r to sample r / rows_per_sample, position
+ * pos_offset + r % rows_per_sample of L. No norm (SDXL's q, k, v and the cached cross-attention k, v, sdxl.cpp:
+ * 443-457, 701-717). */
+mkb_status mkb_proj_heads(const void* x, long ldx, const void* w, long ldw, const float* bias, void* qh, void* kh,
+                          void* vh, int part0, int D, int head_dim, int L, int rows_per_sample, int pos_offset, int M,
+                          int N, int K, void* stream);
+
+/* GEGLU projection: w holds (hidden | gate) rows interleaved in blocks of mkb_swiglu_interleave(); the output is
+ * y[M][N/2] = hidden * GELU_erf(gate), bf16 (geglu_rows, src/kernels/image.metal:476-484). */
+mkb_status mkb_proj_geglu(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy,
+                          int M, int N, int K, void* stream);
+
+/* Convolution on channels-last bf16 input x [B][H][W][C] (C a multiple of 64) with weights w [Cout][taps][C] bf16
+ * (taps 9: 3x3 with padding 1, stride 1 or 2; taps 1: 1x1), as an implicit GEMM on the tensor cores (no im2col
+ * buffer: each 3x3 tap is a shifted window of the input, zero outside the image). Epilogue as mkb_proj_add with
+ * rows = output pixels (b * Ho + y) * Wo + x and addvec per image. Replaces ConvRuntime::conv (sdxl.cpp:729-735,
+ * engine.cpp:737-741, 904-943). The output width must be a multiple of 8. */
+mkb_status mkb_conv2d(const void* x, int B, int H, int W, int C, const void* w, int Cout, int taps, int stride,
+                      const float* bias, const float* addvec, long addvec_stride, const float* resid, long ld_resid,
+                      void* y, long ldy, int out_f32, void* stream);
+
+/* GroupNorm of channels-last fp32 x [B][HW][C] (C / groups consecutive channels per group), y = norm * gamma + beta,
+ * then SiLU if silu != 0, bf16 out. workspace: device scratch of mkb_group_norm_workspace_size() bytes. The
+ * runtime's group_norm (sdxl.cpp:728-762, engine.cpp:722-730). */
+size_t mkb_group_norm_workspace_size(int B, int HW, int C, int groups);
+mkb_status mkb_group_norm(const float* x, void* y, const float* gamma, const float* beta, int B, int HW, int C,
+                          int groups, float eps, int silu, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Attention masks. */
 enum { MKB_MASK_NONE = 0, MKB_MASK_COND_CAUSAL = 1 };
 
-/* Flash attention, head dim 128: out = softmax(q k^T / sqrt(128)) v per (sample, head). q is [B][H][Lq_rows][128],
- * k and v [B][H][Lk_rows][128] (bf16, head-major, as mkb_proj_qkv_heads writes them); the first Lq query rows and Lk
- * keys are used. Query row i sits at joint position q_pos0 + i; keys at positions 0..Lk-1. MKB_MASK_COND_CAUSAL: a
+/* Flash attention, head dim d = 64 or 128: out = softmax(q k^T / sqrt(d)) v per (sample, head). q is
+ * [B][H][Lq_rows][d], k and v [B][H][Lk_rows][d] (bf16, head-major, as mkb_proj_qkv_heads / mkb_proj_heads write
+ * them); the first Lq query rows and Lk keys are used. Query row i sits at joint position q_pos0 + i; keys at positions 0..Lk-1. MKB_MASK_COND_CAUSAL: a
  * query at position < cond_len sees keys < cond_len only (the reference's text rows, which is what lets it cache the
  * text K/V; qwen_image.cpp:251-271). Output rows are bf16 [.][H*128]: position p < split goes to row
  * (b * rows0 + p) of out0, otherwise row (b * rows1 + p - split) of out1 (the text and image streams' inputs of the
- * output projection). Replaces TransformerRuntime::attention() (qwen_image.cpp:271). */
+ * output projection; columns [h * d, h * d + d)). Replaces TransformerRuntime::attention() (qwen_image.cpp:271) and the
+ * hd-64 flash_attn_coop_64_32 the SDXL UNet calls (sdxl.cpp:450-457). */
 mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk, int Lk_rows, int B,
-                         int H, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0, int rows0,
-                         void* out1, long ld1, int rows1, void* stream);
+                         int H, int head_dim, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0,
+                         int rows0, void* out1, long ld1, int rows1, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * The denoiser (image::Engine's model interface, src/image/engine.hpp:158-166, on the Qwen-Image-style MMDiT).

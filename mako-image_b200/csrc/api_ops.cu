@@ -3,6 +3,7 @@
 #include "common.cuh"
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "rowops.cuh"
 #include "sm100.cuh"
 
 #include <atomic>
@@ -171,9 +172,119 @@ mkb_status mkb_proj_swiglu(const void* x, long ldx, const void* w, long ldw, con
     return run_gemm(Epi::kSwiGLU, x, ldx, w, ldw, a, 256, stream);
 }
 
+mkb_status mkb_proj_add(const void* x, long ldx, const void* w, long ldw, const float* bias, const float* addvec,
+                        long addvec_stride, int rows_per_sample, const float* resid, long ld_resid, void* y, long ldy,
+                        int out_f32, int M, int N, int K, void* stream)
+{
+    if (addvec && rows_per_sample <= 0)
+        return fail(MKB_ERR_INVALID, "proj_add: rows_per_sample must be positive");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.addvec = addvec;
+    a.addvec_stride = addvec_stride;
+    a.seg_rows = addvec ? rows_per_sample : (1 << 30);
+    a.add_resid = resid;
+    a.ld_add_resid = ld_resid;
+    a.out = y;
+    a.ldo = ldy;
+    a.out_f32 = out_f32;
+    return run_gemm(Epi::kAdd, x, ldx, w, ldw, a, pick_bn(M, N), stream);
+}
+
+mkb_status mkb_proj_heads(const void* x, long ldx, const void* w, long ldw, const float* bias, void* qh, void* kh,
+                          void* vh, int part0, int D, int head_dim, int L, int rows_per_sample, int pos_offset, int M,
+                          int N, int K, void* stream)
+{
+    if (rows_per_sample <= 0 || pos_offset < 0 || pos_offset + rows_per_sample > L || D <= 0)
+        return fail(MKB_ERR_INVALID, "proj_heads: need pos_offset + rows_per_sample <= L and D > 0");
+    const int parts = (N + D - 1) / D;
+    void* outs[3] = {qh, kh, vh};
+    for (int p = part0; p < part0 + parts && p < 3; ++p)
+        if (!outs[p])
+            return fail(MKB_ERR_INVALID, "proj_heads: missing output for a part");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.qh = static_cast<__nv_bfloat16*>(qh);
+    a.kh = static_cast<__nv_bfloat16*>(kh);
+    a.vh = static_cast<__nv_bfloat16*>(vh);
+    a.part0 = part0;
+    a.D = D;
+    a.head_dim = head_dim;
+    a.L = L;
+    a.seg_rows = rows_per_sample;
+    a.seg_off = pos_offset;
+    return run_gemm(Epi::kHeads, x, ldx, w, ldw, a, pick_bn(M, N), stream);
+}
+
+mkb_status mkb_proj_geglu(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy,
+                          int M, int N, int K, void* stream)
+{
+    if (N % 256)
+        return fail(MKB_ERR_INVALID, "proj_geglu: N (hidden + gate rows) must be a multiple of 256");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.bias = bias;
+    a.out = y;
+    a.ldo = ldy;
+    a.glu = kGluGelu;
+    return run_gemm(Epi::kSwiGLU, x, ldx, w, ldw, a, 256, stream);
+}
+
+mkb_status mkb_conv2d(const void* x, int B, int H, int W, int C, const void* w, int Cout, int taps, int stride,
+                      const float* bias, const float* addvec, long addvec_stride, const float* resid, long ld_resid,
+                      void* y, long ldy, int out_f32, void* stream)
+{
+    if (!x || !w || !y)
+        return fail(MKB_ERR_INVALID, "conv2d: null operand");
+    GemmArgs a;
+    a.bias = bias;
+    a.addvec = addvec;
+    a.addvec_stride = addvec_stride;
+    a.add_resid = resid;
+    a.ld_add_resid = ld_resid;
+    a.out = y;
+    a.ldo = ldy;
+    a.out_f32 = out_f32;
+    a.status = device_status_word();
+    const int Ho = taps == 9 ? (H - 1) / stride + 1 : H, Wo = taps == 9 ? (W - 1) / stride + 1 : W;
+    const int bn = pick_bn(B * Ho * Wo, Cout);
+    GemmOp op;
+    const char* err = nullptr;
+    if (!conv_prepare(op, Epi::kAdd, x, B, H, W, C, w, Cout, taps, stride, a, bn, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "conv2d: unsupported arguments");
+    return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "conv2d launch");
+}
+
+size_t mkb_group_norm_workspace_size(int B, int HW, int C, int groups)
+{
+    return group_norm_workspace(B, HW, C, groups);
+}
+
+mkb_status mkb_group_norm(const float* x, void* y, const float* gamma, const float* beta, int B, int HW, int C,
+                          int groups, float eps, int silu, void* workspace, size_t workspace_bytes, void* stream)
+{
+    if (!x || !y || !gamma || !workspace)
+        return fail(MKB_ERR_INVALID, "group_norm: null argument");
+    if (B <= 0 || HW <= 0 || groups <= 0 || C % groups || C % 4 || C > 6144)
+        return fail(MKB_ERR_INVALID, "group_norm: need C a multiple of groups and of 4, C <= 6144");
+    if (workspace_bytes < group_norm_workspace(B, HW, C, groups))
+        return fail(MKB_ERR_INVALID, "group_norm: workspace too small");
+    GnArgs a{x, static_cast<__nv_bfloat16*>(y), gamma, beta, B, HW, C, groups, eps, silu,
+             static_cast<float*>(workspace)};
+    return cuda_status(group_norm(a, static_cast<cudaStream_t>(stream)), "group_norm launch");
+}
+
 mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk, int Lk_rows, int B,
-                         int H, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0, int rows0,
-                         void* out1, long ld1, int rows1, void* stream)
+                         int H, int head_dim, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0,
+                         int rows0, void* out1, long ld1, int rows1, void* stream)
 {
     if (!q || !k || !v)
         return fail(MKB_ERR_INVALID, "attention: null q/k/v");
@@ -187,7 +298,8 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
     a.q_pos0 = q_pos0;
     a.mask = mask;
     a.cond_len = cond_len;
-    a.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
+    a.head_dim = head_dim;
+    a.scale_log2 = 1.4426950408889634f / sqrtf(float(head_dim));
     a.split = split;
     a.out0 = static_cast<__nv_bfloat16*>(out0);
     a.ld0 = ld0;

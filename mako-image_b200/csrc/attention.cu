@@ -27,8 +27,10 @@ namespace {
 constexpr int kThreads = 320;
 constexpr int kTile = 128;                 // query rows per tile, keys per KV tile
 constexpr int kPanel = kTile * 64 * 2;     // one 64-wide bf16 panel of 128 rows: 16 KB
-constexpr int kTileBytes = 2 * kPanel;     // 32 KB
-constexpr int kSmem = 1024 + 6 * kTileBytes + 256;
+template <int HD>
+constexpr int kTileBytes = (HD / 64) * kPanel;  // a 128-row tile of one head: 16 KB (hd 64) or 32 KB (hd 128)
+template <int HD>
+constexpr int kSmem = 1024 + 6 * kTileBytes<HD> + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Elements [kEmuFrom, 128) of each score row take 2^x from the FMA-pipe polynomial instead of the SFU.
@@ -68,16 +70,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
     tmem_st16(taddr + 16, b);
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     k_attn(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
            const __grid_constant__ CUtensorMap tv, const AttnArgs a)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;                   // [2 tiles][32 KB]
-    uint8_t* sK = smem + 2 * kTileBytes;  // [2 stages][32 KB]
-    uint8_t* sV = smem + 4 * kTileBytes;  // [2 stages][32 KB]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+    constexpr int TB = kTileBytes<HD>;
+    uint8_t* sQ = smem;           // [2 tiles][TB]
+    uint8_t* sK = smem + 2 * TB;  // [2 stages][TB]
+    uint8_t* sV = smem + 4 * TB;  // [2 stages][TB]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * TB);
     uint64_t* q_full = bars + 0;
     uint64_t* k_full = bars + 1;    // [2]
     uint64_t* k_empty = bars + 3;   // [2]
@@ -136,11 +140,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
-            for (int t = 0; t < 2; ++t) {
-                tma_load_3d(sQ + t * kTileBytes, &tq, q_full, 0, a.q_row0 + q0 + t * kTile, bh);
-                tma_load_3d(sQ + t * kTileBytes + kPanel, &tq, q_full, 64, a.q_row0 + q0 + t * kTile, bh);
-            }
+            mbar_arrive_expect_tx(q_full, 2 * TB);
+            for (int t = 0; t < 2; ++t)
+                for (int pn = 0; pn < HD / 64; ++pn)
+                    tma_load_3d(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile, bh);
             for (int j = 0; j < nkv && ok; ++j) {
                 const int st = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
@@ -148,17 +151,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-                tma_load_3d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kTile, bh);
-                tma_load_3d(sK + st * kTileBytes + kPanel, &tk, &k_full[st], 64, j * kTile, bh);
+                mbar_arrive_expect_tx(&k_full[st], TB);
+                for (int pn = 0; pn < HD / 64; ++pn)
+                    tma_load_3d(sK + st * TB + pn * kPanel, &tk, &k_full[st], pn * 64, j * kTile, bh);
                 ++issued_k;
                 if (!mbar_wait(&v_empty[st], ph ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-                tma_load_3d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kTile, bh);
-                tma_load_3d(sV + st * kTileBytes + kPanel, &tv, &v_full[st], 64, j * kTile, bh);
+                mbar_arrive_expect_tx(&v_full[st], TB);
+                for (int pn = 0; pn < HD / 64; ++pn)
+                    tma_load_3d(sV + st * TB + pn * kPanel, &tv, &v_full[st], pn * 64, j * kTile, bh);
                 ++issued_v;
             }
             if (!ok) {  // let the loads already issued land before the CTA can exit
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
-            constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, 0, 1);  // V is MN-major (head dim contiguous)
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, 0, 1);  // V is MN-major (head dim contiguous)
             const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
             bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
             for (int j = 0; j < nkv && ok; ++j) {
@@ -188,10 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
+                    for (int k = 0; k < HD / 16; ++k) {
                         const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
-                        mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * kTileBytes + off),
-                                    desc_kmajor_sw128(k_addr + st * kTileBytes + off), idesc_s, k > 0);
+                        mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
+                                    desc_kmajor_sw128(k_addr + st * TB + off), idesc_s, k > 0);
                     }
                     mma_commit(&s_full[t]);
                 }
@@ -208,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
 #pragma unroll
                     for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms)
-                        mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + 8 * k,
-                                    desc_mnmajor_sw128(v_addr + st * kTileBytes + k * 2048, kPanel, 1024), idesc_o,
+                        mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
+                                    desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
                                     (j > 0) || (k > 0));
                     mma_commit(&o_done[t]);
                 }
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         const uint32_t t_lane = tmem + (uint32_t(quarter * 32) << 16);
-        const uint32_t col_s = t * 128, col_o = 256 + t * 128;
+        const uint32_t col_s = t * 128, col_o = 256 + t * HD;
         const int qrow = q0 + t * kTile + r;
         const int qpos = a.q_pos0 + qrow;
         const bool text_query = a.mask == kMaskCondCausal && qpos < a.cond_len;
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l *= f;
                 if (j > 0) {
 #pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < HD / 32; ++c) {
                         uint32_t o[32];
                         tmem_ld32(t_lane + col_o + c * 32, o);
                         tmem_wait_ld();
@@ -306,10 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (row_ok) {
                 dst = qpos < a.split ? a.out0 + (long(b) * a.rows0 + qpos) * a.ld0
                                      : a.out1 + (long(b) * a.rows1 + (qpos - a.split)) * a.ld1;
-                dst += h * 128;
+                dst += h * HD;
             }
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < HD / 32; ++c) {
                 uint32_t o[32];
                 tmem_ld32(t_lane + col_o + c * 32, o);
                 tmem_wait_ld();
@@ -351,7 +354,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 
 // Head-major [BH][rows][128] bf16 as a 3-D map, box 64 x 128 x 1 with the 128-byte swizzle; rows past `rows` of a
 // head read as zeros.
-bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, const char** err)
+bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, int hd, const char** err)
 {
     auto fn = encode_fn();
     if (!fn) {
@@ -362,8 +365,8 @@ bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, const char*
         *err = "attention: q/k/v must be 16-byte aligned";
         return false;
     }
-    cuuint64_t dims[3] = {128, cuuint64_t(rows), cuuint64_t(bh)};
-    cuuint64_t strides[2] = {128 * 2, cuuint64_t(rows) * 128 * 2};
+    cuuint64_t dims[3] = {cuuint64_t(hd), cuuint64_t(rows), cuuint64_t(bh)};
+    cuuint64_t strides[2] = {cuuint64_t(hd) * 2, cuuint64_t(rows) * hd * 2};
     cuuint32_t box[3] = {64, 128, 1};
     cuuint32_t es[3] = {1, 1, 1};
     if (fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p), dims, strides, box, es,
@@ -401,8 +404,13 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         return false;
     }
     const int bh = args.B * args.H;
-    if (!make_heads_map(&op.tq, q, Lq_rows, bh, err) || !make_heads_map(&op.tk, k, Lk_rows, bh, err) ||
-        !make_heads_map(&op.tv, v, Lk_rows, bh, err))
+    if (args.head_dim != 64 && args.head_dim != 128) {
+        *err = "attention: head dim must be 64 or 128";
+        return false;
+    }
+    const int hd = args.head_dim;
+    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) || !make_heads_map(&op.tk, k, Lk_rows, bh, hd, err) ||
+        !make_heads_map(&op.tv, v, Lk_rows, bh, hd, err))
         return false;
     op.args = args;
     op.grid = dim3((args.Lq + 2 * kTile - 1) / (2 * kTile), args.H, args.B);
@@ -414,14 +422,24 @@ cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
 {
     if (!op.ready)
         return cudaErrorInvalidValue;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        if (e != cudaSuccess)
-            return e;
-        attr = true;
+    static bool attr64 = false, attr128 = false;
+    if (op.args.head_dim == 64) {
+        if (!attr64) {
+            cudaError_t e = cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<64>);
+            if (e != cudaSuccess)
+                return e;
+            attr64 = true;
+        }
+        k_attn<64><<<op.grid, kThreads, kSmem<64>, st>>>(op.tq, op.tk, op.tv, op.args);
+    } else {
+        if (!attr128) {
+            cudaError_t e = cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<128>);
+            if (e != cudaSuccess)
+                return e;
+            attr128 = true;
+        }
+        k_attn<128><<<op.grid, kThreads, kSmem<128>, st>>>(op.tq, op.tk, op.tv, op.args);
     }
-    k_attn<<<op.grid, kThreads, kSmem, st>>>(op.tq, op.tk, op.tv, op.args);
     count_launch();
     return cudaGetLastError();
 }

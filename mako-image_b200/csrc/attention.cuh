@@ -1,4 +1,4 @@
-// Fused flash attention on tcgen05 for head dim 128: softmax(q k^T / sqrt(128)) v over head-major bf16 q/k/v.
+// Fused flash attention on tcgen05 for head dim 64 or 128: softmax(q k^T / sqrt(d)) v over head-major bf16 q/k/v.
 // Replaces the runtime's attention() the reference calls per block (src/image/qwen_image.cpp:271), including its
 // mask modes, and writes each query row straight into the token-major input of the output projection of its
 // stream (text rows and image rows go to separate buffers).
@@ -25,6 +25,7 @@ struct AttnArgs {
     int mask = kMaskNone;
     int cond_len = 0;    // kMaskCondCausal boundary
     float scale_log2 = 0.f;  // softmax scale * log2(e)
+    int head_dim = 128;      // 64 or 128
     // Output routing by joint position p of a query row: p < split -> out0 row (b * rows0 + p),
     // else out1 row (b * rows1 + p - split); columns [h * 128, h * 128 + 128).
     int split = 0;
@@ -44,7 +45,7 @@ struct AttnOp {
     bool ready = false;
 };
 
-// q: [B][H][Lq_rows][128], k/v: [B][H][Lk_rows][128] (bf16, contiguous); Lq_rows >= args.Lq, Lk_rows >= args.Lk.
+// q: [B][H][Lq_rows][d], k/v: [B][H][Lk_rows][d] (bf16, contiguous); Lq_rows >= args.Lq, Lk_rows >= args.Lk.
 bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const void* v, int Lk_rows,
                   const AttnArgs& args, const char** err);
 cudaError_t attn_launch(const AttnOp& op, cudaStream_t stream);

@@ -97,11 +97,12 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
 }
 
 // The epilogue of one tile for one thread (one row). t_row: TMEM address of this row's accumulator, column 0.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
 template <int BN, Epi EPI>
-__device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int row, int n0)
+__device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int row, bool row_ok, int n0)
 {
-    const bool row_ok = row < a.M;
-    if constexpr (EPI == Epi::kBF16 || EPI == Epi::kF32 || EPI == Epi::kResid) {
+    if constexpr (EPI == Epi::kBF16 || EPI == Epi::kF32 || EPI == Epi::kResid || EPI == Epi::kAdd) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
             uint32_t r[32];
@@ -131,6 +132,38 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else if constexpr (EPI == Epi::kAdd) {
+                if (a.addvec) {
+                    const float4* av =
+                        reinterpret_cast<const float4*>(a.addvec + long(row / a.seg_rows) * a.addvec_stride + col0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 t = __ldg(av + j);
+                        v[4 * j] += t.x;
+                        v[4 * j + 1] += t.y;
+                        v[4 * j + 2] += t.z;
+                        v[4 * j + 3] += t.w;
+                    }
+                }
+                if (a.add_resid) {
+                    const float4* rr = reinterpret_cast<const float4*>(a.add_resid + long(row) * a.ld_add_resid + col0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 t = rr[j];
+                        v[4 * j] += t.x;
+                        v[4 * j + 1] += t.y;
+                        v[4 * j + 2] += t.z;
+                        v[4 * j + 3] += t.w;
+                    }
+                }
+                if (a.out_f32) {
+                    float4* d = reinterpret_cast<float4*>(static_cast<float*>(a.out) + long(row) * a.ldo + col0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                } else {
+                    store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + col0, v);
+                }
             } else {
                 const int bsample = row / a.seg_rows;
                 const int within = row - bsample * a.seg_rows;
@@ -168,10 +201,39 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
             float bg[32], bu[32], v[32];
             load_bias32(a.bias, n0 + c, bg);
             load_bias32(a.bias, n0 + BN / 2 + c, bu);
+            if (a.glu == kGluGelu) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    v[j] = (__uint_as_float(rg[j]) + bg[j]) * gelu_erf(__uint_as_float(ru[j]) + bu[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    v[j] = silu(__uint_as_float(rg[j]) + bg[j]) * (__uint_as_float(ru[j]) + bu[j]);
+            }
+            store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + n0 / 2 + c, v);
+        }
+    } else if constexpr (EPI == Epi::kHeads) {
+        // Plain scatter: 32-column chunks never straddle a head (head_dim 64 or 128).
+        const int bsample = row / a.seg_rows;
+        const int pos = a.seg_off + row % a.seg_rows;
+        const int hd = a.head_dim, heads = a.D / hd;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+            tmem_wait_ld();
+            const int col = n0 + c;
+            if (!row_ok || col >= a.N)
+                continue;
+            float b[32], v[32];
+            load_bias32(a.bias, col, b);
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-                v[j] = silu(__uint_as_float(rg[j]) + bg[j]) * (__uint_as_float(ru[j]) + bu[j]);
-            store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + n0 / 2 + c, v);
+                v[j] = __uint_as_float(r[j]) + b[j];
+            const int which = a.part0 + col / a.D;
+            const int head = (col % a.D) / hd;
+            __nv_bfloat16* base = which == 0 ? a.qh : which == 1 ? a.kh : a.vh;
+            store_bf16x32(base + ((long(bsample) * heads + head) * a.L + pos) * hd + (col % hd), v);
         }
     } else {  // kQkv
         const int bsample = row / a.seg_rows;
@@ -244,7 +306,17 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
     }
 }
 
-template <int BN, Epi EPI>
+// Output tile origin of conv m-tile mb: sample, first output row and column.
+__device__ __forceinline__ void conv_tile(const GemmArgs& a, int mb, int& b, int& y0, int& x0)
+{
+    const int tx_n = a.conv_wo / a.conv_tw, ty_n = (a.conv_ho + a.conv_th - 1) / a.conv_th;
+    b = mb / (tx_n * ty_n);
+    const int rem = mb - b * tx_n * ty_n;
+    y0 = (rem / tx_n) * a.conv_th;
+    x0 = (rem % tx_n) * a.conv_tw;
+}
+
+template <int BN, Epi EPI, bool CONV>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs args)
 {
@@ -260,7 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_m = (args.M + kBM - 1) / kBM, num_n = (args.N + BN - 1) / BN;
+    const int num_m = CONV ? args.conv_b * (args.conv_wo / args.conv_tw) *
+                                 ((args.conv_ho + args.conv_th - 1) / args.conv_th)
+                           : (args.M + kBM - 1) / kBM;
+    const int num_n = (args.N + BN - 1) / BN;
     const int num_tiles = num_m * num_n, num_k = (args.K + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
@@ -305,7 +380,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sa = smem + s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-                    tma_load_2d(sa, &tma, &full[s], kb * kBK, mb * kBM);
+                    if constexpr (CONV) {
+                        // k-block kb = (tap, 64-channel chunk): the input window of the tile shifted by the tap,
+                        // zero-filled outside the image (the convolution's padding).
+                        int b, y0, x0;
+                        conv_tile(args, mb, b, y0, x0);
+                        const int cpt = args.conv_c / kBK, tap = kb / cpt, c0 = (kb - tap * cpt) * kBK;
+                        const int dy = args.conv_taps == 9 ? tap / 3 : 0, dx = args.conv_taps == 9 ? tap % 3 : 0;
+                        tma_load_4d(sa, &tma, &full[s], c0, x0 * args.conv_stride + dx - args.conv_pad,
+                                    y0 * args.conv_stride + dy - args.conv_pad, b);
+                    } else {
+                        tma_load_2d(sa, &tma, &full[s], kb * kBK, mb * kBM);
+                    }
                     tma_load_2d(sa + C::kABytes, &tmb, &full[s], kb * kBK, nb * BN);
                 }
             }
@@ -360,7 +446,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-            epilogue<BN, EPI>(args, t_row, mb * kBM + q * 32 + lane, nb * BN);
+            const int r = q * 32 + lane;
+            if constexpr (CONV) {
+                int b, y0, x0;
+                conv_tile(args, mb, b, y0, x0);
+                const int y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
+                epilogue<BN, EPI>(args, t_row, (b * args.conv_ho + y) * args.conv_wo + x, y < args.conv_ho, nb * BN);
+            } else {
+                const int row = mb * kBM + r;
+                epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+            }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
         }
@@ -389,25 +484,39 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-template <int BN, Epi EPI>
-cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
+template <int BN, Epi EPI, bool CONV>
+cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
 {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_gemm<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
         if (e != cudaSuccess)
             return e;
         attr_set = true;
     }
-    k_gemm<BN, EPI><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.ta, op.tb, op.args);
+    k_gemm<BN, EPI, CONV><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.ta, op.tb, op.args);
     count_launch();
     return cudaGetLastError();
+}
+
+template <int BN, Epi EPI>
+cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
+{
+    // Convolutions only use the epilogues a conv needs (plain, activation, add), which keeps the instantiations few.
+    if constexpr (EPI == Epi::kBF16 || EPI == Epi::kAdd) {
+        if (op.conv)
+            return launch_c<BN, EPI, true>(op, st);
+    }
+    return launch_c<BN, EPI, false>(op, st);
 }
 
 template <int BN>
 cudaError_t launch_bn(const GemmOp& op, cudaStream_t st)
 {
     switch (op.epi) {
+    case Epi::kAdd: return launch_t<BN, Epi::kAdd>(op, st);
+    case Epi::kHeads: return launch_t<BN, Epi::kHeads>(op, st);
     case Epi::kBF16: return launch_t<BN, Epi::kBF16>(op, st);
     case Epi::kF32: return launch_t<BN, Epi::kF32>(op, st);
     case Epi::kResid: return launch_t<BN, Epi::kResid>(op, st);
@@ -458,16 +567,13 @@ bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t
     return true;
 }
 
-bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
-                  int bn, const char** err)
+namespace {
+
+// Checks of the epilogue arguments shared by the GEMM and the convolution.
+bool check_epilogue(Epi epi, const GemmArgs& args, int bn, const char** err)
 {
-    op.ready = false;
     if (bn != 64 && bn != 128 && bn != 256) {
         *err = "gemm: tile width must be 64, 128 or 256";
-        return false;
-    }
-    if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
-        *err = "gemm: M, N, K must be positive, N a multiple of 32, K a multiple of 8";
         return false;
     }
     if (epi == Epi::kQkv && (bn < 128 || args.D % bn || args.N != 3 * args.D || !args.qh || !args.kh || !args.vh)) {
@@ -490,6 +596,31 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
         *err = "gemm: f32 output needs out and ldo a multiple of 4";
         return false;
     }
+    if (epi == Epi::kAdd && (!args.out || (args.ldo & (args.out_f32 ? 3 : 7)) || (args.add_resid && (args.ld_add_resid & 3)))) {
+        *err = "gemm: add epilogue needs out with an aligned ldo (and an aligned residual)";
+        return false;
+    }
+    if (epi == Epi::kHeads && ((args.head_dim != 64 && args.head_dim != 128) || args.D % args.head_dim ||
+                               args.part0 < 0 || (args.N + args.D - 1) / args.D + args.part0 > 3)) {
+        *err = "gemm: heads epilogue needs head_dim 64 or 128 dividing D and at most 3 parts";
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
+                  int bn, const char** err)
+{
+    op.ready = false;
+    op.conv = false;
+    if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
+        *err = "gemm: M, N, K must be positive, N a multiple of 32, K a multiple of 8";
+        return false;
+    }
+    if (!check_epilogue(epi, args, bn, err))
+        return false;
     if (!make_tmap_bf16_2d(&op.ta, X, uint64_t(args.K), uint64_t(args.M), uint64_t(ldx) * 2, kBK, kBM, err))
         return false;
     if (!make_tmap_bf16_2d(&op.tb, W, uint64_t(args.K), uint64_t(args.N), uint64_t(ldw) * 2, kBK, uint32_t(bn), err))
@@ -498,6 +629,84 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
     op.epi = epi;
     op.bn = bn;
     const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + bn - 1) / bn);
+    op.grid = tiles < num_sms() ? tiles : num_sms();
+    op.ready = true;
+    return true;
+}
+
+bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int C, const void* W, int Cout,
+                  int taps, int stride, const GemmArgs& args_in, int bn, const char** err)
+{
+    op.ready = false;
+    if (epi != Epi::kBF16 && epi != Epi::kAdd) {
+        *err = "conv: only the plain / activation and add epilogues";
+        return false;
+    }
+    if ((taps != 9 && taps != 1) || (stride != 1 && stride != 2) || (taps == 1 && stride != 1) || B <= 0 ||
+        Hi <= 0 || Wi <= 0 || C <= 0 || C % kBK || Cout <= 0 || Cout % 32) {
+        *err = "conv: taps 9 (3x3, padding 1) or 1, stride 1 or 2 (3x3 only), C a multiple of 64, Cout of 32";
+        return false;
+    }
+    GemmArgs a = args_in;
+    const int Ho = taps == 9 ? (Hi + 2 - 3) / stride + 1 : Hi, Wo = taps == 9 ? (Wi + 2 - 3) / stride + 1 : Wi;
+    // Tile: tw columns x (128 / tw) rows of output pixels, tw the widest power of two <= 128 dividing Wo.
+    int tw = 128;
+    while (tw > 1 && Wo % tw)
+        tw >>= 1;
+    if (tw < 8) {
+        *err = "conv: the output width must be a multiple of 8";
+        return false;
+    }
+    a.conv_b = B;
+    a.conv_hi = Hi;
+    a.conv_wi = Wi;
+    a.conv_c = C;
+    a.conv_ho = Ho;
+    a.conv_wo = Wo;
+    a.conv_stride = stride;
+    a.conv_taps = taps;
+    a.conv_pad = taps == 9 ? 1 : 0;
+    a.conv_tw = tw;
+    a.conv_th = 128 / tw;
+    a.M = B * Ho * Wo;
+    a.N = Cout;
+    a.K = taps * C;
+    if (a.seg_rows == (1 << 30))
+        a.seg_rows = Ho * Wo;  // per-sample vectors index by image
+    if (!check_epilogue(epi, a, bn, err))
+        return false;
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    if (reinterpret_cast<uintptr_t>(X) & 15) {
+        *err = "conv: input not 16-byte aligned";
+        return false;
+    }
+    // Input [B][Hi][Wi][C] read as windows of 64 channels x (tw * stride) x (th * stride) pixels, every stride-th
+    // pixel, 128-byte swizzle: the smem tile is 128 rows (pixels) of 64 channels like the GEMM's A tile.
+    cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(Wi), cuuint64_t(Hi), cuuint64_t(B)};
+    cuuint64_t strides[3] = {cuuint64_t(C) * 2, cuuint64_t(Wi) * C * 2, cuuint64_t(Hi) * Wi * C * 2};
+    cuuint32_t box[4] = {cuuint32_t(kBK), cuuint32_t(tw * stride), cuuint32_t((128 / tw) * stride), 1};
+    cuuint32_t es[4] = {1, cuuint32_t(stride), cuuint32_t(stride), 1};
+    if (box[1] > 256 || box[2] > 256) {
+        *err = "conv: tile window too large";
+        return false;
+    }
+    if (fn(&op.ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(X), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        *err = "conv: input tensor map encoding failed";
+        return false;
+    }
+    if (!make_tmap_bf16_2d(&op.tb, W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
+        return false;
+    op.args = a;
+    op.epi = epi;
+    op.bn = bn;
+    op.conv = true;
+    const int tiles = B * (Wo / tw) * ((Ho + a.conv_th - 1) / a.conv_th) * ((Cout + bn - 1) / bn);
     op.grid = tiles < num_sms() ? tiles : num_sms();
     op.ready = true;
     return true;

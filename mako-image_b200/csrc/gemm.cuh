@@ -18,8 +18,14 @@ enum class Epi : int {
     kF32 = 1,     // out_f32[row][col]  = act(acc + bias)
     kResid = 2,   // resid[row][col] += g(gate[b][col]) * (acc + bias), fp32 residual stream
     kQkv = 3,     // q/k: RMSNorm per 128-wide head, weight, RoPE; v: as is; bf16 into [B][H][L][128]
-    kSwiGLU = 4,  // columns come in 128-wide (gate | up) pairs: out_bf16[row][col/2] = silu(gate) * up
+    kSwiGLU = 4,  // columns come in 128-wide (first | second) pairs: out_bf16[row][col/2] = glu(first, second)
+    kAdd = 5,     // out[row][col] = acc + bias + addvec[sample][col] + resid[row][col], fp32 or bf16 out
+    kHeads = 6,   // scatter into head-major [B][H][L][head_dim] bf16 (no norm): the layout of q/k/v
 };
+
+// kSwiGLU variants: the reference's SwiGLU (gate rows first) and SDXL's GEGLU (hidden rows first, erf GELU on the
+// gate half).
+enum Glu : int { kGluSilu = 0, kGluGelu = 1 };
 
 enum Act : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };
 
@@ -48,9 +54,24 @@ struct GemmArgs {
     const float* norm_q = nullptr;  // [128]
     const float* norm_k = nullptr;  // [128]
     const float* rope = nullptr;    // [L][64][2] (cos, sin) per joint position, or null for no rotation
-    int D = 0;                      // width of each of q, k, v (heads * 128)
+    int D = 0;                      // width of each of q, k, v (heads * head_dim)
     int L = 0;                      // joint sequence length of the head layout
     float eps = 1e-6f;
+    int head_dim = 128;             // kHeads: 64 or 128
+    int part0 = 0;                  // kHeads: the first column block goes to q (0), k (1) or v (2)
+    // kSwiGLU
+    int glu = kGluSilu;
+    // kAdd
+    const float* addvec = nullptr;  // per-sample vector (sample = row / seg_rows), stride addvec_stride
+    long addvec_stride = 0;
+    const float* add_resid = nullptr;  // fp32 [row][col] rows ld_add_resid apart (may alias out)
+    long ld_add_resid = 0;
+    int out_f32 = 1;
+    // 3x3 / 1x1 convolution as an implicit GEMM (k_gemm's conv mode): the A operand is the channels-last bf16
+    // input [B][conv_hi][conv_wi][conv_c], the output pixel grid [B][conv_ho][conv_wo] is cut into tiles of
+    // conv_th x conv_tw pixels (128 rows), and K = conv_taps * conv_c runs tap by tap.
+    int conv_hi = 0, conv_wi = 0, conv_c = 0, conv_ho = 0, conv_wo = 0;
+    int conv_stride = 1, conv_taps = 0, conv_pad = 0, conv_tw = 16, conv_th = 8, conv_b = 0;
     uint32_t* status = nullptr;     // error bits (kErr*), may be null
 };
 
@@ -62,6 +83,7 @@ struct GemmOp {
     Epi epi = Epi::kBF16;
     int bn = 256;
     int grid = 0;
+    bool conv = false;
     bool ready = false;
 };
 
@@ -70,6 +92,12 @@ struct GemmOp {
 bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                   int bn, const char** err);
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+// Builds a convolution as an implicit GEMM: X is the channels-last bf16 input [B][Hi][Wi][C] (C a multiple of 64),
+// W the weights [Cout][taps][C] (taps 9 = 3x3 with padding 1, or 1), stride 1 or 2. args.M / N / K are filled in;
+// the output pixel of tile row r is written at row (b * Ho + y) * Wo + x of the epilogue's output.
+bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int C, const void* W, int Cout,
+                  int taps, int stride, const GemmArgs& args, int bn, const char** err);
 
 int num_sms();
 

@@ -226,6 +226,147 @@ __global__ void k_cfg_euler(float* x, const float* vc, const float* vu, float g,
     }
 }
 
+// ---- GroupNorm
+
+constexpr int kGnChunk = 32;  // pixels per statistics chunk
+
+// Chan et al.'s pairwise combination of (count, mean, M2).
+__device__ __forceinline__ void chan_combine(float& n, float& mean, float& m2, float nb, float meanb, float m2b)
+{
+    const float nn = n + nb;
+    if (nn <= 0.f)
+        return;
+    const float d = meanb - mean;
+    mean += d * (nb / nn);
+    m2 += m2b + d * d * (n * nb / nn);
+    n = nn;
+}
+
+__global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a)
+{
+    extern __shared__ float sh[];  // [C] means, [C] M2
+    const int chunk = blockIdx.x, b = blockIdx.y;
+    const int p0 = chunk * kGnChunk, np = min(kGnChunk, a.HW - p0);
+    const float* xb = a.x + (long(b) * a.HW + p0) * a.C;
+    for (int c = threadIdx.x; c < a.C; c += blockDim.x) {
+        float s = 0.f;
+        for (int p = 0; p < np; ++p)
+            s += xb[long(p) * a.C + c];
+        const float mean = s / float(np);
+        float m2 = 0.f;
+        for (int p = 0; p < np; ++p) {
+            const float d = xb[long(p) * a.C + c] - mean;
+            m2 += d * d;
+        }
+        sh[c] = mean;
+        sh[a.C + c] = m2;
+    }
+    __syncthreads();
+    const int cpg = a.C / a.groups;
+    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
+    for (int g = threadIdx.x; g < a.groups; g += blockDim.x) {
+        float n = 0.f, mean = 0.f, m2 = 0.f;
+        for (int c = g * cpg; c < (g + 1) * cpg; ++c)
+            chan_combine(n, mean, m2, float(np), sh[c], sh[a.C + c]);
+        float* o = a.ws + ((long(b) * nchunks + chunk) * a.groups + g) * 3;
+        o[0] = n;
+        o[1] = mean;
+        o[2] = m2;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a)
+{
+    __shared__ float sn[256], sm[256], sq[256];
+    const int g = blockIdx.x, b = blockIdx.y;
+    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
+    float n = 0.f, mean = 0.f, m2 = 0.f;
+    for (int k = threadIdx.x; k < nchunks; k += blockDim.x) {
+        const float* o = a.ws + ((long(b) * nchunks + k) * a.groups + g) * 3;
+        chan_combine(n, mean, m2, o[0], o[1], o[2]);
+    }
+    sn[threadIdx.x] = n;
+    sm[threadIdx.x] = mean;
+    sq[threadIdx.x] = m2;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            float nn = sn[threadIdx.x], mm = sm[threadIdx.x], qq = sq[threadIdx.x];
+            chan_combine(nn, mm, qq, sn[threadIdx.x + w], sm[threadIdx.x + w], sq[threadIdx.x + w]);
+            sn[threadIdx.x] = nn;
+            sm[threadIdx.x] = mm;
+            sq[threadIdx.x] = qq;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        float* f = a.ws + long(a.B) * nchunks * a.groups * 3 + (long(b) * a.groups + g) * 2;
+        f[0] = sm[0];
+        f[1] = rsqrtf(sq[0] / fmaxf(sn[0], 1.f) + a.eps);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a)
+{
+    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
+    const float* fin = a.ws + long(a.B) * nchunks * a.groups * 3;
+    const int cpg = a.C / a.groups, c4n = a.C / 4;
+    const uint64_t total = uint64_t(a.B) * a.HW * c4n;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % c4n) * 4;
+        const int b = int(i / (uint64_t(a.HW) * c4n));
+        const float4 v = reinterpret_cast<const float4*>(a.x)[i];
+        float r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int g = (c + k) / cpg;
+            const float mean = fin[(long(b) * a.groups + g) * 2], rstd = fin[(long(b) * a.groups + g) * 2 + 1];
+            float y = (r[k] - mean) * rstd * a.gamma[c + k] + (a.beta ? a.beta[c + k] : 0.f);
+            if (a.silu)
+                y = y / (1.f + __expf(-y));
+            r[k] = y;
+        }
+        reinterpret_cast<uint2*>(a.y)[i] = pack4_bf16(r[0], r[1], r[2], r[3]);
+    }
+}
+
+__global__ void k_upsample2x(const float4* x, uint2* y, int B, int H, int W, int C4)
+{
+    const uint64_t total = uint64_t(B) * 2 * H * 2 * W * C4;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % C4);
+        const uint64_t px = i / C4;
+        const int ox = int(px % (2 * W)), oy = int((px / (2 * W)) % (2 * H)), b = int(px / (4ull * W * H));
+        const float4 v = x[((uint64_t(b) * H + oy / 2) * W + ox / 2) * C4 + c];
+        y[i] = pack4_bf16(v.x, v.y, v.z, v.w);
+    }
+}
+
+__global__ void k_concat(const float4* a, int Ca4, const float4* b, int Cb4, float4* y, long P)
+{
+    const int C4 = Ca4 + Cb4;
+    const uint64_t total = uint64_t(P) * C4;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % C4);
+        const uint64_t p = i / C4;
+        y[i] = c < Ca4 ? a[p * Ca4 + c] : b[p * Cb4 + (c - Ca4)];
+    }
+}
+
+__global__ void k_pad_channels(const float* x, int C, __nv_bfloat16* y, int Cp, long P)
+{
+    const uint64_t total = uint64_t(P) * Cp;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % Cp);
+        const uint64_t p = i / Cp;
+        y[i] = __float2bfloat16_rn(c < C ? x[p * C + c] : 0.f);
+    }
+}
+
 int grid_for(uint64_t n, int threads)
 {
     uint64_t g = (n + threads - 1) / threads;
@@ -357,6 +498,61 @@ cudaError_t copy_head_rows(const __nv_bfloat16* src, int src_rows, int src_off, 
     const uint64_t n = uint64_t(heads) * rows * 16;
     k_copy_heads<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(src), src_rows, src_off,
                                                    reinterpret_cast<uint4*>(dst), dst_rows, dst_off, heads, rows);
+    count_launch();
+    return cudaGetLastError();
+}
+
+size_t group_norm_workspace(int B, int HW, int C, int groups)
+{
+    (void)C;
+    const size_t nchunks = (size_t(HW) + kGnChunk - 1) / kGnChunk;
+    return (size_t(B) * nchunks * groups * 3 + size_t(B) * groups * 2) * sizeof(float);
+}
+
+cudaError_t group_norm(const GnArgs& a, cudaStream_t st)
+{
+    if (a.B <= 0 || a.HW <= 0 || a.groups <= 0 || a.C % a.groups || a.C % 4 || a.C > 6144 || !a.ws || !a.gamma)
+        return cudaErrorInvalidValue;
+    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
+    k_gn_stats<<<dim3(nchunks, a.B), 256, 2 * a.C * sizeof(float), st>>>(a);
+    count_launch();
+    k_gn_finalize<<<dim3(a.groups, a.B), 256, 0, st>>>(a);
+    count_launch();
+    const uint64_t n = uint64_t(a.B) * a.HW * (a.C / 4);
+    k_gn_apply<<<grid_for(n, 256), 256, 0, st>>>(a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t upsample2x_bf16(const float* x, __nv_bfloat16* y, int B, int H, int W, int C, cudaStream_t st)
+{
+    if (C % 4)
+        return cudaErrorInvalidValue;
+    const uint64_t n = uint64_t(B) * 4 * H * W * (C / 4);
+    k_upsample2x<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y),
+                                                     B, H, W, C / 4);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t concat_channels(const float* a, int Ca, const float* b, int Cb, float* y, long P, cudaStream_t st)
+{
+    if (Ca % 4 || Cb % 4)
+        return cudaErrorInvalidValue;
+    const uint64_t n = uint64_t(P) * (Ca + Cb) / 4;
+    k_concat<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(a), Ca / 4,
+                                                reinterpret_cast<const float4*>(b), Cb / 4,
+                                                reinterpret_cast<float4*>(y), P);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t pad_channels_bf16(const float* x, int C, __nv_bfloat16* y, int Cp, long P, cudaStream_t st)
+{
+    if (C > Cp)
+        return cudaErrorInvalidValue;
+    const uint64_t n = uint64_t(P) * Cp;
+    k_pad_channels<<<grid_for(n, 256), 256, 0, st>>>(x, C, y, Cp, P);
     count_launch();
     return cudaGetLastError();
 }

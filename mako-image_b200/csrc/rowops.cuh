@@ -60,6 +60,36 @@ cudaError_t silu_f32(const float* x, float* y, uint64_t n, cudaStream_t st);
 cudaError_t copy_head_rows(const __nv_bfloat16* src, int src_rows, int src_off, __nv_bfloat16* dst, int dst_rows,
                            int dst_off, int heads, int rows, cudaStream_t st);
 
+// GroupNorm over channels-last fp32 x [B][HW][C] (groups of C / groups consecutive channels, statistics over the
+// group's channels of all HW pixels of a sample), then y = norm * gamma + beta, optionally SiLU, as bf16. The
+// runtime's group_norm (called at sdxl.cpp:728,732,762,941 and engine.cpp:726). Two passes: per-chunk (count, mean,
+// M2) partials combined with Chan's parallel update, then the apply pass. `ws` is scratch of
+// group_norm_workspace() bytes.
+struct GnArgs {
+    const float* x;
+    __nv_bfloat16* y;
+    const float* gamma;
+    const float* beta;
+    int B, HW, C, groups;
+    float eps;
+    int silu;
+    float* ws;
+};
+size_t group_norm_workspace(int B, int HW, int C, int groups);
+cudaError_t group_norm(const GnArgs& a, cudaStream_t st);
+
+// Nearest 2x upsampling of channels-last fp32 x [B][H][W][C] into bf16 y [B][2H][2W][C] (the upsample2x kernel,
+// src/kernels/image.metal:77-84), ready as a convolution input.
+cudaError_t upsample2x_bf16(const float* x, __nv_bfloat16* y, int B, int H, int W, int C, cudaStream_t st);
+
+// y[p] = [a[p] | b[p]] for pixels p: channel concatenation of fp32 [P][Ca] and [P][Cb] (the skip concat of the
+// UNet's up blocks, sdxl.cpp:910-918).
+cudaError_t concat_channels(const float* a, int Ca, const float* b, int Cb, float* y, long P, cudaStream_t st);
+
+// y[p][0:C] = bf16(x[p][0:C]), y[p][C:Cp] = 0: a thin input (latents) widened to a multiple of 64 channels for the
+// convolution.
+cudaError_t pad_channels_bf16(const float* x, int C, __nv_bfloat16* y, int Cp, long P, cudaStream_t st);
+
 // x[i] += dt * (v_u[i] + g * (v_c[i] - v_u[i])) (classifier-free guidance then an Euler step, engine.cpp:476-480,
 // :500-503); with v_u null: x += dt * v_c.
 cudaError_t cfg_euler(float* x, const float* v_c, const float* v_u, float g, float dt, uint64_t n, cudaStream_t st);

@@ -23,6 +23,12 @@ _SIGS = {
     "mkb_proj_swiglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
     "mkb_swiglu_interleave": (_i, []),
     "mkb_check_kernels": (_i, [_u32p]),
+    "mkb_proj_add": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _vp, _l, _vp, _l, _i, _i, _i, _i, _vp]),
+    "mkb_proj_heads": (_i, [_vp, _l, _vp, _l, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "mkb_proj_geglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
+    "mkb_conv2d": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _i, _vp, _vp, _l, _vp, _l, _vp, _l, _i, _vp]),
+    "mkb_group_norm_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i]),
+    "mkb_group_norm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp, ctypes.c_size_t, _vp]),
     "mkb_dit_create": (_i, [_vp, ctypes.POINTER(_vp)]),
     "mkb_dit_destroy": (None, [_vp]),
     "mkb_dit_init_random": (_i, [_vp, _u64, _f]),
@@ -46,7 +52,7 @@ _SIGS = {
     "mkb_er_sde_destroy": (None, [_vp]),
     "mkb_er_sde_sigma": (_f, [_vp, _i]),
     "mkb_er_sde_step": (_i, [_vp, _i, _vp, _vp, _vp, _l, _f]),
-    "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
+    "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
 }
 
 

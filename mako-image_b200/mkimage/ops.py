@@ -71,14 +71,82 @@ MASK_NONE, MASK_COND_CAUSAL = 0, 1
 
 
 def attention(q, k, v, out0, out1, split, Lq=None, Lk=None, q_pos0=0, mask=MASK_NONE, cond_len=0):
-    """Flash attention over head-major q [B][H][Lq_rows][128], k/v [B][H][Lk_rows][128]; rows routed into out0
+    """Flash attention over head-major q [B][H][Lq_rows][d], k/v [B][H][Lk_rows][d] (d 64 or 128); rows routed into out0
     (joint positions < split) and out1 (see mkb_attention)."""
-    B, H, Lq_rows, _ = q.shape
+    B, H, Lq_rows, hd = q.shape
     Lk_rows = k.shape[2]
     Lq = Lq or Lq_rows
     Lk = Lk or Lk_rows
     rows0 = out0.shape[0] // B if out0 is not None else 0
     rows1 = out1.shape[0] // B
-    check(lib.mkb_attention(_p(q), Lq, Lq_rows, _p(k), _p(v), Lk, Lk_rows, B, H, q_pos0, mask, cond_len, split,
+    check(lib.mkb_attention(_p(q), Lq, Lq_rows, _p(k), _p(v), Lk, Lk_rows, B, H, hd, q_pos0, mask, cond_len, split,
                             _p(out0), out0.stride(0) if out0 is not None else 0, rows0, _p(out1), out1.stride(0),
                             rows1, stream_ptr()))
+
+
+def proj_add(x, w, bias=None, addvec=None, rows_per_sample=None, resid=None, out=None, out_f32=True):
+    """y = x @ w.T + bias + addvec[row // rows_per_sample] + resid (fp32 or bf16 out; resid may be out)."""
+    import torch
+
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=torch.float32 if out_f32 else torch.bfloat16)
+    check(lib.mkb_proj_add(_p(x), x.stride(0), _p(w), w.stride(0), _p(bias), _p(addvec),
+                           addvec.stride(0) if addvec is not None and addvec.dim() > 1 else 0, rows_per_sample or M,
+                           _p(resid), resid.stride(0) if resid is not None else 0, _p(out), out.stride(0),
+                           int(out_f32), M, N, K, stream_ptr()))
+    return out
+
+
+def proj_heads(x, w, bias, qh, kh, vh, part0, D, rows_per_sample, pos_offset):
+    """Scatter x @ w.T + bias into head-major q/k/v [samples][heads][L][head_dim] (no norm)."""
+    M, K = x.shape
+    N = w.shape[0]
+    ref = next(t for t in (qh, kh, vh) if t is not None)
+    L, hd = ref.shape[2], ref.shape[3]
+    check(lib.mkb_proj_heads(_p(x), x.stride(0), _p(w), w.stride(0), _p(bias), _p(qh), _p(kh), _p(vh), part0, D, hd,
+                             L, rows_per_sample, pos_offset, M, N, K, stream_ptr()))
+
+
+def proj_geglu(x, w_interleaved, bias=None, out=None):
+    import torch
+
+    M, K = x.shape
+    N = w_interleaved.shape[0]
+    if out is None:
+        out = torch.empty(M, N // 2, device=x.device, dtype=torch.bfloat16)
+    check(lib.mkb_proj_geglu(_p(x), x.stride(0), _p(w_interleaved), w_interleaved.stride(0), _p(bias), _p(out),
+                             out.stride(0), M, N, K, stream_ptr()))
+    return out
+
+
+def conv2d(x, w, taps=9, stride=1, bias=None, addvec=None, resid=None, out=None, out_f32=True):
+    """x: channels-last bf16 [B][H][W][C]; w: bf16 [Cout][taps * C]; returns [B][Ho][Wo][Cout]."""
+    import torch
+
+    B, H, W, C = x.shape
+    Cout = w.shape[0]
+    Ho = (H - 1) // stride + 1 if taps == 9 else H
+    Wo = (W - 1) // stride + 1 if taps == 9 else W
+    if out is None:
+        out = torch.empty(B, Ho, Wo, Cout, device=x.device, dtype=torch.float32 if out_f32 else torch.bfloat16)
+    check(lib.mkb_conv2d(_p(x), B, H, W, C, _p(w), Cout, taps, stride, _p(bias), _p(addvec),
+                         addvec.stride(0) if addvec is not None else 0, _p(resid), Cout if resid is not None else 0,
+                         _p(out), Cout, int(out_f32), stream_ptr()))
+    return out
+
+
+def group_norm(x, gamma, beta, groups=32, eps=1e-5, silu=False, out=None):
+    """x: fp32 channels-last [B][HW][C] (any shape with that memory order); returns bf16 of the same shape."""
+    import torch
+
+    B, C = x.shape[0], x.shape[-1]
+    HW = x.numel() // (B * C)
+    ws_bytes = lib.mkb_group_norm_workspace_size(B, HW, C, groups)
+    ws = torch.empty(max(ws_bytes, 16) // 4 + 1, device=x.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    check(lib.mkb_group_norm(_p(x), _p(out), _p(gamma), _p(beta), B, HW, C, groups, eps, int(silu), _p(ws),
+                             ws.numel() * 4, stream_ptr()))
+    return out

@@ -89,3 +89,67 @@ def timestep_sinusoid(sigma, dim=256):
     freq = np.exp(-np.log(np.float32(10000.0)) * i / np.float32(half)).astype(np.float32)
     arg = np.float32(1000.0 * sigma) * freq
     return np.concatenate([np.cos(arg), np.sin(arg)]).astype(np.float32)
+
+
+def gelu_erf(x):
+    """GELU with the exact erf (SDXL's GEGLU, src/kernels/image.metal:451-463,476-484; the oracle uses the exact erf
+    rather than the reference's fitted one)."""
+    from math import erf
+
+    x = np.asarray(x, np.float64)
+    v = np.vectorize(erf)(x * 0.7071067811865476) if x.size < 4096 else _erf_np(x * 0.7071067811865476)
+    return (0.5 * x * (1.0 + v)).astype(np.float32)
+
+
+def _erf_np(z):
+    import scipy.special
+
+    return scipy.special.erf(z)
+
+
+def conv2d_nhwc(x, w, stride=1, taps=9, bias=None):
+    """Convolution of channels-last x [B][H][W][C] with w [Cout][taps][C] (taps 9: 3x3, padding 1; taps 1: 1x1):
+    the runtime's conv (im2col + GEMM, docs/architecture.md:178; called at sdxl.cpp:729-735), in fp32."""
+    x = np.asarray(x, np.float32)
+    B, H, W, C = x.shape
+    Cout = w.shape[0]
+    if taps == 1:
+        y = x.reshape(-1, C) @ np.asarray(w, np.float32).reshape(Cout, C).T
+        y = y.reshape(B, H, W, Cout)
+    else:
+        xp = np.zeros((B, H + 2, W + 2, C), np.float32)
+        xp[:, 1:H + 1, 1:W + 1] = x
+        Ho, Wo = (H - 1) // stride + 1, (W - 1) // stride + 1
+        cols = np.empty((B, Ho, Wo, 9, C), np.float32)
+        for dy in range(3):
+            for dx in range(3):
+                cols[:, :, :, dy * 3 + dx] = xp[:, dy:dy + stride * (Ho - 1) + 1:stride, dx:dx + stride * (Wo - 1) + 1:stride]
+        y = cols.reshape(-1, 9 * C) @ np.asarray(w, np.float32).reshape(Cout, 9 * C).T
+        y = y.reshape(B, Ho, Wo, Cout)
+    if bias is not None:
+        y = y + np.asarray(bias, np.float32)
+    return y.astype(np.float32)
+
+
+def group_norm_nhwc(x, gamma, beta, groups=32, eps=1e-5, silu=False):
+    """GroupNorm over channels-last x [B][..][C]: statistics per sample over the group's C/groups consecutive
+    channels and all pixels (the runtime's group_norm, sdxl.cpp:728; optional fused SiLU, its `true` argument)."""
+    x = np.asarray(x, np.float32)
+    B, C = x.shape[0], x.shape[-1]
+    xr = x.reshape(B, -1, groups, C // groups).astype(np.float64)
+    mean = xr.mean(axis=(1, 3), keepdims=True)
+    var = ((xr - mean) ** 2).mean(axis=(1, 3), keepdims=True)
+    y = ((xr - mean) / np.sqrt(var + eps)).reshape(x.shape) * np.asarray(gamma, np.float64)
+    if beta is not None:
+        y = y + np.asarray(beta, np.float64)
+    y = y.astype(np.float32)
+    return silu_(y) if silu else y
+
+
+def silu_(x):
+    return (x / (1.0 + np.exp(-x.astype(np.float64)))).astype(np.float32)
+
+
+def upsample2x_nhwc(x):
+    """Nearest 2x (upsample2x, src/kernels/image.metal:77-84)."""
+    return np.repeat(np.repeat(np.asarray(x, np.float32), 2, axis=1), 2, axis=2)
