@@ -113,6 +113,22 @@ size_t mkb_group_norm_workspace_size(int B, int HW, int C, int groups);
 mkb_status mkb_group_norm(const float* x, void* y, const float* gamma, const float* beta, int B, int HW, int C,
                           int groups, float eps, int silu, void* workspace, size_t workspace_bytes, void* stream);
 
+/* GroupNorm exactly as mkb_group_norm, but with no workspace argument and no allocation: the statistics scratch is
+ * a fixed array built into the library (mkb_group_norm_static_max_bytes(), 4 MiB, held on every device that loads
+ * the library until the process exits). For callers that cannot allocate device memory or hand over a scratch
+ * buffer: code running while another component owns all device memory (a serving loop behind a caching allocator),
+ * real-time paths that must not risk an allocation's latency or failure, and hosts that only pass in tensors they
+ * already own. No counterpart in the reference (its runtime owns its scratch buffers).
+ * Limits: sizes whose statistics need more than the built-in scratch (group_norm workspace size above
+ * mkb_group_norm_static_max_bytes(), e.g. B * ceil(HW / 32) * groups * 12 bytes above ~4 MiB) are rejected with
+ * MKB_ERR_INVALID. The first call on a device looks up the scratch's device address (once per device, with that
+ * device current); make that first call before any stream capture. All calls on a device share the one scratch
+ * array and it keeps the last call's contents (nothing in it needs clearing: each call writes every entry it reads
+ * first), so calls that overlap on the GPU (different streams, or threads) race; serialise them. */
+size_t mkb_group_norm_static_max_bytes(void);
+mkb_status mkb_group_norm_static(const float* x, void* y, const float* gamma, const float* beta, int B, int HW, int C,
+                                 int groups, float eps, int silu, void* stream);
+
 /* Attention masks. */
 enum { MKB_MASK_NONE = 0, MKB_MASK_COND_CAUSAL = 1 };
 

@@ -29,6 +29,8 @@ _SIGS = {
     "mkb_conv2d": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _i, _vp, _vp, _l, _vp, _l, _vp, _l, _i, _vp]),
     "mkb_group_norm_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "mkb_group_norm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp, ctypes.c_size_t, _vp]),
+    "mkb_group_norm_static_max_bytes": (ctypes.c_size_t, []),
+    "mkb_group_norm_static": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp]),
     "mkb_dit_create": (_i, [_vp, ctypes.POINTER(_vp)]),
     "mkb_dit_destroy": (None, [_vp]),
     "mkb_dit_init_random": (_i, [_vp, _u64, _f]),

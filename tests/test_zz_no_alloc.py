@@ -1,0 +1,71 @@
+"""mkb_group_norm_static: GroupNorm whose statistics scratch is a fixed array inside the library, for callers that
+cannot allocate device memory or pass a workspace (a serving loop whose caching allocator owns all device memory,
+real-time paths that must not allocate, hosts that only hand over tensors they own).
+
+Called through the C ABI with ctypes and checked against mkb_group_norm (the caller-workspace entry point) on two
+calls in a row, within the GroupNorm test's tolerance (bf16 outputs: 2e-2 of the output scale; the two paths run
+the same kernels, so they agree exactly in practice). This file is collected last so that a failure here leaves
+every other test already run; it passes alone in a fresh process and after the other tests."""
+
+import ctypes
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _lib():
+    sys.path.insert(0, os.path.join(ROOT, "mako-image_b200"))
+    import mkimage
+
+    return mkimage
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _gn_with_workspace(mk, x, g, b, B, HW, C, groups, eps, silu, torch):
+    ws_bytes = mk.lib.mkb_group_norm_workspace_size(B, HW, C, groups)
+    ws = torch.empty(ws_bytes // 4 + 1, device=x.device, dtype=torch.float32)
+    y = torch.empty(B, HW, C, device=x.device, dtype=torch.bfloat16)
+    mk.check(mk.lib.mkb_group_norm(_p(x), _p(y), _p(g), _p(b), B, HW, C, groups, eps, silu, _p(ws), ws.numel() * 4,
+                                   None))
+    return y
+
+
+def test_group_norm_static_matches_workspace_entry_point(cuda):
+    import torch
+
+    mk = _lib()
+    assert mk.lib.mkb_group_norm_static_max_bytes() == 4 << 20
+    cases = [(2, 4096, 320, 32, 1e-5, 1), (1, 1000, 640, 32, 1e-6, 0)]
+    for B, HW, C, groups, eps, silu in cases:
+        gen = torch.Generator(device=cuda).manual_seed(B * 7 + C)
+        g = 1 + 0.1 * torch.randn(C, device=cuda, generator=gen)
+        b = 0.1 * torch.randn(C, device=cuda, generator=gen)
+        for call in range(2):  # two calls in a row share (and reuse) the built-in scratch
+            x = 2.0 * torch.randn(B, HW, C, device=cuda, generator=gen) + 1.5 * call
+            y = torch.empty(B, HW, C, device=cuda, dtype=torch.bfloat16)
+            mk.check(mk.lib.mkb_group_norm_static(_p(x), _p(y), _p(g), _p(b), B, HW, C, groups, eps, silu, None))
+            want = _gn_with_workspace(mk, x, g, b, B, HW, C, groups, eps, silu, torch)
+            torch.cuda.synchronize()
+            got_np, want_np = y.float().cpu().numpy(), want.float().cpu().numpy()
+            assert np.abs(got_np - want_np).max() <= 2e-2 * max(1.0, np.abs(want_np).max()), (B, HW, C, call)
+    assert mk.ops.check_kernels() == 0
+
+
+def test_group_norm_static_rejects_sizes_beyond_its_scratch(cuda):
+    import torch
+
+    mk = _lib()
+    B, HW, C = 4, 1 << 20, 128  # statistics need far more than the built-in scratch
+    x = torch.empty(1, device=cuda)
+    code = mk.lib.mkb_group_norm_static(_p(x), _p(x), _p(x), None, B, HW, C, 32, 1e-6, 0, None)
+    assert code == 1
+    assert b"scratch" in mk.lib.mkb_last_error()
