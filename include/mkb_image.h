@@ -264,6 +264,77 @@ float mkb_er_sde_sigma(const mkb_er_sde* e, int i);
 mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised, const float* noise, long n,
                            float s_noise);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * The SDXL UNet (Sdxl::begin / step, src/image/sdxl.cpp:672-953) and the SDXL VAE decoder (Engine::decode,
+ * src/image/engine.cpp:862-954 with the AutoencoderKL layout). Latents cross the boundary as the reference's tokens:
+ * [gh * gw][16], each a 2x2 patch of the 4-channel latent image (sdxl.cpp:80-87).
+ * Weights are named by block position ("in4.res.conv1.w", "out3.attn.b1.ff1.w", ...; mkb_unet_weight_info), a
+ * 3x3 convolution is [Cout][3][3][Cin], a 1x1 one [Cout][Cin], q/k/v stacked ([3c][c]) and the GEGLU projection
+ * [8c][c] (hidden rows, then gate rows) as the reference stacks them (sdxl.cpp:285-299).
+ * ------------------------------------------------------------------------------------------------------------- */
+
+typedef struct mkb_unet_config {
+    int channels[3];  /* per level: 320, 640, 1280 (multiples of 64; 128 where a level has attention) */
+    int depth[3];     /* transformer blocks per attention layer of each level: 0, 2, 10 (the middle uses depth[2]) */
+    int layers;       /* residual blocks per down level (2); up levels have layers + 1 */
+    int context_dim;  /* 2048 */
+    int pooled_dim;   /* 1280 */
+    int max_batch;    /* samples per step (sample i uses slot slot0 + i) */
+    int max_gh, max_gw; /* token grid maxima (the latent image is 2gh x 2gw; gw a multiple of 16, gh even) */
+    int max_context;  /* context rows (77) */
+    int slots;        /* text conditionings kept (2 = cond / uncond) */
+} mkb_unet_config;
+
+typedef struct mkb_unet mkb_unet;
+mkb_status mkb_unet_create(const mkb_unet_config* cfg, mkb_unet** out);
+void mkb_unet_destroy(mkb_unet* u);
+mkb_status mkb_unet_init_random(mkb_unet* u, uint64_t seed, float std);
+int mkb_unet_weight_count(const mkb_unet* u);
+/* Name and logical shape (ndim 1, 2 or 4 of dims[4]) of weight i. */
+mkb_status mkb_unet_weight_info(const mkb_unet* u, int i, const char** name, long* dims, int* ndim);
+mkb_status mkb_unet_weight_read(mkb_unet* u, const char* name, float* host);
+mkb_status mkb_unet_weight_write(mkb_unet* u, const char* name, const float* host);
+/* Sdxl::begin: the context [S][context_dim] and pooled state [pooled_dim] of one prompt on a gh x gw token grid:
+ * the added conditioning and every transformer block's cross-attention K/V, kept per slot. */
+mkb_status mkb_unet_begin(mkb_unet* u, const float* context, int S, const float* pooled, int gh, int gw, int slot);
+/* Sdxl::step: predicted noise tokens for latent tokens at noise level sigma (host buffers). */
+mkb_status mkb_unet_step(mkb_unet* u, const float* latents, float sigma, float* out, int slot);
+/* n samples in one pass, sample i on slot slot0 + i (host / device buffers). */
+mkb_status mkb_unet_step_batch(mkb_unet* u, int n, int slot0, const float* latents, const float* sigmas, float* out);
+mkb_status mkb_unet_step_batch_dev(mkb_unet* u, int n, int slot0, const float* latents_dev, const float* sigmas,
+                                   float* out_dev, void* stream);
+/* One guided Euler step of a generation: cond (slot 0) and uncond (slot 1) in one batched pass, then
+ * latents += (sigma_next - sigma) (e_u + guidance (e_c - e_u)) on the device (engine.cpp:471-506). */
+mkb_status mkb_unet_step_cfg_dev(mkb_unet* u, float* latents_dev, float sigma, float sigma_next, float guidance,
+                                 void* stream);
+mkb_status mkb_unet_set_probe(mkb_unet* u, mkb_probe_fn fn, void* user);
+double mkb_unet_step_flops(const mkb_unet* u, int n);
+/* Sdxl::sigmas (sdxl.cpp:653-670): steps levels then 0 (out has steps + 1 entries), and Sdxl::timestep (:643-651). */
+mkb_status mkb_sdxl_sigmas(uint32_t steps, float* out);
+int mkb_sdxl_timestep(float sigma);
+
+typedef struct mkb_vae_config {
+    int channels[4]; /* block widths from the output side: 128, 256, 512, 512 (multiples of 128) */
+    int layers;      /* 2: each up level has layers + 1 residual blocks */
+    int latent;      /* 4 latent channels */
+    float scale;     /* latents are tokens / scale (0.13025 for SDXL) */
+    int max_gh, max_gw;
+} mkb_vae_config;
+
+typedef struct mkb_vae mkb_vae;
+mkb_status mkb_vae_create(const mkb_vae_config* cfg, mkb_vae** out);
+void mkb_vae_destroy(mkb_vae* v);
+mkb_status mkb_vae_init_random(mkb_vae* v, uint64_t seed, float std);
+int mkb_vae_weight_count(const mkb_vae* v);
+mkb_status mkb_vae_weight_info(const mkb_vae* v, int i, const char** name, long* dims, int* ndim);
+mkb_status mkb_vae_weight_read(mkb_vae* v, const char* name, float* host);
+mkb_status mkb_vae_weight_write(mkb_vae* v, const char* name, const float* host);
+/* Engine::decode: tokens [gh * gw][16] to RGBA [16 gh][16 gw][4] in [-1, 1] (alpha 1), host / device buffers. */
+mkb_status mkb_vae_decode(mkb_vae* v, const float* latents, int gh, int gw, float* rgba);
+mkb_status mkb_vae_decode_dev(mkb_vae* v, const float* latents_dev, int gh, int gw, float* rgba_dev, void* stream);
+mkb_status mkb_vae_set_probe(mkb_vae* v, mkb_probe_fn fn, void* user);
+double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw);
+
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */
 mkb_status mkb_check_kernels(uint32_t* bits);

@@ -19,6 +19,15 @@ void count_launch(unsigned long long n = 1);
 // The current device's kernel status word (allocated on first use; lives until process exit).
 uint32_t* device_status_word();
 
+#ifndef MKB_TRY
+#define MKB_TRY(expr)                                                                                                  \
+    do {                                                                                                               \
+        mkb_status s_ = (expr);                                                                                        \
+        if (s_ != MKB_OK)                                                                                              \
+            return s_;                                                                                                 \
+    } while (0)
+#endif
+
 #define MKB_TRY_CUDA(expr, what)                                                                                       \
     do {                                                                                                               \
         cudaError_t e_ = (expr);                                                                                       \

@@ -609,12 +609,6 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
     return MKB_OK;
 }
 
-#define MKB_TRY(expr)                                                                                                  \
-    do {                                                                                                               \
-        mkb_status s_ = (expr);                                                                                        \
-        if (s_ != MKB_OK)                                                                                              \
-            return s_;                                                                                                 \
-    } while (0)
 #define MKB_K(expr, what) MKB_TRY_CUDA((expr), what)
 
 // Runs one step for B samples whose latents are in `lat` (device, [B][N][64]) with host noise levels `sigmas`.

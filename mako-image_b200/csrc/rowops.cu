@@ -59,8 +59,9 @@ __global__ void __launch_bounds__(256) k_ln_mod(const LnModArgs a)
             const int c = i * 32 + lane;
             const float4 g = __ldg(sc + c);
             float4 t = sh ? __ldg(sh + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            yr[c] = pack4_bf16((v[i].x - mean) * rstd * (1.f + g.x) + t.x, (v[i].y - mean) * rstd * (1.f + g.y) + t.y,
-                               (v[i].z - mean) * rstd * (1.f + g.z) + t.z, (v[i].w - mean) * rstd * (1.f + g.w) + t.w);
+            const float off = a.affine ? 0.f : 1.f;
+            yr[c] = pack4_bf16((v[i].x - mean) * rstd * (off + g.x) + t.x, (v[i].y - mean) * rstd * (off + g.y) + t.y,
+                               (v[i].z - mean) * rstd * (off + g.z) + t.z, (v[i].w - mean) * rstd * (off + g.w) + t.w);
         }
 }
 
@@ -367,6 +368,106 @@ __global__ void k_pad_channels(const float* x, int C, __nv_bfloat16* y, int Cp, 
     }
 }
 
+__global__ void k_unpack(const float* tok, __nv_bfloat16* img, int B, int gh, int gw, int Cp, float scale)
+{
+    const uint64_t total = uint64_t(B) * 4 * gh * gw * Cp;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % Cp);
+        const uint64_t px = i / Cp;
+        const int x = int(px % (2 * gw)), y = int((px / (2 * gw)) % (2 * gh)), b = int(px / (4ull * gh * gw));
+        float v = 0.f;
+        if (c < 4)
+            v = tok[((uint64_t(b) * gh + y / 2) * gw + x / 2) * 16 + c * 4 + (y % 2) * 2 + x % 2] * scale;
+        img[i] = __float2bfloat16_rn(v);
+    }
+}
+
+__global__ void k_pack(const float* img, int Cs, float* tok, int B, int gh, int gw)
+{
+    const uint64_t total = uint64_t(B) * gh * gw * 16;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int j = int(i % 16);
+        const uint64_t t = i / 16;
+        const int tx = int(t % gw), ty = int((t / gw) % gh), b = int(t / (uint64_t(gh) * gw));
+        const int c = j / 4, y = 2 * ty + (j % 4) / 2, x = 2 * tx + j % 2;
+        tok[i] = img[((uint64_t(b) * 2 * gh + y) * 2 * gw + x) * Cs + c];
+    }
+}
+
+__global__ void k_add_silu(const float* a, const float* b, float* out, uint64_t n)
+{
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float v = a[i] + b[i];
+        out[i] = v / (1.f + expf(-v));
+    }
+}
+
+__global__ void k_to_rgba(const float* img, int Cs, float4* rgba, long P)
+{
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t p = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < uint64_t(P); p += stride) {
+        const float* s = img + p * Cs;
+        rgba[p] = make_float4(fminf(fmaxf(s[0], -1.f), 1.f), fminf(fmaxf(s[1], -1.f), 1.f),
+                              fminf(fmaxf(s[2], -1.f), 1.f), 1.f);
+    }
+}
+
+// One CTA per row: max, then exp-sum, then normalised bf16 probabilities.
+__global__ void __launch_bounds__(256) k_softmax_rows(const float* s, __nv_bfloat16* p, int n, float scale)
+{
+    __shared__ float red[32];
+    const float* r = s + long(blockIdx.x) * n;
+    __nv_bfloat16* o = p + long(blockIdx.x) * n;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        m = fmaxf(m, r[i] * scale);
+    for (int k = 16; k; k >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < blockDim.x / 32; ++w)
+        m = fmaxf(m, red[w]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        sum += __expf(r[i] * scale - m);
+    sum = warp_sum(sum);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < blockDim.x / 32; ++w)
+        tot += red[w];
+    const float inv = 1.f / tot;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        o[i] = __float2bfloat16_rn(__expf(r[i] * scale - m) * inv);
+}
+
+__global__ void k_transpose(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols)
+{
+    __shared__ __nv_bfloat16 tile[32][33];
+    const long r0 = long(blockIdx.x) * 32;
+    const int cb = blockIdx.y * 32;
+    for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+        const long r = r0 + k;
+        const int c = cb + threadIdx.x;
+        if (r < rows && c < cols)
+            tile[k][threadIdx.x] = x[r * ldx + c0 + c];
+    }
+    __syncthreads();
+    for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+        const int c = cb + k;
+        const long r = r0 + threadIdx.x;
+        if (r < rows && c < cols)
+            y[long(c) * rows + r] = tile[threadIdx.x][k];
+    }
+}
+
 int grid_for(uint64_t n, int threads)
 {
     uint64_t g = (n + threads - 1) / threads;
@@ -553,6 +654,53 @@ cudaError_t pad_channels_bf16(const float* x, int C, __nv_bfloat16* y, int Cp, l
         return cudaErrorInvalidValue;
     const uint64_t n = uint64_t(P) * Cp;
     k_pad_channels<<<grid_for(n, 256), 256, 0, st>>>(x, C, y, Cp, P);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, int gh, int gw, int Cp, float scale,
+                               cudaStream_t st)
+{
+    const uint64_t n = uint64_t(B) * 4 * gh * gw * Cp;
+    k_unpack<<<grid_for(n, 256), 256, 0, st>>>(tokens, img, B, gh, gw, Cp, scale);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t pack_tokens(const float* img, int Cs, float* tokens, int B, int gh, int gw, cudaStream_t st)
+{
+    const uint64_t n = uint64_t(B) * gh * gw * 16;
+    k_pack<<<grid_for(n, 256), 256, 0, st>>>(img, Cs, tokens, B, gh, gw);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t add_silu(const float* a, const float* b, float* out, uint64_t n, cudaStream_t st)
+{
+    k_add_silu<<<grid_for(n, 256), 256, 0, st>>>(a, b, out, n);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t to_rgba(const float* img, int Cs, float* rgba, long P, cudaStream_t st)
+{
+    k_to_rgba<<<grid_for(P, 256), 256, 0, st>>>(img, Cs, reinterpret_cast<float4*>(rgba), P);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n, float scale, cudaStream_t st)
+{
+    k_softmax_rows<<<dim3(unsigned(rows)), 256, 0, st>>>(s, p, n, scale);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t transpose_bf16(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols,
+                           cudaStream_t st)
+{
+    dim3 grid(unsigned((rows + 31) / 32), unsigned((cols + 31) / 32));
+    k_transpose<<<grid, dim3(32, 8), 0, st>>>(x, ldx, c0, y, rows, cols);
     count_launch();
     return cudaGetLastError();
 }

@@ -23,6 +23,7 @@ struct LnModArgs {
     int split;
     int rows, D, rows_per_sample;
     float eps;
+    int affine = 0;  // 1: y = norm * scale + shift (a plain LayerNorm with weight and bias)
 };
 cudaError_t ln_modulate(const LnModArgs& a, cudaStream_t st);
 
@@ -89,6 +90,24 @@ cudaError_t concat_channels(const float* a, int Ca, const float* b, int Cb, floa
 // y[p][0:C] = bf16(x[p][0:C]), y[p][C:Cp] = 0: a thin input (latents) widened to a multiple of 64 channels for the
 // convolution.
 cudaError_t pad_channels_bf16(const float* x, int C, __nv_bfloat16* y, int Cp, long P, cudaStream_t st);
+
+// Latent tokens [B][gh*gw][16] (channel, row, column of a 2x2 patch) to the channels-last image bf16
+// [B][2gh][2gw][Cp] times `scale`, channels 4..Cp-1 zero (sdxl.cpp:80-87, engine.cpp:888-898).
+cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, int gh, int gw, int Cp, float scale,
+                               cudaStream_t st);
+// The inverse for the first 4 of Cs channels of fp32 img [B][2gh][2gw][Cs] (sdxl.cpp:946-952).
+cudaError_t pack_tokens(const float* img, int Cs, float* tokens, int B, int gh, int gw, cudaStream_t st);
+// out[i] = silu(a[i] + b[i]).
+cudaError_t add_silu(const float* a, const float* b, float* out, uint64_t n, cudaStream_t st);
+// RGBA [B][H][W][4] = clamp(img[..][0:3], -1, 1), alpha 1, from fp32 img with Cs channels per pixel
+// (engine.cpp:948-953).
+cudaError_t to_rgba(const float* img, int Cs, float* rgba, long P, cudaStream_t st);
+// Row softmax of scale * s (fp32 [rows][n]) into bf16 p (softmax_rows, src/kernels/image.metal:101-128).
+cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n, float scale, cudaStream_t st);
+// y[c][r] = x[r][c0 + c] for rows r < rows, c < cols of bf16 x with row stride ldx (transpose_f32 / copy_cols,
+// image.metal:134-147): V^T for the VAE's mid attention.
+cudaError_t transpose_bf16(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols,
+                           cudaStream_t st);
 
 // x[i] += dt * (v_u[i] + g * (v_c[i] - v_u[i])) (classifier-free guidance then an Euler step, engine.cpp:476-480,
 // :500-503); with v_u null: x += dt * v_c.

@@ -47,6 +47,33 @@ _SIGS = {
     "mkb_dit_set_probe": (_i, [_vp, _vp, _vp]),
     "mkb_dit_step_flops": (ctypes.c_double, [_vp, _i, _i]),
     "mkb_schedule_default": (None, [_vp]),
+    "mkb_unet_create": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "mkb_unet_destroy": (None, [_vp]),
+    "mkb_unet_init_random": (_i, [_vp, _u64, _f]),
+    "mkb_unet_weight_count": (_i, [_vp]),
+    "mkb_unet_weight_info": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_l), ctypes.POINTER(_i)]),
+    "mkb_unet_weight_read": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_unet_weight_write": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_unet_begin": (_i, [_vp, _vp, _i, _vp, _i, _i, _i]),
+    "mkb_unet_step": (_i, [_vp, _vp, _f, _vp, _i]),
+    "mkb_unet_step_batch": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
+    "mkb_unet_step_batch_dev": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "mkb_unet_step_cfg_dev": (_i, [_vp, _vp, _f, _f, _f, _vp]),
+    "mkb_unet_set_probe": (_i, [_vp, _vp, _vp]),
+    "mkb_unet_step_flops": (ctypes.c_double, [_vp, _i]),
+    "mkb_sdxl_sigmas": (_i, [ctypes.c_uint32, _vp]),
+    "mkb_sdxl_timestep": (_i, [_f]),
+    "mkb_vae_create": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "mkb_vae_destroy": (None, [_vp]),
+    "mkb_vae_init_random": (_i, [_vp, _u64, _f]),
+    "mkb_vae_weight_count": (_i, [_vp]),
+    "mkb_vae_weight_info": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_l), ctypes.POINTER(_i)]),
+    "mkb_vae_weight_read": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_vae_weight_write": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_vae_decode": (_i, [_vp, _vp, _i, _i, _vp]),
+    "mkb_vae_decode_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "mkb_vae_set_probe": (_i, [_vp, _vp, _vp]),
+    "mkb_vae_decode_flops": (ctypes.c_double, [_vp, _i, _i]),
     "mkb_sigmas": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp]),
     "mkb_top_sigma": (_f, [_vp, ctypes.c_uint32]),
     "mkb_guided_euler": (None, [_vp, _vp, _vp, _f, _f, _f, _l]),

@@ -1,0 +1,169 @@
+"""The SDXL UNet and VAE decoder handles (include/mkb_image.h part 3) as Python objects."""
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from ._lib import lib, check
+from .dit import _PROBE_FN, _fptr
+
+
+@dataclass
+class UnetConfig:
+    channels: tuple = (320, 640, 1280)
+    depth: tuple = (0, 2, 10)
+    layers: int = 2
+    context_dim: int = 2048
+    pooled_dim: int = 1280
+    max_batch: int = 2
+    max_gh: int = 64
+    max_gw: int = 64
+    max_context: int = 77
+    slots: int = 2
+
+
+class _CUnet(ctypes.Structure):
+    _fields_ = [("channels", ctypes.c_int * 3), ("depth", ctypes.c_int * 3), ("layers", ctypes.c_int),
+                ("context_dim", ctypes.c_int), ("pooled_dim", ctypes.c_int), ("max_batch", ctypes.c_int),
+                ("max_gh", ctypes.c_int), ("max_gw", ctypes.c_int), ("max_context", ctypes.c_int),
+                ("slots", ctypes.c_int)]
+
+
+@dataclass
+class VaeConfig:
+    channels: tuple = (128, 256, 512, 512)
+    layers: int = 2
+    latent: int = 4
+    scale: float = 0.13025
+    max_gh: int = 64
+    max_gw: int = 64
+
+
+class _CVae(ctypes.Structure):
+    _fields_ = [("channels", ctypes.c_int * 4), ("layers", ctypes.c_int), ("latent", ctypes.c_int),
+                ("scale", ctypes.c_float), ("max_gh", ctypes.c_int), ("max_gw", ctypes.c_int)]
+
+
+class _Weights:
+    _prefix = ""
+
+    def _fn(self, n):
+        return getattr(lib, f"mkb_{self._prefix}_{n}")
+
+    def weight_names(self):
+        out = []
+        name, dims, nd = ctypes.c_char_p(), (ctypes.c_long * 4)(), ctypes.c_int()
+        for i in range(self._fn("weight_count")(self.h)):
+            check(self._fn("weight_info")(self.h, i, ctypes.byref(name), dims, ctypes.byref(nd)))
+            out.append((name.value.decode(), tuple(dims[:nd.value])))
+        return out
+
+    def read_weight(self, name, shape):
+        a = np.empty(shape, np.float32)
+        check(self._fn("weight_read")(self.h, name.encode(), _fptr(a)))
+        return a
+
+    def write_weight(self, name, a):
+        a = np.ascontiguousarray(a, np.float32)
+        check(self._fn("weight_write")(self.h, name.encode(), _fptr(a)))
+
+    def weights(self):
+        return {n: self.read_weight(n, s) for n, s in self.weight_names()}
+
+    def init_random(self, seed, std=0.02):
+        check(self._fn("init_random")(self.h, seed, std))
+
+    def set_probe(self, fn):
+        if fn is None:
+            self._probe = None
+            check(self._fn("set_probe")(self.h, None, None))
+            return
+
+        def tramp(name, layer, data, count, user):
+            fn(name.decode(), layer, np.ctypeslib.as_array(data, shape=(count,)).copy())
+
+        self._probe = _PROBE_FN(tramp)
+        check(self._fn("set_probe")(self.h, ctypes.cast(self._probe, ctypes.c_void_p), None))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._fn("destroy")(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Unet(_Weights):
+    _prefix = "unet"
+
+    def __init__(self, cfg: UnetConfig):
+        self.cfg = cfg
+        c = _CUnet((ctypes.c_int * 3)(*cfg.channels), (ctypes.c_int * 3)(*cfg.depth), cfg.layers, cfg.context_dim,
+                   cfg.pooled_dim, cfg.max_batch, cfg.max_gh, cfg.max_gw, cfg.max_context, cfg.slots)
+        h = ctypes.c_void_p()
+        check(lib.mkb_unet_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+        self._probe = None
+
+    def begin(self, context, pooled, gh, gw, slot=0):
+        ctx = np.ascontiguousarray(context, np.float32)
+        pl = np.ascontiguousarray(pooled, np.float32)
+        check(lib.mkb_unet_begin(self.h, _fptr(ctx), ctx.shape[0], _fptr(pl), gh, gw, slot))
+
+    def step_batch(self, latents, sigmas, slot0=0):
+        x = np.ascontiguousarray(latents, np.float32)
+        out = np.empty_like(x)
+        n = len(sigmas)
+        check(lib.mkb_unet_step_batch(self.h, n, slot0, _fptr(x), (ctypes.c_float * n)(*sigmas), _fptr(out)))
+        return out
+
+    def step(self, latents, sigma, slot=0):
+        x = np.ascontiguousarray(latents, np.float32)
+        out = np.empty_like(x)
+        check(lib.mkb_unet_step(self.h, _fptr(x), sigma, _fptr(out), slot))
+        return out
+
+    def step_cfg_dev(self, latents_dev, sigma, sigma_next, guidance, stream=None):
+        check(lib.mkb_unet_step_cfg_dev(self.h, ctypes.c_void_p(latents_dev), sigma, sigma_next, guidance, stream))
+
+    def step_flops(self, n):
+        return lib.mkb_unet_step_flops(self.h, n)
+
+
+class Vae(_Weights):
+    _prefix = "vae"
+
+    def __init__(self, cfg: VaeConfig):
+        self.cfg = cfg
+        c = _CVae((ctypes.c_int * 4)(*cfg.channels), cfg.layers, cfg.latent, cfg.scale, cfg.max_gh, cfg.max_gw)
+        h = ctypes.c_void_p()
+        check(lib.mkb_vae_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+        self._probe = None
+
+    def decode(self, latents, gh, gw):
+        x = np.ascontiguousarray(latents, np.float32)
+        out = np.empty((16 * gh, 16 * gw, 4), np.float32)
+        check(lib.mkb_vae_decode(self.h, _fptr(x), gh, gw, _fptr(out)))
+        return out
+
+    def decode_dev(self, latents_dev, gh, gw, out_dev, stream=None):
+        check(lib.mkb_vae_decode_dev(self.h, ctypes.c_void_p(latents_dev), gh, gw, ctypes.c_void_p(out_dev), stream))
+
+    def decode_flops(self, gh, gw):
+        return lib.mkb_vae_decode_flops(self.h, gh, gw)
+
+
+def sdxl_sigmas(steps):
+    out = np.empty(steps + 1, np.float32)
+    check(lib.mkb_sdxl_sigmas(steps, _fptr(out)))
+    return out
+
+
+def sdxl_timestep(sigma):
+    return lib.mkb_sdxl_timestep(sigma)

@@ -1,0 +1,95 @@
+"""Parity of the SDXL UNet step and VAE decoder against the numpy oracle (oracle/sdxl.py) at reduced widths
+(the same kernels and block structure as the full model; the full sizes run in bench.py).
+
+Bars: the reference's own (tests/sdxl_ref_test.cpp:242, 301): UNet pass rel-RMS < 0.02, VAE rel-RMS < 0.01; plus a
+cosine >= 0.999 on every probed stage."""
+
+import numpy as np
+import pytest
+
+from oracle import rng
+from oracle import sdxl as OS
+
+pytestmark = pytest.mark.gpu
+
+
+def _cos(a, b):
+    a, b = a.astype(np.float64).ravel(), b.astype(np.float64).ravel()
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+def _rel(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(np.sqrt(((a - b) ** 2).sum() / (b ** 2).sum()))
+
+
+def test_unet_step_reduced(cuda):
+    import mkimage
+
+    cfg = dict(channels=(64, 128, 256), depth=(0, 1, 2), layers=2, context_dim=256, pooled_dim=128)
+    gh, gw, S, B = 16, 16, 77, 2
+    u = mkimage.Unet(mkimage.UnetConfig(max_batch=B, max_gh=gh, max_gw=gw, max_context=S, slots=2, **cfg))
+    u.init_random(17)
+    W = u.weights()
+    oc = OS.unet_default_cfg(**cfg)
+    ctxs = [rng.normal(rng.tensor_key(3, 10 + b), S * 256).reshape(S, 256) for b in range(B)]
+    pooled = [rng.normal(rng.tensor_key(3, 20 + b), 128) for b in range(B)]
+    lats = np.stack([rng.normal(rng.tensor_key(3, 30 + b), gh * gw * 16).reshape(gh * gw, 16) * 3.0
+                     for b in range(B)])
+    sigmas = [2.5, 7.0]
+    for b in range(B):
+        u.begin(ctxs[b], pooled[b], gh, gw, slot=b)
+    got = {}
+    u.set_probe(lambda name, layer, a: got.__setitem__(name, a))
+    eps = u.step_batch(lats, sigmas)
+    u.set_probe(None)
+    for b in range(B):
+        st = OS.unet_begin(oc, W, ctxs[b], pooled[b], gh, gw)
+        want = {}
+        ref = OS.unet_step(oc, W, st, lats[b], sigmas[b], probe=lambda n, a: want.__setitem__(n, a))
+        for name in ("conv_in", "in1.res", "in3.down", "in4.attn", "in8.attn", "mid.attn", "out0.attn", "out2.up",
+                     "out8.res"):
+            g = got[name].reshape(B, -1)[b]
+            w = want[name].ravel()
+            assert _cos(g, w) >= 0.999, (name, _cos(g, w))
+        assert _rel(eps[b], ref) < 0.02 and _cos(eps[b], ref) >= 0.999, (_rel(eps[b], ref), _cos(eps[b], ref))
+    # the graph-replayed step (third call) equals the eager one
+    e2 = u.step_batch(lats, sigmas)
+    e3 = u.step_batch(lats, sigmas)
+    assert np.array_equal(e2, eps) and np.array_equal(e3, eps)
+    # a single step on slot 1 matches that sample of the batch
+    e1 = u.step(lats[1], sigmas[1], slot=1)
+    assert np.abs(e1 - eps[1]).max() <= 1e-5 * max(1.0, np.abs(eps[1]).max())
+
+
+def test_vae_decode_reduced(cuda):
+    import mkimage
+
+    cfg = dict(channels=(128, 128, 256, 256), layers=1)
+    gh, gw = 8, 8
+    v = mkimage.Vae(mkimage.VaeConfig(max_gh=gh, max_gw=gw, **cfg))
+    v.init_random(23)
+    W = v.weights()
+    lat = rng.normal(rng.tensor_key(4, 1), gh * gw * 16).reshape(gh * gw, 16) * 0.13025
+    got = {}
+    v.set_probe(lambda name, layer, a: got.__setitem__(name, a))
+    img = v.decode(lat, gh, gw)
+    v.set_probe(None)
+    want = {}
+    ref = OS.vae_decode(OS.vae_default_cfg(**cfg), W, lat, gh, gw, probe=lambda n, a: want.__setitem__(n, a))
+    for name in ("mid.attn", "mid.res1", "up0.up", "up3.res1"):
+        assert _cos(got[name], want[name].ravel()) >= 0.999, name
+    assert img.shape == (128, 128, 4) and np.all(img[..., 3] == 1.0)
+    assert _rel(img, ref) < 0.01, _rel(img, ref)
+
+
+def test_sdxl_schedule():
+    import mkimage
+
+    s = mkimage.sdxl_sigmas(28)
+    assert s.shape == (29,) and s[-1] == 0 and np.all(np.diff(s[:-1]) < 0)
+    assert abs(s[0] - 14.6146) < 1e-3  # sigma at t = 999 of the scaled-linear schedule
+    table = OS.discrete_log_sigmas()
+    for sg in (0.03, 1.0, 5.5, 14.6):
+        assert mkimage.sdxl_timestep(sg) == OS.timestep(sg)
+    assert np.allclose(np.log(s[[0, 27]]), table[[999, 0]], atol=1e-5)
