@@ -33,6 +33,8 @@ UNIT = "steps/s"
 
 CONFIGS = {
     # name: (grid h, grid w, text tokens, images, blocks)
+    3: dict(workload="SDXL UNet step, 1024^2, CFG batch 2 (BASELINE configs[2])"),
+    4: dict(workload="SDXL VAE decode, 1024^2 (BASELINE configs[3])"),
     1: dict(h=32, w=32, S=128, images=1, blocks=1, cfg=False,
             workload="qwen1 MMDiT, 1 block, 1024 image + 128 text tokens, batch 1 (BASELINE configs[0])"),
     2: dict(h=64, w=64, S=256, images=1, blocks=60, cfg=True,
@@ -328,6 +330,220 @@ def run_mkb(args, cfg):
         torch.distributed.destroy_process_group()
 
 
+SDXL_UNET = dict(channels=(320, 640, 1280), depth=(0, 2, 10), layers=2, context_dim=2048, pooled_dim=1280)
+SDXL_VAE = dict(channels=(128, 256, 512, 512), layers=2)
+
+
+def unet_flops(oc, gh, gw, S, B):
+    """Algorithmic FLOPs of one UNet pass (convolutions, transformer linears, attention) from the block list."""
+    from oracle import sdxl as OS
+
+    f, h, w, c = 0.0, 2 * gh, 2 * gw, 4
+    for op in OS.unet_structure(oc):
+        P = h * w
+        if op[0] == "conv_in":
+            f += 2 * P * op[2] * 9 * 4
+        elif op[0] == "res":
+            _, _, cin, cout = op
+            f += 2 * P * cout * 9 * (cin + cout) + (2 * P * cout * cin if cin != cout else 0)
+        elif op[0] == "attn":
+            cc, d = op[2], op[3]
+            f += 4 * P * cc * cc + d * (36 * P * cc * cc + 4 * P * P * cc + 4 * P * S * cc)
+        elif op[0] == "down":
+            h, w = h // 2, w // 2
+            f += 2 * h * w * op[2] * 9 * op[2]
+        elif op[0] == "up":
+            h, w = h * 2, w * 2
+            f += 2 * h * w * op[2] * 9 * op[2]
+    return (f + 2 * 4 * gh * gw * 4 * 9 * oc["channels"][0]) * B
+
+
+def vae_flops(vc, gh, gw):
+    from oracle import sdxl as OS
+
+    h, w = 2 * gh, 2 * gw
+    f = 2 * h * w * vc["channels"][-1] * 9 * 4
+    for op in OS.vae_structure(vc)[2:]:
+        P = h * w
+        if op[0] == "res":
+            _, _, cin, cout = op
+            f += 2 * P * cout * 9 * (cin + cout) + (2 * P * cout * cin if cin != cout else 0)
+        elif op[0] == "attn":
+            f += 8 * P * op[2] * op[2] + 4 * P * P * op[2]
+        elif op[0] == "up":
+            h, w = h * 2, w * 2
+            f += 2 * h * w * op[2] * 9 * op[2]
+    return f + 2 * h * w * 3 * 9 * vc["channels"][0]
+
+
+def sdxl_cpu_baseline(kind):
+    """The oracle port on the host cores at 256^2 (full widths; UNet transformer depths 1/1 to bound the run),
+    scaled to the 1024^2 workload by the FLOP ratio. Returns (seconds per full unit, cores, sample)."""
+    import numpy as np
+    from oracle import sdxl as OS
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    r = np.random.default_rng(0)
+
+    def weights(shapes):
+        W = {}
+        for k, shp in shapes.items():
+            norm = k.endswith((".gn.w", ".gn1.w", ".gn2.w", ".ln1.w", ".ln2.w", ".ln3.w", "out.gn.w"))
+            W[k] = np.ones(shp, np.float32) if norm else r.standard_normal(shp, dtype=np.float32) * 0.02
+        return W
+
+    gh = gw = 16
+    if kind == "unet":
+        oc = OS.unet_default_cfg(depth=(0, 1, 1))
+        W = weights(OS.unet_weight_shapes(oc))
+        st = OS.unet_begin(oc, W, r.standard_normal((77, 2048), dtype=np.float32),
+                           r.standard_normal(1280, dtype=np.float32), gh, gw)
+        lat = r.standard_normal((gh * gw, 16), dtype=np.float32)
+        t0 = time.perf_counter()
+        OS.unet_step(oc, W, st, lat, 5.0)
+        t = time.perf_counter() - t0
+        full = unet_flops(OS.unet_default_cfg(**SDXL_UNET), 64, 64, 77, 2)
+        small = unet_flops(oc, gh, gw, 77, 1)
+        return t * full / small, cores, (f"UNet pass at 256^2, full widths, transformer depths 0/1/1 ({t:.2f} s), "
+                                         f"scaled by FLOPs to 1024^2 CFG 2 (x{full / small:.1f})")
+    vc = OS.vae_default_cfg(**SDXL_VAE)
+    W = weights(OS.vae_weight_shapes(vc))
+    lat = r.standard_normal((gh * gw, 16), dtype=np.float32) * 0.13
+    t0 = time.perf_counter()
+    OS.vae_decode(vc, W, lat, gh, gw)
+    t = time.perf_counter() - t0
+    full, small = vae_flops(vc, 64, 64), vae_flops(vc, gh, gw)
+    return t * full / small, cores, f"VAE decode at 256^2 ({t:.2f} s), scaled by FLOPs to 1024^2 (x{full / small:.1f})"
+
+
+def run_sdxl(args, which):
+    """config 3 (SDXL UNet step, 1024^2, CFG batch 2, Euler fused) or 4 (SDXL VAE decode 1024^2)."""
+    import numpy as np
+    import torch
+    import mkimage
+    from oracle import rng
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    sp = mkimage.stream_ptr(stream)
+    gh = gw = 64
+    peak_tf, _, peak_kind = _peaks()
+    if which == 3:
+        metric, unit = "SDXL UNet steps/s at 1024^2 (CFG batch 2, Euler fused)", "steps/s"
+        u = mkimage.Unet(mkimage.UnetConfig(max_batch=2, max_gh=gh, max_gw=gw, max_context=77, slots=2, **SDXL_UNET))
+        u.init_random(seed=77)
+        for s in range(2):
+            u.begin(rng.normal(rng.tensor_key(50, s), 77 * 2048).reshape(77, 2048),
+                    rng.normal(rng.tensor_key(51, s), 1280), gh, gw, slot=s)
+        lat_host = rng.normal(rng.tensor_key(52, rank), gh * gw * 16).reshape(gh * gw, 16) * 14.6
+        lat = torch.from_numpy(lat_host).to(dev)
+        sig = mkimage.sdxl_sigmas(28)
+        sigma, sigma_next = float(sig[10]), float(sig[11])
+        one = lambda: u.step_cfg_dev(lat.data_ptr(), sigma, sigma_next, 5.0, sp)  # noqa: E731
+        flops = u.step_flops(2)
+        workload = "SDXL UNet (320/640/1280, depths 0/2/10, hd 64, 77x2048 context), 1024^2, CFG batch 2, Euler fused"
+    else:
+        metric, unit = "SDXL VAE decodes/s at 1024^2", "decodes/s"
+        u = mkimage.Vae(mkimage.VaeConfig(max_gh=gh, max_gw=gw, **SDXL_VAE))
+        u.init_random(seed=78)
+        lat_host = rng.normal(rng.tensor_key(53, rank), gh * gw * 16).reshape(gh * gw, 16) * 0.13
+        lat = torch.from_numpy(lat_host).to(dev)
+        out = torch.empty(16 * gh, 16 * gw, 4, device=dev)
+        one = lambda: u.decode_dev(lat.data_ptr(), gh, gw, out.data_ptr(), sp)  # noqa: E731
+        flops = u.decode_flops(gh, gw)
+        workload = "SDXL VAE decoder (AutoencoderKL 128/256/512/512), 128^2x4 latent -> 1024^2 RGB"
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    launches0 = mkimage.lib.mkb_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("mkb_timed")
+        e0.record(stream)
+        for _ in range(args.steps):
+            one()
+        e1.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    launches = mkimage.lib.mkb_kernel_launches() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    mkimage.ops.check_kernels()
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    value = ws * 1e3 / ms
+    # End to end through the host-buffer API (latents in, result out, every call).
+    if which == 3:
+        x2 = np.stack([lat_host, lat_host]).astype(np.float32)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            eps = u.step_batch(x2, [sigma, sigma])
+            mkimage.guided_euler(x2[0], eps[0], eps[1], 5.0, sigma, sigma_next)
+        t_e2e = (time.perf_counter() - t0) / args.steps
+        e2e = {"value": 1.0 / t_e2e, "unit": unit, "h2d_bytes_per_step": x2.nbytes, "d2h_bytes_per_step": x2.nbytes}
+    else:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            img = u.decode(lat_host, gh, gw)
+        t_e2e = (time.perf_counter() - t0) / args.steps
+        e2e = {"value": 1.0 / t_e2e, "unit": unit, "h2d_bytes_per_step": lat_host.astype(np.float32).nbytes,
+               "d2h_bytes_per_step": img.nbytes}
+    # Dominant kernel: the implicit-GEMM 3x3 convolution (level-2 UNet 1280 -> 1280 at 32^2 x 2 samples; VAE
+    # 256 -> 256 at 512^2), timed alone on the same stream.
+    if which == 3:
+        B_, H_, W_, C_ = 2, 32, 32, 1280
+    else:
+        B_, H_, W_, C_ = 1, 512, 512, 256
+    xa = torch.randn(B_, H_, W_, C_, device=dev).to(torch.bfloat16)
+    wa = (torch.randn(C_, 9 * C_, device=dev) * 0.02).to(torch.bfloat16)
+    ya = torch.empty(B_, H_, W_, C_, device=dev)
+    for _ in range(3):
+        mkimage.ops.conv2d(xa, wa, out=ya)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(10):
+        mkimage.ops.conv2d(xa, wa, out=ya)
+    g1.record(stream)
+    torch.cuda.synchronize()
+    cms = g0.elapsed_time(g1) / 10
+    cfl = 2.0 * B_ * H_ * W_ * C_ * 9 * C_
+    ach = cfl / (cms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": f"k_gemm conv mode (3x3, {C_}->{C_} at {H_}x{W_} x{B_})",
+                "achieved": ach, "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": ach / peak_tf,
+                "traffic": None, "step_tflops": flops / (ms * 1e-3) / 1e12,
+                "step_frac": flops / (ms * 1e-3) / 1e12 / peak_tf}
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        t_unit, cores, sample = sdxl_cpu_baseline("unet" if which == 3 else "vae")
+        cpu = {"value": 1.0 / t_unit, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps({"metric": metric, "value": value, "unit": unit, "n_gpus": ws, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": workload, "tflop_per_step": flops / 1e12,
+                                     "parallelism": f"replicas x{ws}", "l2": "activations and weights above L2"},
+                          "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+                          "gpu_launches": int(launches)}), flush=True)
+    u.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
 def run_kernel(args, cfg):
     """One hot kernel alone at the config's shape, for profiling: 3 warm-up launches then 3 timed ones (CUDA
     events). gemm: the FFN-up projection (GELU epilogue); attention: the joint flash attention of one block;
@@ -386,6 +602,25 @@ def main():
     cfg = CONFIGS[args.config]
     if args.kernel:
         run_kernel(args, cfg)
+    elif args.config in (3, 4) and args.impl != "reference":
+        run_sdxl(args, args.config)
+    elif args.config in (3, 4):
+        ws, rank, _ = _dist()
+        if rank == 0:
+            for _ in range(args.warmup):
+                pass
+            secs = [sdxl_cpu_baseline("unet" if args.config == 3 else "vae") for _ in range(args.steps)]
+            t_unit = statistics.mean(x[0] for x in secs)
+            unit = "steps/s" if args.config == 3 else "decodes/s"
+            print(json.dumps({"impl": "reference", "metric": cfg["workload"], "value": 1.0 / t_unit, "unit": unit,
+                              "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": t_unit * 1e3, "higher_is_better": True, "scaling": "weak",
+                              "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                              "config": {"workload": cfg["workload"]},
+                              "cpu_baseline": {"value": 1.0 / t_unit, "unit": unit, "cores": secs[0][1],
+                                               "kind": "port", "sample": secs[0][2]},
+                              "e2e": {"value": 1.0 / t_unit, "unit": unit, "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:
