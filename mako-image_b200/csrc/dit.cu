@@ -360,9 +360,9 @@ mkb_status DitImpl::check_status()
 
 // Op indices of a plan.
 namespace op {
-// qwen1: per block 8 ops: [qkv_txt, qkv_img, o_txt, o_img, ff1_txt, ff1_img, ff2_txt, ff2_img]; then globals.
+// qwen1: per block 4 ops [qkv, o, ff1, ff2], each the image and text rows in one launch; then globals.
 // ref21: per block 4 ops: [qkv, o, gate_up, down]; then globals.
-constexpr int kQ1PerBlock = 8, kR21PerBlock = 4;
+constexpr int kQ1PerBlock = 4, kR21PerBlock = 4;
 enum Global { kTxtIn = 0, kImgIn = 1, kProjOut = 2, kTxtIn1 = 3, kCount = 4 };
 }  // namespace op
 
@@ -400,12 +400,22 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         float* x_s[2] = {x_txt, x_img};
         const int M_s[2] = {Mt, Mi}, rps[2] = {S, N}, off[2] = {0, S};
         const char* nm[2] = {"txt", "img"};
+        // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
+        // its tail: QKV, O and FFN-down on 256-wide tiles (QKV: two heads per tile), FFN-up on 192-wide ones
+        // (measured fastest at the config-2 shapes).
         for (int i = 0; i < NB; ++i) {
             GemmOp* o = plan->ops.data() + size_t(i) * per;
-            for (int s = 0; s < 2; ++s) {
+            for (int s : {1, 0}) {
                 const std::string p = "blk" + std::to_string(i) + "." + nm[s] + ".";
                 const int stream_idx = s == 0 ? 1 : 0;  // mod order: img then txt per block
                 const float* mb = mod + (size_t(i) * 2 + stream_idx) * 6 * D;
+                auto put = [&](GemmOp& g, Epi epi, const void* X, long ldx, const void* Wt, long ldw, GemmArgs a,
+                               int bn) {
+                    if (s == 1)
+                        return prep(g, epi, X, ldx, Wt, ldw, a, bn);
+                    a.status = status;
+                    return gemm_add_problem(g, X, ldx, Wt, ldw, a, &err);
+                };
                 GemmArgs a;
                 a.M = M_s[s];
                 a.N = 3 * D;
@@ -422,7 +432,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 a.seg_rows = rps[s];
                 a.seg_off = off[s];
                 a.eps = kEps;
-                if (!prep(o[0 + s], Epi::kQkv, xn_s[s], D, M(p + "qkv.w"), D, a, 256))
+                if (!put(o[0], Epi::kQkv, xn_s[s], D, M(p + "qkv.w"), D, a, 256))
                     return fail(MKB_ERR_INVALID, err);
                 GemmArgs r;
                 r.M = M_s[s];
@@ -434,7 +444,8 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 r.gate = mb + 2 * D;
                 r.gate_bstride = mstride;
                 r.seg_rows = rps[s];
-                if (!prep(o[2 + s], Epi::kResid, at_s[s], D, M(p + "o.w"), D, r, bn_for(r.M, D)))
+                const int bn_d = D % 256 == 0 ? 256 : 128;
+                if (!put(o[1], Epi::kResid, at_s[s], D, M(p + "o.w"), D, r, bn_d))
                     return fail(MKB_ERR_INVALID, err);
                 GemmArgs f1;
                 f1.M = M_s[s];
@@ -444,13 +455,13 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 f1.act = kActGeluTanh;
                 f1.out = hd_s[s];
                 f1.ldo = F;
-                if (!prep(o[4 + s], Epi::kBF16, xn_s[s], D, M(p + "ff1.w"), D, f1, bn_for(f1.M, F)))
+                if (!put(o[2], Epi::kBF16, xn_s[s], D, M(p + "ff1.w"), D, f1, F % 192 == 0 ? 192 : 128))
                     return fail(MKB_ERR_INVALID, err);
                 GemmArgs f2 = r;
                 f2.K = F;
                 f2.bias = V(p + "ff2.b");
                 f2.gate = mb + 5 * D;
-                if (!prep(o[6 + s], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_for(f2.M, D)))
+                if (!put(o[3], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_d))
                     return fail(MKB_ERR_INVALID, err);
             }
         }
@@ -746,39 +757,29 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
         if (q1) {
             const int Mt = B * S, Mi = B * N;
             const long mstride = long(NB) * 12 * D;
-            for (int sidx = 0; sidx < 2; ++sidx) {  // 0 txt, 1 img
+            auto ln = [&](int sidx, int scale_off, int shift_off) {
                 const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
                 LnModArgs la{};
                 la.x = sidx == 0 ? x_txt : x_img;
                 la.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
-                la.scale = mb + D;
-                la.shift = mb;
+                la.scale = mb + scale_off * D;
+                la.shift = mb + shift_off * D;
                 la.mod_stride = mstride;
                 la.rows = sidx == 0 ? Mt : Mi;
                 la.D = D;
                 la.rows_per_sample = sidx == 0 ? S : N;
                 la.eps = kEps;
-                MKB_K(ln_modulate(la, s), "ln_modulate 1");
-                MKB_K(gemm_launch(o[0 + sidx], s), "qkv");
-            }
+                return ln_modulate(la, s);
+            };
+            MKB_K(ln(0, 1, 0), "ln_modulate 1");
+            MKB_K(ln(1, 1, 0), "ln_modulate 1");
+            MKB_K(gemm_launch(o[0], s), "qkv");
             MKB_K(attn_launch(plan->att, s), "attention");
-            for (int sidx = 0; sidx < 2; ++sidx) {
-                const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
-                MKB_K(gemm_launch(o[2 + sidx], s), "o proj");
-                LnModArgs la{};
-                la.x = sidx == 0 ? x_txt : x_img;
-                la.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
-                la.scale = mb + 4 * D;
-                la.shift = mb + 3 * D;
-                la.mod_stride = mstride;
-                la.rows = sidx == 0 ? Mt : Mi;
-                la.D = D;
-                la.rows_per_sample = sidx == 0 ? S : N;
-                la.eps = kEps;
-                MKB_K(ln_modulate(la, s), "ln_modulate 2");
-                MKB_K(gemm_launch(o[4 + sidx], s), "ff1");
-                MKB_K(gemm_launch(o[6 + sidx], s), "ff2");
-            }
+            MKB_K(gemm_launch(o[1], s), "o proj");
+            MKB_K(ln(0, 4, 3), "ln_modulate 2");
+            MKB_K(ln(1, 4, 3), "ln_modulate 2");
+            MKB_K(gemm_launch(o[2], s), "ff1");
+            MKB_K(gemm_launch(o[3], s), "ff2");
             if (probe) {
                 MKB_TRY(emit("block.txt", i, x_txt, long(Mt) * D, s));
                 MKB_TRY(emit("block.img", i, x_img, long(Mi) * D, s));

@@ -26,7 +26,7 @@ struct Cfg {
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
-    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     static constexpr int kBarBytes = 256;
     static constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
 };
@@ -316,9 +316,21 @@ __device__ __forceinline__ void conv_tile(const GemmArgs& a, int mb, int& b, int
     x0 = (rem % tx_n) * a.conv_tw;
 }
 
+__device__ __forceinline__ int gemm_num_m(const GemmArgs& a, bool conv)
+{
+    return conv ? a.conv_b * (a.conv_wo / a.conv_tw) * ((a.conv_ho + a.conv_th - 1) / a.conv_th) : (a.M + kBM - 1) / kBM;
+}
+
+// Problem and problem-local tile of a global tile index (problem 0's tiles first).
+__device__ __forceinline__ int gemm_problem(const GemmParams& P, int tile, int& local)
+{
+    const int p = (P.nprob > 1 && tile >= P.tiles0) ? 1 : 0;
+    local = p ? tile - P.tiles0 : tile;
+    return p;
+}
+
 template <int BN, Epi EPI, bool CONV>
-__global__ void __launch_bounds__(kThreads, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, const GemmArgs args)
+__global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams P)
 {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -332,11 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int num_m = CONV ? args.conv_b * (args.conv_wo / args.conv_tw) *
-                                 ((args.conv_ho + args.conv_th - 1) / args.conv_th)
-                           : (args.M + kBM - 1) / kBM;
-    const int num_n = (args.N + BN - 1) / BN;
-    const int num_tiles = num_m * num_n, num_k = (args.K + kBK - 1) / kBK;
+    int num_tiles = P.tiles0;
+    if (P.nprob > 1)
+        num_tiles += gemm_num_m(P.a[1], CONV) * ((P.a[1].N + BN - 1) / BN);
+    uint32_t* status = P.a[0].status;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
@@ -352,8 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tma);
-        prefetch_tmap(&tmb);
+        for (int p = 0; p < P.nprob; ++p) {
+            prefetch_tmap(&P.ta[p]);
+            prefetch_tmap(&P.tb[p]);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -369,12 +382,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                int local;
+                const int p = gemm_problem(P, tile, local);
+                const GemmArgs& args = P.a[p];
+                const int num_m = gemm_num_m(args, CONV), num_n = (args.N + BN - 1) / BN;
+                const int num_k = (args.K + kBK - 1) / kBK;
                 int mb, nb;
-                tile_coords(tile, num_m, num_n, mb, nb);
+                tile_coords(local, num_m, num_n, mb, nb);
                 for (int kb = 0; kb < num_k; ++kb, ++it) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, args.status, kErrWaitEmpty, abort_flag)) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, status, kErrWaitEmpty, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -387,35 +405,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                         conv_tile(args, mb, b, y0, x0);
                         const int cpt = args.conv_c / kBK, tap = kb / cpt, c0 = (kb - tap * cpt) * kBK;
                         const int dy = args.conv_taps == 9 ? tap / 3 : 0, dx = args.conv_taps == 9 ? tap % 3 : 0;
-                        tma_load_4d(sa, &tma, &full[s], c0, x0 * args.conv_stride + dx - args.conv_pad,
+                        tma_load_4d(sa, &P.ta[p], &full[s], c0, x0 * args.conv_stride + dx - args.conv_pad,
                                     y0 * args.conv_stride + dy - args.conv_pad, b);
                     } else {
-                        tma_load_2d(sa, &tma, &full[s], kb * kBK, mb * kBM);
+                        tma_load_2d(sa, &P.ta[p], &full[s], kb * kBK, mb * kBM);
                     }
-                    tma_load_2d(sa + C::kABytes, &tmb, &full[s], kb * kBK, nb * BN);
+                    tma_load_2d(sa + C::kABytes, &P.tb[p], &full[s], kb * kBK, nb * BN);
                 }
             }
             if (!ok) {  // let the loads already issued land before the CTA can exit
                 const uint32_t first = it > uint32_t(C::kStages) ? it - C::kStages : 0;
                 for (uint32_t j = first; j < it; ++j)
-                    mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, args.status, kErrWaitDrain, nullptr);
+                    mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, status, kErrWaitDrain, nullptr);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
-            uint32_t it = 0, local = 0;
+            uint32_t it = 0, lt = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-                const uint32_t acc = local & 1, acc_ph = (local >> 1) & 1;
-                if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, args.status, kErrWaitAccEmpty, abort_flag))
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
+                int local;
+                const int p = gemm_problem(P, tile, local);
+                const int num_k = (P.a[p].K + kBK - 1) / kBK;
+                const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
+                if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, status, kErrWaitAccEmpty, abort_flag))
                     break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
                 for (int kb = 0; kb < num_k; ++kb, ++it) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
-                    if (!mbar_wait(&full[s], ph, args.status, kErrWaitFull, abort_flag)) {
+                    if (!mbar_wait(&full[s], ph, status, kErrWaitFull, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -433,16 +454,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Every MMA must be complete before tensor memory is released.
             mma_commit(drain);
-            mbar_wait(drain, 0, args.status, kErrWaitDrain, nullptr);
+            mbar_wait(drain, 0, status, kErrWaitDrain, nullptr);
         }
     } else {
         const int q = warp & 3;  // the TMEM lane quarter this warp may access
-        uint32_t local = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        uint32_t lt = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+            int local;
+            const int p = gemm_problem(P, tile, local);
+            const GemmArgs& args = P.a[p];
+            const int num_m = gemm_num_m(args, CONV), num_n = (args.N + BN - 1) / BN;
             int mb, nb;
-            tile_coords(tile, num_m, num_n, mb, nb);
-            const uint32_t acc = local & 1, acc_ph = (local >> 1) & 1;
-            if (!mbar_wait(&acc_full[acc], acc_ph, args.status, kErrWaitAccFull, abort_flag))
+            tile_coords(local, num_m, num_n, mb, nb);
+            const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag))
                 break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
@@ -495,7 +520,7 @@ cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
             return e;
         attr_set = true;
     }
-    k_gemm<BN, EPI, CONV><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.ta, op.tb, op.args);
+    k_gemm<BN, EPI, CONV><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.p);
     count_launch();
     return cudaGetLastError();
 }
@@ -572,8 +597,8 @@ namespace {
 // Checks of the epilogue arguments shared by the GEMM and the convolution.
 bool check_epilogue(Epi epi, const GemmArgs& args, int bn, const char** err)
 {
-    if (bn != 64 && bn != 128 && bn != 256) {
-        *err = "gemm: tile width must be 64, 128 or 256";
+    if (bn != 64 && bn != 128 && bn != 192 && bn != 256) {
+        *err = "gemm: tile width must be 64, 128, 192 or 256";
         return false;
     }
     if (epi == Epi::kQkv && (bn < 128 || args.D % bn || args.N != 3 * args.D || !args.qh || !args.kh || !args.vh)) {
@@ -615,22 +640,51 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
 {
     op.ready = false;
     op.conv = false;
+    op.p.nprob = 1;
     if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
         *err = "gemm: M, N, K must be positive, N a multiple of 32, K a multiple of 8";
         return false;
     }
     if (!check_epilogue(epi, args, bn, err))
         return false;
-    if (!make_tmap_bf16_2d(&op.ta, X, uint64_t(args.K), uint64_t(args.M), uint64_t(ldx) * 2, kBK, kBM, err))
+    if (!make_tmap_bf16_2d(&op.p.ta[0], X, uint64_t(args.K), uint64_t(args.M), uint64_t(ldx) * 2, kBK, kBM, err))
         return false;
-    if (!make_tmap_bf16_2d(&op.tb, W, uint64_t(args.K), uint64_t(args.N), uint64_t(ldw) * 2, kBK, uint32_t(bn), err))
+    if (!make_tmap_bf16_2d(&op.p.tb[0], W, uint64_t(args.K), uint64_t(args.N), uint64_t(ldw) * 2, kBK, uint32_t(bn),
+                           err))
         return false;
-    op.args = args;
+    op.p.a[0] = args;
+    op.p.nprob = 1;
+    op.p.tiles0 = ((args.M + kBM - 1) / kBM) * ((args.N + bn - 1) / bn);
     op.epi = epi;
     op.bn = bn;
-    const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + bn - 1) / bn);
-    op.grid = tiles < num_sms() ? tiles : num_sms();
+    op.grid = op.p.tiles0 < num_sms() ? op.p.tiles0 : num_sms();
     op.ready = true;
+    return true;
+}
+
+bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
+                      const char** err)
+{
+    if (!op.ready || op.conv || op.p.nprob != 1) {
+        *err = "gemm: a second problem needs a prepared single GEMM";
+        return false;
+    }
+    if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
+        *err = "gemm: M, N, K must be positive, N a multiple of 32, K a multiple of 8";
+        return false;
+    }
+    if (!check_epilogue(op.epi, args, op.bn, err))
+        return false;
+    if (!make_tmap_bf16_2d(&op.p.ta[1], X, uint64_t(args.K), uint64_t(args.M), uint64_t(ldx) * 2, kBK, kBM, err))
+        return false;
+    if (!make_tmap_bf16_2d(&op.p.tb[1], W, uint64_t(args.K), uint64_t(args.N), uint64_t(ldw) * 2, kBK,
+                           uint32_t(op.bn), err))
+        return false;
+    op.p.a[1] = args;
+    op.p.a[1].status = op.p.a[0].status;
+    op.p.nprob = 2;
+    const int tiles = op.p.tiles0 + ((args.M + kBM - 1) / kBM) * ((args.N + op.bn - 1) / op.bn);
+    op.grid = tiles < num_sms() ? tiles : num_sms();
     return true;
 }
 
@@ -694,19 +748,21 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
         *err = "conv: tile window too large";
         return false;
     }
-    if (fn(&op.ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(X), dims, strides, box, es,
+    if (fn(&op.p.ta[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(X), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
         *err = "conv: input tensor map encoding failed";
         return false;
     }
-    if (!make_tmap_bf16_2d(&op.tb, W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
+    if (!make_tmap_bf16_2d(&op.p.tb[0], W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
         return false;
-    op.args = a;
+    op.p.a[0] = a;
+    op.p.nprob = 1;
     op.epi = epi;
     op.bn = bn;
     op.conv = true;
     const int tiles = B * (Wo / tw) * ((Ho + a.conv_th - 1) / a.conv_th) * ((Cout + bn - 1) / bn);
+    op.p.tiles0 = tiles;
     op.grid = tiles < num_sms() ? tiles : num_sms();
     op.ready = true;
     return true;
@@ -719,6 +775,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t st)
     switch (op.bn) {
     case 64: return launch_bn<64>(op, st);
     case 128: return launch_bn<128>(op, st);
+    case 192: return launch_bn<192>(op, st);
     case 256: return launch_bn<256>(op, st);
     }
     return cudaErrorInvalidValue;

@@ -75,11 +75,20 @@ struct GemmArgs {
     uint32_t* status = nullptr;     // error bits (kErr*), may be null
 };
 
+// The kernel's parameters: one or two problems of the same epilogue kind and tile width run by one persistent
+// launch (problem 0's tiles first, problem 1's filling the tail).
+struct GemmParams {
+    CUtensorMap ta[2];
+    CUtensorMap tb[2];
+    GemmArgs a[2];
+    int nprob = 1;
+    int tiles0 = 0;
+};
+
 // A prepared launch: tensor maps and arguments are built once (buffers are fixed), then launched any number of
 // times, also inside CUDA graph capture.
 struct GemmOp {
-    CUtensorMap ta, tb;
-    GemmArgs args;
+    GemmParams p;
     Epi epi = Epi::kBF16;
     int bn = 256;
     int grid = 0;
@@ -91,6 +100,9 @@ struct GemmOp {
 // message in *err on unsupported shapes or misaligned pointers.
 bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                   int bn, const char** err);
+// Adds a second problem (same epilogue kind and tile width; X [M][K], W [N][K]) to a prepared GEMM.
+bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
+                      const char** err);
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
 
 // Builds a convolution as an implicit GEMM: X is the channels-last bf16 input [B][Hi][Wi][C] (C a multiple of 64),
