@@ -383,6 +383,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         a.status = status;
         return gemm_prepare(o, epi, X, ldx, W, ldw, a, bn, &err);
     };
+    auto bn_for_pairs = [](const GemmOp& g) { return g.bn >= 128; };
     auto bn_for = [&](int M, int Nc) {
         if (Nc % 256 == 0 && long((M + 127) / 128) * (Nc / 256) >= 74)
             return 256;
@@ -402,7 +403,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         const char* nm[2] = {"txt", "img"};
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
         // its tail: QKV, O and FFN-down on 256-wide tiles (QKV: two heads per tile), FFN-up on 192-wide ones
-        // (measured fastest at the config-2 shapes).
+        // (measured fastest at the config-2 shapes), FFN-down on CTA pairs.
         for (int i = 0; i < NB; ++i) {
             GemmOp* o = plan->ops.data() + size_t(i) * per;
             for (int s : {1, 0}) {
@@ -464,6 +465,10 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 if (!put(o[3], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_d))
                     return fail(MKB_ERR_INVALID, err);
             }
+            // FFN-down (K = F) on CTA pairs: its long tiles are bound by shared-memory operand traffic, which the
+            // pair tile halves.
+            if (B * N >= 512 && bn_for_pairs(o[3]) && !gemm_use_pairs(o[3], &err))
+                return fail(MKB_ERR_INVALID, err);
         }
         GemmArgs a;
         a.M = Mt;

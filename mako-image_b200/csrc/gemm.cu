@@ -31,9 +31,24 @@ struct Cfg {
     static constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
 };
 
+// Per-CTA shared memory of the 2-SM kernel: the CTA's 128 rows of A and half (BN / 2 rows) of B per stage.
+template <int BN>
+struct Cfg2 {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = (BN / 2) * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+    static constexpr int kSmem = 1024 + kStages * kStageBytes + 256;
+};
+
+#ifndef MKB_TILE_GROUP
+#define MKB_TILE_GROUP 8  // M-tiles per raster group: concurrent tiles share X and W panels in L2
+#endif
+
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb)
 {
-    constexpr int G = 8;
+    constexpr int G = MKB_TILE_GROUP;
     const int per_group = G * num_n;
     const int group = tile / per_group;
     const int first_m = group * G;
@@ -494,6 +509,161 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     }
 }
 
+
+// The same GEMM on CTA pairs (cta_group::2): a cluster of two CTAs owns each 256 x BN tile. Each CTA loads its 128
+// rows of X and half of the tile's W rows; the pair leader issues 256 x BN x 16 MMAs that read both CTAs' shared
+// memory and accumulate each CTA's 128 rows in its own tensor memory; both CTAs run the epilogue on their rows. Per
+// SM this halves the W traffic through shared memory and L2 of the 1-CTA tile.
+template <int BN, Epi EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2(const __grid_constant__ GemmParams P)
+{
+    using C = Cfg2<BN>;
+    constexpr int kPM = 2 * kBM;  // rows per pair tile
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* acc_full = empty + C::kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+    auto num_m_of = [&](const GemmArgs& a) { return (a.M + kPM - 1) / kPM; };
+    int num_tiles = P.tiles0;
+    if (P.nprob > 1)
+        num_tiles += num_m_of(P.a[1]) * ((P.a[1].N + BN - 1) / BN);
+    uint32_t* status = P.a[0].status;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 2 * 128);  // the epilogue threads of both CTAs (leader's barrier)
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        for (int p = 0; p < P.nprob; ++p) {
+            prefetch_tmap(&P.ta[p]);
+            prefetch_tmap(&P.tb[p]);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+                int local;
+                const int p = gemm_problem(P, tile, local);
+                const GemmArgs& args = P.a[p];
+                const int num_n = (args.N + BN - 1) / BN, num_k = (args.K + kBK - 1) / kBK;
+                int mb, nb;
+                tile_coords(local, num_m_of(args), num_n, mb, nb);
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t ph = (it / C::kStages) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, status, kErrWaitEmpty, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * C::kStageBytes;
+                    if (leader)
+                        mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);  // both CTAs' loads land on it
+                    tma_load_2d_pair(sa, &P.ta[p], &full[s], kb * kBK, mb * kPM + int(rank) * kBM);
+                    tma_load_2d_pair(sa + C::kABytes, &P.tb[p], &full[s], kb * kBK, nb * BN + int(rank) * (BN / 2));
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kPM, BN);
+            uint32_t it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++lt) {
+                int local;
+                const int p = gemm_problem(P, tile, local);
+                const int num_k = (P.a[p].K + kBK - 1) / kBK;
+                const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
+                if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, status, kErrWaitAccEmpty, abort_flag))
+                    break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t ph = (it / C::kStages) & 1;
+                    if (!mbar_wait(&full[s], ph, status, kErrWaitFull, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; ++k)
+                        mma_bf16_ss_pair(d_tmem, desc_kmajor_sw128(a_addr + k * 32),
+                                         desc_kmajor_sw128(b_addr + k * 32), idesc, (kb | k) != 0);
+                    mma_commit_pair(&empty[s]);
+                }
+                if (ok)
+                    mma_commit_pair(&acc_full[acc]);
+            }
+            mma_commit_pair(drain);
+            mbar_wait(drain, 0, status, kErrWaitDrain, nullptr);
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t acc_empty_leader0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
+        uint32_t lt = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
+            int local;
+            const int p = gemm_problem(P, tile, local);
+            const GemmArgs& args = P.a[p];
+            int mb, nb;
+            tile_coords(local, num_m_of(args), (args.N + BN - 1) / BN, mb, nb);
+            const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
+            if (!mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag))
+                break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+            const int row = mb * kPM + int(rank) * kBM + q * 32 + lane;
+            epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+            tc_fence_before();
+            if (leader)
+                mbar_arrive(&acc_empty[acc]);
+            else
+                mbar_arrive_cluster(acc_empty_leader0 + acc * 8);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the leader's MMAs read this CTA's shared memory until here
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -526,8 +696,29 @@ cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
 }
 
 template <int BN, Epi EPI>
+cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
+{
+    if constexpr (BN >= 128 && (BN / 2) % 16 == 0) {
+        static bool attr_set = false;
+        if (!attr_set) {
+            cudaError_t e = cudaFuncSetAttribute(k_gemm2<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 Cfg2<BN>::kSmem);
+            if (e != cudaSuccess)
+                return e;
+            attr_set = true;
+        }
+        k_gemm2<BN, EPI><<<op.grid, kThreads, Cfg2<BN>::kSmem, st>>>(op.p);
+        count_launch();
+        return cudaGetLastError();
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int BN, Epi EPI>
 cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
 {
+    if (op.pair)
+        return launch_pair<BN, EPI>(op, st);
     // Convolutions only use the epilogues a conv needs (plain, activation, add), which keeps the instantiations few.
     if constexpr (EPI == Epi::kBF16 || EPI == Epi::kAdd) {
         if (op.conv)
@@ -654,6 +845,9 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
         return false;
     op.p.a[0] = args;
     op.p.nprob = 1;
+    op.pair = false;
+    op.w_ptr[0] = W;
+    op.ldw[0] = ldw;
     op.p.tiles0 = ((args.M + kBM - 1) / kBM) * ((args.N + bn - 1) / bn);
     op.epi = epi;
     op.bn = bn;
@@ -665,8 +859,8 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
 bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                       const char** err)
 {
-    if (!op.ready || op.conv || op.p.nprob != 1) {
-        *err = "gemm: a second problem needs a prepared single GEMM";
+    if (!op.ready || op.conv || op.pair || op.p.nprob != 1) {
+        *err = "gemm: a second problem needs a prepared single 1-CTA GEMM";
         return false;
     }
     if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.N % 32 || args.K % 8) {
@@ -683,6 +877,8 @@ bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long l
     op.p.a[1] = args;
     op.p.a[1].status = op.p.a[0].status;
     op.p.nprob = 2;
+    op.w_ptr[1] = W;
+    op.ldw[1] = ldw;
     const int tiles = op.p.tiles0 + ((args.M + kBM - 1) / kBM) * ((args.N + op.bn - 1) / op.bn);
     op.grid = tiles < num_sms() ? tiles : num_sms();
     return true;
@@ -765,6 +961,32 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     op.p.tiles0 = tiles;
     op.grid = tiles < num_sms() ? tiles : num_sms();
     op.ready = true;
+    return true;
+}
+
+bool gemm_use_pairs(GemmOp& op, const char** err)
+{
+    if (!op.ready || op.conv || op.bn < 128) {
+        *err = "gemm: CTA pairs need a prepared GEMM with tile width >= 128";
+        return false;
+    }
+    int tiles = 0;
+    for (int p = 0; p < op.p.nprob; ++p) {
+        const GemmArgs& a = op.p.a[p];
+        // W tiles are loaded half per CTA: re-encode W's map with a box of bn / 2 rows.
+        CUtensorMap m;
+        if (!make_tmap_bf16_2d(&m, op.w_ptr[p], uint64_t(a.K), uint64_t(a.N), uint64_t(op.ldw[p]) * 2, kBK,
+                               uint32_t(op.bn / 2), err))
+            return false;
+        op.p.tb[p] = m;
+        const int t = ((a.M + 2 * kBM - 1) / (2 * kBM)) * ((a.N + op.bn - 1) / op.bn);
+        if (p == 0)
+            op.p.tiles0 = t;
+        tiles += t;
+    }
+    const int pairs = num_sms() / 2;
+    op.grid = 2 * (tiles < pairs ? tiles : pairs);
+    op.pair = true;
     return true;
 }
 

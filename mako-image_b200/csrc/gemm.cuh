@@ -93,13 +93,19 @@ struct GemmOp {
     int bn = 256;
     int grid = 0;
     bool conv = false;
+    bool pair = false;  // CTA-pair (cta_group::2) kernel: 256-row tiles shared by two SMs
     bool ready = false;
+    const void* w_ptr[2] = {nullptr, nullptr};  // W operands and their row strides (to re-encode W's maps)
+    long ldw[2] = {0, 0};
 };
 
 // Builds a GemmOp. X: [M][K] bf16 rows `ldx` elements apart; W: [N][K] bf16 rows `ldw` apart. Returns false with a
 // message in *err on unsupported shapes or misaligned pointers.
 bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                   int bn, const char** err);
+// Switches a prepared (non-convolution) GEMM to the CTA-pair kernel: 256-row tiles, each SM loading half of the W
+// tile. Needs the tile width >= 128. Call after adding any second problem.
+bool gemm_use_pairs(GemmOp& op, const char** err);
 // Adds a second problem (same epilogue kind and tile width; X [M][K], W [N][K]) to a prepared GEMM.
 bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                       const char** err);
