@@ -177,31 +177,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
             constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, 0, 1);  // V is MN-major (head dim contiguous)
             const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-            bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
-            for (int j = 0; j < nkv && ok; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&k_full[st], ph, a.status, kErrAttnWait, abort_flag))
-                    break;
-                for (int t = 0; t < 2 && ok; ++t) {
-                    // S_t is overwritten only once the previous O_t += P_t V has read P_t (aliased on S_t).
-                    if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+            // Issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1). Each tile's next S follows its own
+            // P V directly, so tile A's softmax overlaps tile B's two MMAs and the other way round. S_t(j+1)
+            // overwrites the TMEM columns P_t(j) occupies; both come from this thread, and the tensor pipe executes
+            // one CTA's MMAs in issue order, so P_t(j) is read before it is overwritten. The commit after S_t(j+1)
+            // also covers PV_t(j), so when a softmax warp sees s_full its O accumulator is settled for rescaling.
+            const auto issue_s = [&](int t, int st) {
 #pragma unroll
-                    for (int k = 0; k < HD / 16; ++k) {
-                        const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
-                        mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
-                                    desc_kmajor_sw128(k_addr + st * TB + off), idesc_s, k > 0);
-                    }
-                    mma_commit(&s_full[t]);
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
+                    mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
+                                desc_kmajor_sw128(k_addr + st * TB + off), idesc_s, k > 0);
                 }
-                if (!ok)
+                mma_commit(&s_full[t]);
+            };
+            bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
+            if (ok && nkv > 0) {
+                ok = mbar_wait(&k_full[0], 0, a.status, kErrAttnWait, abort_flag);
+                if (ok) {
+                    tc_fence_after();
+                    issue_s(0, 0);
+                    issue_s(1, 0);
+                    mma_commit(&k_empty[0]);
+                }
+            }
+            for (int j = 0; j < nkv && ok; ++j) {
+                const int st = j & 1, st1 = (j + 1) & 1;
+                const bool next = j + 1 < nkv;
+                if (!mbar_wait(&v_full[st], (j >> 1) & 1, a.status, kErrAttnWait, abort_flag))
                     break;
-                mma_commit(&k_empty[st]);
-                if (!mbar_wait(&v_full[st], ph, a.status, kErrAttnWait, abort_flag))
+                if (next && !mbar_wait(&k_full[st1], ((j + 1) >> 1) & 1, a.status, kErrAttnWait, abort_flag))
                     break;
                 for (int t = 0; t < 2 && ok; ++t) {
                     if (!mbar_wait(&p_full[t], j & 1, a.status, kErrAttnWait, abort_flag)) {
@@ -215,9 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
                                     (j > 0) || (k > 0));
                     mma_commit(&o_done[t]);
+                    if (next)
+                        issue_s(t, st1);
                 }
-                if (ok)
-                    mma_commit(&v_empty[st]);
+                if (!ok)
+                    break;
+                mma_commit(&v_empty[st]);
+                if (next)
+                    mma_commit(&k_empty[st1]);
             }
             mma_commit(drain);  // arrives once every MMA issued above has completed
             mbar_wait(drain, 0, a.status, kErrWaitDrain, nullptr);
