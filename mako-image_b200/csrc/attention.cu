@@ -1,15 +1,17 @@
-// Flash attention forward, head dim 128, on tcgen05 (see attention.cuh).
+// Flash attention forward, head dim 64 or 128, on tcgen05 (see attention.cuh).
 //
 // One CTA per SM-sized work item: two 128-row query tiles (A and B) of one (sample, head) share every K/V tile.
+// Three warpgroups:
 //   warp 0     TMA: both Q tiles once, then K and V tiles of 128 keys into 2-stage rings (128-byte swizzle,
 //              two 64-wide panels each)
-//   warp 1     MMA, per KV tile j: S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V, O_B += P_B V, with P read from
-//              tensor memory. While one tile's softmax runs, the tensor pipe works on the other tile.
-//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one thread per query row holds its 128 scores in registers,
+//   warp 1     MMA, per KV tile j: O_A += P_A V, S_A = Q_A K_{j+1}^T, O_B += P_B V, S_B = Q_B K_{j+1}^T, with P read
+//              from tensor memory. While one tile's softmax runs, the tensor pipe works on the other tile.
+//   warps 2-3  idle (they complete the first warpgroup, which gives its registers to the softmax groups)
+//   warps 4-7  softmax of tile A, warps 8-11 of tile B: one thread per query row holds its 128 scores in registers,
 //              keeps a running max with lazy rescaling (O is rescaled only when a row's max grows by more than 2^8),
 //              writes P = 2^(S - m) as bf16 over the first 64 columns of its S, and at the end stores O / l into the
-//              output projection's input rows. Part of each row's exponentials run as a polynomial on the FMA pipe
-//              to offload the SFU.
+//              output projection's input rows. At head dim 64 part of each row's exponentials run as a polynomial on
+//              the FMA pipe to offload the SFU.
 // TMEM columns: S_A [0, 128), S_B [128, 256), O_A [256, 384), O_B [384, 512).
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -24,7 +26,14 @@ namespace mkb {
 
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Registers per thread: the launch bound gives every thread 168 (3 warps share each SM sub-partition's 512 per
+// lane); the control warpgroup drops to kRegsCtl and the two softmax warpgroups rise to kRegsSoftmax, enough to hold
+// a row's 128 scores without spilling.
+constexpr int kLaunchRegs = (65536 / kThreads) / 8 * 8;
+constexpr int kRegsCtl = 56, kRegsSoftmax = 216;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * kLaunchRegs, "register split exceeds the CTA pool");
+static_assert(kRegsCtl + 2 * kRegsSoftmax <= 512, "register split exceeds a sub-partition");
 constexpr int kTile = 128;                 // query rows per tile, keys per KV tile
 constexpr int kPanel = kTile * 64 * 2;     // one 64-wide bf16 panel of 128 rows: 16 KB
 template <int HD>
@@ -33,8 +42,11 @@ template <int HD>
 constexpr int kSmem = 1024 + 6 * kTileBytes<HD> + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-// Elements [kEmuFrom, 128) of each score row take 2^x from the FMA-pipe polynomial instead of the SFU.
-constexpr int kEmuFrom = 96;
+// Elements [kEmuFrom<HD>, 128) of each score row take 2^x from the FMA-pipe polynomial instead of the SFU. At head
+// dim 128 the SFU keeps up with the tensor pipe on its own; at 64 the MMAs are half as long and a quarter of the
+// exponentials moves to the FMA pipe.
+template <int HD>
+constexpr int kEmuFrom = HD == 128 ? 128 : 112;
 
 __device__ __forceinline__ float ex2(float x)
 {
@@ -56,6 +68,29 @@ __device__ __forceinline__ float ex2_poly(float x)
     p = fmaf(p, f, 0.6932609677314758f);
     p = fmaf(p, f, 0.9999281167984009f);
     return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Packed two-lane fp32 arithmetic: one instruction for both lanes.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b),
+             rc = *reinterpret_cast<uint64_t*>(&c), rd;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+    return *reinterpret_cast<float2*>(&rd);
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
+{
+    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b), rd;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    return *reinterpret_cast<float2*>(&rd);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
@@ -136,6 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    if (warp < 4)
+        regs_decrease<kRegsCtl>();
     if (warp == 0) {
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
@@ -232,8 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(drain);  // arrives once every MMA issued above has completed
             mbar_wait(drain, 0, a.status, kErrWaitDrain, nullptr);
         }
-    } else {
-        const int t = (warp - 2) >> 2;  // query tile of this softmax warp group
+    } else if (warp >= 4) {
+        regs_increase<kRegsSoftmax>();
+        const int t = (warp - 4) >> 2;  // query tile of this softmax warp group
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         const uint32_t t_lane = tmem + (uint32_t(quarter * 32) << 16);
@@ -264,10 +302,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (i >= valid)
                         s[i] = __float_as_uint(-INFINITY);
             }
-            float mx = -INFINITY;
+            // Row max as 8 independent chains of 3-input max (a single chain would serialize 64 dependent ops).
+            float mc[8];
 #pragma unroll
-            for (int i = 0; i < 128; i += 2)
-                mx = fmaxf(mx, fmaxf(__uint_as_float(s[i]), __uint_as_float(s[i + 1])));
+            for (int u = 0; u < 8; ++u)
+                mc[u] = fmaxf(__uint_as_float(s[2 * u]), __uint_as_float(s[2 * u + 1]));
+#pragma unroll
+            for (int i = 16; i < 128; i += 16)
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    mc[u] = fmax3(mc[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+            float mx = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
             mx *= sc;
             const bool need = mx > m_used + kRescaleThreshold;
             if (__any_sync(0xffffffffu, need)) {
@@ -288,25 +333,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 m_used = m_new;
             }
-            const float neg_m = -m_used;
-            float l0 = 0.0f, l1 = 0.0f;
+            // x = s * scale - m for two scores per packed FMA; the row sum in 4 packed accumulators.
+            const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m_used, -m_used);
+            float2 ls[4] = {};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t p[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int k = c * 32 + 2 * i;
-                    const float x0 = fmaf(__uint_as_float(s[k]), sc, neg_m);
-                    const float x1 = fmaf(__uint_as_float(s[k + 1]), sc, neg_m);
-                    const float p0 = k >= kEmuFrom ? ex2_poly(x0) : ex2(x0);
-                    const float p1 = k + 1 >= kEmuFrom ? ex2_poly(x1) : ex2(x1);
-                    l0 += p0;
-                    l1 += p1;
-                    p[i] = pack_bf16x2(p0, p1);
+                    const float2 x = ffma2(make_float2(__uint_as_float(s[k]), __uint_as_float(s[k + 1])), sc2, nm2);
+                    float2 e;
+                    e.x = k >= kEmuFrom<HD> ? ex2_poly(x.x) : ex2(x.x);
+                    e.y = k + 1 >= kEmuFrom<HD> ? ex2_poly(x.y) : ex2(x.y);
+                    ls[i & 3] = fadd2(ls[i & 3], e);
+                    p[i] = pack_bf16x2(e.x, e.y);
                 }
                 tmem_st16(t_lane + col_s + c * 16, p);
             }
-            l += l0 + l1;
+            const float2 l01 = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
+            l += l01.x + l01.y;
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[t]);
@@ -428,26 +474,40 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
     return true;
 }
 
+namespace {
+
+// One-time set-up of a kernel instance: its shared memory size, and a check that the compiled launch register count
+// holds the warpgroups' register split (otherwise the softmax groups' increase could never be granted).
+template <int HD>
+cudaError_t attn_setup()
+{
+    static cudaError_t status = [] {
+        cudaFuncAttributes fa{};
+        cudaError_t e = cudaFuncGetAttributes(&fa, k_attn<HD>);
+        if (e != cudaSuccess)
+            return e;
+        if (fa.numRegs * kThreads < 128 * kRegsCtl + 256 * kRegsSoftmax)
+            return cudaErrorInvalidConfiguration;
+        return cudaFuncSetAttribute(k_attn<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<HD>);
+    }();
+    return status;
+}
+
+}  // namespace
+
 cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
 {
     if (!op.ready)
         return cudaErrorInvalidValue;
-    static bool attr64 = false, attr128 = false;
     if (op.args.head_dim == 64) {
-        if (!attr64) {
-            cudaError_t e = cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<64>);
-            if (e != cudaSuccess)
-                return e;
-            attr64 = true;
-        }
+        cudaError_t e = attn_setup<64>();
+        if (e != cudaSuccess)
+            return e;
         k_attn<64><<<op.grid, kThreads, kSmem<64>, st>>>(op.tq, op.tk, op.tv, op.args);
     } else {
-        if (!attr128) {
-            cudaError_t e = cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<128>);
-            if (e != cudaSuccess)
-                return e;
-            attr128 = true;
-        }
+        cudaError_t e = attn_setup<128>();
+        if (e != cudaSuccess)
+            return e;
         k_attn<128><<<op.grid, kThreads, kSmem<128>, st>>>(op.tq, op.tk, op.tv, op.args);
     }
     count_launch();
