@@ -402,8 +402,9 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         const int M_s[2] = {Mt, Mi}, rps[2] = {S, N}, off[2] = {0, S};
         const char* nm[2] = {"txt", "img"};
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
-        // its tail: QKV, O and FFN-down on 256-wide tiles (QKV: two heads per tile), FFN-up on 192-wide ones
-        // (measured fastest at the config-2 shapes), FFN-down on CTA pairs.
+        // its tail, all on 256 x 256 CTA-pair tiles (QKV: two heads per CTA): the pair halves each SM's W traffic
+        // through L2 and shared memory, which is what bounds the 1-CTA tiles (measured fastest for all four at the
+        // config-2 shapes).
         for (int i = 0; i < NB; ++i) {
             GemmOp* o = plan->ops.data() + size_t(i) * per;
             for (int s : {1, 0}) {
@@ -456,7 +457,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 f1.act = kActGeluTanh;
                 f1.out = hd_s[s];
                 f1.ldo = F;
-                if (!put(o[2], Epi::kBF16, xn_s[s], D, M(p + "ff1.w"), D, f1, F % 192 == 0 ? 192 : 128))
+                if (!put(o[2], Epi::kBF16, xn_s[s], D, M(p + "ff1.w"), D, f1, F % 256 == 0 ? 256 : 128))
                     return fail(MKB_ERR_INVALID, err);
                 GemmArgs f2 = r;
                 f2.K = F;
@@ -465,10 +466,10 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 if (!put(o[3], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_d))
                     return fail(MKB_ERR_INVALID, err);
             }
-            // FFN-down (K = F) on CTA pairs: its long tiles are bound by shared-memory operand traffic, which the
-            // pair tile halves.
-            if (B * N >= 512 && bn_for_pairs(o[3]) && !gemm_use_pairs(o[3], &err))
-                return fail(MKB_ERR_INVALID, err);
+            if (B * N >= 512)
+                for (int k = 0; k < 4; ++k)
+                    if (bn_for_pairs(o[k]) && !gemm_use_pairs(o[k], &err))
+                        return fail(MKB_ERR_INVALID, err);
         }
         GemmArgs a;
         a.M = Mt;
@@ -559,6 +560,10 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
             r2.gate = mod + 3 * D;
             if (!prep(o[3], Epi::kResid, hid, F, M(p + "down.w"), F, r2, bn_for(Mr, D)))
                 return fail(MKB_ERR_INVALID, err);
+            if (Mr >= 512)
+                for (int k = 0; k < 4; ++k)
+                    if (bn_for_pairs(o[k]) && !gemm_use_pairs(o[k], &err))
+                        return fail(MKB_ERR_INVALID, err);
         }
         GemmArgs a;
         a.M = B * S;

@@ -74,13 +74,19 @@ __device__ __forceinline__ float gelu_tanh(float x)
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-__device__ __forceinline__ float apply_act(float v, int act)
+// The activation over a 32-column chunk. The switch sits outside the loop so the 32 independent chains interleave
+// (a per-element branch serializes each SFU round trip).
+__device__ __forceinline__ void apply_act32(float (&v)[32], int act)
 {
-    if (act == kActGeluTanh)
-        return gelu_tanh(v);
-    if (act == kActSilu)
-        return silu(v);
-    return v;
+    if (act == kActGeluTanh) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = gelu_tanh(v[j]);
+    } else if (act == kActSilu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = silu(v[j]);
+    }
 }
 
 __device__ __forceinline__ void load_bias32(const float* bias, int col0, float (&b)[32])
@@ -133,16 +139,10 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
             for (int j = 0; j < 32; ++j)
                 v[j] = __uint_as_float(r[j]) + b[j];
             if constexpr (EPI == Epi::kBF16) {
-                if (a.act != kActNone)
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = apply_act(v[j], a.act);
+                apply_act32(v, a.act);
                 store_bf16x32(static_cast<__nv_bfloat16*>(a.out) + long(row) * a.ldo + col0, v);
             } else if constexpr (EPI == Epi::kF32) {
-                if (a.act != kActNone)
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = apply_act(v[j], a.act);
+                apply_act32(v, a.act);
                 float4* d = reinterpret_cast<float4*>(static_cast<float*>(a.out) + long(row) * a.ldo + col0);
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
