@@ -225,10 +225,17 @@ def run_mkb(args, cfg):
     d = mkimage.Dit(mkimage.DitConfig(variant=mkimage.QWEN1, hidden=D, heads=H, ffn=F, blocks=cfg["blocks"],
                                       text_dim=TD, max_batch=B, max_text_tokens=S, max_image_tokens=N, slots=B))
     d.init_random(seed=1234)
+    sp_mode = args.sp and ws > 1
+    if sp_mode:
+        # One sequence-parallel group over all ranks: rank 0's NCCL id to every rank, then the collective set-up.
+        obj = [mkimage.nccl_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(obj, src=0)
+        d.set_sequence_parallel(obj[0], rank, ws)
     for s in range(B):
         prompt = rng.normal(rng.tensor_key(99, s), S * TD).reshape(S, TD)
         d.begin(prompt, h, w, slot=s)
-    lat_host = rng.normal(rng.tensor_key(98, rank), n_img * N * 64).reshape(n_img, N, 64)
+    # Replicas step their own images; a sequence-parallel group steps the same images on every rank.
+    lat_host = rng.normal(rng.tensor_key(98, 0 if sp_mode else rank), n_img * N * 64).reshape(n_img, N, 64)
     lat = torch.from_numpy(lat_host).to(dev)
     sig = mkimage.sigmas(40, N)
     i0 = int(np.argmin(np.abs(sig[:-1] - 0.5)))
@@ -269,8 +276,8 @@ def run_mkb(args, cfg):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
         torch.distributed.barrier()
-    value = n_img * ws * 1e3 / ms
-    flops_step = d.step_flops(B)
+    value = n_img * (1 if sp_mode else ws) * 1e3 / ms
+    flops_step = d.step_flops(B) / (ws if sp_mode else 1)  # this rank's share of the step
 
     # End to end through the public host-buffer API: pinned latents in, updated latents out, every step.
     e2e = None
@@ -320,7 +327,8 @@ def run_mkb(args, cfg):
                     traffic = float(ln.split(":")[1])
     except Exception:
         pass
-    roofline = {"bound": "tensor", "kernel": "k_gemm (tcgen05, FFN-up 8192x12288x3072, GELU epilogue)",
+    roofline = {"bound": "tensor", "kernel": "k_gemm2 (tcgen05 CTA pair, 256x256 tiles, FFN-up 8192x12288x3072, "
+                                              "GELU epilogue)",
                 "achieved": achieved, "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s",
                 "frac": achieved / peak_tf, "traffic": traffic,
                 **_step_fracs(flops_step / (ms * 1e-3) / 1e12)}
@@ -332,11 +340,14 @@ def run_mkb(args, cfg):
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong" if sp_mode else "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": cfg["workload"], "hidden": D, "heads": H, "ffn": F, "blocks": cfg["blocks"],
                            "image_tokens": N, "text_tokens": S, "samples_per_gpu": B,
-                           "parallelism": f"replicas x{ws} (one image per GPU, CFG pair batched)",
+                           "parallelism": (f"sequence parallel x{ws} (each rank 1/{ws} of every sample's joint rows, "
+                                           f"K/V all-gathered per block over NCCL)") if sp_mode else
+                                          f"replicas x{ws} (images per GPU as configured, CFG pair batched)",
                            "l2": "inputs larger than L2 (40.8 GB of weights streamed per step)",
                            "step_tflop": flops_step / 1e12},
                 "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
@@ -612,6 +623,8 @@ def main():
     ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sp", action="store_true",
+                    help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
     ap.add_argument("--kernel", choices=["gemm", "attention"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()

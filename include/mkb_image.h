@@ -144,6 +144,15 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
                          int H, int head_dim, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0,
                          int rows0, void* out1, long ld1, int rows1, void* stream);
 
+/* mkb_attention over keys and values split into shards of kv_shard_rows rows (a multiple of 128), the layout a
+ * sequence-parallel all-gather leaves: key row j of head (b, h) is row j % kv_shard_rows of head-plane
+ * (j / kv_shard_rows) * kv_plane_stride + b * H + h of k (and of v), each plane kv_shard_rows x d. No counterpart in
+ * the reference, which runs on one device; mkb_dit's sequence-parallel step uses the same kernel path. */
+mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk,
+                                   int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
+                                   int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
+                                   int kv_shard_rows, int kv_plane_stride, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * The denoiser (image::Engine's model interface, src/image/engine.hpp:158-166, on the Qwen-Image-style MMDiT).
  * ------------------------------------------------------------------------------------------------------------- */
@@ -220,6 +229,23 @@ mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, fl
  * "norm_out"; qwen1 blocks report "block.txt" and "block.img"). NULL turns it off. Probing synchronises. */
 typedef void (*mkb_probe_fn)(const char* name, int layer, const float* data, long count, void* user);
 mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user);
+
+/* Sequence parallelism (qwen1 variant), for one image batch spread over `world` GPUs, one handle and process per
+ * GPU. No counterpart in the reference, which runs on one device. Each rank owns a contiguous
+ * 1/world of every sample's joint rows (all text rows on rank 0), runs every GEMM, norm and RoPE on its rows, and the
+ * ranks all-gather each block's K and V over NCCL so attention sees every key. Step calls keep their meaning: every
+ * rank passes the same full latents and gets the full velocities / updated latents. Needs (S + N) divisible by
+ * world, (S + N) / world a multiple of 128 and larger than S. Results equal the one-GPU step bit for bit.
+ * mkb_nccl_unique_id makes the communicator id on one rank (MKB_NCCL_ID_BYTES bytes, to be sent to the others);
+ * every rank then calls mkb_dit_set_sequence_parallel with it, collectively, after create and before begin. NCCL is
+ * loaded at run time (libnccl.so.2). */
+#define MKB_NCCL_ID_BYTES 128
+mkb_status mkb_nccl_unique_id(void* out, size_t bytes);
+mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int rank, int world);
+/* The rows rank `rank` of `world` owns for S text and N image tokens per sample: text_rows (S on rank 0, else 0),
+ * image_rows starting at image token image_row0, and shard_rows = (S + N) / world joint rows. Host arithmetic only. */
+mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,
+                           int* shard_rows);
 
 /* Algorithmic FLOPs of one step over n samples at the current grid and prompt length (GEMMs + attention). */
 double mkb_dit_step_flops(const mkb_dit* d, int n, int first_step);

@@ -65,6 +65,10 @@ mkb_status run_gemm(Epi epi, const void* x, long ldx, const void* w, long ldw, G
     const char* err = nullptr;
     if (!gemm_prepare(op, epi, x, ldx, w, ldw, a, bn, &err))
         return fail(MKB_ERR_INVALID, err ? err : "proj: unsupported arguments");
+    // 256-wide tiles run on CTA pairs when there are enough 256-row tiles to occupy every pair of SMs: the pair
+    // halves each SM's W traffic, which bounds the 1-CTA tile at these sizes.
+    if (bn == 256 && long((a.M + 255) / 256) * (a.N / 256) >= num_sms() / 2 && !gemm_use_pairs(op, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "proj: pair set-up failed");
     return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "proj launch");
 }
 
@@ -286,6 +290,15 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
                          int H, int head_dim, int q_pos0, int mask, int cond_len, int split, void* out0, long ld0,
                          int rows0, void* out1, long ld1, int rows1, void* stream)
 {
+    return mkb_attention_kv_shards(q, Lq, Lq_rows, k, v, Lk, Lk_rows, B, H, head_dim, q_pos0, mask, cond_len, split,
+                                   out0, ld0, rows0, out1, ld1, rows1, 0, 0, stream);
+}
+
+mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk,
+                                   int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
+                                   int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
+                                   int kv_shard_rows, int kv_plane_stride, void* stream)
+{
     if (!q || !k || !v)
         return fail(MKB_ERR_INVALID, "attention: null q/k/v");
     if (mask != MKB_MASK_NONE && mask != MKB_MASK_COND_CAUSAL)
@@ -307,6 +320,8 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
     a.out1 = static_cast<__nv_bfloat16*>(out1);
     a.ld1 = ld1;
     a.rows1 = rows1;
+    a.kv_shard_rows = kv_shard_rows;
+    a.kv_plane_stride = kv_plane_stride;
     a.status = device_status_word();
     AttnOp op;
     const char* err = nullptr;

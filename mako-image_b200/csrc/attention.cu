@@ -188,9 +188,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
+                // Row and plane of key tile j (shards never split a tile: kv_shard_rows is a multiple of 128).
+                int krow = j * kTile, kplane = bh;
+                if (a.kv_shard_rows > 0) {
+                    const int g = krow / a.kv_shard_rows;
+                    krow -= g * a.kv_shard_rows;
+                    kplane = g * a.kv_plane_stride + bh;
+                }
                 mbar_arrive_expect_tx(&k_full[st], TB);
                 for (int pn = 0; pn < HD / 64; ++pn)
-                    tma_load_3d(sK + st * TB + pn * kPanel, &tk, &k_full[st], pn * 64, j * kTile, bh);
+                    tma_load_3d(sK + st * TB + pn * kPanel, &tk, &k_full[st], pn * 64, krow, kplane);
                 ++issued_k;
                 if (!mbar_wait(&v_empty[st], ph ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
@@ -198,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_arrive_expect_tx(&v_full[st], TB);
                 for (int pn = 0; pn < HD / 64; ++pn)
-                    tma_load_3d(sV + st * TB + pn * kPanel, &tv, &v_full[st], pn * 64, j * kTile, bh);
+                    tma_load_3d(sV + st * TB + pn * kPanel, &tv, &v_full[st], pn * 64, krow, kplane);
                 ++issued_v;
             }
             if (!ok) {  // let the loads already issued land before the CTA can exit
@@ -465,8 +472,18 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         return false;
     }
     const int hd = args.head_dim;
-    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) || !make_heads_map(&op.tk, k, Lk_rows, bh, hd, err) ||
-        !make_heads_map(&op.tv, v, Lk_rows, bh, hd, err))
+    int kv_rows = Lk_rows, kv_planes = bh;
+    if (args.kv_shard_rows > 0) {
+        if (args.kv_shard_rows % 128 || args.kv_plane_stride < bh) {
+            *err = "attention: K/V shards need a multiple of 128 rows and a plane stride >= B * H";
+            return false;
+        }
+        const int shards = (args.Lk + args.kv_shard_rows - 1) / args.kv_shard_rows;
+        kv_rows = args.kv_shard_rows;
+        kv_planes = (shards - 1) * args.kv_plane_stride + bh;
+    }
+    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) || !make_heads_map(&op.tk, k, kv_rows, kv_planes, hd, err) ||
+        !make_heads_map(&op.tv, v, kv_rows, kv_planes, hd, err))
         return false;
     op.args = args;
     op.grid = dim3((args.Lq + 2 * kTile - 1) / (2 * kTile), args.H, args.B);

@@ -35,6 +35,11 @@ struct AttnArgs {
     __nv_bfloat16* out1 = nullptr;
     long ld1 = 0;
     int rows1 = 0;
+    // Keys and values split into shards of kv_shard_rows rows (a multiple of 128; 0 = one unsplit [B*H][Lk] plane
+    // per head): key row j of head bh is row j % kv_shard_rows of plane (j / kv_shard_rows) * kv_plane_stride + bh
+    // of the k / v maps. This is the layout a sequence-parallel all-gather leaves (one shard per rank).
+    int kv_shard_rows = 0;
+    int kv_plane_stride = 0;
     uint32_t* status = nullptr;
 };
 

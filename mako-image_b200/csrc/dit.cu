@@ -8,6 +8,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "nccl_dl.cuh"
 #include "rowops.cuh"
 
 #include <cmath>
@@ -56,6 +57,36 @@ void rope3(float* cs, long f, long hp, long wp)
             cs[2 * i] = std::cos(ang);
             cs[2 * i + 1] = std::sin(ang);
         }
+}
+
+// Sequence-parallel split of one sample's joint rows (text rows first, then image rows) over `world` ranks: rank r
+// owns joint rows [r * Lg, (r + 1) * Lg). All text rows sit on rank 0 (S < Lg), so each rank runs one stream's
+// weights on its image rows and rank 0 also the text stream's. Lg must be a multiple of 128 so that no attention key
+// tile spans two ranks' shards.
+struct SpRows {
+    int text = 0;    // text rows on this rank (S on rank 0, else 0)
+    int image = 0;   // image rows on this rank
+    int image0 = 0;  // first image row (image-token index) on this rank
+    int shard = 0;   // joint rows per rank, Lg
+};
+
+const char* sp_partition(int S, int N, int world, int rank, SpRows* out)
+{
+    if (world < 1 || rank < 0 || rank >= world || S < 1 || N < 1)
+        return "sequence parallel: bad world, rank or token counts";
+    const int L = S + N;
+    if (L % world)
+        return "sequence parallel: text + image tokens must divide evenly over the ranks";
+    const int Lg = L / world;
+    if (world > 1 && Lg % 128)
+        return "sequence parallel: rows per rank must be a multiple of 128";
+    if (S >= Lg && world > 1)
+        return "sequence parallel: all text rows must fit on rank 0 with image rows to spare";
+    out->shard = Lg;
+    out->text = rank == 0 ? S : 0;
+    out->image = Lg - out->text;
+    out->image0 = rank * Lg - S + out->text;
+    return nullptr;
 }
 
 }  // namespace
@@ -112,6 +143,27 @@ struct DitImpl {
     std::map<std::vector<int>, Graph> graphs;
     bool use_graphs = true;
 
+    // Sequence parallelism (qwen1): this rank's share of every sample's joint rows; per block the ranks all-gather
+    // their K and V shards (the QKV epilogue writes them straight into this rank's slot of kv_all).
+    int sp_world = 1, sp_rank = 0;
+    ncclComm_t sp_comm = nullptr;
+    int sp_lg_max = 0;
+    __nv_bfloat16* kv_all = nullptr;  // [world][2 (K, V)][B][H][Lg][128] for the step's B and Lg
+    float* vel_x = nullptr;           // [world][B][Lg][64]: velocity exchange
+    float* vel_full = nullptr;        // [Bmax][Nmax][64]: all image rows' velocities after the exchange
+    SpRows rows_of(int S, int N) const
+    {
+        SpRows r;
+        if (sp_world > 1)
+            sp_partition(S, N, sp_world, sp_rank, &r);
+        else
+            r = SpRows{S, N, 0, S + N};
+        return r;
+    }
+    mkb_status set_sp(const void* id, int rank, int world);
+    mkb_status sp_gather_velocity(int B, int S, float* out, cudaMemcpyKind kind, cudaStream_t s);
+    mkb_status stage_latents(int n_src, int copies, int S, const float* src, cudaMemcpyKind kind, cudaStream_t s);
+
     ~DitImpl();
     mkb_status create(const mkb_dit_config& c);
     void add_weight(const std::string& name, long rows, long cols, bool norm = false, bool swiglu = false);
@@ -137,7 +189,9 @@ struct DitImpl {
 DitImpl::~DitImpl()
 {
     void* bufs[] = {wmat, wvec, x_txt, x_img, vel, lat, xn, qh, kh, vh, attn, hid, lat_bf, txt_bf, txt_mid,
-                    tp, h1, temb, st, mod, omod, sig, rope, cfg_lat};
+                    tp, h1, temb, st, mod, omod, sig, rope, cfg_lat, kv_all, vel_x, vel_full};
+    if (stream)
+        cudaStreamSynchronize(stream);
     for (void* p : bufs)
         if (p)
             cudaFree(p);
@@ -149,11 +203,62 @@ DitImpl::~DitImpl()
         for (auto* p : s.vc)
             cudaFree(p);
     }
+    // Graphs may hold the communicator's collectives: release them before the communicator.
     for (auto& g : graphs)
         if (g.second.exec)
             cudaGraphExecDestroy(g.second.exec);
+    if (sp_comm) {
+        if (const NcclApi* api = nccl_api(nullptr))
+            api->CommDestroy(sp_comm);
+    }
     if (stream)
         cudaStreamDestroy(stream);
+}
+
+mkb_status DitImpl::set_sp(const void* id, int rank, int world)
+{
+    if (cfg.variant != MKB_VARIANT_QWEN1)
+        return fail(MKB_ERR_INVALID, "sequence parallel: qwen1 variant only");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return fail(MKB_ERR_INVALID, "sequence parallel: need 1 <= world <= 64 and 0 <= rank < world");
+    if (sp_comm || sp_world > 1)
+        return fail(MKB_ERR_STATE, "sequence parallel: already set on this handle");
+    if (world == 1)
+        return MKB_OK;
+    if (!id)
+        return fail(MKB_ERR_INVALID, "sequence parallel: null NCCL id");
+    std::string err;
+    const NcclApi* api = nccl_api(&err);
+    if (!api)
+        return fail(MKB_ERR_CUDA, "sequence parallel: " + err);
+    sp_lg_max = ((Lmax + world - 1) / world + 127) / 128 * 128;
+    const size_t B = Bmax;
+    const size_t kv = size_t(world) * 2 * B * H * sp_lg_max * kHeadDim * 2;
+    const size_t vx = size_t(world) * B * sp_lg_max * kLatent * 4, vf = B * size_t(Nmax) * kLatent * 4;
+    for (auto [p, bytes, what] : {std::tuple<void**, size_t, const char*>{reinterpret_cast<void**>(&kv_all), kv, "kv"},
+                                  {reinterpret_cast<void**>(&vel_x), vx, "velocity exchange"},
+                                  {reinterpret_cast<void**>(&vel_full), vf, "velocities"}}) {
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e != cudaSuccess)
+            return fail(MKB_ERR_ALLOC, std::string("sequence parallel: allocating ") + what + ": " +
+                                           cudaGetErrorString(e));
+    }
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = api->CommInitRank(&comm, world, uid, rank);
+    if (r != ncclSuccess)
+        return fail(MKB_ERR_CUDA, std::string("sequence parallel: ncclCommInitRank: ") + api->GetErrorString(r));
+    sp_comm = comm;
+    sp_world = world;
+    sp_rank = rank;
+    // Plans and graphs were built for the unsplit geometry.
+    for (auto& g : graphs)
+        if (g.second.exec)
+            cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+    plans.clear();
+    return MKB_OK;
 }
 
 void DitImpl::add_weight(const std::string& name, long rows, long cols, bool norm, bool swiglu)
@@ -393,13 +498,24 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
     plan->ops.resize(size_t(NB) * per + op::kCount);
     GemmOp* g = plan->ops.data() + size_t(NB) * per;
     if (q1) {
-        const int Mt = B * S, Mi = B * N;
+        // This rank's rows (all of them without sequence parallelism): St text and Nl image rows per sample, laid
+        // out in the head-major q/k/v buffers as Lh rows per head.
+        const SpRows rw = rows_of(S, N);
+        const bool sp = sp_world > 1;
+        const int St = rw.text, Nl = rw.image, Lh = rw.shard;
+        const int Mt = B * St, Mi = B * Nl;
         const long mstride = long(NB) * 12 * D;  // per-sample stride of the stacked modulation
         __nv_bfloat16* xn_s[2] = {xn, xn + size_t(Mt) * D};
         __nv_bfloat16* at_s[2] = {attn, attn + size_t(Mt) * D};
         __nv_bfloat16* hd_s[2] = {hid, hid + size_t(Mt) * F};
         float* x_s[2] = {x_txt, x_img};
-        const int M_s[2] = {Mt, Mi}, rps[2] = {S, N}, off[2] = {0, S};
+        const int M_s[2] = {Mt, Mi}, rps[2] = {S, Nl}, off[2] = {0, St};
+        // RoPE row of head-layout row p: the joint position, p + rank * Lh.
+        const float* rope_s[2] = {rope, rope + size_t(sp ? sp_rank : 0) * Lh * kHeadDim};
+        // K and V of this rank go straight into its slot of the all-gather buffer.
+        const size_t kv_shard = size_t(B) * H * Lh * kHeadDim;
+        __nv_bfloat16* k_dst = sp ? kv_all + size_t(sp_rank) * 2 * kv_shard : kh;
+        __nv_bfloat16* v_dst = sp ? k_dst + kv_shard : vh;
         const char* nm[2] = {"txt", "img"};
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
         // its tail, all on 256 x 256 CTA-pair tiles (QKV: two heads per CTA): the pair halves each SM's W traffic
@@ -408,6 +524,8 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         for (int i = 0; i < NB; ++i) {
             GemmOp* o = plan->ops.data() + size_t(i) * per;
             for (int s : {1, 0}) {
+                if (M_s[s] == 0)  // a sequence-parallel rank other than 0 has no text rows
+                    continue;
                 const std::string p = "blk" + std::to_string(i) + "." + nm[s] + ".";
                 const int stream_idx = s == 0 ? 1 : 0;  // mod order: img then txt per block
                 const float* mb = mod + (size_t(i) * 2 + stream_idx) * 6 * D;
@@ -424,13 +542,13 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 a.K = D;
                 a.bias = V(p + "qkv.b");
                 a.qh = qh;
-                a.kh = kh;
-                a.vh = vh;
+                a.kh = k_dst;
+                a.vh = v_dst;
                 a.norm_q = V(p + "norm_q");
                 a.norm_k = V(p + "norm_k");
-                a.rope = rope;
+                a.rope = rope_s[s];
                 a.D = D;
-                a.L = L;
+                a.L = Lh;
                 a.seg_rows = rps[s];
                 a.seg_off = off[s];
                 a.eps = kEps;
@@ -466,7 +584,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 if (!put(o[3], Epi::kResid, hd_s[s], F, M(p + "ff2.w"), F, f2, bn_d))
                     return fail(MKB_ERR_INVALID, err);
             }
-            if (B * N >= 512)
+            if (Mi >= 512)
                 for (int k = 0; k < 4; ++k)
                     if (bn_for_pairs(o[k]) && !gemm_use_pairs(o[k], &err))
                         return fail(MKB_ERR_INVALID, err);
@@ -478,7 +596,7 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         a.bias = V("txt_in.b");
         a.out = x_txt;
         a.ldo = D;
-        if (!prep(g[op::kTxtIn], Epi::kF32, txt_bf, TD, M("txt_in.w"), TD, a, bn_for(Mt, D)))
+        if (Mt > 0 && !prep(g[op::kTxtIn], Epi::kF32, txt_bf, TD, M("txt_in.w"), TD, a, bn_for(Mt, D)))
             return fail(MKB_ERR_INVALID, err);
         a.M = Mi;
         a.K = kLatent;
@@ -493,22 +611,29 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         a.ldo = kLatent;
         if (!prep(g[op::kProjOut], Epi::kF32, xn + size_t(Mt) * D, D, M("proj_out.w"), D, a, 64))
             return fail(MKB_ERR_INVALID, err);
+        // Queries: this rank's Lh rows per head at joint positions rank * Lh...; keys: all L, from the gathered
+        // shards when sequence-parallel. Text rows (rank 0) go to the text stream's O input, image rows after them.
         AttnArgs at;
         at.B = B;
         at.H = H;
-        at.Lq = L;
+        at.Lq = Lh;
         at.Lk = L;
+        at.q_pos0 = sp ? sp_rank * Lh : 0;
         at.mask = kMaskNone;
         at.scale_log2 = 1.4426950408889634f / std::sqrt(float(kHeadDim));
-        at.split = S;
+        at.split = sp && sp_rank > 0 ? sp_rank * Lh : S;
         at.out0 = attn;
         at.ld0 = D;
         at.rows0 = S;
         at.out1 = attn + size_t(Mt) * D;
         at.ld1 = D;
-        at.rows1 = N;
+        at.rows1 = Nl;
+        if (sp) {
+            at.kv_shard_rows = Lh;
+            at.kv_plane_stride = 2 * B * H;
+        }
         at.status = status;
-        if (!attn_prepare(plan->att, qh, L, kh, vh, L, at, &err))
+        if (!attn_prepare(plan->att, qh, Lh, sp ? kv_all : kh, sp ? kv_all + kv_shard : vh, L, at, &err))
             return fail(MKB_ERR_INVALID, err);
     } else {
         const int T = first ? L : N, split = first ? S : 0, Mr = B * T;
@@ -653,6 +778,11 @@ mkb_status DitImpl::run(int B, const int* slot_ids, const float* sigmas, cudaStr
     const int N = gh * gw;
     const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
     const int first = q1 ? 1 : (steps == 0);
+    if (sp_world > 1) {
+        SpRows r;
+        if (const char* e = sp_partition(S, N, sp_world, sp_rank, &r))
+            return fail(MKB_ERR_INVALID, e);
+    }
     Plan* plan = nullptr;
     MKB_TRY(upload_rope(S, s));
     MKB_TRY(build_plan(B, S, N, first, &plan));
@@ -713,6 +843,8 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     const bool q1 = cfg.variant == MKB_VARIANT_QWEN1;
     const int L = S + N, T = q1 ? L : (first ? L : N), split = q1 ? S : (first ? S : 0);
     const int per = q1 ? op::kQ1PerBlock : op::kR21PerBlock;
+    const SpRows rw = rows_of(S, N);  // this rank's text and image rows (all of them unless sequence-parallel)
+    const int St = q1 ? rw.text : S, Nl = q1 ? rw.image : N;
     GemmOp* g = plan->ops.data() + size_t(NB) * per;
     const int R = q1 ? B : 2 * B;
     // Time path: sinusoid -> lin1 -> silu -> lin2 (temb) -> silu -> modulations (qwen_image.cpp:179-205).
@@ -732,7 +864,7 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     }
 
     // Inputs: text rows (every step for qwen1, the first for ref21) and image rows.
-    if (first) {
+    if (first && St > 0) {
         RmsArgs ra{};
         for (int b = 0; b < B; ++b)
             ra.src[b] = slots[slot_ids[b]].prompt;
@@ -745,17 +877,17 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
         MKB_K(rms_norm_rows(ra, s), "txt_norm");
         if (q1) {
             MKB_K(gemm_launch(g[op::kTxtIn], s), "txt_in");
-            MKB_TRY(emit("txt_in", -1, x_txt, long(B) * S * D, s));
+            MKB_TRY(emit("txt_in", -1, x_txt, long(B) * St * D, s));
         } else {
             MKB_K(gemm_launch(g[op::kTxtIn1], s), "txt_in1");
             for (int b = 0; b < B; ++b)
                 MKB_K(gemm_launch(plan->per_sample[2 * b], s), "txt_in2");
         }
     }
-    MKB_K(cast_f32_bf16(lat, lat_bf, size_t(B) * N * kLatent, s), "latents cast");
+    MKB_K(cast_f32_bf16(lat, lat_bf, size_t(B) * Nl * kLatent, s), "latents cast");
     if (q1) {
         MKB_K(gemm_launch(g[op::kImgIn], s), "img_in");
-        MKB_TRY(emit("img_in", -1, x_img, long(B) * N * D, s));
+        MKB_TRY(emit("img_in", -1, x_img, long(B) * Nl * D, s));
     } else {
         for (int b = 0; b < B; ++b)
             MKB_K(gemm_launch(plan->per_sample[2 * b + 1], s), "img_in");
@@ -765,9 +897,11 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     for (int i = 0; i < NB; ++i) {
         GemmOp* o = plan->ops.data() + size_t(i) * per;
         if (q1) {
-            const int Mt = B * S, Mi = B * N;
+            const int Mt = B * St, Mi = B * Nl;
             const long mstride = long(NB) * 12 * D;
-            auto ln = [&](int sidx, int scale_off, int shift_off) {
+            auto ln = [&](int sidx, int scale_off, int shift_off) -> cudaError_t {
+                if ((sidx == 0 ? Mt : Mi) == 0)
+                    return cudaSuccess;
                 const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
                 LnModArgs la{};
                 la.x = sidx == 0 ? x_txt : x_img;
@@ -777,13 +911,21 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
                 la.mod_stride = mstride;
                 la.rows = sidx == 0 ? Mt : Mi;
                 la.D = D;
-                la.rows_per_sample = sidx == 0 ? S : N;
+                la.rows_per_sample = sidx == 0 ? S : Nl;
                 la.eps = kEps;
                 return ln_modulate(la, s);
             };
             MKB_K(ln(0, 1, 0), "ln_modulate 1");
             MKB_K(ln(1, 1, 0), "ln_modulate 1");
             MKB_K(gemm_launch(o[0], s), "qkv");
+            if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
+                const size_t count = size_t(2) * B * H * rw.shard * kHeadDim;
+                const ncclResult_t r = nccl_api(nullptr)->AllGather(kv_all + size_t(sp_rank) * count, kv_all, count,
+                                                                   ncclBfloat16, sp_comm, s);
+                if (r != ncclSuccess)
+                    return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
+                                                  nccl_api(nullptr)->GetErrorString(r));
+            }
             MKB_K(attn_launch(plan->att, s), "attention");
             MKB_K(gemm_launch(o[1], s), "o proj");
             MKB_K(ln(0, 4, 3), "ln_modulate 2");
@@ -837,12 +979,12 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     la.eps = kEps;
     if (q1) {
         la.x = x_img;
-        la.y = xn + size_t(B) * S * D;
+        la.y = xn + size_t(B) * St * D;
         la.scale = omod;
         la.shift = omod + D;
         la.mod_stride = 2L * D;
-        la.rows = B * N;
-        la.rows_per_sample = N;
+        la.rows = B * Nl;
+        la.rows_per_sample = Nl;
         MKB_K(ln_modulate(la, s), "norm_out");
     } else {
         la.x = x_img;
@@ -856,6 +998,45 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
         MKB_K(ln_modulate(la, s), "norm_out");
     }
     MKB_K(gemm_launch(g[op::kProjOut], s), "proj_out");
+    return MKB_OK;
+}
+
+// Latents into `lat`: sample (i * copies + k) takes source sample i's image rows on this rank (all of them unless
+// sequence-parallel), for i < n_src and k < copies. Source samples are [N][64] fp32, `kind` says where they live.
+mkb_status DitImpl::stage_latents(int n_src, int copies, int S, const float* src, cudaMemcpyKind kind, cudaStream_t s)
+{
+    const int N = gh * gw;
+    const SpRows rw = cfg.variant == MKB_VARIANT_QWEN1 ? rows_of(S, N) : SpRows{S, N, 0, S + N};
+    const size_t row = size_t(kLatent) * 4;
+    for (int k = 0; k < copies; ++k)
+        MKB_K(cudaMemcpy2DAsync(lat + size_t(k) * rw.image * kLatent, copies * rw.image * row,
+                                src + size_t(rw.image0) * kLatent, N * row, rw.image * row, n_src, kind, s),
+              "latents");
+    return MKB_OK;
+}
+
+// Sequence-parallel velocities: this rank's image rows of B samples (vel, [B][Nl][64]) into its slot of vel_x at
+// their shard positions, an all-gather, then every shard's image rows into out ([B][N][64]).
+mkb_status DitImpl::sp_gather_velocity(int B, int S, float* out, cudaMemcpyKind kind, cudaStream_t s)
+{
+    const int N = gh * gw;
+    const SpRows rw = rows_of(S, N);
+    const int Lg = rw.shard;
+    const size_t row = size_t(kLatent) * 4, slot = size_t(B) * Lg * kLatent;
+    MKB_K(cudaMemcpy2DAsync(vel_x + sp_rank * slot + size_t(rw.text) * kLatent, Lg * row, vel, rw.image * row,
+                            rw.image * row, B, cudaMemcpyDeviceToDevice, s),
+          "velocity exchange");
+    const ncclResult_t r = nccl_api(nullptr)->AllGather(vel_x + sp_rank * slot, vel_x, slot, ncclFloat32, sp_comm, s);
+    if (r != ncclSuccess)
+        return fail(MKB_ERR_CUDA, std::string("dit: velocity all-gather: ") + nccl_api(nullptr)->GetErrorString(r));
+    for (int g = 0; g < sp_world; ++g) {
+        const int p0 = std::max(g * Lg, S), p1 = (g + 1) * Lg;  // joint rows of shard g that are image rows
+        if (p0 >= p1)
+            continue;
+        MKB_K(cudaMemcpy2DAsync(out + size_t(p0 - S) * kLatent, N * row, vel_x + g * slot + size_t(p0 - g * Lg) * kLatent,
+                                Lg * row, (p1 - p0) * row, B, kind, s),
+              "velocity exchange");
+    }
     return MKB_OK;
 }
 
@@ -877,6 +1058,8 @@ mkb_status check_handle(const mkb_dit* d)
 // Copies the image rows' velocities of B samples from vel to out_dev (device) on stream s.
 mkb_status gather_velocity(DitImpl& m, int B, int S, bool first, float* out, cudaMemcpyKind kind, cudaStream_t s)
 {
+    if (m.sp_world > 1)
+        return m.sp_gather_velocity(B, S, out, kind, s);
     const int N = m.gh * m.gw;
     const bool q1 = m.cfg.variant == MKB_VARIANT_QWEN1;
     const int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
@@ -1036,11 +1219,12 @@ mkb_status mkb_dit_step_batch_dev(mkb_dit* d, int n, const int* slots, const flo
     if (m.gh * m.gw == 0)
         return fail(MKB_ERR_STATE, "step before begin");
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
-    const int N = m.gh * m.gw;
-    MKB_TRY_CUDA(cudaMemcpyAsync(m.lat, latents_dev, size_t(n) * N * kLatent * 4, cudaMemcpyDeviceToDevice, s),
-                 "latents");
+    for (int i = 0; i < n; ++i)
+        if (slots[i] < 0 || slots[i] >= int(m.slots.size()) || !m.slots[slots[i]].begun)
+            return fail(MKB_ERR_STATE, "step on a slot without begin");
     bool first = false;
     const int S = m.slots[slots[0]].S;
+    MKB_TRY(m.stage_latents(n, 1, S, latents_dev, cudaMemcpyDeviceToDevice, s));
     MKB_TRY(m.run(n, slots, sigmas, s, &first));
     return gather_velocity(m, n, S, first, out_dev, cudaMemcpyDeviceToDevice, s);
 }
@@ -1054,14 +1238,12 @@ mkb_status mkb_dit_step_batch(mkb_dit* d, int n, const int* slots, const float* 
         return fail(MKB_ERR_INVALID, "step: bad arguments");
     if (m.gh * m.gw == 0)
         return fail(MKB_ERR_STATE, "step before begin");
-    const int N = m.gh * m.gw;
     for (int i = 0; i < n; ++i)
         if (slots[i] < 0 || slots[i] >= int(m.slots.size()) || !m.slots[slots[i]].begun)
             return fail(MKB_ERR_STATE, "step on a slot without begin");
-    MKB_TRY_CUDA(cudaMemcpyAsync(m.lat, latents, size_t(n) * N * kLatent * 4, cudaMemcpyHostToDevice, m.stream),
-                 "latents upload");
     bool first = false;
     const int S = m.slots[slots[0]].S;
+    MKB_TRY(m.stage_latents(n, 1, S, latents, cudaMemcpyHostToDevice, m.stream));
     MKB_TRY(m.run(n, slots, sigmas, m.stream, &first));
     MKB_TRY(gather_velocity(m, n, S, first, out, cudaMemcpyDeviceToHost, m.stream));
     MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "step sync");
@@ -1086,22 +1268,28 @@ mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, fl
     const size_t img = size_t(N) * kLatent;
     std::vector<int> ids(B);
     std::vector<float> sg(B, sigma);
-    for (int i = 0; i < B; ++i)
+    for (int i = 0; i < B; ++i) {
         ids[i] = i;
+        if (!m.slots[i].begun)
+            return fail(MKB_ERR_STATE, "step_cfg: slots 0 .. 2 * n_images - 1 need begin");
+    }
+    const int S = m.slots[0].S;
     // Both predictions of image i see the same latents.
-    for (int i = 0; i < n_images; ++i)
-        for (int k = 0; k < 2; ++k)
-            MKB_TRY_CUDA(cudaMemcpyAsync(m.lat + (2 * i + k) * img, latents_dev + i * img, img * 4,
-                                         cudaMemcpyDeviceToDevice, s),
-                         "latents");
+    MKB_TRY(m.stage_latents(n_images, 2, S, latents_dev, cudaMemcpyDeviceToDevice, s));
     bool first = false;
     MKB_TRY(m.run(B, ids.data(), sg.data(), s, &first));
-    const int S = m.slots[0].S;
     const bool q1 = m.cfg.variant == MKB_VARIANT_QWEN1;
-    const int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
+    int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
+    const float* vel = m.vel;
+    if (m.sp_world > 1) {  // every rank applies the update to all rows, from the gathered velocities
+        MKB_TRY(m.sp_gather_velocity(B, S, m.vel_full, cudaMemcpyDeviceToDevice, s));
+        vel = m.vel_full;
+        T = N;
+        split = 0;
+    }
     for (int i = 0; i < n_images; ++i) {
-        const float* vc = m.vel + (size_t(2 * i) * T + split) * kLatent;
-        const float* vu = m.vel + (size_t(2 * i + 1) * T + split) * kLatent;
+        const float* vc = vel + (size_t(2 * i) * T + split) * kLatent;
+        const float* vu = vel + (size_t(2 * i + 1) * T + split) * kLatent;
         MKB_TRY_CUDA(cfg_euler(latents_dev + i * img, vc, vu, guidance, sigma_next - sigma, img, s), "cfg euler");
     }
     return MKB_OK;
@@ -1127,6 +1315,45 @@ mkb_status mkb_dit_step_cfg(mkb_dit* d, float* latents, float sigma, float sigma
     if (st == MKB_OK)
         st = m.check_status();
     return st;
+}
+
+mkb_status mkb_nccl_unique_id(void* out, size_t bytes)
+{
+    if (!out || bytes < sizeof(ncclUniqueId))
+        return fail(MKB_ERR_INVALID, "nccl_unique_id: need a buffer of MKB_NCCL_ID_BYTES");
+    std::string err;
+    const NcclApi* api = nccl_api(&err);
+    if (!api)
+        return fail(MKB_ERR_CUDA, "nccl_unique_id: " + err);
+    ncclUniqueId id;
+    const ncclResult_t r = api->GetUniqueId(&id);
+    if (r != ncclSuccess)
+        return fail(MKB_ERR_CUDA, std::string("ncclGetUniqueId: ") + api->GetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int rank, int world)
+{
+    MKB_TRY(check_handle(d));
+    return d->impl.set_sp(nccl_id, rank, world);
+}
+
+mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,
+                           int* shard_rows)
+{
+    SpRows r;
+    if (const char* e = sp_partition(S, N, world, rank, &r))
+        return fail(MKB_ERR_INVALID, e);
+    if (text_rows)
+        *text_rows = r.text;
+    if (image_rows)
+        *image_rows = r.image;
+    if (image_row0)
+        *image_row0 = r.image0;
+    if (shard_rows)
+        *shard_rows = r.shard;
+    return MKB_OK;
 }
 
 mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user)

@@ -82,6 +82,12 @@ _SIGS = {
     "mkb_er_sde_sigma": (_f, [_vp, _i]),
     "mkb_er_sde_step": (_i, [_vp, _i, _vp, _vp, _vp, _l, _f]),
     "mkb_attention": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l, _i, _vp]),
+    "mkb_attention_kv_shards": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l,
+                                     _i, _i, _i, _vp]),
+    "mkb_nccl_unique_id": (_i, [_vp, ctypes.c_size_t]),
+    "mkb_dit_set_sequence_parallel": (_i, [_vp, _vp, _i, _i]),
+    "mkb_dit_sp_rows": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i),
+                             ctypes.POINTER(_i)]),
 }
 
 

@@ -140,3 +140,26 @@ class Dit:
 
     def step_flops(self, n, first_step=True):
         return lib.mkb_dit_step_flops(self.h, n, int(first_step))
+
+    def set_sequence_parallel(self, nccl_id: bytes, rank: int, world: int):
+        """Joins this handle to a sequence-parallel group (collective over the `world` ranks; see
+        mkb_dit_set_sequence_parallel). nccl_id comes from nccl_unique_id() on one rank."""
+        buf = ctypes.create_string_buffer(bytes(nccl_id), NCCL_ID_BYTES)
+        check(lib.mkb_dit_set_sequence_parallel(self.h, buf, rank, world))
+
+
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL communicator id (NCCL_ID_BYTES bytes) for set_sequence_parallel."""
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    check(lib.mkb_nccl_unique_id(buf, NCCL_ID_BYTES))
+    return buf.raw
+
+
+def sp_rows(S, N, world, rank):
+    """(text_rows, image_rows, image_row0, shard_rows) that rank `rank` of `world` owns (mkb_dit_sp_rows)."""
+    out = [ctypes.c_int() for _ in range(4)]
+    check(lib.mkb_dit_sp_rows(S, N, world, rank, *[ctypes.byref(o) for o in out]))
+    return tuple(o.value for o in out)

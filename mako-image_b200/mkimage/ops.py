@@ -84,6 +84,20 @@ def attention(q, k, v, out0, out1, split, Lq=None, Lk=None, q_pos0=0, mask=MASK_
                             rows1, stream_ptr()))
 
 
+def attention_kv_shards(q, k, v, out0, out1, split, Lk, kv_shard_rows, kv_plane_stride, Lq=None, q_pos0=0,
+                        mask=MASK_NONE, cond_len=0):
+    """attention() with keys and values in shards of kv_shard_rows rows: k and v are [planes][kv_shard_rows][d] and
+    key row j of head bh is row j % kv_shard_rows of plane (j // kv_shard_rows) * kv_plane_stride + bh (see
+    mkb_attention_kv_shards)."""
+    B, H, Lq_rows, hd = q.shape
+    Lq = Lq or Lq_rows
+    rows0 = out0.shape[0] // B if out0 is not None else 0
+    rows1 = out1.shape[0] // B
+    check(lib.mkb_attention_kv_shards(_p(q), Lq, Lq_rows, _p(k), _p(v), Lk, Lk, B, H, hd, q_pos0, mask, cond_len,
+                                      split, _p(out0), out0.stride(0) if out0 is not None else 0, rows0, _p(out1),
+                                      out1.stride(0), rows1, kv_shard_rows, kv_plane_stride, stream_ptr()))
+
+
 def proj_add(x, w, bias=None, addvec=None, rows_per_sample=None, resid=None, out=None, out_f32=True):
     """y = x @ w.T + bias + addvec[row // rows_per_sample] + resid (fp32 or bf16 out; resid may be out)."""
     import torch

@@ -74,3 +74,41 @@ def test_attention_rejects_bad_routing(cuda):
     out1 = torch.zeros(100, 128, dtype=torch.bfloat16, device=cuda)  # too few rows for 256 queries
     with pytest.raises(mkimage.MkbError):
         mkimage.ops.attention(q, q, q, None, out1, split=0)
+
+
+@pytest.mark.parametrize("hd,G,B,H,S,N", [(128, 2, 2, 3, 100, 412), (128, 4, 1, 2, 64, 960), (64, 2, 2, 2, 77, 435)])
+def test_attention_kv_shards_bit_exact(cuda, hd, G, B, H, S, N):
+    """K/V split into G shards of L/G rows (K and V of a shard interleaved, as the sequence-parallel step gathers
+    them) gives bit-identical outputs to the unsplit call: same key tiles, same order."""
+    import torch
+    import mkimage
+
+    L = S + N
+    Lg = L // G
+    assert L % G == 0 and Lg % 128 == 0
+    q = _heads((B, H, L, hd), 11, cuda)
+    k = _heads((B, H, L, hd), 12, cuda)
+    v = _heads((B, H, L, hd), 13, cuda)
+    ref0 = torch.zeros(B * S, H * hd, dtype=torch.bfloat16, device=cuda)
+    ref1 = torch.zeros(B * N, H * hd, dtype=torch.bfloat16, device=cuda)
+    mkimage.ops.attention(q, k, v, ref0, ref1, split=S)
+    # [G][2][B*H][Lg][hd]: shard g holds key rows [g*Lg, (g+1)*Lg) of every head, K then V.
+    kv = torch.empty(G, 2, B * H, Lg, hd, dtype=torch.bfloat16, device=cuda)
+    for g in range(G):
+        kv[g, 0] = k.reshape(B * H, L, hd)[:, g * Lg:(g + 1) * Lg]
+        kv[g, 1] = v.reshape(B * H, L, hd)[:, g * Lg:(g + 1) * Lg]
+    out0 = torch.zeros_like(ref0)
+    out1 = torch.zeros_like(ref1)
+    mkimage.ops.attention_kv_shards(q, kv[0, 0], kv[0, 1], out0, out1, split=S, Lk=L, kv_shard_rows=Lg,
+                                    kv_plane_stride=2 * B * H)
+    assert mkimage.ops.check_kernels() == 0
+    assert torch.equal(out0, ref0) and torch.equal(out1, ref1)
+    # The queries of one shard alone (a sequence-parallel rank's rows), routed past the text rows.
+    r = G - 1
+    qr = q[:, :, r * Lg:(r + 1) * Lg].contiguous()
+    outr = torch.zeros(B * Lg, H * hd, dtype=torch.bfloat16, device=cuda)
+    mkimage.ops.attention_kv_shards(qr, kv[0, 0], kv[0, 1], None, outr, split=r * Lg, Lk=L, kv_shard_rows=Lg,
+                                    kv_plane_stride=2 * B * H, q_pos0=r * Lg)
+    assert mkimage.ops.check_kernels() == 0
+    for b in range(B):
+        assert torch.equal(outr[b * Lg:(b + 1) * Lg], ref1[b * N + r * Lg - S:b * N + (r + 1) * Lg - S])
