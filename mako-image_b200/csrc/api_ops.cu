@@ -72,15 +72,7 @@ mkb_status run_gemm(Epi epi, const void* x, long ldx, const void* w, long ldw, G
     return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "proj launch");
 }
 
-int pick_bn(int M, int N)
-{
-    // Wide tiles halve the X re-reads; narrow ones fill the SMs when there are few tiles.
-    if (N % 256 == 0 && long((M + 127) / 128) * (N / 256) >= num_sms() / 2)
-        return 256;
-    if (N % 128 == 0)
-        return 128;
-    return 64;
-}
+int pick_bn(int M, int N) { return gemm_pick_bn(M, N); }
 
 }  // namespace
 

@@ -744,6 +744,27 @@ cudaError_t launch_bn(const GemmOp& op, cudaStream_t st)
 
 }  // namespace
 
+int gemm_pick_bn(long M, int N, bool pairs)
+{
+    // Makespan in units of one 128-column tile: rounds of tiles over the SMs (pairs of SMs for 256-row pair tiles)
+    // times the tile width. 64-wide tiles pay 1.5x: their X + W stage traffic (24 KB per 128 MMA cycles) exceeds
+    // what shared memory delivers per cycle.
+    const long sms = num_sms(), rows = pairs ? 2 * kBM : kBM, slots = pairs ? sms / 2 : sms;
+    int best = 0;
+    double best_cost = 0;
+    for (int bn : {256, 192, 160, 128, 64}) {
+        if (N % bn && !(bn == 64 && N % 32 == 0))
+            continue;
+        const long tiles = ((M + rows - 1) / rows) * ((N + bn - 1) / bn);
+        const double cost = double((tiles + slots - 1) / slots) * bn * (bn == 64 ? 1.5 : 1.0);
+        if (!best || cost < best_cost - 1e-9) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
 int num_sms()
 {
     static int n = 0;
@@ -788,16 +809,16 @@ namespace {
 // Checks of the epilogue arguments shared by the GEMM and the convolution.
 bool check_epilogue(Epi epi, const GemmArgs& args, int bn, const char** err)
 {
-    if (bn != 64 && bn != 128 && bn != 192 && bn != 256) {
-        *err = "gemm: tile width must be 64, 128, 192 or 256";
+    if (bn != 64 && bn != 128 && bn != 160 && bn != 192 && bn != 256) {
+        *err = "gemm: tile width must be 64, 128, 160, 192 or 256";
         return false;
     }
     if (epi == Epi::kQkv && (bn < 128 || args.D % bn || args.N != 3 * args.D || !args.qh || !args.kh || !args.vh)) {
         *err = "gemm: qkv epilogue needs N = 3 D, D a multiple of the tile width, and q/k/v outputs";
         return false;
     }
-    if (epi == Epi::kSwiGLU && args.N % bn) {
-        *err = "gemm: swiglu epilogue needs N a multiple of the tile width";
+    if (epi == Epi::kSwiGLU && (bn != 256 || args.N % bn)) {
+        *err = "gemm: swiglu epilogue needs 256-wide tiles (128 gate + 128 up columns) and N a multiple of 256";
         return false;
     }
     if (epi == Epi::kResid && (!args.resid || !args.gate || (args.ldr & 3))) {
@@ -997,6 +1018,7 @@ cudaError_t gemm_launch(const GemmOp& op, cudaStream_t st)
     switch (op.bn) {
     case 64: return launch_bn<64>(op, st);
     case 128: return launch_bn<128>(op, st);
+    case 160: return launch_bn<160>(op, st);
     case 192: return launch_bn<192>(op, st);
     case 256: return launch_bn<256>(op, st);
     }

@@ -330,7 +330,8 @@ struct Builder {
         a.ldo = ldy;
         a.out_f32 = out_f32;
         a.status = status;
-        const int bn = Cout % 256 == 0 && Cout >= 512 ? 256 : Cout % 128 == 0 ? 128 : 64;
+        const int Ho = stride == 2 ? H / 2 : H, Wo = stride == 2 ? W / 2 : W;
+        const int bn = gemm_pick_bn(long(B) * Ho * Wo, Cout);
         GemmOp op;
         if (!conv_prepare(op, Epi::kAdd, x, B, H, W, Cin, w, Cout, taps, stride, a, bn, &err))
             return bad(err);
@@ -342,7 +343,7 @@ struct Builder {
             return;
         a.status = status;
         if (!bn)
-            bn = a.N % 256 == 0 && a.M >= 4096 ? 256 : a.N % 128 == 0 ? 128 : 64;
+            bn = gemm_pick_bn(a.M, a.N);
         if (epi == Epi::kSwiGLU)
             bn = 256;
         GemmOp op;
