@@ -2,6 +2,7 @@
 #include "rowops.cuh"
 #include "common.cuh"
 
+#include <algorithm>
 #include <cstdint>
 
 namespace mkb {
@@ -190,11 +191,36 @@ __global__ void k_fill_normal(void* out, int bf16, uint64_t n, uint64_t key, uin
     }
 }
 
-__global__ void k_cast(const float* x, __nv_bfloat16* y, uint64_t n)
+__global__ void k_cast_scalar(const float* x, __nv_bfloat16* y, uint64_t n)
 {
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
         y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// fp32 -> bf16: float4 in, four bf16 out per step, four steps in flight; the n % 4 tail by scalars. Needs x 16-byte
+// and y 8-byte aligned (k_cast_scalar otherwise).
+__global__ void k_cast(const float* x, __nv_bfloat16* y, uint64_t n)
+{
+    const uint64_t n4 = n / 4, stride = uint64_t(gridDim.x) * blockDim.x;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    uint2* y4 = reinterpret_cast<uint2*>(y);
+    uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            v[u] = x4[i + u * stride];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            y4[i + u * stride] = pack4_bf16(v[u].x, v[u].y, v[u].z, v[u].w);
+    }
+    for (; i < n4; i += stride) {
+        const float4 v = x4[i];
+        y4[i] = pack4_bf16(v.x, v.y, v.z, v.w);
+    }
+    for (uint64_t j = 4 * n4 + uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += stride)
+        y[j] = __float2bfloat16_rn(x[j]);
 }
 
 __global__ void k_silu(const float* x, float* y, uint64_t n)
@@ -228,8 +254,17 @@ __global__ void k_cfg_euler(float* x, const float* vc, const float* vu, float g,
 }
 
 // ---- GroupNorm
+//
+// x is channels-last fp32 [B][HW][C]. Thread t of a 256-thread block owns channel quad q = t % Qb (Qb = min(C/4,
+// 256); quads q + 256, q + 512, ... too when C > 1024) and pixel lane r = t / Qb of Rb = 256 / Qb lanes, so a warp
+// reads contiguous float4s and no thread divides per element.
 
-constexpr int kGnChunk = 32;  // pixels per statistics chunk
+// Pixels per statistics chunk: about four chunks per SM over the whole batch, at least 64 pixels.
+__host__ __device__ inline int gn_chunk_px(int B, int HW)
+{
+    const long want = (long(B) * HW + 4 * 148 - 1) / (4 * 148);
+    return int(want < 64 ? 64 : want);
+}
 
 // Chan et al.'s pairwise combination of (count, mean, M2).
 __device__ __forceinline__ void chan_combine(float& n, float& mean, float& m2, float nb, float meanb, float m2b)
@@ -243,32 +278,52 @@ __device__ __forceinline__ void chan_combine(float& n, float& mean, float& m2, f
     n = nn;
 }
 
-__global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a)
+// Per (sample, chunk, group): count, mean and M2 of the chunk's pixels, from per-thread running (Welford)
+// statistics per channel, combined through shared memory [Rb][C] by one thread per group.
+__global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a, int chunk_px, int nchunks)
 {
-    extern __shared__ float sh[];  // [C] means, [C] M2
+    extern __shared__ float sh[];  // mean [Rb][C], M2 [Rb][C], count [Rb]
     const int chunk = blockIdx.x, b = blockIdx.y;
-    const int p0 = chunk * kGnChunk, np = min(kGnChunk, a.HW - p0);
-    const float* xb = a.x + (long(b) * a.HW + p0) * a.C;
-    for (int c = threadIdx.x; c < a.C; c += blockDim.x) {
-        float s = 0.f;
-        for (int p = 0; p < np; ++p)
-            s += xb[long(p) * a.C + c];
-        const float mean = s / float(np);
-        float m2 = 0.f;
-        for (int p = 0; p < np; ++p) {
-            const float d = xb[long(p) * a.C + c] - mean;
-            m2 += d * d;
+    const int Q = a.C / 4, Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
+    const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
+    const int p0 = chunk * chunk_px, np = min(chunk_px, a.HW - p0);
+    float* smean = sh;
+    float* sm2 = sh + Rb * a.C;
+    float* scount = sh + 2 * Rb * a.C;
+    if (r < Rb) {
+        const float4* xb = reinterpret_cast<const float4*>(a.x + (long(b) * a.HW + p0) * a.C);
+        float n = 0.f;
+        for (int q = q0; q < Q; q += Qb) {
+            float mean[4] = {0.f, 0.f, 0.f, 0.f}, m2[4] = {0.f, 0.f, 0.f, 0.f};
+            n = 0.f;
+            for (int p = r; p < np; p += Rb) {
+                const float4 v = xb[long(p) * Q + q];
+                n += 1.f;
+                const float rn = 1.f / n;
+                const float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float d = xv[k] - mean[k];
+                    mean[k] += d * rn;
+                    m2[k] += d * (xv[k] - mean[k]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                smean[r * a.C + 4 * q + k] = mean[k];
+                sm2[r * a.C + 4 * q + k] = m2[k];
+            }
         }
-        sh[c] = mean;
-        sh[a.C + c] = m2;
+        if (q0 == 0)
+            scount[r] = n;
     }
     __syncthreads();
     const int cpg = a.C / a.groups;
-    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
-    for (int g = threadIdx.x; g < a.groups; g += blockDim.x) {
+    for (int g = t; g < a.groups; g += blockDim.x) {
         float n = 0.f, mean = 0.f, m2 = 0.f;
-        for (int c = g * cpg; c < (g + 1) * cpg; ++c)
-            chan_combine(n, mean, m2, float(np), sh[c], sh[a.C + c]);
+        for (int rr = 0; rr < Rb; ++rr)
+            for (int c = g * cpg; c < (g + 1) * cpg; ++c)
+                chan_combine(n, mean, m2, scount[rr], smean[rr * a.C + c], sm2[rr * a.C + c]);
         float* o = a.ws + ((long(b) * nchunks + chunk) * a.groups + g) * 3;
         o[0] = n;
         o[1] = mean;
@@ -276,11 +331,11 @@ __global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a)
     }
 }
 
-__global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a)
+// Per (sample, group): the chunks combined by a tree, then mean and 1 / sqrt(var + eps).
+__global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a, int nchunks)
 {
     __shared__ float sn[256], sm[256], sq[256];
     const int g = blockIdx.x, b = blockIdx.y;
-    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
     float n = 0.f, mean = 0.f, m2 = 0.f;
     for (int k = threadIdx.x; k < nchunks; k += blockDim.x) {
         const float* o = a.ws + ((long(b) * nchunks + k) * a.groups + g) * 3;
@@ -307,42 +362,82 @@ __global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a)
     }
 }
 
-__global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a)
+// y = x * scale_c + shift_c (then SiLU) as bf16, scale_c = rstd_g gamma_c, shift_c = beta_c - mean_g scale_c; each
+// thread keeps its quad's four (scale, shift) in registers. Block (x, b) covers pixels [x * px, (x + 1) * px).
+__global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a, int nchunks, int px)
 {
-    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
-    const float* fin = a.ws + long(a.B) * nchunks * a.groups * 3;
-    const int cpg = a.C / a.groups, c4n = a.C / 4;
-    const uint64_t total = uint64_t(a.B) * a.HW * c4n;
-    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int c = int(i % c4n) * 4;
-        const int b = int(i / (uint64_t(a.HW) * c4n));
-        const float4 v = reinterpret_cast<const float4*>(a.x)[i];
-        float r[4] = {v.x, v.y, v.z, v.w};
+    const int b = blockIdx.y;
+    const int Q = a.C / 4, Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
+    const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
+    if (r >= Rb)
+        return;
+    const int p0 = blockIdx.x * px, np = min(px, a.HW - p0);
+    const float* fin = a.ws + long(a.B) * nchunks * a.groups * 3 + long(b) * a.groups * 2;
+    const int cpg = a.C / a.groups;
+    const float4* xb = reinterpret_cast<const float4*>(a.x + (long(b) * a.HW + p0) * a.C);
+    uint2* yb = reinterpret_cast<uint2*>(a.y + (long(b) * a.HW + p0) * a.C);
+    for (int q = q0; q < Q; q += Qb) {
+        float sc[4], sf[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int g = (c + k) / cpg;
-            const float mean = fin[(long(b) * a.groups + g) * 2], rstd = fin[(long(b) * a.groups + g) * 2 + 1];
-            float y = (r[k] - mean) * rstd * a.gamma[c + k] + (a.beta ? a.beta[c + k] : 0.f);
-            if (a.silu)
-                y = y / (1.f + __expf(-y));
-            r[k] = y;
+            const int c = 4 * q + k, g = c / cpg;
+            sc[k] = fin[2 * g + 1] * a.gamma[c];
+            sf[k] = (a.beta ? a.beta[c] : 0.f) - fin[2 * g] * sc[k];
         }
-        reinterpret_cast<uint2*>(a.y)[i] = pack4_bf16(r[0], r[1], r[2], r[3]);
+        int p = r;
+        for (; p + 3 * Rb < np; p += 4 * Rb) {  // four loads in flight
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                v[u] = xb[long(p + u * Rb) * Q + q];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float y[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    y[k] = fmaf(y[k], sc[k], sf[k]);
+                    if (a.silu)
+                        y[k] = y[k] / (1.f + __expf(-y[k]));
+                }
+                yb[long(p + u * Rb) * Q + q] = pack4_bf16(y[0], y[1], y[2], y[3]);
+            }
+        }
+        for (; p < np; p += Rb) {
+            const float4 v = xb[long(p) * Q + q];
+            float y[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                y[k] = fmaf(y[k], sc[k], sf[k]);
+                if (a.silu)
+                    y[k] = y[k] / (1.f + __expf(-y[k]));
+            }
+            yb[long(p) * Q + q] = pack4_bf16(y[0], y[1], y[2], y[3]);
+        }
     }
 }
 
-__global__ void k_upsample2x(const float4* x, uint2* y, int B, int H, int W, int C4)
+// Nearest 2x upsampling: block (y, b) reads input row y once (float4 per thread, the quad/lane mapping of the
+// GroupNorm kernels) and writes it to output rows 2y and 2y + 1, each pixel twice.
+__global__ void __launch_bounds__(256) k_upsample2x(const float4* x, uint2* y, int H, int W, int Q)
 {
-    const uint64_t total = uint64_t(B) * 2 * H * 2 * W * C4;
-    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-        const int c = int(i % C4);
-        const uint64_t px = i / C4;
-        const int ox = int(px % (2 * W)), oy = int((px / (2 * W)) % (2 * H)), b = int(px / (4ull * W * H));
-        const float4 v = x[((uint64_t(b) * H + oy / 2) * W + ox / 2) * C4 + c];
-        y[i] = pack4_bf16(v.x, v.y, v.z, v.w);
-    }
+    const int iy = blockIdx.x, b = blockIdx.y;
+    const int Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
+    const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
+    if (r >= Rb)
+        return;
+    const float4* xr = x + (long(b) * H + iy) * W * Q;
+    uint2* y0 = y + (long(b) * 2 * H + 2 * iy) * 2 * W * Q;
+    uint2* y1 = y0 + long(2 * W) * Q;
+    for (int q = q0; q < Q; q += Qb)
+        for (int ix = r; ix < W; ix += Rb) {
+            const float4 v = xr[long(ix) * Q + q];
+            const uint2 o = pack4_bf16(v.x, v.y, v.z, v.w);
+            const long j = long(2 * ix) * Q + q;
+            y0[j] = o;
+            y0[j + Q] = o;
+            y1[j] = o;
+            y1[j + Q] = o;
+        }
 }
 
 __global__ void k_concat(const float4* a, int Ca4, const float4* b, int Cb4, float4* y, long P)
@@ -575,7 +670,10 @@ cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStre
 {
     if (!n)
         return cudaSuccess;
-    k_cast<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 7))
+        k_cast_scalar<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    else
+        k_cast<<<grid_for(n / 4 + 1, 256), 256, 0, st>>>(x, y, n);
     count_launch();
     return cudaGetLastError();
 }
@@ -606,7 +704,7 @@ cudaError_t copy_head_rows(const __nv_bfloat16* src, int src_rows, int src_off, 
 size_t group_norm_workspace(int B, int HW, int C, int groups)
 {
     (void)C;
-    const size_t nchunks = (size_t(HW) + kGnChunk - 1) / kGnChunk;
+    const size_t px = gn_chunk_px(B, HW), nchunks = (size_t(HW) + px - 1) / px;
     return (size_t(B) * nchunks * groups * 3 + size_t(B) * groups * 2) * sizeof(float);
 }
 
@@ -614,24 +712,34 @@ cudaError_t group_norm(const GnArgs& a, cudaStream_t st)
 {
     if (a.B <= 0 || a.HW <= 0 || a.groups <= 0 || a.C % a.groups || a.C % 4 || a.C > 6144 || !a.ws || !a.gamma)
         return cudaErrorInvalidValue;
-    const int nchunks = (a.HW + kGnChunk - 1) / kGnChunk;
-    k_gn_stats<<<dim3(nchunks, a.B), 256, 2 * a.C * sizeof(float), st>>>(a);
+    const int px = gn_chunk_px(a.B, a.HW), nchunks = (a.HW + px - 1) / px;
+    const int Q = a.C / 4, Rb = 256 / (Q < 256 ? Q : 256);
+    const size_t smem = (size_t(2) * Rb * a.C + Rb) * sizeof(float);  // <= 48 KB + 4 B at C = 6144
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_gn_stats, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (2 * 6144 + 1) * int(sizeof(float)));
+        if (e != cudaSuccess)
+            return e;
+        attr = true;
+    }
+    k_gn_stats<<<dim3(nchunks, a.B), 256, smem, st>>>(a, px, nchunks);
     count_launch();
-    k_gn_finalize<<<dim3(a.groups, a.B), 256, 0, st>>>(a);
+    k_gn_finalize<<<dim3(a.groups, a.B), 256, 0, st>>>(a, nchunks);
     count_launch();
-    const uint64_t n = uint64_t(a.B) * a.HW * (a.C / 4);
-    k_gn_apply<<<grid_for(n, 256), 256, 0, st>>>(a);
+    // Apply: about eight blocks per SM over the batch.
+    const int apx = int(std::max<long>(16, (long(a.B) * a.HW + 8 * 148 - 1) / (8 * 148)));
+    k_gn_apply<<<dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st>>>(a, nchunks, apx);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t upsample2x_bf16(const float* x, __nv_bfloat16* y, int B, int H, int W, int C, cudaStream_t st)
 {
-    if (C % 4)
+    if (C % 4 || B <= 0 || H <= 0 || W <= 0)
         return cudaErrorInvalidValue;
-    const uint64_t n = uint64_t(B) * 4 * H * W * (C / 4);
-    k_upsample2x<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y),
-                                                     B, H, W, C / 4);
+    k_upsample2x<<<dim3(H, B), 256, 0, st>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), H, W,
+                                             C / 4);
     count_launch();
     return cudaGetLastError();
 }
