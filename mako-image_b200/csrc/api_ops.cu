@@ -65,14 +65,13 @@ mkb_status run_gemm(Epi epi, const void* x, long ldx, const void* w, long ldw, G
     const char* err = nullptr;
     if (!gemm_prepare(op, epi, x, ldx, w, ldw, a, bn, &err))
         return fail(MKB_ERR_INVALID, err ? err : "proj: unsupported arguments");
-    // 256-wide tiles run on CTA pairs when there are enough 256-row tiles to occupy every pair of SMs: the pair
-    // halves each SM's W traffic, which bounds the 1-CTA tile at these sizes.
-    if (bn == 256 && long((a.M + 255) / 256) * (a.N / 256) >= num_sms() / 2 && !gemm_use_pairs(op, &err))
+    // CTA pairs when the makespan estimate prefers them at this width: the pair halves each SM's W traffic.
+    if (bn >= 128 && gemm_pick_tile(a.M, a.N, true, bn).pairs && !gemm_use_pairs(op, &err))
         return fail(MKB_ERR_INVALID, err ? err : "proj: pair set-up failed");
     return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "proj launch");
 }
 
-int pick_bn(int M, int N) { return gemm_pick_bn(M, N); }
+int pick_bn(int M, int N) { return gemm_pick_tile(M, N, true).bn; }
 
 }  // namespace
 
@@ -251,11 +250,13 @@ mkb_status mkb_conv2d(const void* x, int B, int H, int W, int C, const void* w, 
     a.out_f32 = out_f32;
     a.status = device_status_word();
     const int Ho = taps == 9 ? (H - 1) / stride + 1 : H, Wo = taps == 9 ? (W - 1) / stride + 1 : W;
-    const int bn = pick_bn(B * Ho * Wo, Cout);
+    const GemmTile t = gemm_pick_tile(long(B) * Ho * Wo, Cout, true);
     GemmOp op;
     const char* err = nullptr;
-    if (!conv_prepare(op, Epi::kAdd, x, B, H, W, C, w, Cout, taps, stride, a, bn, &err))
+    if (!conv_prepare(op, Epi::kAdd, x, B, H, W, C, w, Cout, taps, stride, a, t.bn, &err))
         return fail(MKB_ERR_INVALID, err ? err : "conv2d: unsupported arguments");
+    if (t.pairs && !gemm_use_pairs(op, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "conv2d: pair set-up failed");
     return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "conv2d launch");
 }
 

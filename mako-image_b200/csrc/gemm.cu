@@ -10,6 +10,7 @@
 #include "common.cuh"
 
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -331,6 +332,41 @@ __device__ __forceinline__ void conv_tile(const GemmArgs& a, int mb, int& b, int
     x0 = (rem % tx_n) * a.conv_tw;
 }
 
+// The convolution's k-blocks in order: (tap, 64-channel chunk), each the tile's input window shifted by the tap
+// (zero-filled outside the image: the padding). The TMA producer steps it with additions only; the tile origin is
+// computed once per tile.
+struct ConvWalk {
+    int b = 0, x = 0, y = 0, c0 = 0;  // TMA coordinates of the current k-block's window
+    int x_base = 0, y_base = 0, dx = 0;
+    __device__ __forceinline__ void start(const GemmArgs& a, int mtile)
+    {
+        int y0, x0;
+        conv_tile(a, mtile, b, y0, x0);
+        x_base = x0 * a.conv_stride - a.conv_pad;
+        y_base = y0 * a.conv_stride - a.conv_pad;
+        x = x_base;
+        y = y_base;
+        c0 = 0;
+        dx = 0;
+    }
+    __device__ __forceinline__ void next(const GemmArgs& a)
+    {
+        c0 += 64;
+        if (c0 < a.conv_c)
+            return;
+        c0 = 0;
+        if (a.conv_taps != 9)
+            return;
+        if (++dx < 3) {
+            ++x;
+        } else {
+            dx = 0;
+            x = x_base;
+            ++y;
+        }
+    }
+};
+
 __device__ __forceinline__ int gemm_num_m(const GemmArgs& a, bool conv)
 {
     return conv ? a.conv_b * (a.conv_wo / a.conv_tw) * ((a.conv_ho + a.conv_th - 1) / a.conv_th) : (a.M + kBM - 1) / kBM;
@@ -404,6 +440,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                 const int num_k = (args.K + kBK - 1) / kBK;
                 int mb, nb;
                 tile_coords(local, num_m, num_n, mb, nb);
+                ConvWalk cw;
+                if constexpr (CONV)
+                    cw.start(args, mb);
                 for (int kb = 0; kb < num_k; ++kb, ++it) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
@@ -414,14 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                     uint8_t* sa = smem + s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], C::kStageBytes);
                     if constexpr (CONV) {
-                        // k-block kb = (tap, 64-channel chunk): the input window of the tile shifted by the tap,
-                        // zero-filled outside the image (the convolution's padding).
-                        int b, y0, x0;
-                        conv_tile(args, mb, b, y0, x0);
-                        const int cpt = args.conv_c / kBK, tap = kb / cpt, c0 = (kb - tap * cpt) * kBK;
-                        const int dy = args.conv_taps == 9 ? tap / 3 : 0, dx = args.conv_taps == 9 ? tap % 3 : 0;
-                        tma_load_4d(sa, &P.ta[p], &full[s], c0, x0 * args.conv_stride + dx - args.conv_pad,
-                                    y0 * args.conv_stride + dy - args.conv_pad, b);
+                        tma_load_4d(sa, &P.ta[p], &full[s], cw.c0, cw.x, cw.y, cw.b);
+                        cw.next(args);
                     } else {
                         tma_load_2d(sa, &P.ta[p], &full[s], kb * kBK, mb * kBM);
                     }
@@ -513,8 +546,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
 // The same GEMM on CTA pairs (cta_group::2): a cluster of two CTAs owns each 256 x BN tile. Each CTA loads its 128
 // rows of X and half of the tile's W rows; the pair leader issues 256 x BN x 16 MMAs that read both CTAs' shared
 // memory and accumulate each CTA's 128 rows in its own tensor memory; both CTAs run the epilogue on their rows. Per
-// SM this halves the W traffic through shared memory and L2 of the 1-CTA tile.
-template <int BN, Epi EPI>
+// SM this halves the W traffic through shared memory and L2 of the 1-CTA tile. In convolution mode a pair tile is
+// two consecutive 128-pixel output tiles (CTA rank r takes tile 2 m + r); a CTA whose tile lies past the last one
+// (odd count) loads zeros through out-of-range TMA coordinates and stores nothing.
+template <int BN, Epi EPI, bool CONV>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2(const __grid_constant__ GemmParams P)
 {
     using C = Cfg2<BN>;
@@ -533,7 +568,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
-    auto num_m_of = [&](const GemmArgs& a) { return (a.M + kPM - 1) / kPM; };
+    auto num_m_of = [&](const GemmArgs& a) { return (gemm_num_m(a, CONV) + 1) / 2; };
     int num_tiles = P.tiles0;
     if (P.nprob > 1)
         num_tiles += num_m_of(P.a[1]) * ((P.a[1].N + BN - 1) / BN);
@@ -579,6 +614,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                 const int num_n = (args.N + BN - 1) / BN, num_k = (args.K + kBK - 1) / kBK;
                 int mb, nb;
                 tile_coords(local, num_m_of(args), num_n, mb, nb);
+                ConvWalk cw;
+                if constexpr (CONV)
+                    cw.start(args, 2 * mb + int(rank));
                 for (int kb = 0; kb < num_k; ++kb, ++it) {
                     const int s = it % C::kStages;
                     const uint32_t ph = (it / C::kStages) & 1;
@@ -589,7 +627,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                     uint8_t* sa = smem + s * C::kStageBytes;
                     if (leader)
                         mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);  // both CTAs' loads land on it
-                    tma_load_2d_pair(sa, &P.ta[p], &full[s], kb * kBK, mb * kPM + int(rank) * kBM);
+                    if constexpr (CONV) {
+                        tma_load_4d_pair(sa, &P.ta[p], &full[s], cw.c0, cw.x, cw.y, cw.b);
+                        cw.next(args);
+                    } else {
+                        tma_load_2d_pair(sa, &P.ta[p], &full[s], kb * kBK, mb * kPM + int(rank) * kBM);
+                    }
                     tma_load_2d_pair(sa + C::kABytes, &P.tb[p], &full[s], kb * kBK, nb * BN + int(rank) * (BN / 2));
                 }
             }
@@ -645,8 +688,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                 break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-            const int row = mb * kPM + int(rank) * kBM + q * 32 + lane;
-            epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+            if constexpr (CONV) {
+                int b, y0, x0;
+                conv_tile(args, 2 * mb + int(rank), b, y0, x0);
+                const int r = q * 32 + lane, y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
+                epilogue<BN, EPI>(args, t_row, (b * args.conv_ho + y) * args.conv_wo + x,
+                                  b < args.conv_b && y < args.conv_ho, nb * BN);
+            } else {
+                const int row = mb * kPM + int(rank) * kBM + q * 32 + lane;
+                epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+            }
             tc_fence_before();
             if (leader)
                 mbar_arrive(&acc_empty[acc]);
@@ -695,19 +746,19 @@ cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
     return cudaGetLastError();
 }
 
-template <int BN, Epi EPI>
+template <int BN, Epi EPI, bool CONV>
 cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
 {
     if constexpr (BN >= 128 && (BN / 2) % 16 == 0) {
         static bool attr_set = false;
         if (!attr_set) {
-            cudaError_t e = cudaFuncSetAttribute(k_gemm2<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaError_t e = cudaFuncSetAttribute(k_gemm2<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  Cfg2<BN>::kSmem);
             if (e != cudaSuccess)
                 return e;
             attr_set = true;
         }
-        k_gemm2<BN, EPI><<<op.grid, kThreads, Cfg2<BN>::kSmem, st>>>(op.p);
+        k_gemm2<BN, EPI, CONV><<<op.grid, kThreads, Cfg2<BN>::kSmem, st>>>(op.p);
         count_launch();
         return cudaGetLastError();
     }
@@ -717,13 +768,13 @@ cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
 template <int BN, Epi EPI>
 cudaError_t launch_t(const GemmOp& op, cudaStream_t st)
 {
-    if (op.pair)
-        return launch_pair<BN, EPI>(op, st);
     // Convolutions only use the epilogues a conv needs (plain, activation, add), which keeps the instantiations few.
     if constexpr (EPI == Epi::kBF16 || EPI == Epi::kAdd) {
         if (op.conv)
-            return launch_c<BN, EPI, true>(op, st);
+            return op.pair ? launch_pair<BN, EPI, true>(op, st) : launch_c<BN, EPI, true>(op, st);
     }
+    if (op.pair)
+        return launch_pair<BN, EPI, false>(op, st);
     return launch_c<BN, EPI, false>(op, st);
 }
 
@@ -744,26 +795,37 @@ cudaError_t launch_bn(const GemmOp& op, cudaStream_t st)
 
 }  // namespace
 
-int gemm_pick_bn(long M, int N, bool pairs)
+GemmTile gemm_pick_tile(long M, int N, bool allow_pairs, int only_bn)
 {
-    // Makespan in units of one 128-column tile: rounds of tiles over the SMs (pairs of SMs for 256-row pair tiles)
-    // times the tile width. 64-wide tiles pay 1.5x: their X + W stage traffic (24 KB per 128 MMA cycles) exceeds
-    // what shared memory delivers per cycle.
-    const long sms = num_sms(), rows = pairs ? 2 * kBM : kBM, slots = pairs ? sms / 2 : sms;
-    int best = 0;
+    // Makespan in units of one 128-column mainloop: rounds of tiles over the SMs (pair tiles over pairs of SMs, each
+    // SM doing 128 of the 256 rows), times the tile width, times a shared-memory factor. Per SM and MMA cycle a
+    // 1-CTA tile reads 8192 / BN + 64 bytes of X and W operands, a pair tile 8192 / BN + 32; above ~88 B/clk the
+    // tensor pipe waits for shared memory (calibrated on the FFN-up shape: 1-CTA 256 1.10x and 192 1.22x slower
+    // than the 256 pair).
+    const long sms = num_sms();
+    GemmTile best{0, false};
     double best_cost = 0;
-    for (int bn : {256, 192, 160, 128, 64}) {
-        if (N % bn && !(bn == 64 && N % 32 == 0))
-            continue;
-        const long tiles = ((M + rows - 1) / rows) * ((N + bn - 1) / bn);
-        const double cost = double((tiles + slots - 1) / slots) * bn * (bn == 64 ? 1.5 : 1.0);
-        if (!best || cost < best_cost - 1e-9) {
-            best = bn;
-            best_cost = cost;
+    for (int pairs = 0; pairs <= (allow_pairs ? 1 : 0); ++pairs)
+        for (int bn : {256, 192, 160, 128, 64}) {
+            if (only_bn && bn != only_bn)
+                continue;
+            if (N % bn && !(bn == 64 && N % 32 == 0))
+                continue;
+            if (pairs && bn < 128)
+                continue;
+            const long rows = pairs ? 2 * kBM : kBM, slots = pairs ? sms / 2 : sms;
+            const long tiles = ((M + rows - 1) / rows) * ((N + bn - 1) / bn);
+            const double bpc = 8192.0 / bn + (pairs ? 32.0 : 64.0);
+            const double cost = double((tiles + slots - 1) / slots) * bn * std::max(1.0, bpc / 88.0);
+            if (!best.bn || cost < best_cost - 1e-9) {
+                best = GemmTile{bn, pairs != 0};
+                best_cost = cost;
+            }
         }
-    }
     return best;
 }
+
+int gemm_pick_bn(long M, int N, bool pairs) { return gemm_pick_tile(M, N, pairs).bn; }
 
 int num_sms()
 {
@@ -978,6 +1040,9 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     op.epi = epi;
     op.bn = bn;
     op.conv = true;
+    op.pair = false;
+    op.w_ptr[0] = W;
+    op.ldw[0] = a.K;
     const int tiles = B * (Wo / tw) * ((Ho + a.conv_th - 1) / a.conv_th) * ((Cout + bn - 1) / bn);
     op.p.tiles0 = tiles;
     op.grid = tiles < num_sms() ? tiles : num_sms();
@@ -987,8 +1052,8 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
 
 bool gemm_use_pairs(GemmOp& op, const char** err)
 {
-    if (!op.ready || op.conv || op.bn < 128) {
-        *err = "gemm: CTA pairs need a prepared GEMM with tile width >= 128";
+    if (!op.ready || op.bn < 128 || (op.conv && op.p.nprob != 1)) {
+        *err = "gemm: CTA pairs need a prepared GEMM or convolution with tile width >= 128";
         return false;
     }
     int tiles = 0;
@@ -1000,7 +1065,10 @@ bool gemm_use_pairs(GemmOp& op, const char** err)
                                uint32_t(op.bn / 2), err))
             return false;
         op.p.tb[p] = m;
-        const int t = ((a.M + 2 * kBM - 1) / (2 * kBM)) * ((a.N + op.bn - 1) / op.bn);
+        // Pair tiles: 256 rows, or two consecutive 128-pixel output tiles of a convolution.
+        const int m128 = op.conv ? a.conv_b * (a.conv_wo / a.conv_tw) * ((a.conv_ho + a.conv_th - 1) / a.conv_th)
+                                 : (a.M + kBM - 1) / kBM;
+        const int t = ((m128 + 1) / 2) * ((a.N + op.bn - 1) / op.bn);
         if (p == 0)
             op.p.tiles0 = t;
         tiles += t;

@@ -107,8 +107,14 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
 // tile. Needs the tile width >= 128. Call after adding any second problem.
 bool gemm_use_pairs(GemmOp& op, const char** err);
 
-// The tile width (64, 128, 160, 192 or 256) with the shortest makespan for an M x N output on this GPU's SMs, for
-// the 1-CTA kernel or (pairs) the CTA-pair kernel. N must be a multiple of 32.
+// The tile (width 64, 128, 160, 192 or 256; 1-CTA or, when allowed, CTA pair) with the shortest estimated makespan
+// for an M x N output on this GPU's SMs; only_bn restricts the width. N must be a multiple of 32.
+struct GemmTile {
+    int bn;
+    bool pairs;
+};
+GemmTile gemm_pick_tile(long M, int N, bool allow_pairs, int only_bn = 0);
+// The width alone, for the 1-CTA kernel or (pairs) the CTA-pair kernel.
 int gemm_pick_bn(long M, int N, bool pairs = false);
 // Adds a second problem (same epilogue kind and tile width; X [M][K], W [N][K]) to a prepared GEMM.
 bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,

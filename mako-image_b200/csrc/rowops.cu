@@ -259,11 +259,12 @@ __global__ void k_cfg_euler(float* x, const float* vc, const float* vu, float g,
 // 256); quads q + 256, q + 512, ... too when C > 1024) and pixel lane r = t / Qb of Rb = 256 / Qb lanes, so a warp
 // reads contiguous float4s and no thread divides per element.
 
-// Pixels per statistics chunk: about four chunks per SM over the whole batch, at least 64 pixels.
+// Pixels per statistics chunk: about eight chunks per SM over the whole batch, at least 16 pixels (small images
+// with many channels still spread over most SMs).
 __host__ __device__ inline int gn_chunk_px(int B, int HW)
 {
-    const long want = (long(B) * HW + 4 * 148 - 1) / (4 * 148);
-    return int(want < 64 ? 64 : want);
+    const long want = (long(B) * HW + 8 * 148 - 1) / (8 * 148);
+    return int(want < 16 ? 16 : want);
 }
 
 // Chan et al.'s pairwise combination of (count, mean, M2).

@@ -331,9 +331,11 @@ struct Builder {
         a.out_f32 = out_f32;
         a.status = status;
         const int Ho = stride == 2 ? H / 2 : H, Wo = stride == 2 ? W / 2 : W;
-        const int bn = gemm_pick_bn(long(B) * Ho * Wo, Cout);
+        const GemmTile t = gemm_pick_tile(long(B) * Ho * Wo, Cout, true);
         GemmOp op;
-        if (!conv_prepare(op, Epi::kAdd, x, B, H, W, Cin, w, Cout, taps, stride, a, bn, &err))
+        if (!conv_prepare(op, Epi::kAdd, x, B, H, W, Cin, w, Cout, taps, stride, a, t.bn, &err))
+            return bad(err);
+        if (t.pairs && !gemm_use_pairs(op, &err))
             return bad(err);
         P.add([op](cudaStream_t s) { return gemm_launch(op, s); });
     }
@@ -342,12 +344,15 @@ struct Builder {
         if (!ok())
             return;
         a.status = status;
-        if (!bn)
-            bn = gemm_pick_bn(a.M, a.N);
+        GemmTile t{bn, false};
         if (epi == Epi::kSwiGLU)
-            bn = 256;
+            t = gemm_pick_tile(a.M, a.N, true, 256);
+        else if (!bn)
+            t = gemm_pick_tile(a.M, a.N, true);
         GemmOp op;
-        if (!gemm_prepare(op, epi, x, ldx, w, ldw, a, bn, &err))
+        if (!gemm_prepare(op, epi, x, ldx, w, ldw, a, t.bn, &err))
+            return bad(err);
+        if (t.pairs && !gemm_use_pairs(op, &err))
             return bad(err);
         P.add([op](cudaStream_t s) { return gemm_launch(op, s); });
     }

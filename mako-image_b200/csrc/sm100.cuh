@@ -318,6 +318,17 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, ui
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2,
+                                                 int c3)
+{
+    const uint32_t leader_bar = map_to_cta(smem_u32(bar), 0);
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(leader_bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols)
 {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)

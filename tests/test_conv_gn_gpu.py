@@ -28,9 +28,10 @@ def _np(t):
     (2, 16, 32, 64, 96, 9, 1),     # 3x3, tiles 8 x 16
     (1, 32, 32, 128, 64, 9, 2),    # stride 2 (downsample)
     (1, 12, 8, 64, 64, 9, 1),      # width 8 (tiles 16 x 8), ragged rows
-    (1, 16, 16, 128, 256, 1, 1),   # 1x1
-    (2, 64, 64, 320, 320, 9, 1),   # SDXL level-0 width
+    (1, 16, 16, 128, 256, 1, 1),   # 1x1 (one CTA-pair tile)
+    (2, 64, 64, 320, 320, 9, 1),   # SDXL level-0 width (CTA pairs, 160-wide tiles)
     (1, 17, 32, 64, 32, 9, 2),     # odd input height, stride 2
+    (1, 24, 16, 64, 256, 9, 1),    # CTA pairs over an odd count (3) of 128-pixel tiles
 ])
 def test_conv2d(cuda, B, H, W, C, Cout, taps, stride):
     import torch
