@@ -4,7 +4,9 @@ fallback implementation."""
 import ctypes
 import os
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "lib", "libmkb_image.so")
+# MKB_IMAGE_LIB overrides the in-tree build (an alternative build of the same library, e.g. for A/B timing).
+LIB_PATH = os.environ.get("MKB_IMAGE_LIB") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "lib", "libmkb_image.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing: build it with `make -C mako-image_b200` (or __graft_entry__.build())")
