@@ -196,6 +196,42 @@ mkb_status mkb_dit_weight_info(const mkb_dit* d, int i, const char** name, long*
 mkb_status mkb_dit_weight_read(mkb_dit* d, const char* name, float* host);
 mkb_status mkb_dit_weight_write(mkb_dit* d, const char* name, const float* host);
 
+/* ---- Weights from files (replaces QwenImage::load_transformer, src/image/qwen_image.cpp:79-111, and
+ * Engine::add_lora / QwenImage::lora_target, src/image/engine.hpp:195-197, qwen_image.cpp:295-331). */
+
+/* The handle's variant (MKB_VARIANT_*), or -1 for a null handle. */
+int mkb_dit_variant(const mkb_dit* d);
+/* Rows [row0, row0 + rows) of weight `name` from host fp32 [rows][cols] (a vector's elements for cols 0). */
+mkb_status mkb_dit_weight_write_rows(mkb_dit* d, const char* name, long row0, long rows, const float* host);
+/* W[row0 .. row0 + rows) += scale * B A on the device, W a matrix of the table, A [rank][cols] and B [rows][rank]
+ * host fp32 (rank <= 512). */
+mkb_status mkb_dit_weight_lora_rows(mkb_dit* d, const char* name, long row0, long rows, const float* A,
+                                    const float* B, int rank, float scale);
+/* Loads safetensors checkpoint files (F32 / F16 / BF16) by the checkpoint's tensor names: the reference's for
+ * MKB_VARIANT_REF21 (q/k/v and gate/up row-stacked, txt_in.text_norm stored zero-centred), the published Qwen-Image
+ * transformer's for MKB_VARIANT_QWEN1 (img_mod.1, attn.to_q / add_q_proj, img_mlp.net.0.proj, ... with biases).
+ * Tensors must match the model's shapes. strict != 0: an unknown tensor, or a weight the files leave unwritten, is
+ * an error. *loaded (optional) counts the tensors written. */
+mkb_status mkb_dit_load_safetensors(mkb_dit* d, const char* const* paths, int n_paths, int strict, int* loaded);
+/* Merges one LoRA pair into the module's rows, W += scale * B A: `module` by checkpoint name without ".weight"
+ * ("transformer_blocks.3.attn.to_q", "img_mlp.gate_up", ...), A [rank][in_features], B [out_features][rank]. */
+mkb_status mkb_dit_lora_merge(mkb_dit* d, const char* module, const float* A, const float* B, int rank,
+                              int in_features, int out_features, float scale);
+/* Merges every pair of a LoRA safetensors file: <module>.lora_A / lora_B (or lora_down / lora_up) .weight, with an
+ * optional scalar <module>.alpha scaling by alpha / rank; "transformer." / "diffusion_model." prefixes are dropped.
+ * *merged (optional) counts the modules. */
+mkb_status mkb_dit_load_lora(mkb_dit* d, const char* path, float scale, int* merged);
+
+/* The safetensors reader behind the loaders, for callers that inspect files. */
+typedef struct mkb_st_file mkb_st_file;
+mkb_status mkb_st_open(const char* path, mkb_st_file** out);
+void mkb_st_close(mkb_st_file* f);
+int mkb_st_count(const mkb_st_file* f);
+/* Tensor i: name, dtype as written ("F32", "BF16", ...), up to 8 dims. */
+mkb_status mkb_st_info(const mkb_st_file* f, int i, const char** name, const char** dtype, int64_t* dims, int* ndim);
+/* Tensor `name` as fp32 (F32 / F16 / BF16 files); count must equal its element count. */
+mkb_status mkb_st_read_f32(const mkb_st_file* f, const char* name, float* out, int64_t count);
+
 /* Engine::begin (engine.hpp:165): prompt embeddings [S][text_dim] (host fp32) for `slot` on an h x w token grid.
  * Slots share the grid (the last begin sets it). Resets the slot's step count (ref21: its text K/V cache). */
 mkb_status mkb_dit_begin(mkb_dit* d, const float* prompt, int S, int h, int w, int slot);

@@ -87,6 +87,18 @@ _SIGS = {
     "mkb_attention_kv_shards": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp, _l,
                                      _i, _i, _i, _vp]),
     "mkb_nccl_unique_id": (_i, [_vp, ctypes.c_size_t]),
+    "mkb_dit_variant": (_i, [_vp]),
+    "mkb_dit_weight_write_rows": (_i, [_vp, ctypes.c_char_p, _l, _l, _vp]),
+    "mkb_dit_weight_lora_rows": (_i, [_vp, ctypes.c_char_p, _l, _l, _vp, _vp, _i, _f]),
+    "mkb_dit_load_safetensors": (_i, [_vp, ctypes.POINTER(ctypes.c_char_p), _i, _i, ctypes.POINTER(_i)]),
+    "mkb_dit_lora_merge": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _i, _i, _i, _f]),
+    "mkb_dit_load_lora": (_i, [_vp, ctypes.c_char_p, _f, ctypes.POINTER(_i)]),
+    "mkb_st_open": (_i, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "mkb_st_close": (None, [_vp]),
+    "mkb_st_count": (_i, [_vp]),
+    "mkb_st_info": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p),
+                         ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_i)]),
+    "mkb_st_read_f32": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.c_int64]),
     "mkb_dit_set_sequence_parallel": (_i, [_vp, _vp, _i, _i]),
     "mkb_dit_sp_rows": (_i, [_i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i),
                              ctypes.POINTER(_i)]),

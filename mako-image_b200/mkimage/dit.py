@@ -141,6 +141,30 @@ class Dit:
     def step_flops(self, n, first_step=True):
         return lib.mkb_dit_step_flops(self.h, n, int(first_step))
 
+    def load_safetensors(self, paths, strict=True):
+        """Loads checkpoint files by their tensor names (mkb_dit_load_safetensors); returns the tensors written."""
+        if isinstance(paths, (str, bytes)):
+            paths = [paths]
+        arr = (ctypes.c_char_p * len(paths))(*[str(p).encode() for p in paths])
+        n = ctypes.c_int()
+        check(lib.mkb_dit_load_safetensors(self.h, arr, len(paths), int(strict), ctypes.byref(n)))
+        return n.value
+
+    def lora_merge(self, module, A, B, scale=1.0):
+        """W += scale * B A for module `module` (A [rank][in], B [out][rank])."""
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        if A.ndim != 2 or B.ndim != 2 or B.shape[1] != A.shape[0]:
+            raise ValueError(f"lora_merge: A {A.shape} and B {B.shape} are not [rank][in] and [out][rank]")
+        check(lib.mkb_dit_lora_merge(self.h, module.encode(), _fptr(A), _fptr(B), A.shape[0], A.shape[1], B.shape[0],
+                                     scale))
+
+    def load_lora(self, path, scale=1.0):
+        """Merges every pair of a LoRA safetensors file; returns the number of modules."""
+        n = ctypes.c_int()
+        check(lib.mkb_dit_load_lora(self.h, str(path).encode(), scale, ctypes.byref(n)))
+        return n.value
+
     def set_sequence_parallel(self, nccl_id: bytes, rank: int, world: int):
         """Joins this handle to a sequence-parallel group (collective over the `world` ranks; see
         mkb_dit_set_sequence_parallel). nccl_id comes from nccl_unique_id() on one rank."""
@@ -163,3 +187,22 @@ def sp_rows(S, N, world, rank):
     out = [ctypes.c_int() for _ in range(4)]
     check(lib.mkb_dit_sp_rows(S, N, world, rank, *[ctypes.byref(o) for o in out]))
     return tuple(o.value for o in out)
+
+
+def st_read(path):
+    """Every tensor of a safetensors file as {name: (dtype, float32 array)} through the library's reader."""
+    h = ctypes.c_void_p()
+    check(lib.mkb_st_open(str(path).encode(), ctypes.byref(h)))
+    try:
+        out = {}
+        name, dtype = ctypes.c_char_p(), ctypes.c_char_p()
+        dims, nd = (ctypes.c_int64 * 8)(), ctypes.c_int()
+        for i in range(lib.mkb_st_count(h)):
+            check(lib.mkb_st_info(h, i, ctypes.byref(name), ctypes.byref(dtype), dims, ctypes.byref(nd)))
+            shape = tuple(dims[k] for k in range(nd.value))
+            a = np.empty(shape, np.float32)
+            check(lib.mkb_st_read_f32(h, name.value, _fptr(a), a.size))
+            out[name.value.decode()] = (dtype.value.decode(), a)
+        return out
+    finally:
+        lib.mkb_st_close(h)

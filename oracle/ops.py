@@ -153,3 +153,16 @@ def silu_(x):
 def upsample2x_nhwc(x):
     """Nearest 2x (upsample2x, src/kernels/image.metal:77-84)."""
     return np.repeat(np.repeat(np.asarray(x, np.float32), 2, axis=1), 2, axis=2)
+
+
+def lora_merge(W, A, B, scale, alpha=None):
+    """A LoRA pair merged into a bf16 matrix: W + scale * (alpha / rank) * B A, rounded to bf16 (alpha None: 1).
+
+    The reference adds adapters by module (Engine::add_lora, src/image/engine.hpp:195-197), each module a row range
+    of a stacked matrix (QwenImage::lora_target, src/image/qwen_image.cpp:295-331); the merge itself runs in the
+    absent mako-common runtime, so this restates the standard LoRA update (Hu et al., 2021) on those rows."""
+    W = np.asarray(W, np.float32)
+    A = np.asarray(A, np.float64)
+    B = np.asarray(B, np.float64)
+    s = scale * (alpha / A.shape[0] if alpha is not None else 1.0)
+    return bf16_round((W.astype(np.float64) + s * (B @ A)).astype(np.float32))
