@@ -2,6 +2,7 @@
 numpy arrays, plus the batched, guided and device-buffer steps."""
 
 import ctypes
+import os
 from dataclasses import dataclass, asdict
 
 import numpy as np
@@ -143,7 +144,7 @@ class Dit:
 
     def load_safetensors(self, paths, strict=True):
         """Loads checkpoint files by their tensor names (mkb_dit_load_safetensors); returns the tensors written."""
-        if isinstance(paths, (str, bytes)):
+        if isinstance(paths, (str, bytes, os.PathLike)):
             paths = [paths]
         arr = (ctypes.c_char_p * len(paths))(*[str(p).encode() for p in paths])
         n = ctypes.c_int()

@@ -197,11 +197,13 @@ def test_load_errors(cuda, tmp_path):
     assert d.load_safetensors(p, strict=False) == len(ck)
 
 
-def _bf16_steps(got, want):
-    """Largest distance, in bf16 steps, between two arrays of bf16 values."""
-    g = got.astype(np.float32).view(np.int32) >> 16
-    w = want.astype(np.float32).view(np.int32) >> 16
-    return int(np.abs(g.astype(np.int64) - w.astype(np.int64)).max())
+def _merged_ok(got, W, A, B, s):
+    """The device merge within one bf16 step of the oracle (2^-7 relative, the device sums in fp32 and rounds once,
+    the oracle in float64 and rounds twice, so the two can straddle a rounding tie), measured against the operands'
+    size: where W and s B A nearly cancel, a fixed rounding difference is many steps of the small result."""
+    want = O.lora_merge(W, A, B, s)
+    delta = s * (B.astype(np.float64) @ A.astype(np.float64))
+    return bool(np.all(np.abs(got - want) <= 2.0 ** -7 * (np.abs(W) + np.abs(delta)) + 1e-30))
 
 
 def test_lora_file_ref21(cuda, tmp_path):
@@ -230,8 +232,8 @@ def test_lora_file_ref21(cuda, tmp_path):
     touched = {}
     for m, (w, r0, rows, _, _) in mods.items():
         A, B, alpha = pairs[m]
-        want = O.lora_merge(before[w][r0:r0 + rows], A, B, scale, alpha)
-        assert _bf16_steps(after[w][r0:r0 + rows], want) <= 1, m
+        s = scale * (alpha / r if alpha is not None else 1.0)
+        assert _merged_ok(after[w][r0:r0 + rows], before[w][r0:r0 + rows], A, B, s), m
         touched.setdefault(w, []).append((r0, rows))
     for w, a in before.items():
         mask = np.ones(a.shape[0], bool)
@@ -254,10 +256,10 @@ def test_lora_merge_qwen1_and_errors(cuda, tmp_path):
     d.lora_merge("transformer_blocks.0.img_mlp.net.2", A2, B2, 1.0)
     after = d.weights()
     w = "blk1.txt.qkv.w"
-    assert _bf16_steps(after[w][2 * D:], O.lora_merge(before[w][2 * D:], A, B, 1.5)) <= 1
+    assert _merged_ok(after[w][2 * D:], before[w][2 * D:], A, B, 1.5)
     assert np.array_equal(after[w][:2 * D], before[w][:2 * D])
     w = "blk0.img.ff2.w"
-    assert _bf16_steps(after[w], O.lora_merge(before[w], A2, B2, 1.0)) <= 1
+    assert _merged_ok(after[w], before[w], A2, B2, 1.0)
     assert np.array_equal(after["blk0.txt.ff2.w"], before["blk0.txt.ff2.w"])
     with pytest.raises(mkimage.MkbError, match="adapter"):  # D inputs where the module takes F
         d.lora_merge("transformer_blocks.0.img_mlp.net.2", A2[:, :D].copy(), B2, 1.0)
