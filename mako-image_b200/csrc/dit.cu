@@ -130,11 +130,6 @@ struct DitImpl {
         std::vector<GemmOp> ops;  // indexed by the builder
         AttnOp att;
         std::vector<GemmOp> per_sample;  // ref21 txt_in2 / img_in per sample
-        // Sequence parallel with two sample groups: per block the QKV of each group ([block][group]) and per group
-        // the attention, so one group's K/V all-gather overlaps the other group's QKV or attention.
-        int groups = 1;
-        std::vector<GemmOp> qkv_g;
-        std::vector<AttnOp> att_g;
     };
     std::map<std::tuple<int, int, int, int>, std::unique_ptr<Plan>> plans;
 
@@ -152,8 +147,6 @@ struct DitImpl {
     // their K and V shards (the QKV epilogue writes them straight into this rank's slot of kv_all).
     int sp_world = 1, sp_rank = 0;
     ncclComm_t sp_comm = nullptr;
-    cudaStream_t sp_stream = nullptr;  // the K/V all-gathers of the grouped schedule
-    cudaEvent_t sp_ev[4] = {};         // per group: QKV written (0, 1); K/V gathered (2, 3)
     int sp_lg_max = 0;
     __nv_bfloat16* kv_all = nullptr;  // [world][2 (K, V)][B][H][Lg][128] for the step's B and Lg
     float* vel_x = nullptr;           // [world][B][Lg][64]: velocity exchange
@@ -218,11 +211,6 @@ DitImpl::~DitImpl()
         if (const NcclApi* api = nccl_api(nullptr))
             api->CommDestroy(sp_comm);
     }
-    for (cudaEvent_t e : sp_ev)
-        if (e)
-            cudaEventDestroy(e);
-    if (sp_stream)
-        cudaStreamDestroy(sp_stream);
     if (stream)
         cudaStreamDestroy(stream);
 }
@@ -255,9 +243,6 @@ mkb_status DitImpl::set_sp(const void* id, int rank, int world)
             return fail(MKB_ERR_ALLOC, std::string("sequence parallel: allocating ") + what + ": " +
                                            cudaGetErrorString(e));
     }
-    MKB_TRY_CUDA(cudaStreamCreateWithFlags(&sp_stream, cudaStreamNonBlocking), "sequence parallel: stream");
-    for (cudaEvent_t& e : sp_ev)
-        MKB_TRY_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "sequence parallel: events");
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     ncclComm_t comm = nullptr;
@@ -527,49 +512,11 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         const int M_s[2] = {Mt, Mi}, rps[2] = {S, Nl}, off[2] = {0, St};
         // RoPE row of head-layout row p: the joint position, p + rank * Lh.
         const float* rope_s[2] = {rope, rope + size_t(sp ? sp_rank : 0) * Lh * kHeadDim};
-        // Sequence parallel: two sample groups when the batch splits evenly (one group's K/V gather overlaps the
-        // other's work). kv_all holds per group [world][K, V][Bg][H][Lh][128]; this rank's K and V of group g go
-        // straight into its slot.
-        const int groups = sp && B % 2 == 0 ? 2 : 1, Bg = B / groups;
-        plan->groups = groups;
-        const size_t kv_shard = size_t(Bg) * H * Lh * kHeadDim;  // one rank's K (or V) of one group
-        auto kv_group = [&](int g) { return kv_all + size_t(g) * sp_world * 2 * kv_shard; };
-        __nv_bfloat16* k_dst = sp ? kv_group(0) + size_t(sp_rank) * 2 * kv_shard : kh;
+        // K and V of this rank go straight into its slot of the all-gather buffer.
+        const size_t kv_shard = size_t(B) * H * Lh * kHeadDim;
+        __nv_bfloat16* k_dst = sp ? kv_all + size_t(sp_rank) * 2 * kv_shard : kh;
         __nv_bfloat16* v_dst = sp ? k_dst + kv_shard : vh;
         const char* nm[2] = {"txt", "img"};
-        // QKV of block i over samples [s0, s0 + nb), writing q at qh's rows of those samples and K / V at kd / vd.
-        auto build_qkv = [&](GemmOp& op, int i, int s0, int nb, __nv_bfloat16* kd, __nv_bfloat16* vd) -> bool {
-            bool first_prob = true;
-            for (int s : {1, 0}) {
-                const int rows = s == 0 ? St : Nl;
-                if (rows == 0)
-                    continue;
-                const std::string p = "blk" + std::to_string(i) + "." + nm[s] + ".";
-                GemmArgs a;
-                a.M = nb * rows;
-                a.N = 3 * D;
-                a.K = D;
-                a.bias = V(p + "qkv.b");
-                a.qh = qh + size_t(s0) * H * Lh * kHeadDim;
-                a.kh = kd;
-                a.vh = vd;
-                a.norm_q = V(p + "norm_q");
-                a.norm_k = V(p + "norm_k");
-                a.rope = rope_s[s];
-                a.D = D;
-                a.L = Lh;
-                a.seg_rows = rows;
-                a.seg_off = off[s];
-                a.eps = kEps;
-                a.status = status;
-                const __nv_bfloat16* X = xn_s[s] + size_t(s0) * rows * D;
-                if (first_prob ? !gemm_prepare(op, Epi::kQkv, X, D, M(p + "qkv.w"), D, a, 256, &err)
-                               : !gemm_add_problem(op, X, D, M(p + "qkv.w"), D, a, &err))
-                    return false;
-                first_prob = false;
-            }
-            return nb * Nl < 512 || gemm_use_pairs(op, &err);
-        };
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
         // its tail, all on 256 x 256 CTA-pair tiles (QKV: two heads per CTA): the pair halves each SM's W traffic
         // through L2 and shared memory, which is what bounds the 1-CTA tiles (measured fastest for all four at the
@@ -589,6 +536,24 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                     a.status = status;
                     return gemm_add_problem(g, X, ldx, Wt, ldw, a, &err);
                 };
+                GemmArgs a;
+                a.M = M_s[s];
+                a.N = 3 * D;
+                a.K = D;
+                a.bias = V(p + "qkv.b");
+                a.qh = qh;
+                a.kh = k_dst;
+                a.vh = v_dst;
+                a.norm_q = V(p + "norm_q");
+                a.norm_k = V(p + "norm_k");
+                a.rope = rope_s[s];
+                a.D = D;
+                a.L = Lh;
+                a.seg_rows = rps[s];
+                a.seg_off = off[s];
+                a.eps = kEps;
+                if (!put(o[0], Epi::kQkv, xn_s[s], D, M(p + "qkv.w"), D, a, 256))
+                    return fail(MKB_ERR_INVALID, err);
                 GemmArgs r;
                 r.M = M_s[s];
                 r.N = D;
@@ -620,20 +585,9 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                     return fail(MKB_ERR_INVALID, err);
             }
             if (Mi >= 512)
-                for (int k = 1; k < 4; ++k)
+                for (int k = 0; k < 4; ++k)
                     if (bn_for_pairs(o[k]) && !gemm_use_pairs(o[k], &err))
                         return fail(MKB_ERR_INVALID, err);
-            if (groups == 1) {
-                if (!build_qkv(o[0], i, 0, B, k_dst, v_dst))
-                    return fail(MKB_ERR_INVALID, err);
-            } else {
-                plan->qkv_g.resize(size_t(NB) * groups);
-                for (int g = 0; g < groups; ++g) {
-                    __nv_bfloat16* kd = kv_group(g) + size_t(sp_rank) * 2 * kv_shard;
-                    if (!build_qkv(plan->qkv_g[size_t(i) * groups + g], i, g * Bg, Bg, kd, kd + kv_shard))
-                        return fail(MKB_ERR_INVALID, err);
-                }
-            }
         }
         GemmArgs a;
         a.M = Mt;
@@ -676,24 +630,11 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         at.rows1 = Nl;
         if (sp) {
             at.kv_shard_rows = Lh;
-            at.kv_plane_stride = 2 * Bg * H;
+            at.kv_plane_stride = 2 * B * H;
         }
         at.status = status;
-        if (groups == 1) {
-            if (!attn_prepare(plan->att, qh, Lh, sp ? kv_all : kh, sp ? kv_all + kv_shard : vh, L, at, &err))
-                return fail(MKB_ERR_INVALID, err);
-        } else {
-            plan->att_g.resize(groups);
-            for (int g = 0; g < groups; ++g) {
-                AttnArgs ag = at;
-                ag.B = Bg;
-                ag.out0 = attn + size_t(g) * Bg * St * D;
-                ag.out1 = attn + size_t(Mt) * D + size_t(g) * Bg * Nl * D;
-                if (!attn_prepare(plan->att_g[g], qh + size_t(g) * Bg * H * Lh * kHeadDim, Lh, kv_group(g),
-                                  kv_group(g) + kv_shard, L, ag, &err))
-                    return fail(MKB_ERR_INVALID, err);
-            }
-        }
+        if (!attn_prepare(plan->att, qh, Lh, sp ? kv_all : kh, sp ? kv_all + kv_shard : vh, L, at, &err))
+            return fail(MKB_ERR_INVALID, err);
     } else {
         const int T = first ? L : N, split = first ? S : 0, Mr = B * T;
         const long mstride = 8L * D;  // two modulation rows of 4D per sample
@@ -976,39 +917,16 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
             };
             MKB_K(ln(0, 1, 0), "ln_modulate 1");
             MKB_K(ln(1, 1, 0), "ln_modulate 1");
-            if (plan->groups > 1) {
-                // Per group: QKV on the main stream, then its in-place K/V all-gather on the gather stream, which
-                // overlaps the next group's QKV and this group's successor's attention.
-                const int G = plan->groups, Bg = B / G;
-                const size_t count = size_t(2) * Bg * H * rw.shard * kHeadDim;  // one rank's slot of one group
-                for (int g = 0; g < G; ++g) {
-                    MKB_K(gemm_launch(plan->qkv_g[size_t(i) * G + g], s), "qkv");
-                    MKB_K(cudaEventRecord(sp_ev[g], s), "qkv event");
-                    MKB_K(cudaStreamWaitEvent(sp_stream, sp_ev[g], 0), "gather wait");
-                    __nv_bfloat16* base = kv_all + size_t(g) * sp_world * count;
-                    const ncclResult_t r = nccl_api(nullptr)->AllGather(base + size_t(sp_rank) * count, base, count,
-                                                                       ncclBfloat16, sp_comm, sp_stream);
-                    if (r != ncclSuccess)
-                        return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
-                                                      nccl_api(nullptr)->GetErrorString(r));
-                    MKB_K(cudaEventRecord(sp_ev[2 + g], sp_stream), "gather event");
-                }
-                for (int g = 0; g < G; ++g) {
-                    MKB_K(cudaStreamWaitEvent(s, sp_ev[2 + g], 0), "attention wait");
-                    MKB_K(attn_launch(plan->att_g[g], s), "attention");
-                }
-            } else {
-                MKB_K(gemm_launch(o[0], s), "qkv");
-                if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
-                    const size_t count = size_t(2) * B * H * rw.shard * kHeadDim;
-                    const ncclResult_t r = nccl_api(nullptr)->AllGather(kv_all + size_t(sp_rank) * count, kv_all,
-                                                                       count, ncclBfloat16, sp_comm, s);
-                    if (r != ncclSuccess)
-                        return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
-                                                      nccl_api(nullptr)->GetErrorString(r));
-                }
-                MKB_K(attn_launch(plan->att, s), "attention");
+            MKB_K(gemm_launch(o[0], s), "qkv");
+            if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
+                const size_t count = size_t(2) * B * H * rw.shard * kHeadDim;
+                const ncclResult_t r = nccl_api(nullptr)->AllGather(kv_all + size_t(sp_rank) * count, kv_all, count,
+                                                                   ncclBfloat16, sp_comm, s);
+                if (r != ncclSuccess)
+                    return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
+                                                  nccl_api(nullptr)->GetErrorString(r));
             }
+            MKB_K(attn_launch(plan->att, s), "attention");
             MKB_K(gemm_launch(o[1], s), "o proj");
             MKB_K(ln(0, 4, 3), "ln_modulate 2");
             MKB_K(ln(1, 4, 3), "ln_modulate 2");
