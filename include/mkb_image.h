@@ -259,6 +259,10 @@ mkb_status mkb_dit_step_cfg(mkb_dit* d, float* latents, float sigma, float sigma
  * 2i and 2i+1): latents_dev [n_images][N][64] updated in place on `stream`. */
 mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, float sigma, float sigma_next,
                                 float guidance, void* stream);
+/* The guided velocity of the same CFG batch, v = v_u + guidance (v_c - v_u), into v_out_dev [n_images][N][64]
+ * without updating the latents: the model output for the device samplers below (engine.cpp:474-480). */
+mkb_status mkb_dit_guided_velocity_dev(mkb_dit* d, int n_images, const float* latents_dev, float sigma,
+                                       float guidance, float* v_out_dev, void* stream);
 
 /* Stage probe, as the reference's probe() hooks (qwen_image.cpp:200-287): when set, step calls fn(name, layer,
  * data, count, user) with host fp32 copies of named stages ("temb", "txt_in", "img_in", "block" with the block index,
@@ -325,6 +329,25 @@ float mkb_er_sde_sigma(const mkb_er_sde* e, int i);
  * s_noise (ErSde::step, er_sde.cpp:27-74). */
 mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised, const float* noise, long n,
                            float s_noise);
+
+/* ---- Samplers on the device (the updates of Engine::generate's loop, src/image/engine.cpp:471-506, on device
+ * latents; stream-ordered, no host round trip). Noise is the counter-based generator's stream `noise_key`: element j
+ * of a step draws element noise_offset + j (splitmix64 + Box-Muller, the generator of the synthetic inputs), so a run
+ * is reproducible from (key, offsets). The reference draws from its host RNG; only the distribution matches. */
+
+/* out = v_uncond + guidance (v_cond - v_uncond), n floats (engine.cpp:476-480). */
+mkb_status mkb_cfg_combine_dev(float* out, const float* v_cond, const float* v_uncond, float guidance, long n,
+                               void* stream);
+/* Euler-ancestral (engine.cpp:492-499): up = min(s', sqrt(s'^2 (s^2 - s'^2) / s^2)), x += (sqrt(s'^2 - up^2) - s) v,
+ * then + up * noise. s = sigma > 0, s' = sigma_next in [0, s]. */
+mkb_status mkb_euler_ancestral_dev(float* x, const float* v, float sigma, float sigma_next, uint64_t noise_key,
+                                   uint64_t noise_offset, long n, void* stream);
+/* ER-SDE step i on device latents x, v the guided model output: the image estimate x - sigma_i v
+ * (engine.cpp:483-487) enters mkb_er_sde_step's update with the same coefficients. state_dev: 2n floats the caller
+ * keeps for one run (previous estimate, previous difference); the run's steps go 0, 1, 2, ... (step 0 starts a new
+ * run). Noise is drawn when sigma_{i+1} > 0 and s_noise > 0. */
+mkb_status mkb_er_sde_step_dev(mkb_er_sde* e, int i, float* x, const float* v, float* state_dev, uint64_t noise_key,
+                               uint64_t noise_offset, long n, float s_noise, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * The SDXL UNet (Sdxl::begin / step, src/image/sdxl.cpp:672-953) and the SDXL VAE decoder (Engine::decode,

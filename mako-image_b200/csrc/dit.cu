@@ -1355,23 +1355,25 @@ mkb_status mkb_dit_step(mkb_dit* d, const float* latents, float sigma, float* ou
     return mkb_dit_step_batch(d, 1, &slot, latents, &sigma, out);
 }
 
-mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, float sigma, float sigma_next,
-                                float guidance, void* stream)
+}  // extern "C"
+
+namespace {
+
+// The CFG batch of n_images images (slots 2i / 2i + 1 = cond / uncond) on device latents [n][N][64]; *vel, *T and
+// *split locate sample b's velocities at vel + (b * T + split) * 64 (all image rows on every sequence-parallel rank).
+mkb_status guided_run(DitImpl& m, int n_images, const float* latents_dev, float sigma, cudaStream_t s,
+                      const float** vel, int* T, int* split)
 {
-    MKB_TRY(check_handle(d));
-    DitImpl& m = d->impl;
     const int B = 2 * n_images;
     if (n_images < 1 || B > m.Bmax || int(m.slots.size()) < B || !latents_dev)
-        return fail(MKB_ERR_INVALID, "step_cfg: need 2 * n_images <= max_batch and as many slots");
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+        return fail(MKB_ERR_INVALID, "guided step: need 2 * n_images <= max_batch and as many slots");
     const int N = m.gh * m.gw;
-    const size_t img = size_t(N) * kLatent;
     std::vector<int> ids(B);
     std::vector<float> sg(B, sigma);
     for (int i = 0; i < B; ++i) {
         ids[i] = i;
         if (!m.slots[i].begun)
-            return fail(MKB_ERR_STATE, "step_cfg: slots 0 .. 2 * n_images - 1 need begin");
+            return fail(MKB_ERR_STATE, "guided step: slots 0 .. 2 * n_images - 1 need begin");
     }
     const int S = m.slots[0].S;
     // Both predictions of image i see the same latents.
@@ -1379,19 +1381,55 @@ mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, fl
     bool first = false;
     MKB_TRY(m.run(B, ids.data(), sg.data(), s, &first));
     const bool q1 = m.cfg.variant == MKB_VARIANT_QWEN1;
-    int T = q1 ? N : (first ? S + N : N), split = q1 ? 0 : (first ? S : 0);
-    const float* vel = m.vel;
+    *T = q1 ? N : (first ? S + N : N);
+    *split = q1 ? 0 : (first ? S : 0);
+    *vel = m.vel;
     if (m.sp_world > 1) {  // every rank applies the update to all rows, from the gathered velocities
         MKB_TRY(m.sp_gather_velocity(B, S, m.vel_full, cudaMemcpyDeviceToDevice, s));
-        vel = m.vel_full;
-        T = N;
-        split = 0;
+        *vel = m.vel_full;
+        *T = N;
+        *split = 0;
     }
+    return MKB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mkb_status mkb_dit_step_cfg_dev(mkb_dit* d, int n_images, float* latents_dev, float sigma, float sigma_next,
+                                float guidance, void* stream)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+    const float* vel = nullptr;
+    int T = 0, split = 0;
+    MKB_TRY(guided_run(m, n_images, latents_dev, sigma, s, &vel, &T, &split));
+    const size_t img = size_t(m.gh) * m.gw * kLatent;
     for (int i = 0; i < n_images; ++i) {
         const float* vc = vel + (size_t(2 * i) * T + split) * kLatent;
         const float* vu = vel + (size_t(2 * i + 1) * T + split) * kLatent;
         MKB_TRY_CUDA(cfg_euler(latents_dev + i * img, vc, vu, guidance, sigma_next - sigma, img, s), "cfg euler");
     }
+    return MKB_OK;
+}
+
+mkb_status mkb_dit_guided_velocity_dev(mkb_dit* d, int n_images, const float* latents_dev, float sigma,
+                                       float guidance, float* v_out_dev, void* stream)
+{
+    MKB_TRY(check_handle(d));
+    DitImpl& m = d->impl;
+    if (!v_out_dev)
+        return fail(MKB_ERR_INVALID, "guided_velocity: null output");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
+    const float* vel = nullptr;
+    int T = 0, split = 0;
+    MKB_TRY(guided_run(m, n_images, latents_dev, sigma, s, &vel, &T, &split));
+    const long img = long(m.gh) * m.gw * kLatent;
+    for (int i = 0; i < n_images; ++i)
+        MKB_TRY(mkb_cfg_combine_dev(v_out_dev + i * img, vel + (size_t(2 * i) * T + split) * kLatent,
+                                    vel + (size_t(2 * i + 1) * T + split) * kLatent, guidance, img, s));
     return MKB_OK;
 }
 

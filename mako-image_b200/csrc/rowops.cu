@@ -1,6 +1,7 @@
 // Row and element kernels (see rowops.cuh).
 #include "rowops.cuh"
 #include "common.cuh"
+#include "rng.cuh"
 
 #include <algorithm>
 #include <cstdint>
@@ -164,25 +165,11 @@ __global__ void k_sinusoid(const float* t, float* tp, int rows)
     tp[r * 256 + 128 + i] = sinf(arg);
 }
 
-__device__ __forceinline__ uint64_t splitmix64(uint64_t x)
-{
-    uint64_t z = x + 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-}
-
 __global__ void k_fill_normal(void* out, int bf16, uint64_t n, uint64_t key, uint64_t offset, float stdv, float mean)
 {
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint64_t e = offset + i;
-        const uint64_t h = splitmix64(key + (e >> 1));
-        const double u1 = (double(h >> 40) + 0.5) / 16777216.0;
-        const double u2 = double(h & 0xFFFFFFull) / 16777216.0;
-        const double rr = sqrt(-2.0 * log(u1));
-        const double ang = 6.283185307179586 * u2;
-        const double z = (e & 1) ? rr * sin(ang) : rr * cos(ang);
+        const double z = counter_normal(key, offset + i);
         const float v = float(z * double(stdv) + double(mean));
         if (bf16)
             static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);

@@ -2,6 +2,7 @@
 // src/image/er_sde.cpp), restated for the C ABI: the shifted flow-matching schedule, the guided Euler update and the
 // ER-SDE solver. Host code; the guided Euler update also runs fused on the device (mkb_dit_step_cfg).
 #include "../../include/mkb_image.h"
+#include "er_sde_coef.hpp"
 
 #include <algorithm>
 #include <cmath>
@@ -29,6 +30,7 @@ struct mkb_er_sde {
     std::vector<double> sigmas, lambdas;
     std::vector<float> old, old_d;
     bool have_old = false, have_old_d = false;
+    int dev_next = 0;  // the device step expected next (its state lives in the caller's device buffer)
 };
 
 extern "C" {
@@ -119,50 +121,31 @@ mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised
         return MKB_ERR_INVALID;
     if ((e->have_old && long(e->old.size()) != n))
         return MKB_ERR_INVALID;
-    const int stage = std::min(3, i + 1);
-    if (e->sigmas[i + 1] == 0) {
+    mkb::ErSdeCoef c;
+    mkb::er_sde_coef(e, i, s_noise, &c);
+    if (c.last) {
         // The last step lands on the model's image (er_sde.cpp:33-34).
         std::copy(denoised, denoised + n, x);
     } else {
         if (!noise && s_noise > 0)
             return MKB_ERR_INVALID;
-        if ((stage >= 2 && !e->have_old) || (stage >= 3 && !e->have_old_d))
+        if ((c.stage >= 2 && !e->have_old) || (c.stage >= 3 && !e->have_old_d))
             return MKB_ERR_STATE;
-        // Three-stage update from the image estimates' first and second differences (er_sde.cpp:36-69); the
-        // integrals of 1 / scaler over [lambda_t, lambda_s] are Riemann sums over 200 points.
-        const double ls = e->lambdas[i], lt = e->lambdas[i + 1];
-        const double alpha_s = e->sigmas[i] / ls, alpha_t = e->sigmas[i + 1] / lt;
-        const double r = er_scaler(lt) / er_scaler(ls);
-        const double c1 = alpha_t / alpha_s * r, c2 = alpha_t * (1 - r);
-        const int points = 200;
-        const double dt = lt - ls, h = -dt / points;
-        double s = 0, su = 0;
-        for (int k = 0; k < points; ++k) {
-            const double pos = lt + k * h, sp = er_scaler(pos);
-            s += 1 / sp;
-            su += (pos - ls) / sp;
-        }
-        s *= h;
-        su *= h;
-        const double c3 = alpha_t * (dt + s * er_scaler(lt)), c4 = alpha_t * (dt * dt / 2 + su * er_scaler(lt));
-        const double d_den = stage >= 2 ? ls - e->lambdas[i - 1] : 1;
-        const double u_den = stage >= 3 ? (ls - e->lambdas[i - 2]) / 2 : 1;
-        const double cn = alpha_t * double(s_noise) * std::sqrt(std::max(0.0, lt * lt - ls * ls * r * r));
-        std::vector<float> dd(stage >= 2 ? n : 0);
+        std::vector<float> dd(c.stage >= 2 ? n : 0);
         for (long j = 0; j < n; ++j) {
-            double v = c1 * x[j] + c2 * denoised[j];
-            if (stage >= 2) {
-                const double d = (double(denoised[j]) - e->old[j]) / d_den;
+            double v = c.c1 * x[j] + c.c2 * denoised[j];
+            if (c.stage >= 2) {
+                const double d = (double(denoised[j]) - e->old[j]) / c.d_den;
                 dd[j] = float(d);
-                v += c3 * d;
-                if (stage >= 3)
-                    v += c4 * (d - e->old_d[j]) / u_den;
+                v += c.c3 * d;
+                if (c.stage >= 3)
+                    v += c.c4 * (d - e->old_d[j]) / c.u_den;
             }
             if (s_noise > 0)
-                v += cn * noise[j];
+                v += c.cn * noise[j];
             x[j] = float(v);
         }
-        if (stage >= 2) {
+        if (c.stage >= 2) {
             e->old_d = std::move(dd);
             e->have_old_d = true;
         }
@@ -173,3 +156,55 @@ mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised
 }
 
 }  // extern "C"
+
+namespace mkb {
+
+bool er_sde_coef(const mkb_er_sde* e, int i, float s_noise, ErSdeCoef* c)
+{
+    if (!e || i < 0 || i + 1 >= int(e->sigmas.size()))
+        return false;
+    *c = ErSdeCoef{};
+    c->stage = std::min(3, i + 1);
+    if (e->sigmas[i + 1] == 0) {
+        c->last = true;
+        return true;
+    }
+    // Three-stage update from the image estimates' first and second differences (er_sde.cpp:36-69); the
+    // integrals of 1 / scaler over [lambda_t, lambda_s] are Riemann sums over 200 points.
+    const double ls = e->lambdas[i], lt = e->lambdas[i + 1];
+    const double alpha_s = e->sigmas[i] / ls, alpha_t = e->sigmas[i + 1] / lt;
+    const double r = er_scaler(lt) / er_scaler(ls);
+    c->c1 = alpha_t / alpha_s * r;
+    c->c2 = alpha_t * (1 - r);
+    const int points = 200;
+    const double dt = lt - ls, h = -dt / points;
+    double s = 0, su = 0;
+    for (int k = 0; k < points; ++k) {
+        const double pos = lt + k * h, sp = er_scaler(pos);
+        s += 1 / sp;
+        su += (pos - ls) / sp;
+    }
+    s *= h;
+    su *= h;
+    c->c3 = alpha_t * (dt + s * er_scaler(lt));
+    c->c4 = alpha_t * (dt * dt / 2 + su * er_scaler(lt));
+    c->d_den = c->stage >= 2 ? ls - e->lambdas[i - 1] : 1;
+    c->u_den = c->stage >= 3 ? (ls - e->lambdas[i - 2]) / 2 : 1;
+    c->cn = alpha_t * double(s_noise) * std::sqrt(std::max(0.0, lt * lt - ls * ls * r * r));
+    return true;
+}
+
+double er_sde_sigma_d(const mkb_er_sde* e, int i)
+{
+    return e && i >= 0 && i < int(e->sigmas.size()) ? e->sigmas[i] : 0.0;
+}
+
+bool er_sde_dev_order(mkb_er_sde* e, int i)
+{
+    if (!e || (i != 0 && i != e->dev_next))
+        return false;
+    e->dev_next = i + 1;
+    return true;
+}
+
+}  // namespace mkb

@@ -126,6 +126,11 @@ class Dit:
         check(lib.mkb_dit_step_cfg_dev(self.h, n_images, ctypes.c_void_p(latents_dev), sigma, sigma_next, guidance,
                                        stream))
 
+    def guided_velocity_dev(self, n_images, latents_dev, sigma, guidance, v_out_dev, stream=None):
+        """The guided velocity of the CFG batch into v_out_dev (device pointers), latents unchanged."""
+        check(lib.mkb_dit_guided_velocity_dev(self.h, n_images, ctypes.c_void_p(latents_dev), sigma, guidance,
+                                              ctypes.c_void_p(v_out_dev), stream))
+
     def set_probe(self, fn):
         """fn(name, layer, array) is called with host copies of named stages; None turns probing off."""
         if fn is None:

@@ -4,7 +4,7 @@ import ctypes
 
 import numpy as np
 
-from ._lib import lib, check
+from ._lib import lib, check, stream_ptr
 
 
 class Schedule(ctypes.Structure):
@@ -54,8 +54,26 @@ class ErSde:
     def sigma(self, i):
         return lib.mkb_er_sde_sigma(self.h, i)
 
+    def step_dev(self, i, x, v, state, noise_key, noise_offset=0, s_noise=1.0):
+        """The device step on torch CUDA float32 tensors (mkb_er_sde_step_dev): x updated in place from the guided
+        model output v; state: 2 * x.numel() floats kept across the run's steps."""
+        check(lib.mkb_er_sde_step_dev(self.h, i, x.data_ptr(), v.data_ptr(), state.data_ptr(), noise_key,
+                                      noise_offset, x.numel(), s_noise, stream_ptr()))
+
     def step(self, i, x, denoised, noise, s_noise=1.0):
         """x updated in place (float32 numpy)."""
         d = np.ascontiguousarray(denoised, np.float32)
         nz = np.ascontiguousarray(noise, np.float32) if noise is not None else None
         check(lib.mkb_er_sde_step(self.h, i, _f(x), _f(d), _f(nz) if nz is not None else None, x.size, s_noise))
+
+
+def cfg_combine_dev(out, v_cond, v_uncond, guidance):
+    """out = v_uncond + guidance (v_cond - v_uncond) on torch CUDA float32 tensors."""
+    check(lib.mkb_cfg_combine_dev(out.data_ptr(), v_cond.data_ptr(), v_uncond.data_ptr(), guidance, out.numel(),
+                                  stream_ptr()))
+
+
+def euler_ancestral_dev(x, v, sigma, sigma_next, noise_key, noise_offset=0):
+    """The Euler-ancestral update of device latents x (torch CUDA float32) from the guided velocity v."""
+    check(lib.mkb_euler_ancestral_dev(x.data_ptr(), v.data_ptr(), sigma, sigma_next, noise_key, noise_offset, x.numel(),
+                                      stream_ptr()))

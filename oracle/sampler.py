@@ -46,6 +46,18 @@ def guided_euler(x, v_cond, v_uncond, guidance, sigma, sigma_next):
     return (x + np.float32(sigma_next - sigma) * v).astype(np.float32)
 
 
+def euler_ancestral(x, v, sigma, sigma_next, noise):
+    """Euler-ancestral update of Engine::generate (src/image/engine.cpp:492-499), in place on float32 x: down to the
+    level whose noise, with fresh noise of the remainder added, makes the next level's."""
+    frm, to = float(sigma), float(sigma_next)
+    up = min(to, np.sqrt(to * to * (frm * frm - to * to) / (frm * frm)))
+    dt = np.float32(np.sqrt(to * to - up * up) - frm)
+    x += dt * np.asarray(v, np.float32)
+    if up > 0:
+        x += np.float32(up) * np.asarray(noise, np.float32)
+    return x
+
+
 def _scaler(x):
     return x * (math.exp(x ** 0.3) + 10.0)
 
