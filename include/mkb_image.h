@@ -338,6 +338,8 @@ mkb_status mkb_er_sde_step(mkb_er_sde* e, int i, float* x, const float* denoised
 /* out = v_uncond + guidance (v_cond - v_uncond), n floats (engine.cpp:476-480). */
 mkb_status mkb_cfg_combine_dev(float* out, const float* v_cond, const float* v_uncond, float guidance, long n,
                                void* stream);
+/* x += a v, n floats: the plain Euler update with a = sigma_next - sigma (engine.cpp:500-503). */
+mkb_status mkb_axpy_dev(float* x, const float* v, float a, long n, void* stream);
 /* Euler-ancestral (engine.cpp:492-499): up = min(s', sqrt(s'^2 (s^2 - s'^2) / s^2)), x += (sqrt(s'^2 - up^2) - s) v,
  * then + up * noise. s = sigma > 0, s' = sigma_next in [0, s]. */
 mkb_status mkb_euler_ancestral_dev(float* x, const float* v, float sigma, float sigma_next, uint64_t noise_key,

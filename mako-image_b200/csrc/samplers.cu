@@ -17,6 +17,12 @@ namespace {
 
 int grid_of(long n) { return int(std::min<long>((n + 255) / 256, 148L * 16)); }
 
+__global__ void k_axpy(float* x, const float* v, float a, long n)
+{
+    for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x)
+        x[j] += a * v[j];
+}
+
 __global__ void k_cfg_combine(float* out, const float* vc, const float* vu, float g, long n)
 {
     for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x)
@@ -81,6 +87,15 @@ mkb_status mkb_cfg_combine_dev(float* out, const float* v_cond, const float* v_u
     k_cfg_combine<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(out, v_cond, v_uncond, guidance, n);
     count_launch();
     return cuda_status(cudaGetLastError(), "cfg_combine launch");
+}
+
+mkb_status mkb_axpy_dev(float* x, const float* v, float a, long n, void* stream)
+{
+    if (!x || !v || n <= 0)
+        return fail(MKB_ERR_INVALID, "axpy: bad arguments");
+    k_axpy<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, v, a, n);
+    count_launch();
+    return cuda_status(cudaGetLastError(), "axpy launch");
 }
 
 mkb_status mkb_euler_ancestral_dev(float* x, const float* v, float sigma, float sigma_next, uint64_t noise_key,

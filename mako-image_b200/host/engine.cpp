@@ -1,6 +1,8 @@
 // The C++ Engine mirror over the C ABI (see engine.hpp).
 #include "engine.hpp"
 
+#include <cuda_runtime.h>
+
 #include <algorithm>
 #include <cmath>
 #include <random>
@@ -162,6 +164,101 @@ std::vector<float> QwenImage::step(std::span<const float> latents, float sigma, 
     std::vector<float> out(latents.size());
     check(mkb_dit_step(d_, latents.data(), sigma, out.data(), int(slot)), "step");
     return out;
+}
+
+std::vector<float> QwenImage::denoise_device(const Request& r)
+{
+    const uint32_t N = r.h * r.w;
+    const long n = long(N) * latent_width();
+    const Sampler sampler = r.sampler.value_or(default_sampler());
+    if (sampler == Sampler::euler_ancestral && !predicts_noise())
+        throw std::runtime_error(std::string(name()) + ": Euler a needs a model that predicts the noise");
+    std::vector<float> x(static_cast<size_t>(n));
+    std::mt19937_64 rng(r.seed);
+    std::normal_distribution<float> nd;
+    if (!r.noise.empty()) {
+        if (r.noise.size() != x.size())
+            throw std::runtime_error("noise must be [h * w][64]");
+        std::copy(r.noise.begin(), r.noise.end(), x.begin());
+    } else {
+        for (float& v : x)
+            v = nd(rng);
+    }
+    const auto sig = sigmas(r.steps ? r.steps : default_steps(), N, r.terminal);
+    const uint32_t steps = uint32_t(sig.size() - 1);
+    begin(r.prompt, r.h, r.w, 0);
+    const float scale = r.guidance.value_or(default_guidance());
+    const bool guided = scale != 1.0f && !r.negative.empty();
+    if (guided)
+        begin(r.negative, r.h, r.w, 1);
+    const bool batched = guided && prompt_rows_[0] == prompt_rows_[1] && cfg_.max_batch >= 2 && cfg_.slots >= 2;
+
+    // One stream for the model's and the sampler's launches; device buffers released on every exit path.
+    struct Dev {
+        cudaStream_t st = nullptr;
+        float *x = nullptr, *v = nullptr, *u = nullptr, *state = nullptr;
+        mkb_er_sde* er = nullptr;
+        ~Dev()
+        {
+            if (st)
+                cudaStreamSynchronize(st);
+            for (float* p : {x, v, u, state})
+                if (p)
+                    cudaFree(p);
+            if (st)
+                cudaStreamDestroy(st);
+            mkb_er_sde_destroy(er);
+        }
+    } dev;
+    auto cu = [](cudaError_t e, const char* what) {
+        if (e != cudaSuccess)
+            throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    cu(cudaStreamCreateWithFlags(&dev.st, cudaStreamNonBlocking), "stream");
+    cu(cudaMalloc(&dev.x, size_t(n) * 4), "latents");
+    cu(cudaMalloc(&dev.v, size_t(n) * 4), "velocity");
+    if (guided && !batched)
+        cu(cudaMalloc(&dev.u, size_t(n) * 4), "velocity");
+    if (sampler == Sampler::er_sde) {
+        check(mkb_er_sde_create(sig.data(), int(sig.size()), predicts_noise() ? 0 : 1, top_sigma(N), &dev.er),
+              "ER-SDE");
+        cu(cudaMalloc(&dev.state, size_t(2 * n) * 4), "ER-SDE state");
+    }
+    cu(cudaMemcpyAsync(dev.x, x.data(), size_t(n) * 4, cudaMemcpyHostToDevice, dev.st), "latents upload");
+    // The noise stream's key from the seed (a splitmix64 step of it).
+    uint64_t key = r.seed + 0x9E3779B97F4A7C15ull;
+    key = (key ^ (key >> 30)) * 0xBF58476D1CE4E5B9ull;
+    key = (key ^ (key >> 27)) * 0x94D049BB133111EBull;
+    key ^= key >> 31;
+    const int slot0 = 0, slot1 = 1;
+    for (uint32_t i = 0; i < steps; ++i) {
+        const float s = dev.er ? mkb_er_sde_sigma(dev.er, int(i)) : sig[i];
+        if (batched) {
+            check(mkb_dit_guided_velocity_dev(d_, 1, dev.x, s, scale, dev.v, dev.st), "guided velocity");
+        } else {
+            check(mkb_dit_step_batch_dev(d_, 1, &slot0, dev.x, &s, dev.v, dev.st), "step");
+            if (guided) {
+                check(mkb_dit_step_batch_dev(d_, 1, &slot1, dev.x, &s, dev.u, dev.st), "step");
+                check(mkb_cfg_combine_dev(dev.v, dev.v, dev.u, scale, n, dev.st), "guidance");
+            }
+        }
+        const uint64_t off = uint64_t(i) * uint64_t(n);
+        if (dev.er)
+            check(mkb_er_sde_step_dev(dev.er, int(i), dev.x, dev.v, dev.state, key, off, n, 1.0f, dev.st), "ER-SDE");
+        else if (sampler == Sampler::euler_ancestral)
+            check(mkb_euler_ancestral_dev(dev.x, dev.v, sig[i], sig[i + 1], key, off, n, dev.st), "Euler a");
+        else
+            check(mkb_axpy_dev(dev.x, dev.v, sig[i + 1] - sig[i], n, dev.st), "Euler");
+        if (r.progress)
+            r.progress(i + 1, steps);
+    }
+    cu(cudaMemcpyAsync(x.data(), dev.x, size_t(n) * 4, cudaMemcpyDeviceToHost, dev.st), "latents download");
+    cu(cudaStreamSynchronize(dev.st), "denoise");
+    uint32_t bits = 0;
+    check(mkb_check_kernels(&bits), "kernel status");
+    if (bits)
+        throw std::runtime_error("denoise_device: kernel status bits " + std::to_string(bits));
+    return x;
 }
 
 bool QwenImage::guided_step(std::vector<float>& x, float sigma, float sigma_next, float scale)

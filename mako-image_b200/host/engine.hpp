@@ -88,6 +88,12 @@ public:
     void begin(std::span<const float> prompt, uint32_t h, uint32_t w, uint32_t slot = 0) override;
     std::vector<float> step(std::span<const float> latents, float sigma, uint32_t slot = 0) override;
 
+    // Engine::denoise with the latents kept on the device: the guided velocity of both slots in one pass
+    // (mkb_dit_guided_velocity_dev) and the sampler update on the device (mkb_axpy_dev / mkb_euler_ancestral_dev /
+    // mkb_er_sde_step_dev) on one stream, so only the final latents come back. Same initial latents as denoise();
+    // the ancestral and ER-SDE noise is the device's counter-based stream keyed by the seed.
+    std::vector<float> denoise_device(const Request& r);
+
     // Synthetic weights by seed (mkb_dit_init_random), or named weights from host memory (mkb_dit_weight_write).
     void init_random(uint64_t seed, float std = 0.02f);
     void load_weight(const std::string& name, std::span<const float> values);

@@ -1,6 +1,7 @@
 // The C++ Engine mirror on the B200 kernels: a small Qwen-Image-shape model (random weights), three guided Euler
 // steps through Engine::denoise (cond + uncond batched on the device, update fused) against the same steps as two
-// step() calls combined on the host, for both block variants. Exit 0 on success.
+// step() calls combined on the host, for both block variants; then the device loop (QwenImage::denoise_device)
+// against the host loop, and its ER-SDE run for reproducibility. Exit 0 on success.
 #include "../../mako-image_b200/host/engine.hpp"
 
 #include <cmath>
@@ -62,6 +63,37 @@ int main()
         std::printf("  %-4s variant %d: batched guided steps vs two step() calls, max-abs %.3e\n", ok ? "ok" : "FAIL",
                     variant, err);
         failures += !ok;
+
+        // The device loop (latents stay on the GPU): guided Euler equals the host loop's result.
+        mkb::image::QwenImage e(c);
+        e.init_random(11);
+        const auto dev = e.denoise_device(r);
+        double derr = 0;
+        for (size_t j = 0; j < dev.size(); ++j)
+            derr = std::max(derr, double(std::fabs(dev[j] - got[j])));
+        const bool dok = derr <= 1e-4 * std::max(1.0, mx);
+        std::printf("  %-4s variant %d: device loop (guided Euler) vs host loop, max-abs %.3e\n", dok ? "ok" : "FAIL",
+                    variant, derr);
+        failures += !dok;
+
+        // Device ER-SDE: finite, reproducible from the seed, and not the Euler result.
+        mkb::image::Engine::Request r2 = r;
+        r2.sampler = mkb::image::Sampler::er_sde;
+        r2.seed = 5;
+        mkb::image::QwenImage f(c), g(c);
+        f.init_random(11);
+        g.init_random(11);
+        const auto e1 = f.denoise_device(r2), e2 = g.denoise_device(r2);
+        bool same = e1 == e2, fin = true;
+        double diff = 0;
+        for (size_t j = 0; j < e1.size(); ++j) {
+            fin &= std::isfinite(e1[j]);
+            diff = std::max(diff, double(std::fabs(e1[j] - dev[j])));
+        }
+        const bool eok = same && fin && diff > 0;
+        std::printf("  %-4s variant %d: device ER-SDE reproducible (%d), finite (%d), differs from Euler by %.3e\n",
+                    eok ? "ok" : "FAIL", variant, int(same), int(fin), diff);
+        failures += !eok;
     }
     std::printf("%s\n", failures ? "FAILED" : "passed");
     return failures ? 1 : 0;
