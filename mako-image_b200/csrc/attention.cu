@@ -47,6 +47,11 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // exponentials moves to the FMA pipe.
 template <int HD>
 constexpr int kEmuFrom = HD == 128 ? 128 : 112;
+// P published in two 64-key halves so P V of the first half starts while the second half's exponentials run: a
+// gain at head dim 64 (where P V of a tile is half as long), a loss at 128 (measured 440 -> 464 and 1057 -> 1012
+// TFLOP/s), so only there. Unsplit, the whole P is published on the second half's barrier.
+template <int HD>
+constexpr bool kSplitP = HD == 64;
 
 __device__ __forceinline__ float ex2(float x)
 {
@@ -123,10 +128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* v_full = bars + 5;    // [2]
     uint64_t* v_empty = bars + 7;   // [2]
     uint64_t* s_full = bars + 9;    // [2 tiles]
-    uint64_t* p_full = bars + 11;   // [2 tiles]
-    uint64_t* o_done = bars + 13;   // [2 tiles]
-    uint64_t* drain = bars + 15;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* p_full = bars + 11;   // [2 tiles][2 halves of the keys]
+    uint64_t* o_done = bars + 15;   // [2 tiles]
+    uint64_t* drain = bars + 17;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -150,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[2 * i], 128);
+            mbar_init(&p_full[2 * i + 1], 128);
             mbar_init(&o_done[i], 1);
         }
         mbar_init(drain, 1);
@@ -253,16 +259,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (next && !mbar_wait(&k_full[st1], ((j + 1) >> 1) & 1, a.status, kErrAttnWait, abort_flag))
                     break;
                 for (int t = 0; t < 2 && ok; ++t) {
-                    if (!mbar_wait(&p_full[t], j & 1, a.status, kErrAttnWait, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                    for (int half = kSplitP<HD> ? 0 : 1; half < 2 && ok; ++half) {
+                        if (!mbar_wait(&p_full[2 * t + half], j & 1, a.status, kErrAttnWait, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms).
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)  // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms)
-                        mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
-                                    desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
-                                    (j > 0) || (k > 0));
+                        for (int k = kSplitP<HD> ? 4 * half : 0; k < 4 * half + 4; ++k)
+                            mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
+                                        desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
+                                        (j > 0) || (k > 0));
+                    }
+                    if (!ok)
+                        break;
                     mma_commit(&o_done[t]);
                     if (next)
                         issue_s(t, st1);
@@ -357,12 +368,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     p[i] = pack_bf16x2(e.x, e.y);
                 }
                 tmem_st16(t_lane + col_s + c * 16, p);
+                if (c == 3 || (kSplitP<HD> && c == 1)) {  // keys up to 64 (c + 1) / 2 published
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&p_full[2 * t + c / 2]);
+                }
             }
             const float2 l01 = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
             l += l01.x + l01.y;
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[t]);
         }
         if (ok && nkv > 0 && mbar_wait(&o_done[t], (nkv - 1) & 1, a.status, kErrAttnWait, abort_flag)) {
             tc_fence_after();
