@@ -416,6 +416,14 @@ int mkb_vae_weight_count(const mkb_vae* v);
 mkb_status mkb_vae_weight_info(const mkb_vae* v, int i, const char** name, long* dims, int* ndim);
 mkb_status mkb_vae_weight_read(mkb_vae* v, const char* name, float* host);
 mkb_status mkb_vae_weight_write(mkb_vae* v, const char* name, const float* host);
+/* The UNet's and the VAE decoder's weights from safetensors checkpoints (F32 / F16 / BF16): the UNet under the
+ * original checkpoint names, optionally prefixed "model.diffusion_model." (Sdxl::load_unet, src/image/sdxl.cpp:
+ * 238-362); the VAE under the Diffusers names or the original AutoencoderKL ones, optionally prefixed
+ * "first_stage_model." or "vae." (engine.cpp:92-118, 590-640). Convolutions are converted from [out][in][ky][kx],
+ * q/k/v and cross k/v rows stacked. Other tensors in the files (a single-file checkpoint's text encoders) are ignored.
+ * strict != 0: a weight the files lack is an error. *loaded (optional) counts the weights written. */
+mkb_status mkb_unet_load_safetensors(mkb_unet* u, const char* const* paths, int n_paths, int strict, int* loaded);
+mkb_status mkb_vae_load_safetensors(mkb_vae* v, const char* const* paths, int n_paths, int strict, int* loaded);
 /* Engine::decode: tokens [gh * gw][16] to RGBA [16 gh][16 gw][4] in [-1, 1] (alpha 1), host / device buffers. */
 mkb_status mkb_vae_decode(mkb_vae* v, const float* latents, int gh, int gw, float* rgba);
 mkb_status mkb_vae_decode_dev(mkb_vae* v, const float* latents_dev, int gh, int gw, float* rgba_dev, void* stream);

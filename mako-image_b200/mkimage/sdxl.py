@@ -74,6 +74,18 @@ class _Weights:
     def init_random(self, seed, std=0.02):
         check(self._fn("init_random")(self.h, seed, std))
 
+    def load_safetensors(self, paths, strict=True):
+        """Weights from checkpoint files by their own tensor names (mkb_unet / mkb_vae_load_safetensors); returns
+        the number of weights written."""
+        import os
+
+        if isinstance(paths, (str, bytes, os.PathLike)):
+            paths = [paths]
+        arr = (ctypes.c_char_p * len(paths))(*[str(p).encode() for p in paths])
+        n = ctypes.c_int()
+        check(self._fn("load_safetensors")(self.h, arr, len(paths), int(strict), ctypes.byref(n)))
+        return n.value
+
     def set_probe(self, fn):
         if fn is None:
             self._probe = None
