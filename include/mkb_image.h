@@ -424,6 +424,16 @@ mkb_status mkb_vae_weight_write(mkb_vae* v, const char* name, const float* host)
  * strict != 0: a weight the files lack is an error. *loaded (optional) counts the weights written. */
 mkb_status mkb_unet_load_safetensors(mkb_unet* u, const char* const* paths, int n_paths, int strict, int* loaded);
 mkb_status mkb_vae_load_safetensors(mkb_vae* v, const char* const* paths, int n_paths, int strict, int* loaded);
+/* LoRA on the UNet (Sdxl::lora_target, src/image/sdxl.cpp:385-417): the transformers' proj_in / proj_out, attn1
+ * to_q / to_k / to_v / to_out.0, attn2 (the same), ff.net.0.proj and ff.net.2, by checkpoint module name
+ * ("input_blocks.4.1.transformer_blocks.0.attn1.to_q"; '_' and '.' compare equal, as the reference's lora_key does).
+ * mkb_unet_weight_lora_rows merges into rows of a named matrix of the table; the file form reads pairs as
+ * mkb_dit_load_lora does ("lora_unet_" prefixes dropped). */
+mkb_status mkb_unet_weight_lora_rows(mkb_unet* u, const char* name, long row0, long rows, const float* A,
+                                     const float* B, int rank, float scale);
+mkb_status mkb_unet_lora_merge(mkb_unet* u, const char* module, const float* A, const float* B, int rank,
+                               int in_features, int out_features, float scale);
+mkb_status mkb_unet_load_lora(mkb_unet* u, const char* path, float scale, int* merged);
 /* Engine::decode: tokens [gh * gw][16] to RGBA [16 gh][16 gw][4] in [-1, 1] (alpha 1), host / device buffers. */
 mkb_status mkb_vae_decode(mkb_vae* v, const float* latents, int gh, int gw, float* rgba);
 mkb_status mkb_vae_decode_dev(mkb_vae* v, const float* latents_dev, int gh, int gw, float* rgba_dev, void* stream);

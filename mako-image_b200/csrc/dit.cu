@@ -8,6 +8,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "lora.cuh"
 #include "nccl_dl.cuh"
 #include "rowops.cuh"
 
@@ -1050,40 +1051,6 @@ __host__ __device__ inline long swiglu_row(long r, long F)
     return (j / kSwigluBlock) * 2 * kSwigluBlock + (up ? kSwigluBlock : 0) + j % kSwigluBlock;
 }
 
-// W[rows row0 .. row0 + rows) += scale * B A with A [rank][cols] and B [rows][rank] fp32 (a LoRA pair), W bf16;
-// `swiglu_F` > 0 maps rows through the gate/up interleave of a [2F][cols] matrix. Block (x, y) covers 256 columns
-// of 16 rows: the 16 rows of B sit in shared memory and each A row is read once per 16 rows.
-constexpr int kLoraRows = 16;
-__global__ void __launch_bounds__(256) k_lora_merge(__nv_bfloat16* W, long ldw, long row0, int rows, int cols,
-                                                     const float* A, const float* Bm, int rank, float scale,
-                                                     long swiglu_F)
-{
-    extern __shared__ float sB[];  // [kLoraRows][rank]
-    const int r0 = blockIdx.y * kLoraRows, c = blockIdx.x * 256 + threadIdx.x;
-    for (int i = threadIdx.x; i < kLoraRows * rank; i += 256) {
-        const int rr = i / rank, k = i - rr * rank;
-        sB[i] = r0 + rr < rows ? Bm[long(r0 + rr) * rank + k] : 0.f;
-    }
-    __syncthreads();
-    if (c >= cols)
-        return;
-    float acc[kLoraRows] = {};
-    for (int k = 0; k < rank; ++k) {
-        const float a = A[long(k) * cols + c];
-#pragma unroll
-        for (int rr = 0; rr < kLoraRows; ++rr)
-            acc[rr] = fmaf(sB[rr * rank + k], a, acc[rr]);
-    }
-#pragma unroll
-    for (int rr = 0; rr < kLoraRows; ++rr) {
-        if (r0 + rr >= rows)
-            break;
-        const long r = row0 + r0 + rr, dr = swiglu_F > 0 ? swiglu_row(r, swiglu_F) : r;
-        __nv_bfloat16& w = W[dr * ldw + c];
-        w = __float2bfloat16_rn(__bfloat162float(w) + scale * acc[rr]);
-    }
-}
-
 }  // namespace
 
 }  // namespace mkb
@@ -1217,30 +1184,8 @@ mkb_status mkb_dit_weight_lora_rows(mkb_dit* d, const char* name, long row0, lon
         return fail(MKB_ERR_INVALID, std::string("lora: unknown matrix ") + (name ? name : "(null)"));
     if (row0 < 0 || rows <= 0 || row0 + rows > w->rows)
         return fail(MKB_ERR_INVALID, std::string("lora: rows out of range for ") + name);
-    if (rank < 1 || rank > 512)
-        return fail(MKB_ERR_INVALID, "lora: rank must be 1..512");
-    float *dA = nullptr, *dB = nullptr;
-    const size_t nA = size_t(rank) * w->cols, nB = size_t(rows) * rank;
-    mkb_status st = MKB_OK;
-    if (cudaMalloc(&dA, nA * 4) != cudaSuccess || cudaMalloc(&dB, nB * 4) != cudaSuccess)
-        st = fail(MKB_ERR_ALLOC, "lora: device staging");
-    if (st == MKB_OK && (cudaMemcpyAsync(dA, A, nA * 4, cudaMemcpyHostToDevice, m.stream) != cudaSuccess ||
-                         cudaMemcpyAsync(dB, B, nB * 4, cudaMemcpyHostToDevice, m.stream) != cudaSuccess))
-        st = fail(MKB_ERR_CUDA, "lora: upload");
-    if (st == MKB_OK) {
-        const dim3 grid(unsigned((w->cols + 255) / 256), unsigned((rows + kLoraRows - 1) / kLoraRows));
-        k_lora_merge<<<grid, 256, size_t(kLoraRows) * rank * 4, m.stream>>>(
-            m.wmat + w->off, w->cols, row0, int(rows), int(w->cols), dA, dB, rank, scale, w->swiglu ? w->rows / 2 : 0);
-        count_launch();
-        st = cuda_status(cudaGetLastError(), "lora merge launch");
-    }
-    if (cudaStreamSynchronize(m.stream) != cudaSuccess && st == MKB_OK)
-        st = fail(MKB_ERR_CUDA, "lora: merge");
-    if (dA)
-        cudaFree(dA);
-    if (dB)
-        cudaFree(dB);
-    return st;
+    return lora_merge_rows(m.wmat + w->off, w->cols, row0, rows, w->cols, w->swiglu ? w->rows / 2 : 0, A, B, rank,
+                           scale, m.stream);
 }
 
 mkb_status mkb_dit_weight_read(mkb_dit* d, const char* name, float* host)

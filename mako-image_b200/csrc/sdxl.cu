@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "lora.cuh"
 #include "rowops.cuh"
 
 #include <cmath>
@@ -1331,6 +1332,21 @@ mkb_status mkb_unet_init_random(mkb_unet* u, uint64_t seed, float std)
 }
 
 int mkb_unet_weight_count(const mkb_unet* u) { return u ? int(u->impl.W.ws.size()) : 0; }
+
+mkb_status mkb_unet_weight_lora_rows(mkb_unet* u, const char* name, long row0, long rows, const float* A,
+                                     const float* B, int rank, float scale)
+{
+    if (!u || !name)
+        return fail(MKB_ERR_INVALID, "unet lora: null argument");
+    WTable& W = u->impl.W;
+    const WTable::W* w = W.find(name);
+    if (!w || (w->kind != WTable::kMat && w->kind != WTable::kGlu))
+        return fail(MKB_ERR_INVALID, std::string("unet lora: ") + name + " is not a matrix");
+    if (row0 < 0 || rows <= 0 || row0 + rows > w->r)
+        return fail(MKB_ERR_INVALID, std::string("unet lora: rows out of range for ") + name);
+    return lora_merge_rows(W.mat + w->off, w->cp, row0, rows, w->c, w->kind == WTable::kGlu ? w->r / 2 : 0, A, B,
+                           rank, scale, u->impl.stream);
+}
 
 mkb_status mkb_unet_weight_info(const mkb_unet* u, int i, const char** name, long* dims, int* ndim)
 {

@@ -9,6 +9,7 @@
 // 1x1 convolutions used as matrices are squeezed, stacked rows are concatenated. Tensors the model does not use (a
 // single-file checkpoint also holds the text encoders) are ignored.
 #include "mkb_image.h"
+#include "lora_file.hpp"
 #include "safetensors.hpp"
 
 #include <cstdio>
@@ -373,6 +374,130 @@ mkb_status mkb_vae_load_safetensors(mkb_vae* v, const char* const* paths, int n_
             {"", "first_stage_model.", "vae."},
             "vae"};
     return load(m, paths, n_paths, strict, loaded);
+}
+
+}  // extern "C"
+
+namespace {
+
+// A UNet LoRA module -> (weight, first row, rows): the transformers' projections, as Sdxl::load_unet registers them
+// (sdxl.cpp:385-410). Names compare with '_' read as '.' (the reference's lora_key, sdxl.cpp:54-58), so the
+// checkpoint spelling ("input_blocks.4.1.transformer_blocks.0.attn1.to_q") and the flattened one of many adapter
+// files ("input_blocks_4_1_transformer_blocks_0_attn1_to_q") both resolve.
+bool unet_lora_target(const std::string& module, const std::map<std::string, std::vector<long>>& dims,
+                      std::string* weight, long* row0, long* rows)
+{
+    std::string m = module;
+    for (char& ch : m)
+        if (ch == '_')
+            ch = '.';
+    unsigned k = 0, j = 0;
+    int used = 0;
+    std::string base, rest;
+    if (std::sscanf(m.c_str(), "input.blocks.%u.1.%n", &k, &used) == 1 && used > 0)
+        base = "in" + std::to_string(k) + ".attn.";
+    else if (used = 0; std::sscanf(m.c_str(), "output.blocks.%u.1.%n", &k, &used) == 1 && used > 0)
+        base = "out" + std::to_string(k) + ".attn.";
+    else if (used = 0; m.rfind("middle.block.1.", 0) == 0)
+        base = "mid.attn.", used = int(std::strlen("middle.block.1."));
+    else
+        return false;
+    rest = m.substr(size_t(used));
+    auto whole = [&](const std::string& w) {
+        const auto it = dims.find(w);
+        if (it == dims.end())
+            return false;
+        *weight = w;
+        *row0 = 0;
+        *rows = it->second[0];
+        return true;
+    };
+    if (rest == "proj.in")
+        return whole(base + "proj_in.w");
+    if (rest == "proj.out")
+        return whole(base + "proj_out.w");
+    used = 0;
+    if (std::sscanf(rest.c_str(), "transformer.blocks.%u.%n", &j, &used) != 1 || used <= 0)
+        return false;
+    const std::string b = base + "b" + std::to_string(j) + ".", what = rest.substr(size_t(used));
+    const auto o1 = dims.find(b + "o1.w");
+    if (o1 == dims.end())
+        return false;
+    const long c = o1->second[0];
+    struct Part {
+        const char* name;
+        const char* weight;
+        long row0, rows;  // in units of c; rows 0: the whole matrix
+    };
+    const Part parts[] = {{"attn1.to.q", "qkv.w", 0, 1},    {"attn1.to.k", "qkv.w", 1, 1},
+                          {"attn1.to.v", "qkv.w", 2, 1},    {"attn1.to.out.0", "o1.w", 0, 0},
+                          {"attn2.to.q", "q2.w", 0, 0},     {"attn2.to.k", "kv2.w", 0, 1},
+                          {"attn2.to.v", "kv2.w", 1, 1},    {"attn2.to.out.0", "o2.w", 0, 0},
+                          {"ff.net.0.proj", "ff1.w", 0, 0}, {"ff.net.2", "ff2.w", 0, 0}};
+    for (const Part& p : parts)
+        if (what == p.name) {
+            if (!whole(b + p.weight))
+                return false;
+            if (p.rows) {
+                *row0 = p.row0 * c;
+                *rows = p.rows * c;
+            }
+            return true;
+        }
+    return false;
+}
+
+std::map<std::string, std::vector<long>> unet_dims(const mkb_unet* u)
+{
+    std::map<std::string, std::vector<long>> out;
+    for (int i = 0; i < mkb_unet_weight_count(u); ++i) {
+        const char* name = nullptr;
+        long d[4] = {0, 0, 0, 0};
+        int nd = 0;
+        if (mkb_unet_weight_info(u, i, &name, d, &nd) == MKB_OK)
+            out[name] = std::vector<long>(d, d + nd);
+    }
+    return out;
+}
+
+mkb_status unet_merge(mkb_unet* u, const std::map<std::string, std::vector<long>>& dims, const std::string& module,
+                      const float* A, const float* B, int rank, int in, int out, float scale)
+{
+    std::string w;
+    long row0 = 0, rows = 0;
+    if (!unet_lora_target(module, dims, &w, &row0, &rows))
+        return fail(MKB_ERR_INVALID, "unet lora: " + module + " is not a projection of this UNet");
+    const auto& d = dims.at(w);
+    if (d.size() != 2 || in != d[1] || out != rows)
+        return fail(MKB_ERR_INVALID, "unet lora: " + module + " is " + std::to_string(rows) + " x " +
+                                         std::to_string(d.size() == 2 ? d[1] : 0) + ", the adapter " +
+                                         std::to_string(out) + " x " + std::to_string(in));
+    return mkb_unet_weight_lora_rows(u, w.c_str(), row0, rows, A, B, rank, scale);
+}
+
+}  // namespace
+
+extern "C" {
+
+mkb_status mkb_unet_lora_merge(mkb_unet* u, const char* module, const float* A, const float* B, int rank,
+                               int in_features, int out_features, float scale)
+{
+    if (!u || !module || !A || !B)
+        return fail(MKB_ERR_INVALID, "unet lora: null argument");
+    return unet_merge(u, unet_dims(u), module, A, B, rank, in_features, out_features, scale);
+}
+
+mkb_status mkb_unet_load_lora(mkb_unet* u, const char* path, float scale, int* merged)
+{
+    if (!u)
+        return fail(MKB_ERR_INVALID, "unet lora: null handle");
+    const auto dims = unet_dims(u);
+    return mkb::load_lora_file(
+        path, scale,
+        [u, &dims](const std::string& m, const float* A, const float* B, int r, int in, int out, float s) {
+            return unet_merge(u, dims, m, A, B, r, in, out, s);
+        },
+        merged);
 }
 
 }  // extern "C"

@@ -7,6 +7,7 @@
 // uses the reference's names, MKB_VARIANT_QWEN1 the published Qwen-Image transformer's (separate image / text stream
 // weights, biases, per-block modulation).
 #include "mkb_image.h"
+#include "lora_file.hpp"
 #include "safetensors.hpp"
 
 #include <cstdio>
@@ -319,60 +320,14 @@ mkb_status mkb_dit_lora_merge(mkb_dit* d, const char* module, const float* A, co
 
 mkb_status mkb_dit_load_lora(mkb_dit* d, const char* path, float scale, int* merged)
 {
-    if (!d || !path)
-        return fail(MKB_ERR_INVALID, "load_lora: null argument");
-    std::string err;
-    auto f = mkb::st::File::open(path, &err);
-    if (!f)
-        return fail(MKB_ERR_INVALID, err);
-    // Pairs by module: <m>.lora_A.weight [r][in] + <m>.lora_B.weight [out][r] (or lora_down / lora_up), an
-    // optional scalar <m>.alpha scaling by alpha / r. Common file prefixes are dropped.
-    struct Pair {
-        const mkb::st::Tensor *a = nullptr, *b = nullptr, *alpha = nullptr;
-    };
-    std::map<std::string, Pair> mods;
-    for (const auto& t : f->tensors()) {
-        std::string name = t.name, stem;
-        for (const char* pre : {"transformer.", "diffusion_model.", "base_model.model."})
-            if (name.rfind(pre, 0) == 0)
-                name = name.substr(std::strlen(pre));
-        if (ends_with(name, ".lora_A.weight", &stem) || ends_with(name, ".lora_down.weight", &stem))
-            mods[stem].a = &t;
-        else if (ends_with(name, ".lora_B.weight", &stem) || ends_with(name, ".lora_up.weight", &stem))
-            mods[stem].b = &t;
-        else if (ends_with(name, ".alpha", &stem))
-            mods[stem].alpha = &t;
-        else
-            return fail(MKB_ERR_INVALID, "load_lora: " + t.name + " is not a LoRA tensor");
-    }
-    int n = 0;
-    std::vector<float> a, b;
-    for (const auto& [m, p] : mods) {
-        if (!p.a || !p.b || p.a->shape.size() != 2 || p.b->shape.size() != 2 || p.a->shape[0] != p.b->shape[1])
-            return fail(MKB_ERR_INVALID, "load_lora: " + m + " lacks a matching A / B pair");
-        const int r = int(p.a->shape[0]);
-        float s = scale;
-        if (p.alpha) {
-            if (p.alpha->count() != 1)
-                return fail(MKB_ERR_INVALID, "load_lora: " + m + ".alpha is not a scalar");
-            float al = 0.f;
-            if (!f->read_f32(*p.alpha, &al, &err))
-                return fail(MKB_ERR_INVALID, err);
-            s *= al / float(r);
-        }
-        a.resize(size_t(p.a->count()));
-        b.resize(size_t(p.b->count()));
-        if (!f->read_f32(*p.a, a.data(), &err) || !f->read_f32(*p.b, b.data(), &err))
-            return fail(MKB_ERR_INVALID, err);
-        if (mkb_status st = mkb_dit_lora_merge(d, m.c_str(), a.data(), b.data(), r, int(p.a->shape[1]),
-                                               int(p.b->shape[0]), s);
-            st != MKB_OK)
-            return st;
-        ++n;
-    }
-    if (merged)
-        *merged = n;
-    return MKB_OK;
+    if (!d)
+        return fail(MKB_ERR_INVALID, "load_lora: null handle");
+    return mkb::load_lora_file(
+        path, scale,
+        [d](const std::string& m, const float* A, const float* B, int r, int in, int out, float s) {
+            return mkb_dit_lora_merge(d, m.c_str(), A, B, r, in, out, s);
+        },
+        merged);
 }
 
 struct mkb_st_file {

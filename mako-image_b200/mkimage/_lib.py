@@ -94,6 +94,9 @@ _SIGS = {
     "mkb_dit_variant": (_i, [_vp]),
     "mkb_unet_load_safetensors": (_i, [_vp, ctypes.POINTER(ctypes.c_char_p), _i, _i, ctypes.POINTER(_i)]),
     "mkb_vae_load_safetensors": (_i, [_vp, ctypes.POINTER(ctypes.c_char_p), _i, _i, ctypes.POINTER(_i)]),
+    "mkb_unet_lora_merge": (_i, [_vp, ctypes.c_char_p, _vp, _vp, _i, _i, _i, _f]),
+    "mkb_unet_load_lora": (_i, [_vp, ctypes.c_char_p, _f, ctypes.POINTER(_i)]),
+    "mkb_unet_weight_lora_rows": (_i, [_vp, ctypes.c_char_p, _l, _l, _vp, _vp, _i, _f]),
     "mkb_dit_weight_write_rows": (_i, [_vp, ctypes.c_char_p, _l, _l, _vp]),
     "mkb_dit_weight_lora_rows": (_i, [_vp, ctypes.c_char_p, _l, _l, _vp, _vp, _i, _f]),
     "mkb_dit_load_safetensors": (_i, [_vp, ctypes.POINTER(ctypes.c_char_p), _i, _i, ctypes.POINTER(_i)]),

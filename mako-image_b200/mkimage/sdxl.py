@@ -146,6 +146,21 @@ class Unet(_Weights):
     def step_flops(self, n):
         return lib.mkb_unet_step_flops(self.h, n)
 
+    def lora_merge(self, module, A, B, scale=1.0):
+        """W += scale * B A for a transformer projection of the UNet (mkb_unet_lora_merge)."""
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        if A.ndim != 2 or B.ndim != 2 or B.shape[1] != A.shape[0]:
+            raise ValueError(f"lora_merge: A {A.shape} and B {B.shape} are not [rank][in] and [out][rank]")
+        check(lib.mkb_unet_lora_merge(self.h, module.encode(), _fptr(A), _fptr(B), A.shape[0], A.shape[1], B.shape[0],
+                                      scale))
+
+    def load_lora(self, path, scale=1.0):
+        """Merges every pair of a LoRA safetensors file into the UNet; returns the number of modules."""
+        n = ctypes.c_int()
+        check(lib.mkb_unet_load_lora(self.h, str(path).encode(), scale, ctypes.byref(n)))
+        return n.value
+
 
 class Vae(_Weights):
     _prefix = "vae"

@@ -155,3 +155,54 @@ def test_vae_checkpoint_round_trip(cuda, tmp_path, ldm):
     got = dst.weights()
     for n, a in W.items():
         assert np.array_equal(got[n], a), n
+
+
+def test_unet_lora(cuda, tmp_path):
+    """LoRA on the UNet's transformer projections (sdxl.cpp:385-417) against oracle.ops.lora_merge: a kohya-style
+    flattened module name with alpha, a PEFT-style name on the GEGLU projection (interleaved rows), a direct merge;
+    every other row untouched."""
+    import mkimage
+    from oracle import ops as O
+
+    cfg = mkimage.UnetConfig(channels=(64, 128, 128), depth=(0, 1, 1), layers=1, context_dim=64, pooled_dim=64,
+                             max_batch=2, max_gh=8, max_gw=8, max_context=8, slots=2)
+    u = mkimage.Unet(cfg)
+    u.init_random(seed=23)
+    before = u.weights()
+    rng = np.random.RandomState(24)
+    c = 128
+    r = 8
+    A1, B1 = rng.standard_normal((r, c)).astype(np.float32) * 0.1, rng.standard_normal((c, r)).astype(np.float32) * 0.1
+    A2 = rng.standard_normal((r, c)).astype(np.float32) * 0.1
+    B2 = rng.standard_normal((8 * c, r)).astype(np.float32) * 0.1
+    p = tmp_path / "lora.safetensors"
+    write_safetensors(p, {"lora_unet_input_blocks_3_1_transformer_blocks_0_attn1_to_k.lora_down.weight": A1,
+                          "lora_unet_input_blocks_3_1_transformer_blocks_0_attn1_to_k.lora_up.weight": B1,
+                          "lora_unet_input_blocks_3_1_transformer_blocks_0_attn1_to_k.alpha": np.array(4.0, np.float32),
+                          "input_blocks.3.1.transformer_blocks.0.ff.net.0.proj.lora_A.weight": A2,
+                          "input_blocks.3.1.transformer_blocks.0.ff.net.0.proj.lora_B.weight": B2})
+    assert u.load_lora(p, 0.8) == 2
+    A3 = rng.standard_normal((4, 64)).astype(np.float32) * 0.1  # cross-attention reads 64-wide context
+    B3 = rng.standard_normal((c, 4)).astype(np.float32) * 0.1
+    u.lora_merge("middle_block.1.transformer_blocks.0.attn2.to_v", A3, B3, 1.2)
+    after = u.weights()
+
+    def ok(got, W, A, B, s):
+        want = O.lora_merge(W, A, B, s)
+        delta = s * (B.astype(np.float64) @ A.astype(np.float64))
+        return bool(np.all(np.abs(got - want) <= 2.0 ** -7 * (np.abs(W) + np.abs(delta)) + 1e-30))
+
+    changed = {"in3.attn.b0.qkv.w": (c, 2 * c), "in3.attn.b0.ff1.w": (0, 8 * c), "mid.attn.b0.kv2.w": (c, 2 * c)}
+    q = "in3.attn.b0.qkv.w"
+    assert ok(after[q][c:2 * c], before[q][c:2 * c], A1, B1, 0.8 * 4.0 / r)
+    f = "in3.attn.b0.ff1.w"
+    assert ok(after[f], before[f], A2, B2, 0.8)
+    k = "mid.attn.b0.kv2.w"
+    assert ok(after[k][c:], before[k][c:], A3, B3, 1.2)
+    for n, a in before.items():
+        mask = np.ones(a.shape[0], bool)
+        if n in changed:
+            mask[changed[n][0]:changed[n][1]] = False
+        assert np.array_equal(after[n][mask], a[mask]), n
+    with pytest.raises(mkimage.MkbError, match="not a projection"):
+        u.lora_merge("input_blocks.1.0.in_layers.2", A1, B1, 1.0)
