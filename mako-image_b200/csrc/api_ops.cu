@@ -1,12 +1,14 @@
 // The runtime-operation layer of the C ABI (include/mkb_image.h, part 1): argument checks, then one prepared
 // kernel launch each.
 #include "common.cuh"
+#include "launch.cuh"
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "rowops.cuh"
 #include "sm100.cuh"
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -21,6 +23,15 @@ std::vector<uint32_t*> g_status_words;  // per device
 }  // namespace
 
 void count_launch(unsigned long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("MKB_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
 
 mkb_status fail(mkb_status code, const std::string& msg)
 {

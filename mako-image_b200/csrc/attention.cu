@@ -17,6 +17,7 @@
 #include "gemm.cuh"
 #include "sm100.cuh"
 #include "common.cuh"
+#include "launch.cuh"
 
 #include <cudaTypedefs.h>
 #include <cmath>
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tk);
         prefetch_tmap(&tv);
     }
+    grid_dep_wait();  // before TMEM allocation and the first global access
     if (warp == 1) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
@@ -175,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem = *tmem_slot;
 
     if (warp < 4)
@@ -533,12 +536,12 @@ cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
         cudaError_t e = attn_setup<64>();
         if (e != cudaSuccess)
             return e;
-        k_attn<64><<<op.grid, kThreads, kSmem<64>, st>>>(op.tq, op.tk, op.tv, op.args);
+        launch_k(k_attn<64>, op.grid, kThreads, kSmem<64>, st, op.tq, op.tk, op.tv, op.args);
     } else {
         cudaError_t e = attn_setup<128>();
         if (e != cudaSuccess)
             return e;
-        k_attn<128><<<op.grid, kThreads, kSmem<128>, st>>>(op.tq, op.tk, op.tv, op.args);
+        launch_k(k_attn<128>, op.grid, kThreads, kSmem<128>, st, op.tq, op.tk, op.tv, op.args);
     }
     count_launch();
     return cudaGetLastError();

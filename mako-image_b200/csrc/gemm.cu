@@ -8,6 +8,7 @@
 #include "gemm.cuh"
 #include "sm100.cuh"
 #include "common.cuh"
+#include "launch.cuh"
 
 #include <cudaTypedefs.h>
 #include <algorithm>
@@ -419,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
             prefetch_tmap(&P.tb[p]);
         }
     }
+    grid_dep_wait();  // before TMEM allocation and the first global access
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::kTmemCols);
         tmem_relinquish();
@@ -426,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -593,6 +596,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
             prefetch_tmap(&P.tb[p]);
         }
     }
+    grid_dep_wait();  // before TMEM allocation and the first global access
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, C::kTmemCols);
         tmem_relinquish_pair();
@@ -601,6 +605,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
     __syncthreads();
     cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
     tc_fence_after();
+    grid_dep_launch();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
@@ -741,7 +746,7 @@ cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
             return e;
         attr_set = true;
     }
-    k_gemm<BN, EPI, CONV><<<op.grid, kThreads, Cfg<BN>::kSmem, st>>>(op.p);
+    launch_k(k_gemm<BN, EPI, CONV>, op.grid, kThreads, Cfg<BN>::kSmem, st, op.p);
     count_launch();
     return cudaGetLastError();
 }
@@ -758,7 +763,7 @@ cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
                 return e;
             attr_set = true;
         }
-        k_gemm2<BN, EPI, CONV><<<op.grid, kThreads, Cfg2<BN>::kSmem, st>>>(op.p);
+        launch_k(k_gemm2<BN, EPI, CONV>, op.grid, kThreads, Cfg2<BN>::kSmem, st, op.p);
         count_launch();
         return cudaGetLastError();
     }

@@ -1,4 +1,5 @@
 #include "lora.cuh"
+#include "launch.cuh"
 
 namespace mkb {
 
@@ -19,6 +20,8 @@ __device__ __forceinline__ long glu_device_row(long r, long F)
 __global__ void __launch_bounds__(256) k_lora_merge(__nv_bfloat16* W, long ldw, long row0, int rows, int cols,
                                                      const float* A, const float* Bm, int rank, float scale, long glu_F)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     extern __shared__ float sB[];  // [kLoraRows][rank]
     const int r0 = blockIdx.y * kLoraRows, c = blockIdx.x * 256 + threadIdx.x;
     for (int i = threadIdx.x; i < kLoraRows * rank; i += 256) {
@@ -64,8 +67,8 @@ mkb_status lora_merge_rows(__nv_bfloat16* W, long ldw, long row0, long rows, lon
         s = fail(MKB_ERR_CUDA, "lora: upload");
     if (s == MKB_OK) {
         const dim3 grid(unsigned((cols + 255) / 256), unsigned((rows + kLoraRows - 1) / kLoraRows));
-        k_lora_merge<<<grid, 256, size_t(kLoraRows) * rank * 4, st>>>(W, ldw, row0, int(rows), int(cols), dA, dB, rank,
-                                                                      scale, glu_F);
+        launch_k(k_lora_merge, grid, 256, size_t(kLoraRows) * rank * 4, st, W, ldw, row0, int(rows), int(cols), dA,
+                 dB, rank, scale, glu_F);
         count_launch();
         s = cuda_status(cudaGetLastError(), "lora merge launch");
     }

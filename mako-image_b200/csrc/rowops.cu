@@ -1,6 +1,7 @@
 // Row and element kernels (see rowops.cuh).
 #include "rowops.cuh"
 #include "common.cuh"
+#include "launch.cuh"
 #include "rng.cuh"
 
 #include <algorithm>
@@ -28,6 +29,8 @@ __device__ __forceinline__ uint2 pack4_bf16(float a, float b, float c, float d)
 template <int NV>
 __global__ void __launch_bounds__(256) k_ln_mod(const LnModArgs a)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= a.rows)
         return;
@@ -70,6 +73,8 @@ __global__ void __launch_bounds__(256) k_ln_mod(const LnModArgs a)
 template <int NV>
 __global__ void __launch_bounds__(256) k_rms(const RmsArgs a)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= a.samples * a.rows_per_sample)
         return;
@@ -104,6 +109,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __nv_bfloat16* __restrict__ 
                                               long ldx, const float* __restrict__ bias, float* __restrict__ y,
                                               long ldy, int N, int K, int act)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     extern __shared__ float xs[];  // [B][K]
     for (int i = threadIdx.x; i < B * K; i += blockDim.x)
         xs[i] = x[long(i / K) * ldx + i % K];
@@ -156,6 +163,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __nv_bfloat16* __restrict__ 
 
 __global__ void k_sinusoid(const float* t, float* tp, int rows)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int r = blockIdx.x, i = threadIdx.x;  // 128 threads
     if (r >= rows)
         return;
@@ -167,6 +176,8 @@ __global__ void k_sinusoid(const float* t, float* tp, int rows)
 
 __global__ void k_fill_normal(void* out, int bf16, uint64_t n, uint64_t key, uint64_t offset, float stdv, float mean)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const double z = counter_normal(key, offset + i);
@@ -180,6 +191,8 @@ __global__ void k_fill_normal(void* out, int bf16, uint64_t n, uint64_t key, uin
 
 __global__ void k_cast_scalar(const float* x, __nv_bfloat16* y, uint64_t n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
         y[i] = __float2bfloat16_rn(x[i]);
@@ -189,6 +202,8 @@ __global__ void k_cast_scalar(const float* x, __nv_bfloat16* y, uint64_t n)
 // and y 8-byte aligned (k_cast_scalar otherwise).
 __global__ void k_cast(const float* x, __nv_bfloat16* y, uint64_t n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t n4 = n / 4, stride = uint64_t(gridDim.x) * blockDim.x;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     uint2* y4 = reinterpret_cast<uint2*>(y);
@@ -212,6 +227,8 @@ __global__ void k_cast(const float* x, __nv_bfloat16* y, uint64_t n)
 
 __global__ void k_silu(const float* x, float* y, uint64_t n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
         y[i] = x[i] / (1.0f + expf(-x[i]));
@@ -220,6 +237,8 @@ __global__ void k_silu(const float* x, float* y, uint64_t n)
 __global__ void k_copy_heads(const uint4* src, int src_rows, int src_off, uint4* dst, int dst_rows, int dst_off,
                              int heads, int rows)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     // 16 uint4 per 128-wide bf16 row
     const uint64_t total = uint64_t(heads) * rows * 16;
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
@@ -233,6 +252,8 @@ __global__ void k_copy_heads(const uint4* src, int src_rows, int src_off, uint4*
 
 __global__ void k_cfg_euler(float* x, const float* vc, const float* vu, float g, float dt, uint64_t n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const float v = vu ? vu[i] + g * (vc[i] - vu[i]) : vc[i];
@@ -270,6 +291,8 @@ __device__ __forceinline__ void chan_combine(float& n, float& mean, float& m2, f
 // statistics per channel, combined through shared memory [Rb][C] by one thread per group.
 __global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a, int chunk_px, int nchunks)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     extern __shared__ float sh[];  // mean [Rb][C], M2 [Rb][C], count [Rb]
     const int chunk = blockIdx.x, b = blockIdx.y;
     const int Q = a.C / 4, Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
@@ -322,6 +345,8 @@ __global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a, int chunk_px, 
 // Per (sample, group): the chunks combined by a tree, then mean and 1 / sqrt(var + eps).
 __global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a, int nchunks)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     __shared__ float sn[256], sm[256], sq[256];
     const int g = blockIdx.x, b = blockIdx.y;
     float n = 0.f, mean = 0.f, m2 = 0.f;
@@ -354,6 +379,8 @@ __global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a, int nchunks
 // thread keeps its quad's four (scale, shift) in registers. Block (x, b) covers pixels [x * px, (x + 1) * px).
 __global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a, int nchunks, int px)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int b = blockIdx.y;
     const int Q = a.C / 4, Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
     const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
@@ -408,6 +435,8 @@ __global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a, int nchunks, i
 // GroupNorm kernels) and writes it to output rows 2y and 2y + 1, each pixel twice.
 __global__ void __launch_bounds__(256) k_upsample2x(const float4* x, uint2* y, int H, int W, int Q)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int iy = blockIdx.x, b = blockIdx.y;
     const int Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
     const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
@@ -430,6 +459,8 @@ __global__ void __launch_bounds__(256) k_upsample2x(const float4* x, uint2* y, i
 
 __global__ void k_concat(const float4* a, int Ca4, const float4* b, int Cb4, float4* y, long P)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int C4 = Ca4 + Cb4;
     const uint64_t total = uint64_t(P) * C4;
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
@@ -442,6 +473,8 @@ __global__ void k_concat(const float4* a, int Ca4, const float4* b, int Cb4, flo
 
 __global__ void k_pad_channels(const float* x, int C, __nv_bfloat16* y, int Cp, long P)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t total = uint64_t(P) * Cp;
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -453,6 +486,8 @@ __global__ void k_pad_channels(const float* x, int C, __nv_bfloat16* y, int Cp, 
 
 __global__ void k_unpack(const float* tok, __nv_bfloat16* img, int B, int gh, int gw, int Cp, float scale)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t total = uint64_t(B) * 4 * gh * gw * Cp;
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -468,6 +503,8 @@ __global__ void k_unpack(const float* tok, __nv_bfloat16* img, int B, int gh, in
 
 __global__ void k_pack(const float* img, int Cs, float* tok, int B, int gh, int gw)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t total = uint64_t(B) * gh * gw * 16;
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -481,6 +518,8 @@ __global__ void k_pack(const float* img, int Cs, float* tok, int B, int gh, int 
 
 __global__ void k_add_silu(const float* a, const float* b, float* out, uint64_t n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         const float v = a[i] + b[i];
@@ -490,6 +529,8 @@ __global__ void k_add_silu(const float* a, const float* b, float* out, uint64_t 
 
 __global__ void k_to_rgba(const float* img, int Cs, float4* rgba, long P)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
     for (uint64_t p = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < uint64_t(P); p += stride) {
         const float* s = img + p * Cs;
@@ -501,6 +542,8 @@ __global__ void k_to_rgba(const float* img, int Cs, float4* rgba, long P)
 // One CTA per row: max, then exp-sum, then normalised bf16 probabilities.
 __global__ void __launch_bounds__(256) k_softmax_rows(const float* s, __nv_bfloat16* p, int n, float scale)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     __shared__ float red[32];
     const float* r = s + long(blockIdx.x) * n;
     __nv_bfloat16* o = p + long(blockIdx.x) * n;
@@ -533,6 +576,8 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* s, __nv_bfloa
 
 __global__ void k_transpose(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     __shared__ __nv_bfloat16 tile[32][33];
     const long r0 = long(blockIdx.x) * 32;
     const int cb = blockIdx.y * 32;
@@ -567,13 +612,13 @@ cudaError_t ln_modulate(const LnModArgs& a, cudaStream_t st)
         return cudaSuccess;
     const int nv = a.D / 128, blocks = (a.rows + 7) / 8;
     if (nv <= 8)
-        k_ln_mod<8><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_ln_mod<8>, blocks, 256, 0, st, a);
     else if (nv <= 16)
-        k_ln_mod<16><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_ln_mod<16>, blocks, 256, 0, st, a);
     else if (nv <= 24)
-        k_ln_mod<24><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_ln_mod<24>, blocks, 256, 0, st, a);
     else
-        k_ln_mod<32><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_ln_mod<32>, blocks, 256, 0, st, a);
     count_launch();
     return cudaGetLastError();
 }
@@ -587,13 +632,13 @@ cudaError_t rms_norm_rows(const RmsArgs& a, cudaStream_t st)
         return cudaSuccess;
     const int nv = a.C / 128, blocks = (rows + 7) / 8;
     if (nv <= 8)
-        k_rms<8><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_rms<8>, blocks, 256, 0, st, a);
     else if (nv <= 16)
-        k_rms<16><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_rms<16>, blocks, 256, 0, st, a);
     else if (nv <= 24)
-        k_rms<24><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_rms<24>, blocks, 256, 0, st, a);
     else
-        k_rms<32><<<blocks, 256, 0, st>>>(a);
+        launch_k(k_rms<32>, blocks, 256, 0, st, a);
     count_launch();
     return cudaGetLastError();
 }
@@ -617,7 +662,7 @@ cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* 
                 return e;                                                                                              \
             smem_set[BB] = smem;                                                                                       \
         }                                                                                                              \
-        k_gemv<BB><<<blocks, 256, smem, st>>>(W, x, ldx, bias, y, ldy, N, K, act);                                     \
+        launch_k(k_gemv<BB>, blocks, 256, smem, st, W, x, ldx, bias, y, ldy, N, K, act);                               \
         break;                                                                                                         \
     }
     switch (B) {
@@ -639,7 +684,7 @@ cudaError_t timestep_sinusoid(const float* t, float* tp, int rows, cudaStream_t 
 {
     if (rows <= 0)
         return cudaSuccess;
-    k_sinusoid<<<rows, 128, 0, st>>>(t, tp, rows);
+    launch_k(k_sinusoid, rows, 128, 0, st, t, tp, rows);
     count_launch();
     return cudaGetLastError();
 }
@@ -649,7 +694,7 @@ cudaError_t fill_normal(void* out, bool bf16, uint64_t n, uint64_t key, uint64_t
 {
     if (!n)
         return cudaSuccess;
-    k_fill_normal<<<grid_for(n, 256), 256, 0, st>>>(out, bf16 ? 1 : 0, n, key, offset, std, mean);
+    launch_k(k_fill_normal, grid_for(n, 256), 256, 0, st, out, bf16 ? 1 : 0, n, key, offset, std, mean);
     count_launch();
     return cudaGetLastError();
 }
@@ -659,9 +704,9 @@ cudaError_t cast_f32_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStre
     if (!n)
         return cudaSuccess;
     if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 7))
-        k_cast_scalar<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+        launch_k(k_cast_scalar, grid_for(n, 256), 256, 0, st, x, y, n);
     else
-        k_cast<<<grid_for(n / 4 + 1, 256), 256, 0, st>>>(x, y, n);
+        launch_k(k_cast, grid_for(n / 4 + 1, 256), 256, 0, st, x, y, n);
     count_launch();
     return cudaGetLastError();
 }
@@ -670,7 +715,7 @@ cudaError_t silu_f32(const float* x, float* y, uint64_t n, cudaStream_t st)
 {
     if (!n)
         return cudaSuccess;
-    k_silu<<<grid_for(n, 256), 256, 0, st>>>(x, y, n);
+    launch_k(k_silu, grid_for(n, 256), 256, 0, st, x, y, n);
     count_launch();
     return cudaGetLastError();
 }
@@ -683,8 +728,8 @@ cudaError_t copy_head_rows(const __nv_bfloat16* src, int src_rows, int src_off, 
     if (src_off + rows > src_rows || dst_off + rows > dst_rows)
         return cudaErrorInvalidValue;
     const uint64_t n = uint64_t(heads) * rows * 16;
-    k_copy_heads<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(src), src_rows, src_off,
-                                                   reinterpret_cast<uint4*>(dst), dst_rows, dst_off, heads, rows);
+    launch_k(k_copy_heads, grid_for(n, 256), 256, 0, st, reinterpret_cast<const uint4*>(src), src_rows, src_off,
+             reinterpret_cast<uint4*>(dst), dst_rows, dst_off, heads, rows);
     count_launch();
     return cudaGetLastError();
 }
@@ -711,13 +756,13 @@ cudaError_t group_norm(const GnArgs& a, cudaStream_t st)
             return e;
         attr = true;
     }
-    k_gn_stats<<<dim3(nchunks, a.B), 256, smem, st>>>(a, px, nchunks);
+    launch_k(k_gn_stats, dim3(nchunks, a.B), 256, smem, st, a, px, nchunks);
     count_launch();
-    k_gn_finalize<<<dim3(a.groups, a.B), 256, 0, st>>>(a, nchunks);
+    launch_k(k_gn_finalize, dim3(a.groups, a.B), 256, 0, st, a, nchunks);
     count_launch();
     // Apply: about eight blocks per SM over the batch.
     const int apx = int(std::max<long>(16, (long(a.B) * a.HW + 8 * 148 - 1) / (8 * 148)));
-    k_gn_apply<<<dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st>>>(a, nchunks, apx);
+    launch_k(k_gn_apply, dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st, a, nchunks, apx);
     count_launch();
     return cudaGetLastError();
 }
@@ -726,8 +771,8 @@ cudaError_t upsample2x_bf16(const float* x, __nv_bfloat16* y, int B, int H, int 
 {
     if (C % 4 || B <= 0 || H <= 0 || W <= 0)
         return cudaErrorInvalidValue;
-    k_upsample2x<<<dim3(H, B), 256, 0, st>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), H, W,
-                                             C / 4);
+    launch_k(k_upsample2x, dim3(H, B), 256, 0, st, reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y),
+             H, W, C / 4);
     count_launch();
     return cudaGetLastError();
 }
@@ -737,9 +782,8 @@ cudaError_t concat_channels(const float* a, int Ca, const float* b, int Cb, floa
     if (Ca % 4 || Cb % 4)
         return cudaErrorInvalidValue;
     const uint64_t n = uint64_t(P) * (Ca + Cb) / 4;
-    k_concat<<<grid_for(n, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(a), Ca / 4,
-                                                reinterpret_cast<const float4*>(b), Cb / 4,
-                                                reinterpret_cast<float4*>(y), P);
+    launch_k(k_concat, grid_for(n, 256), 256, 0, st, reinterpret_cast<const float4*>(a), Ca / 4,
+             reinterpret_cast<const float4*>(b), Cb / 4, reinterpret_cast<float4*>(y), P);
     count_launch();
     return cudaGetLastError();
 }
@@ -749,7 +793,7 @@ cudaError_t pad_channels_bf16(const float* x, int C, __nv_bfloat16* y, int Cp, l
     if (C > Cp)
         return cudaErrorInvalidValue;
     const uint64_t n = uint64_t(P) * Cp;
-    k_pad_channels<<<grid_for(n, 256), 256, 0, st>>>(x, C, y, Cp, P);
+    launch_k(k_pad_channels, grid_for(n, 256), 256, 0, st, x, C, y, Cp, P);
     count_launch();
     return cudaGetLastError();
 }
@@ -758,7 +802,7 @@ cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, i
                                cudaStream_t st)
 {
     const uint64_t n = uint64_t(B) * 4 * gh * gw * Cp;
-    k_unpack<<<grid_for(n, 256), 256, 0, st>>>(tokens, img, B, gh, gw, Cp, scale);
+    launch_k(k_unpack, grid_for(n, 256), 256, 0, st, tokens, img, B, gh, gw, Cp, scale);
     count_launch();
     return cudaGetLastError();
 }
@@ -766,28 +810,28 @@ cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, i
 cudaError_t pack_tokens(const float* img, int Cs, float* tokens, int B, int gh, int gw, cudaStream_t st)
 {
     const uint64_t n = uint64_t(B) * gh * gw * 16;
-    k_pack<<<grid_for(n, 256), 256, 0, st>>>(img, Cs, tokens, B, gh, gw);
+    launch_k(k_pack, grid_for(n, 256), 256, 0, st, img, Cs, tokens, B, gh, gw);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t add_silu(const float* a, const float* b, float* out, uint64_t n, cudaStream_t st)
 {
-    k_add_silu<<<grid_for(n, 256), 256, 0, st>>>(a, b, out, n);
+    launch_k(k_add_silu, grid_for(n, 256), 256, 0, st, a, b, out, n);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t to_rgba(const float* img, int Cs, float* rgba, long P, cudaStream_t st)
 {
-    k_to_rgba<<<grid_for(P, 256), 256, 0, st>>>(img, Cs, reinterpret_cast<float4*>(rgba), P);
+    launch_k(k_to_rgba, grid_for(P, 256), 256, 0, st, img, Cs, reinterpret_cast<float4*>(rgba), P);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n, float scale, cudaStream_t st)
 {
-    k_softmax_rows<<<dim3(unsigned(rows)), 256, 0, st>>>(s, p, n, scale);
+    launch_k(k_softmax_rows, dim3(unsigned(rows)), 256, 0, st, s, p, n, scale);
     count_launch();
     return cudaGetLastError();
 }
@@ -796,7 +840,7 @@ cudaError_t transpose_bf16(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat
                            cudaStream_t st)
 {
     dim3 grid(unsigned((rows + 31) / 32), unsigned((cols + 31) / 32));
-    k_transpose<<<grid, dim3(32, 8), 0, st>>>(x, ldx, c0, y, rows, cols);
+    launch_k(k_transpose, grid, dim3(32, 8), 0, st, x, ldx, c0, y, rows, cols);
     count_launch();
     return cudaGetLastError();
 }
@@ -805,7 +849,7 @@ cudaError_t cfg_euler(float* x, const float* v_c, const float* v_u, float g, flo
 {
     if (!n)
         return cudaSuccess;
-    k_cfg_euler<<<grid_for(n, 256), 256, 0, st>>>(x, v_c, v_u, g, dt, n);
+    launch_k(k_cfg_euler, grid_for(n, 256), 256, 0, st, x, v_c, v_u, g, dt, n);
     count_launch();
     return cudaGetLastError();
 }

@@ -6,6 +6,7 @@
 // (offset + j) of the stream `key`, so runs are reproducible and the oracle draws the same numbers.
 #include "../host/er_sde_coef.hpp"
 #include "common.cuh"
+#include "launch.cuh"
 #include "rng.cuh"
 
 #include <algorithm>
@@ -19,12 +20,16 @@ int grid_of(long n) { return int(std::min<long>((n + 255) / 256, 148L * 16)); }
 
 __global__ void k_axpy(float* x, const float* v, float a, long n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x)
         x[j] += a * v[j];
 }
 
 __global__ void k_cfg_combine(float* out, const float* vc, const float* vu, float g, long n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x)
         out[j] = vu[j] + g * (vc[j] - vu[j]);
 }
@@ -32,6 +37,8 @@ __global__ void k_cfg_combine(float* out, const float* vc, const float* vu, floa
 // x += dt v, then + up * N(0, 1) (engine.cpp:492-499).
 __global__ void k_euler_ancestral(float* x, const float* v, float dt, float up, uint64_t key, uint64_t off, long n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x) {
         float xv = x[j] + dt * v[j];
         if (up > 0.f)
@@ -50,6 +57,8 @@ struct ErSdeArgs {
 __global__ void k_er_sde(float* x, const float* v, float* old, float* old_d, ErSdeArgs a, uint64_t key, uint64_t off,
                          long n)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long j = long(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += long(gridDim.x) * blockDim.x) {
         const float den = x[j] - a.sigma * v[j];
         if (a.last) {
@@ -84,7 +93,8 @@ mkb_status mkb_cfg_combine_dev(float* out, const float* v_cond, const float* v_u
 {
     if (!out || !v_cond || !v_uncond || n <= 0)
         return fail(MKB_ERR_INVALID, "cfg_combine: bad arguments");
-    k_cfg_combine<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(out, v_cond, v_uncond, guidance, n);
+    launch_k(k_cfg_combine, grid_of(n), 256, 0, static_cast<cudaStream_t>(stream), out, v_cond, v_uncond, guidance,
+             n);
     count_launch();
     return cuda_status(cudaGetLastError(), "cfg_combine launch");
 }
@@ -93,7 +103,7 @@ mkb_status mkb_axpy_dev(float* x, const float* v, float a, long n, void* stream)
 {
     if (!x || !v || n <= 0)
         return fail(MKB_ERR_INVALID, "axpy: bad arguments");
-    k_axpy<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, v, a, n);
+    launch_k(k_axpy, grid_of(n), 256, 0, static_cast<cudaStream_t>(stream), x, v, a, n);
     count_launch();
     return cuda_status(cudaGetLastError(), "axpy launch");
 }
@@ -107,8 +117,8 @@ mkb_status mkb_euler_ancestral_dev(float* x, const float* v, float sigma, float 
     const double from = sigma, to = sigma_next;
     const double up = std::min(to, std::sqrt(to * to * (from * from - to * to) / (from * from)));
     const float dt = float(std::sqrt(to * to - up * up) - from);
-    k_euler_ancestral<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, v, dt, float(up), noise_key,
-                                                                                  noise_offset, n);
+    launch_k(k_euler_ancestral, grid_of(n), 256, 0, static_cast<cudaStream_t>(stream), x, v, dt, float(up),
+             noise_key, noise_offset, n);
     count_launch();
     return cuda_status(cudaGetLastError(), "euler_ancestral launch");
 }
@@ -125,8 +135,8 @@ mkb_status mkb_er_sde_step_dev(mkb_er_sde* e, int i, float* x, const float* v, f
         return fail(MKB_ERR_STATE, "er_sde_step_dev: steps of a run must go 0, 1, 2, ...");
     ErSdeArgs a{c.c1, c.c2, c.c3, c.c4, c.d_den, c.u_den, c.cn, float(er_sde_sigma_d(e, i)), c.stage,
                 c.last ? 1 : 0, s_noise > 0.f ? 1 : 0};
-    k_er_sde<<<grid_of(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, v, state, state + n, a, noise_key,
-                                                                         noise_offset, n);
+    launch_k(k_er_sde, grid_of(n), 256, 0, static_cast<cudaStream_t>(stream), x, v, state, state + n, a,
+             noise_key, noise_offset, n);
     count_launch();
     return cuda_status(cudaGetLastError(), "er_sde launch");
 }
