@@ -13,6 +13,7 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace mkb {
@@ -22,26 +23,42 @@ namespace {
 constexpr int kBM = 128, kBK = 64;
 constexpr int kThreads = 192;
 
-template <int BN>
+// The TMA epilogue's staging (kAdd): two boxes of 32 fp32 columns x 128 rows after the stages.
+constexpr int kEpiBox = 128 * 32 * 4;
+constexpr int epi_staging(Epi e) { return e == Epi::kAdd ? 2 * kEpiBox : 0; }
+
+// Stages: up to 8 within 200 KB, fewer where the epilogue's staging would not fit beside them in 227 KB.
+constexpr int stages_for(int stage_bytes, int staging)
+{
+    const int by_budget = (200 * 1024) / stage_bytes > 8 ? 8 : (200 * 1024) / stage_bytes;
+    const int fit = (227 * 1024 - 1024 - 256 - staging) / stage_bytes;
+    return by_budget < fit ? by_budget : fit;
+}
+
+template <int BN, int STG = 0>
 struct Cfg {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kStages = stages_for(kStageBytes, STG);
     static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+    static constexpr int kStaging = STG;
     static constexpr int kBarBytes = 256;
-    static constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
+    static constexpr int kSmem = 1024 + kStages * kStageBytes + STG + kBarBytes;
+    static_assert(kStageBytes % 1024 == 0, "stages and staging boxes must stay 1024-byte aligned");
 };
 
 // Per-CTA shared memory of the 2-SM kernel: the CTA's 128 rows of A and half (BN / 2 rows) of B per stage.
-template <int BN>
+template <int BN, int STG = 0>
 struct Cfg2 {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = (BN / 2) * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kStages = stages_for(kStageBytes, STG);
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-    static constexpr int kSmem = 1024 + kStages * kStageBytes + 256;
+    static constexpr int kStaging = STG;
+    static constexpr int kSmem = 1024 + kStages * kStageBytes + STG + 256;
+    static_assert(kStageBytes % 1024 == 0, "stages and staging boxes must stay 1024-byte aligned");
 };
 
 #ifndef MKB_TILE_GROUP
@@ -373,6 +390,108 @@ __device__ __forceinline__ int gemm_num_m(const GemmArgs& a, bool conv)
     return conv ? a.conv_b * (a.conv_wo / a.conv_tw) * ((a.conv_ho + a.conv_th - 1) / a.conv_th) : (a.M + kBM - 1) / kBM;
 }
 
+// 16-byte chunk j of row r of a staging box (128-byte rows, 128-byte swizzle: the chunk index XOR the row mod 8,
+// which is the layout TMA reads and writes, and keeps a warp's row-per-lane accesses free of bank conflicts).
+__device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int j)
+{
+    return reinterpret_cast<float4*>(box + r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// State of the TMA epilogue across the tiles of one CTA.
+struct EpiTma {
+    uint8_t* boxes;       // two kEpiBox boxes
+    uint64_t* rbar;       // [2] residual-box barriers
+    uint32_t chunk = 0;   // chunks issued so far: chunk & 1 is the box in use
+    uint32_t rphase = 0;  // parity bit per box of its residual barrier
+    bool issuer = false;  // the one epilogue thread that issues the TMA copies
+};
+
+// The kAdd epilogue with fp32 output through TMA. Per 32-column chunk the 128 epilogue threads (one row each, r =
+// row within the tile) write acc + bias + addvec (+ the residual box, out_mode 3) into a staging box, then one
+// thread stores it (out_mode 1, 3) or reduce-adds it into out (out_mode 2: out is the residual). The box is the
+// tile's 128 rows: c1 the first row (2-D), or c1..c3 = x0, y0, image of a convolution's pixel tile. The sums are
+// those of the per-thread epilogue in the same order, so both paths give the same bits.
+template <int BN, bool CONV>
+__device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMap* to, const CUtensorMap* tr,
+                                             uint32_t t_row, int r, int row, bool row_ok, bool tile_ok, int n0,
+                                             int c1, int c2, int c3, EpiTma& e, uint32_t* status,
+                                             volatile int* abort)
+{
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32, ++e.chunk) {
+        const uint32_t buf = e.chunk & 1;
+        uint8_t* box = e.boxes + buf * kEpiBox;
+        const int col0 = n0 + c;
+        const bool active = tile_ok && col0 < a.N;  // the same in every epilogue thread
+        if (e.issuer) {
+            bulk_wait_read<1>();  // the copy issued from this box two chunks ago has read it
+            if (active && a.out_mode == 3) {
+                mbar_arrive_expect_tx(&e.rbar[buf], kEpiBox);
+                if constexpr (CONV)
+                    tma_load_4d(box, tr, &e.rbar[buf], col0, c1, c2, c3);
+                else
+                    tma_load_2d(box, tr, &e.rbar[buf], col0, c1);
+            }
+        }
+        named_barrier_sync<1, 128>();
+        uint32_t acc[32];
+        tmem_ld32(t_row + c, acc);
+        tmem_wait_ld();
+        if (active) {
+            float b[32];
+            load_bias32(a.bias, col0, b);
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                v[j] = __uint_as_float(acc[j]) + b[j];
+            if (a.addvec && row_ok) {
+                const float4* av =
+                    reinterpret_cast<const float4*>(a.addvec + long(row / a.seg_rows) * a.addvec_stride + col0);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 t = __ldg(av + j);
+                    v[4 * j] += t.x;
+                    v[4 * j + 1] += t.y;
+                    v[4 * j + 2] += t.z;
+                    v[4 * j + 3] += t.w;
+                }
+            }
+            if (a.out_mode == 3) {
+                // On a timed-out wait the box is added as it is; the status bit reports the failure.
+                mbar_wait(&e.rbar[buf], (e.rphase >> buf) & 1, status, kErrWaitEpiLoad, abort);
+                e.rphase ^= 1u << buf;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 t = *box_chunk(box, r, j);
+                    v[4 * j] += t.x;
+                    v[4 * j + 1] += t.y;
+                    v[4 * j + 2] += t.z;
+                    v[4 * j + 3] += t.w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                *box_chunk(box, r, j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+        }
+        named_barrier_sync<1, 128>();
+        if (e.issuer && active) {
+            if (a.out_mode == 2) {
+                if constexpr (CONV)
+                    tma_reduce_add_4d(to, box, col0, c1, c2, c3);
+                else
+                    tma_reduce_add_2d(to, box, col0, c1);
+            } else {
+                if constexpr (CONV)
+                    tma_store_4d(to, box, col0, c1, c2, c3);
+                else
+                    tma_store_2d(to, box, col0, c1);
+            }
+            bulk_commit();
+        }
+    }
+}
+
 // Problem and problem-local tile of a global tile index (problem 0's tiles first).
 __device__ __forceinline__ int gemm_problem(const GemmParams& P, int tile, int& local)
 {
@@ -384,15 +503,17 @@ __device__ __forceinline__ int gemm_problem(const GemmParams& P, int tile, int& 
 template <int BN, Epi EPI, bool CONV>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams P)
 {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, epi_staging(EPI)>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint8_t* staging = smem + C::kStages * C::kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::kStaging);
     uint64_t* empty = full + C::kStages;
     uint64_t* acc_full = empty + C::kStages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rbar = drain + 1;  // [2] residual boxes of the TMA epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -409,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 128);
+            mbar_init(&rbar[i], 1);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -510,6 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     } else {
         const int q = warp & 3;  // the TMEM lane quarter this warp may access
         uint32_t lt = 0;
+        EpiTma et;
+        et.boxes = staging;
+        et.rbar = rbar;
+        et.issuer = threadIdx.x == 64;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
             int local;
             const int p = gemm_problem(P, tile, local);
@@ -518,7 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
             int mb, nb;
             tile_coords(local, num_m, num_n, mb, nb);
             const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
-            if (!mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag))
+            const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
+            // The TMA epilogue synchronises its 128 threads: all of them leave together or none does.
+            if (EPI == Epi::kAdd && args.out_mode ? named_barrier_or<1, 128>(!got) : !got)
                 break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
@@ -527,14 +655,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                 int b, y0, x0;
                 conv_tile(args, mb, b, y0, x0);
                 const int y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
-                epilogue<BN, EPI>(args, t_row, (b * args.conv_ho + y) * args.conv_wo + x, y < args.conv_ho, nb * BN);
+                const int row = (b * args.conv_ho + y) * args.conv_wo + x;
+                const bool row_ok = b < args.conv_b && y < args.conv_ho;
+                if (EPI == Epi::kAdd && args.out_mode)
+                    epilogue_tma<BN, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
+                                           nb * BN, x0, y0, b, et, status, abort_flag);
+                else
+                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN);
             } else {
-                const int row = mb * kBM + r;
-                epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+                const int row0 = mb * kBM, row = row0 + r;
+                if (EPI == Epi::kAdd && args.out_mode)
+                    epilogue_tma<BN, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
+                                            nb * BN, row0, 0, 0, et, status, abort_flag);
+                else
+                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
         }
+        if (et.issuer)
+            bulk_wait_all();  // the last boxes' copies finish before the CTA (and its shared memory) goes
     }
 
     tc_fence_before();
@@ -555,16 +695,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
 template <int BN, Epi EPI, bool CONV>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2(const __grid_constant__ GemmParams P)
 {
-    using C = Cfg2<BN>;
+    using C = Cfg2<BN, epi_staging(EPI)>;
     constexpr int kPM = 2 * kBM;  // rows per pair tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint8_t* staging = smem + C::kStages * C::kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::kStaging);
     uint64_t* empty = full + C::kStages;
     uint64_t* acc_full = empty + C::kStages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rbar = drain + 1;  // [2] residual boxes of the TMA epilogue
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -585,6 +727,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 2 * 128);  // the epilogue threads of both CTAs (leader's barrier)
+            mbar_init(&rbar[i], 1);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -682,6 +825,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
         const int q = warp & 3;
         const uint32_t acc_empty_leader0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
         uint32_t lt = 0;
+        EpiTma et;
+        et.boxes = staging;
+        et.rbar = rbar;
+        et.issuer = threadIdx.x == 64;
         for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
             int local;
             const int p = gemm_problem(P, tile, local);
@@ -689,19 +836,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
             int mb, nb;
             tile_coords(local, num_m_of(args), (args.N + BN - 1) / BN, mb, nb);
             const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
-            if (!mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag))
+            const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
+            // The TMA epilogue synchronises its 128 threads: all of them leave together or none does.
+            if (EPI == Epi::kAdd && args.out_mode ? named_barrier_or<1, 128>(!got) : !got)
                 break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+            const int r = q * 32 + lane;
             if constexpr (CONV) {
                 int b, y0, x0;
                 conv_tile(args, 2 * mb + int(rank), b, y0, x0);
-                const int r = q * 32 + lane, y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
-                epilogue<BN, EPI>(args, t_row, (b * args.conv_ho + y) * args.conv_wo + x,
-                                  b < args.conv_b && y < args.conv_ho, nb * BN);
+                const int y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
+                const int row = (b * args.conv_ho + y) * args.conv_wo + x;
+                const bool row_ok = b < args.conv_b && y < args.conv_ho;
+                if (EPI == Epi::kAdd && args.out_mode)
+                    epilogue_tma<BN, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
+                                           nb * BN, x0, y0, b, et, status, abort_flag);
+                else
+                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN);
             } else {
-                const int row = mb * kPM + int(rank) * kBM + q * 32 + lane;
-                epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
+                const int row0 = mb * kPM + int(rank) * kBM, row = row0 + r;
+                if (EPI == Epi::kAdd && args.out_mode)
+                    epilogue_tma<BN, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
+                                            nb * BN, row0, 0, 0, et, status, abort_flag);
+                else
+                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN);
             }
             tc_fence_before();
             if (leader)
@@ -709,6 +868,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
             else
                 mbar_arrive_cluster(acc_empty_leader0 + acc * 8);
         }
+        if (et.issuer)
+            bulk_wait_all();  // the last boxes' copies finish before the CTA (and its shared memory) goes
     }
 
     tc_fence_before();
@@ -738,15 +899,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 template <int BN, Epi EPI, bool CONV>
 cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
 {
+    constexpr int kSmem = Cfg<BN, epi_staging(EPI)>::kSmem;
     static bool attr_set = false;
     if (!attr_set) {
         cudaError_t e =
-            cudaFuncSetAttribute(k_gemm<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
+            cudaFuncSetAttribute(k_gemm<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         if (e != cudaSuccess)
             return e;
         attr_set = true;
     }
-    launch_k(k_gemm<BN, EPI, CONV>, op.grid, kThreads, Cfg<BN>::kSmem, st, op.p);
+    launch_k(k_gemm<BN, EPI, CONV>, op.grid, kThreads, kSmem, st, op.p);
     count_launch();
     return cudaGetLastError();
 }
@@ -755,15 +917,16 @@ template <int BN, Epi EPI, bool CONV>
 cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
 {
     if constexpr (BN >= 128 && (BN / 2) % 16 == 0) {
+        constexpr int kSmem = Cfg2<BN, epi_staging(EPI)>::kSmem;
         static bool attr_set = false;
         if (!attr_set) {
             cudaError_t e = cudaFuncSetAttribute(k_gemm2<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 Cfg2<BN>::kSmem);
+                                                 kSmem);
             if (e != cudaSuccess)
                 return e;
             attr_set = true;
         }
-        launch_k(k_gemm2<BN, EPI, CONV>, op.grid, kThreads, Cfg2<BN>::kSmem, st, op.p);
+        launch_k(k_gemm2<BN, EPI, CONV>, op.grid, kThreads, kSmem, st, op.p);
         count_launch();
         return cudaGetLastError();
     }
@@ -873,6 +1036,68 @@ bool make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t
 
 namespace {
 
+bool tma_epilogue_enabled()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("MKB_TMA_EPI");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+bool make_tmap_f32(CUtensorMap* m, const void* ptr, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                   const cuuint32_t* box, const char** err)
+{
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cuuint32_t(rank), const_cast<void*>(ptr), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        *err = "gemm: output tensor map encoding failed";
+        return false;
+    }
+    return true;
+}
+
+// Chooses how a kAdd problem with fp32 output leaves the SM (GemmArgs::out_mode) and encodes its output and
+// residual boxes: 32 columns x the tile's 128 rows, or for a convolution 32 channels x tw x th pixels of one image
+// over the output viewed as [B][Ho][Wo][N]. Outputs TMA cannot address (unaligned) keep the per-thread stores.
+bool prepare_out_boxes(GemmParams& P, int prob, bool conv, const char** err)
+{
+    GemmArgs& a = P.a[prob];
+    a.out_mode = 0;
+    if (!tma_epilogue_enabled() || !a.out_f32 || !a.out)
+        return true;
+    if ((reinterpret_cast<uintptr_t>(a.out) & 15) || (a.ldo & 3) ||
+        (a.add_resid && ((reinterpret_cast<uintptr_t>(a.add_resid) & 15) || (a.ld_add_resid & 3))))
+        return true;
+    const int mode = !a.add_resid ? 1 : (a.add_resid == a.out && a.ld_add_resid == a.ldo) ? 2 : 3;
+    auto encode = [&](CUtensorMap* m, const void* ptr, long ld) {
+        const cuuint64_t row_bytes = cuuint64_t(ld) * 4;
+        if (conv) {
+            const cuuint64_t dims[4] = {cuuint64_t(a.N), cuuint64_t(a.conv_wo), cuuint64_t(a.conv_ho),
+                                        cuuint64_t(a.conv_b)};
+            const cuuint64_t strides[3] = {row_bytes, row_bytes * a.conv_wo, row_bytes * a.conv_wo * a.conv_ho};
+            const cuuint32_t box[4] = {32, cuuint32_t(a.conv_tw), cuuint32_t(a.conv_th), 1};
+            return make_tmap_f32(m, ptr, 4, dims, strides, box, err);
+        }
+        const cuuint64_t dims[2] = {cuuint64_t(a.N), cuuint64_t(a.M)};
+        const cuuint64_t strides[1] = {row_bytes};
+        const cuuint32_t box[2] = {32, cuuint32_t(kBM)};
+        return make_tmap_f32(m, ptr, 2, dims, strides, box, err);
+    };
+    if (!encode(&P.to[prob], a.out, a.ldo))
+        return false;
+    if (mode == 3 && !encode(&P.tr[prob], a.add_resid, a.ld_add_resid))
+        return false;
+    a.out_mode = mode;
+    return true;
+}
+
 // Checks of the epilogue arguments shared by the GEMM and the convolution.
 bool check_epilogue(Epi epi, const GemmArgs& args, int bn, const char** err)
 {
@@ -932,6 +1157,8 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
                            err))
         return false;
     op.p.a[0] = args;
+    if (epi == Epi::kAdd && !prepare_out_boxes(op.p, 0, false, err))
+        return false;
     op.p.nprob = 1;
     op.pair = false;
     op.w_ptr[0] = W;
@@ -964,6 +1191,8 @@ bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long l
         return false;
     op.p.a[1] = args;
     op.p.a[1].status = op.p.a[0].status;
+    if (op.epi == Epi::kAdd && !prepare_out_boxes(op.p, 1, false, err))
+        return false;
     op.p.nprob = 2;
     op.w_ptr[1] = W;
     op.ldw[1] = ldw;
@@ -1041,6 +1270,8 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     if (!make_tmap_bf16_2d(&op.p.tb[0], W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
         return false;
     op.p.a[0] = a;
+    if (epi == Epi::kAdd && !prepare_out_boxes(op.p, 0, true, err))
+        return false;
     op.p.nprob = 1;
     op.epi = epi;
     op.bn = bn;

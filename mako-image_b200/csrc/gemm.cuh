@@ -67,6 +67,10 @@ struct GemmArgs {
     const float* add_resid = nullptr;  // fp32 [row][col] rows ld_add_resid apart (may alias out)
     long ld_add_resid = 0;
     int out_f32 = 1;
+    // Set by the prepare functions: how a kAdd fp32 tile leaves the SM. 0: each epilogue thread stores its row;
+    // otherwise 32-column boxes staged in shared memory go out with TMA: 1 store, 2 reduce-add into out (the
+    // residual is out itself), 3 residual box loaded with TMA, added, stored.
+    int out_mode = 0;
     // 3x3 / 1x1 convolution as an implicit GEMM (k_gemm's conv mode): the A operand is the channels-last bf16
     // input [B][conv_hi][conv_wi][conv_c], the output pixel grid [B][conv_ho][conv_wo] is cut into tiles of
     // conv_th x conv_tw pixels (128 rows), and K = conv_taps * conv_c runs tap by tap.
@@ -80,6 +84,8 @@ struct GemmArgs {
 struct GemmParams {
     CUtensorMap ta[2];
     CUtensorMap tb[2];
+    CUtensorMap to[2];  // output boxes (out_mode != 0)
+    CUtensorMap tr[2];  // residual boxes (out_mode 3)
     GemmArgs a[2];
     int nprob = 1;
     int tiles0 = 0;

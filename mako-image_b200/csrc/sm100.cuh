@@ -19,6 +19,7 @@ enum : uint32_t {
     kErrWaitDrain = 1u << 4,     // final drain of in-flight copies / MMAs timed out
     kErrAttnWait = 1u << 5,      // attention pipeline wait timed out
     kErrShape = 1u << 6,         // a kernel was launched with a shape it does not support
+    kErrWaitEpiLoad = 1u << 7,   // GEMM epilogue gave up waiting for its residual box
 };
 
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far above any legitimate stage wait
@@ -130,6 +131,53 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
+
+// Shared -> global tensor copies, tracked as bulk groups of the issuing thread. The store writes the box; the
+// reduce adds it element-wise into global memory (the tensor map's element type). Boxes that reach past the
+// tensor's extent are clipped.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int c0, int c1)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const void* tmap, const void* src, int c0, int c1, int c2, int c3)
+{
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, const void* src, int c0, int c1)
+{
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, const void* src, int c0, int c1, int c2, int c3)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(tmap),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N of this thread's bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until all of this thread's bulk groups have completed (their global writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------- tcgen05
 
@@ -375,9 +423,24 @@ __device__ __forceinline__ uint32_t elect_one_lane()
     return (threadIdx.x & 31) == 0;
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int nthreads)
+// Named barriers take their id as an immediate, so ptxas reserves it for the kernel.
+template <int ID, int NTHREADS>
+__device__ __forceinline__ void named_barrier_sync()
 {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+    asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NTHREADS) : "memory");
+}
+
+// Named barrier that also returns the OR of every participating thread's `pred` (one uniform decision).
+template <int ID, int NTHREADS>
+__device__ __forceinline__ bool named_barrier_or(bool pred)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(uint32_t(pred)), "n"(ID), "n"(NTHREADS)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
