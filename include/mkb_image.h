@@ -106,6 +106,14 @@ mkb_status mkb_conv2d(const void* x, int B, int H, int W, int C, const void* w, 
                       const float* bias, const float* addvec, long addvec_stride, const float* resid, long ld_resid,
                       void* y, long ldy, int out_f32, void* stream);
 
+/* LayerNorm without weights, times (1 + scale), plus an optional shift, of `rows` rows of n floats; y is bf16 (the
+ * next projection's input). Row r's scale is mod[(r < split ? mod_stride : 0) + mod_off + i] and its shift, when
+ * shift is not null, shift at the same offset: the reference's ln_modulate (src/kernels/image.metal:33-53, ModArgs
+ * :23-30, dispatched by qwen_image.cpp:223, 276, 286), whose shift-less form is shift == NULL. n a multiple of 128,
+ * at most 4096; x, mod + mod_off and shift + mod_off 16-byte aligned, mod_stride a multiple of 4. */
+mkb_status mkb_ln_modulate(const float* x, const float* mod, const float* shift, void* y, long rows, int n, float eps,
+                           long split, long mod_stride, long mod_off, void* stream);
+
 /* GroupNorm of channels-last fp32 x [B][HW][C] (C / groups consecutive channels per group), y = norm * gamma + beta,
  * then SiLU if silu != 0, bf16 out. workspace: device scratch of mkb_group_norm_workspace_size() bytes. The
  * runtime's group_norm (sdxl.cpp:728-762, engine.cpp:722-730). */

@@ -7,6 +7,7 @@
 #include "rowops.cuh"
 #include "sm100.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
@@ -269,6 +270,30 @@ mkb_status mkb_conv2d(const void* x, int B, int H, int W, int C, const void* w, 
     if (t.pairs && !gemm_use_pairs(op, &err))
         return fail(MKB_ERR_INVALID, err ? err : "conv2d: pair set-up failed");
     return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "conv2d launch");
+}
+
+mkb_status mkb_ln_modulate(const float* x, const float* mod, const float* shift, void* y, long rows, int n, float eps,
+                           long split, long mod_stride, long mod_off, void* stream)
+{
+    if (!x || !mod || !y || rows < 0 || rows > (1L << 30) || n <= 0 || n % 128 || n > 4096)
+        return fail(MKB_ERR_INVALID, "ln_modulate: need rows >= 0 and n a multiple of 128 up to 4096");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(mod + mod_off) & 15) ||
+        (shift && (reinterpret_cast<uintptr_t>(shift + mod_off) & 15)) || (mod_stride & 3) ||
+        (reinterpret_cast<uintptr_t>(y) & 7))
+        return fail(MKB_ERR_INVALID, "ln_modulate: x, mod + mod_off, shift + mod_off need 16-byte alignment");
+    LnModArgs a{};
+    a.x = x;
+    a.y = static_cast<__nv_bfloat16*>(y);
+    a.scale = mod + mod_off;
+    a.shift = shift ? shift + mod_off : nullptr;
+    a.mod_stride = 0;
+    a.alt_off = mod_stride;  // rows before split read the second modulation row
+    a.split = int(std::min(std::max(split, 0L), rows));
+    a.rows = int(rows);
+    a.D = n;
+    a.rows_per_sample = rows > 0 ? int(rows) : 1;
+    a.eps = eps;
+    return cuda_status(ln_modulate(a, static_cast<cudaStream_t>(stream)), "ln_modulate");
 }
 
 size_t mkb_group_norm_workspace_size(int B, int HW, int C, int groups)

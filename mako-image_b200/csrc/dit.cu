@@ -900,24 +900,26 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
         if (q1) {
             const int Mt = B * St, Mi = B * Nl;
             const long mstride = long(NB) * 12 * D;
-            auto ln = [&](int sidx, int scale_off, int shift_off) -> cudaError_t {
-                if ((sidx == 0 ? Mt : Mi) == 0)
-                    return cudaSuccess;
-                const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
-                LnModArgs la{};
-                la.x = sidx == 0 ? x_txt : x_img;
-                la.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
-                la.scale = mb + scale_off * D;
-                la.shift = mb + shift_off * D;
-                la.mod_stride = mstride;
-                la.rows = sidx == 0 ? Mt : Mi;
-                la.D = D;
-                la.rows_per_sample = sidx == 0 ? S : Nl;
-                la.eps = kEps;
-                return ln_modulate(la, s);
+            // The text and image rows' modulated LayerNorms, one launch for both streams.
+            auto ln = [&](int scale_off, int shift_off) -> cudaError_t {
+                LnModArgs la[2];
+                for (int sidx = 0; sidx < 2; ++sidx) {
+                    const float* mb = mod + (size_t(i) * 2 + (sidx == 0 ? 1 : 0)) * 6 * D;
+                    LnModArgs& l = la[sidx];
+                    l = LnModArgs{};
+                    l.x = sidx == 0 ? x_txt : x_img;
+                    l.y = xn + (sidx == 0 ? 0 : size_t(Mt) * D);
+                    l.scale = mb + scale_off * D;
+                    l.shift = mb + shift_off * D;
+                    l.mod_stride = mstride;
+                    l.rows = sidx == 0 ? Mt : Mi;
+                    l.D = D;
+                    l.rows_per_sample = sidx == 0 ? S : Nl;
+                    l.eps = kEps;
+                }
+                return ln_modulate2(la[0], la[1], s);
             };
-            MKB_K(ln(0, 1, 0), "ln_modulate 1");
-            MKB_K(ln(1, 1, 0), "ln_modulate 1");
+            MKB_K(ln(1, 0), "ln_modulate 1");
             MKB_K(gemm_launch(o[0], s), "qkv");
             if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
                 const size_t count = size_t(2) * B * H * rw.shard * kHeadDim;
@@ -929,8 +931,7 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
             }
             MKB_K(attn_launch(plan->att, s), "attention");
             MKB_K(gemm_launch(o[1], s), "o proj");
-            MKB_K(ln(0, 4, 3), "ln_modulate 2");
-            MKB_K(ln(1, 4, 3), "ln_modulate 2");
+            MKB_K(ln(4, 3), "ln_modulate 2");
             MKB_K(gemm_launch(o[2], s), "ff1");
             MKB_K(gemm_launch(o[3], s), "ff2");
             if (probe) {

@@ -26,6 +26,8 @@ struct LnModArgs {
     int affine = 0;  // 1: y = norm * scale + shift (a plain LayerNorm with weight and bias)
 };
 cudaError_t ln_modulate(const LnModArgs& a, cudaStream_t st);
+// Both row sets (same D) in one launch.
+cudaError_t ln_modulate2(const LnModArgs& a, const LnModArgs& b, cudaStream_t st);
 
 // y[row] = x[row] / rms(x[row]) * w, fp32 in, bf16 out. Sample s's rows come from src[s] (rows_per_sample each).
 struct RmsArgs {

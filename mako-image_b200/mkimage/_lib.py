@@ -29,6 +29,7 @@ _SIGS = {
     "mkb_proj_heads": (_i, [_vp, _l, _vp, _l, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "mkb_proj_geglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),
     "mkb_conv2d": (_i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _i, _vp, _vp, _l, _vp, _l, _vp, _l, _i, _vp]),
+    "mkb_ln_modulate": (_i, [_vp, _vp, _vp, _vp, _l, _i, _f, _l, _l, _l, _vp]),
     "mkb_group_norm_workspace_size": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "mkb_group_norm": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp, ctypes.c_size_t, _vp]),
     "mkb_group_norm_static_max_bytes": (ctypes.c_size_t, []),

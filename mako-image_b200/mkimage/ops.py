@@ -151,6 +151,19 @@ def conv2d(x, w, taps=9, stride=1, bias=None, addvec=None, resid=None, out=None,
     return out
 
 
+def ln_modulate(x, mod, shift=None, eps=1e-6, split=0, mod_stride=0, mod_off=0, out=None):
+    """bf16 LayerNorm(x) * (1 + scale) (+ shift) of fp32 rows x [rows][n]; row r's scale is
+    mod.flatten()[(r < split ? mod_stride : 0) + mod_off + i] (see mkb_ln_modulate)."""
+    import torch
+
+    rows, n = x.shape
+    if out is None:
+        out = torch.empty(rows, n, device=x.device, dtype=torch.bfloat16)
+    check(lib.mkb_ln_modulate(_p(x), _p(mod), _p(shift), _p(out), rows, n, eps, split, mod_stride, mod_off,
+                              stream_ptr()))
+    return out
+
+
 def group_norm(x, gamma, beta, groups=32, eps=1e-5, silu=False, out=None):
     """x: fp32 channels-last [B][HW][C] (any shape with that memory order); returns bf16 of the same shape."""
     import torch
