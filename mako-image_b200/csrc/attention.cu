@@ -43,11 +43,13 @@ template <int HD>
 constexpr int kSmem = 1024 + 6 * kTileBytes<HD> + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-// Elements [kEmuFrom<HD>, 128) of each score row take 2^x from the FMA-pipe polynomial instead of the SFU. At head
-// dim 128 the SFU keeps up with the tensor pipe on its own; at 64 the MMAs are half as long and a quarter of the
-// exponentials moves to the FMA pipe.
+// Score pair i of every 16-pair chunk with i % kEmuEvery == kEmuEvery - 1 takes 2^x from the FMA pipe (the packed
+// two-lane polynomial) instead of the SFU; 0: none. At head dim 128 the SFU keeps up with the tensor pipe (moving
+// 1/8, 1/4 or 1/3 of the exponentials measured 2-6% slower). At 64 the MMAs are half as long and 1/8 moves, spread
+// through the row (162 us against 166 us at the 64^2 UNet shape for the same share as one block at the row's end,
+// 167 us for 1/4).
 template <int HD>
-constexpr int kEmuFrom = HD == 128 ? 128 : 112;
+constexpr int kEmuEvery = HD == 128 ? 0 : 8;
 // P published in two 64-key halves so P V of the first half starts while the second half's exponentials run: a
 // gain at head dim 64 (where P V of a tile is half as long), a loss at 128 (measured 440 -> 464 and 1057 -> 1012
 // TFLOP/s), so only there. Unsplit, the whole P is published on the second half's barrier.
@@ -61,19 +63,25 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-// 2^x on the FMA pipe: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted here for
-// least maximum relative error on that interval (7.5e-5, below bf16's 3.9e-3), 2^n added to the exponent bits.
-// Arguments below -126 flush to 0 like ex2.approx.ftz.
-__device__ __forceinline__ float ex2_poly(float x)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c);
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b);
+
+// 2^x for two lanes on the FMA pipe with packed f32x2 arithmetic: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f
+// by a degree-3 polynomial fitted here for least maximum relative error on that interval (7.5e-5, below bf16's
+// 3.9e-3), 2^n added to the exponent bits. Arguments below -126 flush to 0 like ex2.approx.ftz.
+__device__ __forceinline__ float2 ex2_poly2(float2 x)
 {
-    x = fmaxf(x, -126.0f);
-    const float t = x + 12582912.0f;  // 1.5 * 2^23: the rounded integer lands in the low mantissa bits
-    const int n = __float_as_int(t) - 0x4B400000;
-    const float f = x - (t - 12582912.0f);
-    float p = fmaf(0.055171459913253784f, f, 0.2426108568906784f);
-    p = fmaf(p, f, 0.6932609677314758f);
-    p = fmaf(p, f, 0.9999281167984009f);
-    return __int_as_float(__float_as_int(p) + (n << 23));
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
+    const float2 n = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+    float2 p = ffma2(make_float2(0.055171459913253784f, 0.055171459913253784f), f,
+                     make_float2(0.2426108568906784f, 0.2426108568906784f));
+    p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    p = ffma2(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + ((__float_as_int(t.x) - 0x4B400000) << 23)),
+                       __int_as_float(__float_as_int(p.y) + ((__float_as_int(t.y) - 0x4B400000) << 23)));
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c)
@@ -365,8 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int k = c * 32 + 2 * i;
                     const float2 x = ffma2(make_float2(__uint_as_float(s[k]), __uint_as_float(s[k + 1])), sc2, nm2);
                     float2 e;
-                    e.x = k >= kEmuFrom<HD> ? ex2_poly(x.x) : ex2(x.x);
-                    e.y = k + 1 >= kEmuFrom<HD> ? ex2_poly(x.y) : ex2(x.y);
+                    constexpr int kEvery = kEmuEvery<HD> ? kEmuEvery<HD> : 1 << 30;
+                    if (i % kEvery == kEvery - 1) {
+                        e = ex2_poly2(x);
+                    } else {
+                        e.x = ex2(x.x);
+                        e.y = ex2(x.y);
+                    }
                     ls[i & 3] = fadd2(ls[i & 3], e);
                     p[i] = pack_bf16x2(e.x, e.y);
                 }
