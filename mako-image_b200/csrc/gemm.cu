@@ -27,7 +27,8 @@ constexpr int kThreads = 192;
 // bias (at most 256 floats).
 constexpr int kEpiBox = 128 * 32 * 4;
 constexpr int kBiasBytes = 256 * 4;
-constexpr int epi_staging(Epi e) { return e == Epi::kAdd ? 2 * kEpiBox + kBiasBytes : 0; }
+constexpr bool epi_tma(Epi e) { return e == Epi::kAdd || e == Epi::kResid; }
+constexpr int epi_staging(Epi e) { return epi_tma(e) ? 2 * kEpiBox + kBiasBytes : 0; }
 
 // Stages: up to 8 within 200 KB, fewer where the epilogue's staging would not fit beside them in 227 KB.
 constexpr int stages_for(int stage_bytes, int staging)
@@ -197,7 +198,7 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
             if (!row_ok || col0 >= a.N)
                 continue;
             float b[32];
-            if constexpr (EPI == Epi::kAdd)
+            if constexpr (epi_tma(EPI))
                 load_bias32(sb, c, b);
             else
                 load_bias32g(a.bias, col0, b);
@@ -454,12 +455,14 @@ struct EpiTma {
     bool issuer = false;  // the one epilogue thread that issues the TMA copies
 };
 
-// The kAdd epilogue with fp32 output through TMA. Per 32-column chunk the 128 epilogue threads (one row each, r =
-// row within the tile) write acc + bias + addvec (+ the residual box, out_mode 3) into a staging box, then one
-// thread stores it (out_mode 1, 3) or reduce-adds it into out (out_mode 2: out is the residual). The box is the
-// tile's 128 rows: c1 the first row (2-D), or c1..c3 = x0, y0, image of a convolution's pixel tile. The sums are
-// those of the per-thread epilogue in the same order, so both paths give the same bits.
-template <int BN, bool CONV>
+// The fp32 epilogues through TMA. Per 32-column chunk the 128 epilogue threads (one row each, r = row within the
+// tile) write their row of a staging box, then one thread stores it (out_mode 1, 3) or reduce-adds it into the
+// output (out_mode 2: the output is the residual). kAdd writes acc + bias + addvec (+ the residual box, out_mode 3);
+// its sums are those of the per-thread epilogue in the same order, so both paths give the same bits. kResid writes
+// g * (acc + bias) with g the row's gate (tanh'd for tanh_gate), reduce-added into the residual stream: one rounding
+// more than the per-thread fused multiply-add. The box is the tile's 128 rows: c1 the first row (2-D), or c1..c3 =
+// x0, y0, image of a convolution's pixel tile.
+template <int BN, Epi EPI, bool CONV>
 __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMap* to, const CUtensorMap* tr,
                                              uint32_t t_row, int r, int row, bool row_ok, bool tile_ok, int n0,
                                              int c1, int c2, int c3, const float* sb, EpiTma& e,
@@ -492,7 +495,29 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMa
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 v[j] = __uint_as_float(acc[j]) + b[j];
-            if (a.addvec && row_ok) {
+            if constexpr (EPI == Epi::kResid) {
+                if (row_ok) {
+                    const int bsample = row / a.seg_rows;
+                    const int within = row - bsample * a.seg_rows;
+                    const float4* g4 = reinterpret_cast<const float4*>(
+                        a.gate + long(bsample) * a.gate_bstride + (within < a.gate_split ? a.gate_alt_off : 0) + col0);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float4 g = __ldg(g4 + j);
+                        if (a.tanh_gate) {
+                            g.x = tanh_fast(g.x);
+                            g.y = tanh_fast(g.y);
+                            g.z = tanh_fast(g.z);
+                            g.w = tanh_fast(g.w);
+                        }
+                        v[4 * j] *= g.x;
+                        v[4 * j + 1] *= g.y;
+                        v[4 * j + 2] *= g.z;
+                        v[4 * j + 3] *= g.w;
+                    }
+                }
+            }
+            if (EPI == Epi::kAdd && a.addvec && row_ok) {
                 const float4* av =
                     reinterpret_cast<const float4*>(a.addvec + long(row / a.seg_rows) * a.addvec_stride + col0);
 #pragma unroll
@@ -504,7 +529,7 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMa
                     v[4 * j + 3] += t.w;
                 }
             }
-            if (a.out_mode == 3) {
+            if (EPI == Epi::kAdd && a.out_mode == 3) {
                 // On a timed-out wait the box is added as it is; the status bit reports the failure.
                 mbar_wait(&e.rbar[buf], (e.rphase >> buf) & 1, status, kErrWaitEpiLoad, abort);
                 e.rphase ^= 1u << buf;
@@ -680,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         }
     } else {
         const int q = warp & 3;  // the TMEM lane quarter this warp may access
-        constexpr bool kStageBias = EPI == Epi::kAdd;
+        constexpr bool kStageBias = epi_tma(EPI);
         const int et_idx = int(threadIdx.x) - 64;
         BiasStage<BN> bias_next;
         uint32_t lt = 0;
@@ -722,15 +747,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                 const int y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
                 const int row = (b * args.conv_ho + y) * args.conv_wo + x;
                 const bool row_ok = b < args.conv_b && y < args.conv_ho;
-                if (EPI == Epi::kAdd && args.out_mode)
-                    epilogue_tma<BN, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
+                if (epi_tma(EPI) && args.out_mode)
+                    epilogue_tma<BN, EPI, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
                                            nb * BN, x0, y0, b, sb, et, status, abort_flag);
                 else
                     epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb);
             } else {
                 const int row0 = mb * kBM, row = row0 + r;
-                if (EPI == Epi::kAdd && args.out_mode)
-                    epilogue_tma<BN, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
+                if (epi_tma(EPI) && args.out_mode)
+                    epilogue_tma<BN, EPI, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
                                             nb * BN, row0, 0, 0, sb, et, status, abort_flag);
                 else
                     epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
@@ -896,7 +921,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
     } else {
         const int q = warp & 3;
         const uint32_t acc_empty_leader0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
-        constexpr bool kStageBias = EPI == Epi::kAdd;
+        constexpr bool kStageBias = epi_tma(EPI);
         const int et_idx = int(threadIdx.x) - 64;
         BiasStage<BN> bias_next;
         uint32_t lt = 0;
@@ -937,15 +962,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                 const int y = y0 + r / args.conv_tw, x = x0 + r % args.conv_tw;
                 const int row = (b * args.conv_ho + y) * args.conv_wo + x;
                 const bool row_ok = b < args.conv_b && y < args.conv_ho;
-                if (EPI == Epi::kAdd && args.out_mode)
-                    epilogue_tma<BN, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
+                if (epi_tma(EPI) && args.out_mode)
+                    epilogue_tma<BN, EPI, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
                                            nb * BN, x0, y0, b, sb, et, status, abort_flag);
                 else
                     epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb);
             } else {
                 const int row0 = mb * kPM + int(rank) * kBM, row = row0 + r;
-                if (EPI == Epi::kAdd && args.out_mode)
-                    epilogue_tma<BN, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
+                if (epi_tma(EPI) && args.out_mode)
+                    epilogue_tma<BN, EPI, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
                                             nb * BN, row0, 0, 0, sb, et, status, abort_flag);
                 else
                     epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
@@ -1160,10 +1185,21 @@ bool make_tmap_f32(CUtensorMap* m, const void* ptr, int rank, const cuuint64_t* 
 // Chooses how a kAdd problem with fp32 output leaves the SM (GemmArgs::out_mode) and encodes its output and
 // residual boxes: 32 columns x the tile's 128 rows, or for a convolution 32 channels x tw x th pixels of one image
 // over the output viewed as [B][Ho][Wo][N]. Outputs TMA cannot address (unaligned) keep the per-thread stores.
-bool prepare_out_boxes(GemmParams& P, int prob, bool conv, const char** err)
+bool prepare_out_boxes(GemmParams& P, int prob, Epi epi, bool conv, const char** err)
 {
     GemmArgs& a = P.a[prob];
     a.out_mode = 0;
+    if (epi == Epi::kResid) {  // the gated residual, always in place: reduce-add into resid
+        if (!tma_epilogue_enabled() || (reinterpret_cast<uintptr_t>(a.resid) & 15) || (a.ldr & 3) || conv)
+            return true;
+        const cuuint64_t dims[2] = {cuuint64_t(a.N), cuuint64_t(a.M)};
+        const cuuint64_t strides[1] = {cuuint64_t(a.ldr) * 4};
+        const cuuint32_t box[2] = {32, cuuint32_t(kBM)};
+        if (!make_tmap_f32(&P.to[prob], a.resid, 2, dims, strides, box, err))
+            return false;
+        a.out_mode = 2;
+        return true;
+    }
     if (!tma_epilogue_enabled() || !a.out_f32 || !a.out)
         return true;
     if ((reinterpret_cast<uintptr_t>(a.out) & 15) || (a.ldo & 3) ||
@@ -1251,7 +1287,7 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
                            err))
         return false;
     op.p.a[0] = args;
-    if (epi == Epi::kAdd && !prepare_out_boxes(op.p, 0, false, err))
+    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, false, err))
         return false;
     op.p.nprob = 1;
     op.pair = false;
@@ -1285,7 +1321,7 @@ bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long l
         return false;
     op.p.a[1] = args;
     op.p.a[1].status = op.p.a[0].status;
-    if (op.epi == Epi::kAdd && !prepare_out_boxes(op.p, 1, false, err))
+    if (epi_tma(op.epi) && !prepare_out_boxes(op.p, 1, op.epi, false, err))
         return false;
     op.p.nprob = 2;
     op.w_ptr[1] = W;
@@ -1364,7 +1400,7 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     if (!make_tmap_bf16_2d(&op.p.tb[0], W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
         return false;
     op.p.a[0] = a;
-    if (epi == Epi::kAdd && !prepare_out_boxes(op.p, 0, true, err))
+    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, true, err))
         return false;
     op.p.nprob = 1;
     op.epi = epi;

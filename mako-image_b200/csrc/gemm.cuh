@@ -67,9 +67,10 @@ struct GemmArgs {
     const float* add_resid = nullptr;  // fp32 [row][col] rows ld_add_resid apart (may alias out)
     long ld_add_resid = 0;
     int out_f32 = 1;
-    // Set by the prepare functions: how a kAdd fp32 tile leaves the SM. 0: each epilogue thread stores its row;
-    // otherwise 32-column boxes staged in shared memory go out with TMA: 1 store, 2 reduce-add into out (the
-    // residual is out itself), 3 residual box loaded with TMA, added, stored.
+    // Set by the prepare functions: how a kAdd fp32 or kResid tile leaves the SM. 0: each epilogue thread stores
+    // its row; otherwise 32-column boxes staged in shared memory go out with TMA: 1 store, 2 reduce-add into the
+    // output (the residual is the output itself; always so for kResid), 3 residual box loaded with TMA, added,
+    // stored.
     int out_mode = 0;
     // 3x3 / 1x1 convolution as an implicit GEMM (k_gemm's conv mode): the A operand is the channels-last bf16
     // input [B][conv_hi][conv_wi][conv_c], the output pixel grid [B][conv_ho][conv_wo] is cut into tiles of
