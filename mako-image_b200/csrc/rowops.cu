@@ -600,6 +600,60 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const float* s, __nv_bfloa
         o[i] = __float2bfloat16_rn(__expf(r[i] * scale - m) * inv);
 }
 
+// The same softmax with the row held in shared memory (n * 4 bytes, 512 threads): one read of s instead of three.
+// The scaled scores, then their exponentials, stay in shared memory between the passes.
+__global__ void __launch_bounds__(512) k_softmax_rows_smem(const float* s, __nv_bfloat16* p, int n, float scale)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    extern __shared__ float4 srow[];
+    __shared__ float red[16];
+    const float4* r = reinterpret_cast<const float4*>(s + long(blockIdx.x) * n);
+    const int n4 = n / 4, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v = r[i];
+        v.x *= scale;
+        v.y *= scale;
+        v.z *= scale;
+        v.w *= scale;
+        srow[i] = v;
+        m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+    for (int k = 16; k; k >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, k));
+    if (lane == 0)
+        red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < blockDim.x / 32; ++w)
+        m = fmaxf(m, red[w]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v = srow[i];
+        v.x = __expf(v.x - m);
+        v.y = __expf(v.y - m);
+        v.z = __expf(v.z - m);
+        v.w = __expf(v.w - m);
+        srow[i] = v;
+        sum += (v.x + v.y) + (v.z + v.w);
+    }
+    sum = warp_sum(sum);
+    if (lane == 0)
+        red[warp] = sum;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < blockDim.x / 32; ++w)
+        tot += red[w];
+    const float inv = 1.f / tot;
+    uint2* o = reinterpret_cast<uint2*>(p + long(blockIdx.x) * n);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = srow[i];
+        o[i] = pack4_bf16(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+    }
+}
+
 __global__ void k_transpose(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols)
 {
     grid_dep_wait();
@@ -875,6 +929,22 @@ cudaError_t to_rgba(const float* img, int Cs, float* rgba, long P, cudaStream_t 
 
 cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n, float scale, cudaStream_t st)
 {
+    // Rows of up to 24K floats (96 KB: two or more blocks per SM) are held in shared memory.
+    const size_t smem = size_t(n) * 4;
+    if (n % 4 == 0 && smem <= 96 * 1024 && !(reinterpret_cast<uintptr_t>(s) & 15) &&
+        !(reinterpret_cast<uintptr_t>(p) & 7)) {
+        static size_t smem_set = 0;
+        if (smem > 48 * 1024 && smem > smem_set) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(k_softmax_rows_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+            if (e != cudaSuccess)
+                return e;
+            smem_set = 96 * 1024;
+        }
+        launch_k(k_softmax_rows_smem, dim3(unsigned(rows)), 512, smem, st, s, p, n, scale);
+        count_launch();
+        return cudaGetLastError();
+    }
     launch_k(k_softmax_rows, dim3(unsigned(rows)), 256, 0, st, s, p, n, scale);
     count_launch();
     return cudaGetLastError();
