@@ -27,7 +27,7 @@ constexpr int kThreads = 192;
 // bias (at most 256 floats).
 constexpr int kEpiBox = 128 * 32 * 4;
 constexpr int kBiasBytes = 256 * 4;
-constexpr bool epi_tma(Epi e) { return e == Epi::kAdd || e == Epi::kResid; }
+constexpr bool epi_tma(Epi e) { return e == Epi::kAdd || e == Epi::kResid || e == Epi::kBF16; }
 constexpr int epi_staging(Epi e) { return epi_tma(e) ? 2 * kEpiBox + kBiasBytes : 0; }
 
 // Stages: up to 8 within 200 KB, fewer where the epilogue's staging would not fit beside them in 227 KB.
@@ -198,7 +198,7 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
             if (!row_ok || col0 >= a.N)
                 continue;
             float b[32];
-            if constexpr (epi_tma(EPI))
+            if constexpr (EPI == Epi::kAdd || EPI == Epi::kResid)
                 load_bias32(sb, c, b);
             else
                 load_bias32g(a.bias, col0, b);
@@ -468,6 +468,56 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMa
                                              int c1, int c2, int c3, const float* sb, EpiTma& e,
                                              uint32_t* status, volatile int* abort)
 {
+    if constexpr (EPI == Epi::kBF16) {
+        // bf16 output (out_mode 4): boxes of 64 columns (128 bytes a row), act(acc + bias) packed as the per-thread
+        // path packs it. Tile widths are multiples of 64, so a box never reaches into a neighbouring tile.
+        if constexpr (BN % 64 == 0 && !CONV) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 64, ++e.chunk) {
+                uint8_t* box = e.boxes + (e.chunk & 1) * kEpiBox;
+                const int col0 = n0 + c;
+                const bool active = tile_ok && col0 < a.N;
+                if (e.issuer)
+                    bulk_wait_read<1>();
+                named_barrier_sync<1, 128>();
+                uint32_t acc0[32], acc1[32];
+                tmem_ld32(t_row + c, acc0);
+                tmem_ld32(t_row + c + 32, acc1);
+                tmem_wait_ld();
+                if (active) {
+                    float b[32], v[32];
+                    uint32_t w[32];
+                    load_bias32(sb, c, b);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __uint_as_float(acc0[j]) + b[j];
+                    apply_act32(v, a.act);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                    load_bias32(sb, c + 32, b);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __uint_as_float(acc1[j]) + b[j];
+                    apply_act32(v, a.act);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        w[16 + j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<uint4*>(box_chunk(box, r, j)) =
+                            make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+                    fence_proxy_async_smem();
+                }
+                named_barrier_sync<1, 128>();
+                if (e.issuer && active) {
+                    tma_store_2d(to, box, col0, c1);
+                    bulk_commit();
+                }
+            }
+        }
+        return;
+    }
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32, ++e.chunk) {
         const uint32_t buf = e.chunk & 1;
@@ -705,7 +755,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         }
     } else {
         const int q = warp & 3;  // the TMEM lane quarter this warp may access
-        constexpr bool kStageBias = epi_tma(EPI);
+        // kAdd and kResid always stage the bias; kBF16 only for tiles that leave through TMA (out_mode 4).
+        constexpr bool kStageAlways = EPI == Epi::kAdd || EPI == Epi::kResid;
         const int et_idx = int(threadIdx.x) - 64;
         BiasStage<BN> bias_next;
         uint32_t lt = 0;
@@ -722,21 +773,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
             tile_coords(local, num_m, num_n, mb, nb);
             const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
             const float* sb = sbias;
-            if (kStageBias && lt == 0) {
+            const bool stage = epi_tma(EPI) && (kStageAlways || args.out_mode);
+            if (stage && lt == 0) {
                 bias_next.load(args, nb * BN, et_idx);
                 bias_next.store(sbias, et_idx);
             }
             const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
             // The staged bias and the TMA boxes synchronise the 128 epilogue threads: they leave together or not
             // at all.
-            if (kStageBias ? named_barrier_or<1, 128>(!got) : !got)
+            if (stage ? named_barrier_or<1, 128>(!got) : !got)
                 break;
-            const bool has_next = kStageBias && tile + int(gridDim.x) < num_tiles;
-            if (has_next) {  // the next tile's bias, in flight while this tile drains
+            bool has_next = false;
+            if (epi_tma(EPI) && tile + int(gridDim.x) < num_tiles) {  // the next tile's bias, in flight while this tile drains
                 int local2, mb2, nb2;
                 const GemmArgs& a2 = P.a[gemm_problem(P, tile + int(gridDim.x), local2)];
-                tile_coords(local2, gemm_num_m(a2, CONV), (a2.N + BN - 1) / BN, mb2, nb2);
-                bias_next.load(a2, nb2 * BN, et_idx);
+                has_next = kStageAlways || a2.out_mode;
+                if (has_next) {
+                    tile_coords(local2, gemm_num_m(a2, CONV), (a2.N + BN - 1) / BN, mb2, nb2);
+                    bias_next.load(a2, nb2 * BN, et_idx);
+                }
             }
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
@@ -761,8 +816,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                     epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
             }
             if (has_next) {
-                // The TMA boxes' last barrier already follows every read of the current copy.
-                if (!args.out_mode)
+                // The TMA boxes' last barrier already follows every read of the current copy; a per-thread tile
+                // that read it needs one.
+                if (!args.out_mode && kStageAlways)
                     named_barrier_sync<1, 128>();
                 bias_next.store(sbias, et_idx);
             }
@@ -921,7 +977,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
     } else {
         const int q = warp & 3;
         const uint32_t acc_empty_leader0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
-        constexpr bool kStageBias = epi_tma(EPI);
+        // kAdd and kResid always stage the bias; kBF16 only for tiles that leave through TMA (out_mode 4).
+        constexpr bool kStageAlways = EPI == Epi::kAdd || EPI == Epi::kResid;
         const int et_idx = int(threadIdx.x) - 64;
         BiasStage<BN> bias_next;
         uint32_t lt = 0;
@@ -937,21 +994,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
             tile_coords(local, num_m_of(args), (args.N + BN - 1) / BN, mb, nb);
             const uint32_t acc = lt & 1, acc_ph = (lt >> 1) & 1;
             const float* sb = sbias;
-            if (kStageBias && lt == 0) {
+            const bool stage = epi_tma(EPI) && (kStageAlways || args.out_mode);
+            if (stage && lt == 0) {
                 bias_next.load(args, nb * BN, et_idx);
                 bias_next.store(sbias, et_idx);
             }
             const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
             // The staged bias and the TMA boxes synchronise the 128 epilogue threads: they leave together or not
             // at all.
-            if (kStageBias ? named_barrier_or<1, 128>(!got) : !got)
+            if (stage ? named_barrier_or<1, 128>(!got) : !got)
                 break;
-            const bool has_next = kStageBias && tile + npairs < num_tiles;
-            if (has_next) {  // the next tile's bias, in flight while this tile drains
+            bool has_next = false;
+            if (epi_tma(EPI) && tile + npairs < num_tiles) {  // the next tile's bias, in flight while this tile drains
                 int local2, mb2, nb2;
                 const GemmArgs& a2 = P.a[gemm_problem(P, tile + npairs, local2)];
-                tile_coords(local2, num_m_of(a2), (a2.N + BN - 1) / BN, mb2, nb2);
-                bias_next.load(a2, nb2 * BN, et_idx);
+                has_next = kStageAlways || a2.out_mode;
+                if (has_next) {
+                    tile_coords(local2, num_m_of(a2), (a2.N + BN - 1) / BN, mb2, nb2);
+                    bias_next.load(a2, nb2 * BN, et_idx);
+                }
             }
             tc_fence_after();
             const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
@@ -976,8 +1037,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                     epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
             }
             if (has_next) {
-                // The TMA boxes' last barrier already follows every read of the current copy.
-                if (!args.out_mode)
+                // The TMA boxes' last barrier already follows every read of the current copy; a per-thread tile
+                // that read it needs one.
+                if (!args.out_mode && kStageAlways)
                     named_barrier_sync<1, 128>();
                 bias_next.store(sbias, et_idx);
             }
@@ -1185,7 +1247,7 @@ bool make_tmap_f32(CUtensorMap* m, const void* ptr, int rank, const cuuint64_t* 
 // Chooses how a kAdd problem with fp32 output leaves the SM (GemmArgs::out_mode) and encodes its output and
 // residual boxes: 32 columns x the tile's 128 rows, or for a convolution 32 channels x tw x th pixels of one image
 // over the output viewed as [B][Ho][Wo][N]. Outputs TMA cannot address (unaligned) keep the per-thread stores.
-bool prepare_out_boxes(GemmParams& P, int prob, Epi epi, bool conv, const char** err)
+bool prepare_out_boxes(GemmParams& P, int prob, Epi epi, int bn, bool conv, const char** err)
 {
     GemmArgs& a = P.a[prob];
     a.out_mode = 0;
@@ -1198,6 +1260,24 @@ bool prepare_out_boxes(GemmParams& P, int prob, Epi epi, bool conv, const char**
         if (!make_tmap_f32(&P.to[prob], a.resid, 2, dims, strides, box, err))
             return false;
         a.out_mode = 2;
+        return true;
+    }
+    if (epi == Epi::kBF16) {  // bf16 output: 64-column boxes, tile widths that are multiples of 64
+        if (!tma_epilogue_enabled() || conv || bn % 64 || !a.out || (reinterpret_cast<uintptr_t>(a.out) & 15) ||
+            (a.ldo & 7))
+            return true;
+        const cuuint64_t dims[2] = {cuuint64_t(a.N), cuuint64_t(a.M)};
+        const cuuint64_t strides[1] = {cuuint64_t(a.ldo) * 2};
+        const cuuint32_t box[2] = {64, cuuint32_t(kBM)};
+        auto fn = encode_fn();
+        const cuuint32_t es[2] = {1, 1};
+        if (!fn || fn(&P.to[prob], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.out, dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            *err = "gemm: output tensor map encoding failed";
+            return false;
+        }
+        a.out_mode = 4;
         return true;
     }
     if (!tma_epilogue_enabled() || !a.out_f32 || !a.out)
@@ -1287,7 +1367,7 @@ bool gemm_prepare(GemmOp& op, Epi epi, const void* X, long ldx, const void* W, l
                            err))
         return false;
     op.p.a[0] = args;
-    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, false, err))
+    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, bn, false, err))
         return false;
     op.p.nprob = 1;
     op.pair = false;
@@ -1321,7 +1401,7 @@ bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long l
         return false;
     op.p.a[1] = args;
     op.p.a[1].status = op.p.a[0].status;
-    if (epi_tma(op.epi) && !prepare_out_boxes(op.p, 1, op.epi, false, err))
+    if (epi_tma(op.epi) && !prepare_out_boxes(op.p, 1, op.epi, op.bn, false, err))
         return false;
     op.p.nprob = 2;
     op.w_ptr[1] = W;
@@ -1400,7 +1480,7 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     if (!make_tmap_bf16_2d(&op.p.tb[0], W, uint64_t(a.K), uint64_t(Cout), uint64_t(a.K) * 2, kBK, uint32_t(bn), err))
         return false;
     op.p.a[0] = a;
-    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, true, err))
+    if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, bn, true, err))
         return false;
     op.p.nprob = 1;
     op.epi = epi;

@@ -1,7 +1,7 @@
-"""The add epilogue's two output paths agree bit for bit: fp32 tiles staged in shared memory and written by TMA
-(a store, a reduce-add into an in-place residual, or a residual box loaded, added and stored) against per-thread
-row stores (MKB_TMA_EPI=0, in a child process), for GEMMs and convolutions on ragged shapes; and the outputs match
-the oracle (fp32 accumulation: max-abs <= 1e-3 of the output scale)."""
+"""The GEMM epilogues' two output paths agree bit for bit: tiles staged in shared memory and written by TMA (fp32:
+a store, a reduce-add into an in-place residual, or a residual box loaded, added and stored; bf16: a box store)
+against per-thread row stores (MKB_TMA_EPI=0, in a child process), for GEMMs, convolutions and GELU projections on
+ragged shapes; and the outputs match the oracle (fp32 outputs: max-abs <= 1e-3 of the output scale; bf16: 1e-2)."""
 
 import os
 import subprocess
@@ -39,7 +39,14 @@ def test_add_epilogue_oracle(cuda):
     got, _ = cases_mod.run(cuda)
     for kind, shape, d in cases_mod.inputs("cpu"):
         key = kind + "_" + "x".join(str(s) for s in shape)
-        x, w, b, av, r = (d[n].float().numpy() for n in ("x", "w", "b", "av", "r"))
+        x, w, b = (d[n].float().numpy() for n in ("x", "w", "b"))
+        av, r = (d[n].float().numpy() if n in d else None for n in ("av", "r"))
+        if kind == "proj":
+            ref = O.linear(x, w, b)
+            ref = 0.5 * ref * (1.0 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+            y = got[f"{key}_gelu"]
+            assert np.abs(y - ref).max() < 1e-2 * np.abs(ref).max() + 1e-2, key
+            continue
         if kind == "gemm":
             M = shape[0]
             rps = (M + 1) // 2
