@@ -333,8 +333,7 @@ __global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a, int chunk_px, 
         for (int q = q0; q < Q; q += Qb) {
             float mean[4] = {0.f, 0.f, 0.f, 0.f}, m2[4] = {0.f, 0.f, 0.f, 0.f};
             n = 0.f;
-            for (int p = r; p < np; p += Rb) {
-                const float4 v = xb[long(p) * Q + q];
+            auto update = [&](const float4 v) {
                 n += 1.f;
                 const float rn = 1.f / n;
                 const float xv[4] = {v.x, v.y, v.z, v.w};
@@ -344,7 +343,19 @@ __global__ void __launch_bounds__(256) k_gn_stats(const GnArgs a, int chunk_px, 
                     mean[k] += d * rn;
                     m2[k] += d * (xv[k] - mean[k]);
                 }
+            };
+            // Four pixels' loads issued before their (serial) updates: four loads in flight per thread.
+            int p = r;
+            for (; p + 3 * Rb < np; p += 4 * Rb) {
+                const float4 v0 = xb[long(p) * Q + q], v1 = xb[long(p + Rb) * Q + q];
+                const float4 v2 = xb[long(p + 2 * Rb) * Q + q], v3 = xb[long(p + 3 * Rb) * Q + q];
+                update(v0);
+                update(v1);
+                update(v2);
+                update(v3);
             }
+            for (; p < np; p += Rb)
+                update(xb[long(p) * Q + q]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 smean[r * a.C + 4 * q + k] = mean[k];
