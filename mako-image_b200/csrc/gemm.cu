@@ -4,7 +4,9 @@
 // shared-memory stages with TMA (128-byte swizzle); warp 1 issues tcgen05.mma 128xBNx16 into one of two tensor-memory
 // accumulators; warps 2-5 drain the other accumulator through the fused epilogue while the next tile accumulates.
 // tcgen05.ld's 32x32b shape gives each epilogue thread one output row, so row-wise epilogue maths (per-head RMSNorm,
-// RoPE pairs, SwiGLU pairs) needs no shuffles.
+// RoPE pairs, SwiGLU pairs) needs no shuffles. The add, gated-residual and plain bf16 epilogues hand their rows to
+// TMA instead of storing them thread by thread: each thread writes its row of a 128-byte-swizzled shared-memory box
+// and one thread issues a tensor store, or a reduce-add into the residual stream.
 #include "gemm.cuh"
 #include "sm100.cuh"
 #include "common.cuh"
