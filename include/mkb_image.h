@@ -127,9 +127,10 @@ mkb_status mkb_group_norm(const float* x, void* y, const float* gamma, const flo
  * buffer: code running while another component owns all device memory (a serving loop behind a caching allocator),
  * real-time paths that must not risk an allocation's latency or failure, and hosts that only pass in tensors they
  * already own. No counterpart in the reference (its runtime owns its scratch buffers).
- * Limits: sizes whose statistics need more than the built-in scratch (group_norm workspace size above
- * mkb_group_norm_static_max_bytes(), e.g. B * ceil(HW / 32) * groups * 12 bytes above ~4 MiB) are rejected with
- * MKB_ERR_INVALID. The first call on a device looks up the scratch's device address (once per device, with that
+ * Limits: sizes whose statistics need more than the built-in scratch (mkb_group_norm_workspace_size() above
+ * mkb_group_norm_static_max_bytes()) are rejected with MKB_ERR_INVALID. That size is B * nchunks * groups * 12 +
+ * B * groups * 8 bytes, with B * nchunks about 1184 (eight statistics chunks per SM) for large images and
+ * B * ceil(HW / 16) for small ones: about groups * 14 KB, so up to roughly 290 groups fit whatever the image size. The first call on a device looks up the scratch's device address (once per device, with that
  * device current); make that first call before any stream capture. All calls on a device share the one scratch
  * array and it keeps the last call's contents (nothing in it needs clearing: each call writes every entry it reads
  * first), so calls that overlap on the GPU (different streams, or threads) race; serialise them. */
