@@ -450,12 +450,47 @@ __device__ __forceinline__ float4* box_chunk(uint8_t* box, int r, int j)
 
 // State of the TMA epilogue across the tiles of one CTA.
 struct EpiTma {
-    uint8_t* boxes;       // two kEpiBox boxes
-    uint64_t* rbar;       // [2] residual-box barriers
-    uint32_t chunk = 0;   // chunks issued so far: chunk & 1 is the box in use
-    uint32_t rphase = 0;  // parity bit per box of its residual barrier
-    bool issuer = false;  // the one epilogue thread that issues the TMA copies
+    uint8_t* boxes;         // two kEpiBox boxes
+    uint64_t* rbar;         // [2] residual-box barriers
+    uint32_t chunk = 0;     // chunks issued so far: chunk & 1 is the box in use
+    uint32_t rphase = 0;    // parity bit per box of its residual barrier
+    uint32_t rpending = 0;  // (issuer) bit per box: a residual load for a coming chunk is in flight
+    bool issuer = false;    // the one epilogue thread that issues the TMA copies
 };
+
+// (issuer, out_mode 3) Loads the residual box of tile columns [col0, col0 + 32) into box `b`.
+template <bool CONV>
+__device__ __forceinline__ void epi_load_resid(EpiTma& e, const CUtensorMap* tr, int b, int col0, int c1, int c2,
+                                               int c3)
+{
+    uint8_t* box = e.boxes + b * kEpiBox;
+    mbar_arrive_expect_tx(&e.rbar[b], kEpiBox);
+    if constexpr (CONV)
+        tma_load_4d(box, tr, &e.rbar[b], col0, c1, c2, c3);
+    else
+        tma_load_2d(box, tr, &e.rbar[b], col0, c1);
+    e.rpending |= 1u << b;
+}
+
+// (issuer) Before a tile's accumulator is ready: starts the load of its first residual box, so the epilogue does
+// not begin with an L2 round trip. The box is free once at most one store (the previous chunk's) still reads.
+template <bool CONV>
+__device__ __forceinline__ void epi_prefetch_tile(EpiTma& e, const GemmArgs& a, const CUtensorMap* tr, int n0,
+                                                  bool tile_ok, int c1, int c2, int c3)
+{
+    if (a.out_mode != 3 || !tile_ok || n0 >= a.N)
+        return;
+    bulk_wait_read<1>();
+    epi_load_resid<CONV>(e, tr, int(e.chunk & 1), n0, c1, c2, c3);
+}
+
+// (issuer) After an early exit: lets residual loads still in flight land before the CTA's shared memory goes.
+__device__ __forceinline__ void epi_drain_resid(EpiTma& e, uint32_t* status)
+{
+    for (int b = 0; b < 2; ++b)
+        if (e.rpending >> b & 1)
+            mbar_wait(&e.rbar[b], (e.rphase >> b) & 1, status, kErrWaitDrain, nullptr);
+}
 
 // The fp32 epilogues through TMA. Per 32-column chunk the 128 epilogue threads (one row each, r = row within the
 // tile) write their row of a staging box, then one thread stores it (out_mode 1, 3) or reduce-adds it into the
@@ -530,12 +565,16 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMa
         const bool active = tile_ok && col0 < a.N;  // the same in every epilogue thread
         if (e.issuer) {
             bulk_wait_read<1>();  // the copy issued from this box two chunks ago has read it
-            if (active && a.out_mode == 3) {
-                mbar_arrive_expect_tx(&e.rbar[buf], kEpiBox);
-                if constexpr (CONV)
-                    tma_load_4d(box, tr, &e.rbar[buf], col0, c1, c2, c3);
-                else
-                    tma_load_2d(box, tr, &e.rbar[buf], col0, c1);
+            if (EPI == Epi::kAdd && a.out_mode == 3) {
+                if (active && !(e.rpending >> buf & 1))  // not prefetched
+                    epi_load_resid<CONV>(e, tr, int(buf), col0, c1, c2, c3);
+                e.rpending &= ~(1u << buf);
+                // The next chunk's residual into the other box, once the previous chunk's store has read it: its
+                // round trip overlaps this chunk.
+                if (tile_ok && c + 32 < BN && col0 + 32 < a.N) {
+                    bulk_wait_read<0>();
+                    epi_load_resid<CONV>(e, tr, int(buf ^ 1), col0 + 32, c1, c2, c3);
+                }
             }
         }
         named_barrier_sync<1, 128>();
@@ -782,6 +821,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                 bias_next.load(args, nb * BN, et_idx);
                 bias_next.store(sbias, et_idx);
             }
+            if (EPI == Epi::kAdd && et.issuer && args.out_mode == 3) {  // first residual box, during the mainloop
+                if constexpr (CONV) {
+                    int pb, py0, px0;
+                    conv_tile(args, mb, pb, py0, px0);
+                    epi_prefetch_tile<true>(et, args, &P.tr[p], nb * BN, pb < args.conv_b, px0, py0, pb);
+                } else {
+                    const int prow0 = mb * kBM;
+                    epi_prefetch_tile<false>(et, args, &P.tr[p], nb * BN, prow0 < args.M, prow0, 0, 0);
+                }
+            }
             const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
             // The staged bias and the TMA boxes synchronise the 128 epilogue threads: they leave together or not
             // at all.
@@ -829,8 +878,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
         }
-        if (et.issuer)
-            bulk_wait_all();  // the last boxes' copies finish before the CTA (and its shared memory) goes
+        if (et.issuer) {
+            epi_drain_resid(et, status);  // residual loads of a tile left early
+            bulk_wait_all();              // the last boxes' copies finish before the CTA (and its shared memory) goes
+        }
     }
 
     tc_fence_before();
@@ -1003,6 +1054,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                 bias_next.load(args, nb * BN, et_idx);
                 bias_next.store(sbias, et_idx);
             }
+            if (EPI == Epi::kAdd && et.issuer && args.out_mode == 3) {  // first residual box, during the mainloop
+                if constexpr (CONV) {
+                    int pb, py0, px0;
+                    conv_tile(args, 2 * mb + int(rank), pb, py0, px0);
+                    epi_prefetch_tile<true>(et, args, &P.tr[p], nb * BN, pb < args.conv_b, px0, py0, pb);
+                } else {
+                    const int prow0 = mb * kPM + int(rank) * kBM;
+                    epi_prefetch_tile<false>(et, args, &P.tr[p], nb * BN, prow0 < args.M, prow0, 0, 0);
+                }
+            }
             const bool got = mbar_wait(&acc_full[acc], acc_ph, status, kErrWaitAccFull, abort_flag);
             // The staged bias and the TMA boxes synchronise the 128 epilogue threads: they leave together or not
             // at all.
@@ -1053,8 +1114,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
             else
                 mbar_arrive_cluster(acc_empty_leader0 + acc * 8);
         }
-        if (et.issuer)
-            bulk_wait_all();  // the last boxes' copies finish before the CTA (and its shared memory) goes
+        if (et.issuer) {
+            epi_drain_resid(et, status);  // residual loads of a tile left early
+            bulk_wait_all();              // the last boxes' copies finish before the CTA (and its shared memory) goes
+        }
     }
 
     tc_fence_before();
