@@ -574,7 +574,7 @@ def run_sdxl(args, which):
 def run_kernel(args, cfg):
     """One hot kernel alone at the config's shape, for profiling: 3 warm-up launches then 3 timed ones (CUDA
     events). gemm: the FFN-up projection (GELU epilogue); attention: the joint flash attention of one block;
-    lnmod: the modulated LayerNorm of the image rows."""
+    oproj: the image rows' O-projection with the gated residual (TMA reduce-add into the fp32 residual stream)."""
     import torch
     import mkimage
 
@@ -591,6 +591,14 @@ def run_kernel(args, cfg):
         y = torch.empty(B * N, F, device=dev, dtype=torch.bfloat16)
         fn = lambda: mkimage.ops.proj(x, wt, b, act=mkimage.ops.ACT_GELU_TANH, out=y)  # noqa: E731
         work, unit = 2.0 * B * N * F * D, "TFLOP/s"
+    elif args.kernel == "oproj":
+        x = torch.randn(B * N, D, device=dev, generator=g).to(torch.bfloat16)
+        wt = (torch.randn(D, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        b = torch.zeros(D, device=dev)
+        resid = torch.randn(B * N, D, device=dev, generator=g)
+        gate = torch.randn(B, D, device=dev, generator=g) * 0.1
+        fn = lambda: mkimage.ops.proj_gate_add(x, wt, resid, gate, bias=b, rows_per_sample=N)  # noqa: E731
+        work, unit = 2.0 * B * N * D * D, "TFLOP/s"
     elif args.kernel == "attention":
         q = torch.randn(B, H, L, 128, device=dev, generator=g).to(torch.bfloat16)
         k, v = torch.randn_like(q), torch.randn_like(q)
@@ -625,7 +633,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sp", action="store_true",
                     help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
-    ap.add_argument("--kernel", choices=["gemm", "attention"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "oproj", "attention"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
