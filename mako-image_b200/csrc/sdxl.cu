@@ -43,8 +43,10 @@ uint64_t mix64(uint64_t x)
 //   mat    bf16 [r][c] -> [rp][cp]               (zero rows / columns beyond r / c)
 //   conv3  bf16 [r][3][3][c] -> [rp][9][cp]      (3x3 convolution, tap-major, input channels padded)
 //   glu    bf16 [r][c], r = 2F (first half / second half) -> rows interleaved in blocks of 128 for the GLU epilogue
+//   gluvec fp32 [r], the bias of a glu matrix, interleaved the same way (the GLU epilogue reads bias by device column)
 struct WTable {
-    enum Kind { kVec, kMat, kConv3, kGlu };
+    enum Kind { kVec, kMat, kConv3, kGlu, kGluVec };
+    static bool is_vec(Kind k) { return k == kVec || k == kGluVec; }
     struct W {
         std::string name;
         Kind kind;
@@ -53,7 +55,7 @@ struct WTable {
         bool norm;
         size_t dev_count() const
         {
-            return kind == kVec ? size_t(rp) : kind == kConv3 ? size_t(rp) * 9 * cp : size_t(rp) * cp;
+            return is_vec(kind) ? size_t(rp) : kind == kConv3 ? size_t(rp) * 9 * cp : size_t(rp) * cp;
         }
     };
     std::vector<W> ws;
@@ -65,7 +67,7 @@ struct WTable {
     void add(const std::string& name, Kind k, long r, long c = 0, long rp = 0, long cp = 0, bool norm = false)
     {
         W w{name, k, r, c, rp ? rp : r, cp ? cp : c, 0, norm};
-        if (k == kVec) {
+        if (is_vec(k)) {
             w.rp = (w.rp + 3) & ~3L;
             w.off = nvec;
             nvec += w.dev_count();
@@ -122,7 +124,7 @@ struct WTable {
             const W& w = ws[i];
             const uint64_t key = mix64(seed * 0x100000001B3ull + i);
             const float sd = w.norm ? 0.1f : std, mean = w.norm ? 1.0f : 0.0f;
-            if (w.kind == kVec) {
+            if (is_vec(w.kind)) {
                 MKB_TRY_CUDA(fill_normal(vec + w.off, false, w.r, key, 0, sd, mean, s), "init");
                 continue;
             }
@@ -151,6 +153,13 @@ struct WTable {
             MKB_TRY_CUDA(cudaMemcpy(host, vec + w->off, w->r * 4, cudaMemcpyDeviceToHost), "weight read");
             return MKB_OK;
         }
+        if (w->kind == kGluVec) {
+            std::vector<float> t(w->r);
+            MKB_TRY_CUDA(cudaMemcpy(t.data(), vec + w->off, w->r * 4, cudaMemcpyDeviceToHost), "weight read");
+            for (long i = 0; i < w->r; ++i)
+                host[i] = t[glu_row(i, w->r)];
+            return MKB_OK;
+        }
         std::vector<__nv_bfloat16> t(w->dev_count());
         MKB_TRY_CUDA(cudaMemcpy(t.data(), mat + w->off, t.size() * 2, cudaMemcpyDeviceToHost), "weight read");
         const long taps = w->kind == kConv3 ? 9 : 1;
@@ -169,6 +178,13 @@ struct WTable {
             return fail(MKB_ERR_INVALID, "weight_write: unknown weight " + name);
         if (w->kind == kVec) {
             MKB_TRY_CUDA(cudaMemcpy(vec + w->off, host, w->r * 4, cudaMemcpyHostToDevice), "weight write");
+            return MKB_OK;
+        }
+        if (w->kind == kGluVec) {
+            std::vector<float> t(w->r);
+            for (long i = 0; i < w->r; ++i)
+                t[glu_row(i, w->r)] = host[i];
+            MKB_TRY_CUDA(cudaMemcpy(vec + w->off, t.data(), w->r * 4, cudaMemcpyHostToDevice), "weight write");
             return MKB_OK;
         }
         std::vector<__nv_bfloat16> t(w->dev_count(), __float2bfloat16_rn(0.f));
@@ -191,7 +207,7 @@ struct WTable {
             *name = w.name.c_str();
         int n = 0;
         long d[4] = {w.r, 0, 0, 0};
-        if (w.kind == kVec)
+        if (is_vec(w.kind))
             n = 1;
         else if (w.kind == kConv3) {
             d[1] = 3, d[2] = 3, d[3] = w.c;
@@ -239,6 +255,7 @@ struct Plan {
     {
         void* p = nullptr;
         if (cudaMalloc(&p, count * sizeof(T) + 256) != cudaSuccess) {
+            cudaGetLastError();  // not sticky: keep it out of later launch checks
             *st = fail(MKB_ERR_ALLOC, "sdxl plan: device allocation failed");
             return nullptr;
         }
@@ -570,7 +587,7 @@ mkb_status UnetImpl::create(const mkb_unet_config& c)
                 W.add(p + "ln3.w", WTable::kVec, cc, 0, 0, 0, true);
                 W.add(p + "ln3.b", WTable::kVec, cc);
                 W.add(p + "ff1.w", WTable::kGlu, 8 * cc, cc);
-                W.add(p + "ff1.b", WTable::kVec, 8 * cc);
+                W.add(p + "ff1.b", WTable::kGluVec, 8 * cc);
                 W.add(p + "ff2.w", WTable::kMat, cc, 4 * cc);
                 W.add(p + "ff2.b", WTable::kVec, cc);
             }

@@ -62,6 +62,29 @@ def test_unet_step_reduced(cuda):
     assert np.abs(e1 - eps[1]).max() <= 1e-5 * max(1.0, np.abs(eps[1]).max())
 
 
+def test_unet_geglu_bias_order(cuda):
+    """The GEGLU projection's bias follows its rows into the interleaved device layout: with unit-scale ff1 biases
+    (the random init's 0.02 hides a misplaced bias) the step still matches the oracle."""
+    import mkimage
+
+    cfg = dict(channels=(64, 128, 256), depth=(0, 1, 2), layers=1, context_dim=256, pooled_dim=128)
+    gh, gw, S = 8, 16, 77
+    u = mkimage.Unet(mkimage.UnetConfig(max_batch=1, max_gh=gh, max_gw=gw, max_context=S, slots=1, **cfg))
+    u.init_random(19)
+    for i, (name, shape) in enumerate(u.weight_names()):
+        if name.endswith(".ff1.b"):
+            u.write_weight(name, rng.normal(rng.tensor_key(6, i), shape[0]))
+    W = u.weights()
+    ctx = rng.normal(rng.tensor_key(6, 1000), S * 256).reshape(S, 256)
+    pooled = rng.normal(rng.tensor_key(6, 1001), 128)
+    lat = rng.normal(rng.tensor_key(6, 1002), gh * gw * 16).reshape(gh * gw, 16)
+    u.begin(ctx, pooled, gh, gw, slot=0)
+    eps = u.step(lat, 3.0, slot=0)
+    oc = OS.unet_default_cfg(**cfg)
+    ref = OS.unet_step(oc, W, OS.unet_begin(oc, W, ctx, pooled, gh, gw), lat, 3.0)
+    assert _rel(eps, ref) < 0.02 and _cos(eps, ref) >= 0.999, (_rel(eps, ref), _cos(eps, ref))
+
+
 def test_vae_decode_reduced(cuda):
     import mkimage
 
