@@ -131,7 +131,8 @@ mkb_status mkb_group_norm(const float* x, void* y, const float* gamma, const flo
  * mkb_group_norm_static_max_bytes()) are rejected with MKB_ERR_INVALID. That size is B * nchunks * groups * 12 +
  * B * groups * 8 bytes, with B * nchunks about 1184 (eight statistics chunks per SM) for large images and
  * B * ceil(HW / 16) for small ones: about groups * 14 KB, so up to roughly 290 groups fit whatever the image size. The first call on a device looks up the scratch's device address (once per device, with that
- * device current); make that first call before any stream capture. All calls on a device share the one scratch
+ * device current); make that first call before any stream capture. That address is kept for the life of the
+ * process, so do not call this entry point on a device after cudaDeviceReset of it. All calls on a device share the one scratch
  * array and it keeps the last call's contents (nothing in it needs clearing: each call writes every entry it reads
  * first), so calls that overlap on the GPU (different streams, or threads) race; serialise them. */
 size_t mkb_group_norm_static_max_bytes(void);
@@ -287,7 +288,9 @@ mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user);
  * world, (S + N) / world a multiple of 128 and larger than S. Results equal the one-GPU step bit for bit.
  * mkb_nccl_unique_id makes the communicator id on one rank (MKB_NCCL_ID_BYTES bytes, to be sent to the others);
  * every rank then calls mkb_dit_set_sequence_parallel with it, collectively, after create and before begin. NCCL is
- * loaded at run time (libnccl.so.2). */
+ * loaded at run time: the process's libnccl.so.2, or the library the environment variable MKB_NCCL_LIB names. If the
+ * communicator cannot be made (MKB_ERR_CUDA) or its buffers not allocated (MKB_ERR_ALLOC), the handle is left as it
+ * was, single-GPU and usable. */
 #define MKB_NCCL_ID_BYTES 128
 mkb_status mkb_nccl_unique_id(void* out, size_t bytes);
 mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int rank, int world);
@@ -452,6 +455,17 @@ double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw);
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */
 mkb_status mkb_check_kernels(uint32_t* bits);
+
+/* Failure-path self-test of the bounded waits (no counterpart in the reference, whose Metal command buffers have no
+ * kernel-side timeouts). Launches the fp32-output projection of mkb_proj (y = x * w^T, tile width 128, one CTA per
+ * SM) with the first shared-memory stage of CTA 0 never loaded: that CTA's MMA warp waits for it until its 2 s
+ * limit, marks the status word and the CTA's abort flag, every role drains what it issued (another bounded wait on
+ * the withheld stage) and the kernel returns after about 4 s. The other CTAs finish their tiles normally; y is left
+ * incomplete. Afterwards mkb_check_kernels returns MKB_ERR_KERNEL with bit 0 (a stage that never filled) or bit 1
+ * (a stage never released: the producer's own wait, whichever gives up first) and bit 4 (the drain of the withheld
+ * load) set, and the context stays usable. For tests of error detection; nothing else calls it. */
+mkb_status mkb_selftest_stalled_gemm(const void* x, long ldx, const void* w, long ldw, float* y, long ldy, int M,
+                                     int N, int K, void* stream);
 
 #ifdef __cplusplus
 }

@@ -44,6 +44,9 @@ mkb_status cuda_status(cudaError_t e, const char* what)
 {
     if (e == cudaSuccess)
         return MKB_OK;
+    // The error is reported here; clear the thread's last-error state so a later launch check does not report a
+    // non-sticky one (a failed allocation) a second time.
+    cudaGetLastError();
     return fail(e == cudaErrorMemoryAllocation ? MKB_ERR_ALLOC : MKB_ERR_CUDA,
                 std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -58,8 +61,10 @@ uint32_t* device_status_word()
         g_status_words.resize(dev + 1, nullptr);
     if (!g_status_words[dev]) {
         uint32_t* p = nullptr;
-        if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess)
+        if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess) {
+            cudaGetLastError();
             return nullptr;
+        }
         cudaMemset(p, 0, sizeof(uint32_t));
         g_status_words[dev] = p;
     }
@@ -357,6 +362,26 @@ mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const voi
     if (!attn_prepare(op, q, Lq_rows, k, v, Lk_rows, a, &err))
         return fail(MKB_ERR_INVALID, err ? err : "attention: unsupported arguments");
     return cuda_status(attn_launch(op, static_cast<cudaStream_t>(stream)), "attention launch");
+}
+
+mkb_status mkb_selftest_stalled_gemm(const void* x, long ldx, const void* w, long ldw, float* y, long ldy, int M,
+                                     int N, int K, void* stream)
+{
+    if (!x || !w || !y)
+        return fail(MKB_ERR_INVALID, "selftest: null operand");
+    GemmArgs a;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.out = y;
+    a.ldo = ldy;
+    a.status = device_status_word();
+    GemmOp op;
+    const char* err = nullptr;
+    if (!gemm_prepare(op, Epi::kF32, x, ldx, w, ldw, a, 128, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "selftest: unsupported arguments");
+    op.p.test_stall = 1;  // the 1-CTA kernel: CTA 0 withholds its first stage's load
+    return cuda_status(gemm_launch(op, static_cast<cudaStream_t>(stream)), "selftest launch");
 }
 
 mkb_status mkb_check_kernels(uint32_t* bits)

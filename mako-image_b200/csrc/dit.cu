@@ -233,6 +233,15 @@ mkb_status DitImpl::set_sp(const void* id, int rank, int world)
     if (!api)
         return fail(MKB_ERR_CUDA, "sequence parallel: " + err);
     sp_lg_max = ((Lmax + world - 1) / world + 127) / 128 * 128;
+    // On any failure below the handle stays as it was: the exchange buffers are released again.
+    auto release = [&] {
+        for (void** p : {reinterpret_cast<void**>(&kv_all), reinterpret_cast<void**>(&vel_x),
+                         reinterpret_cast<void**>(&vel_full)}) {
+            if (*p)
+                cudaFree(*p);
+            *p = nullptr;
+        }
+    };
     const size_t B = Bmax;
     const size_t kv = size_t(world) * 2 * B * H * sp_lg_max * kHeadDim * 2;
     const size_t vx = size_t(world) * B * sp_lg_max * kLatent * 4, vf = B * size_t(Nmax) * kLatent * 4;
@@ -240,16 +249,21 @@ mkb_status DitImpl::set_sp(const void* id, int rank, int world)
                                   {reinterpret_cast<void**>(&vel_x), vx, "velocity exchange"},
                                   {reinterpret_cast<void**>(&vel_full), vf, "velocities"}}) {
         cudaError_t e = cudaMalloc(p, bytes);
-        if (e != cudaSuccess)
+        if (e != cudaSuccess) {
+            cudaGetLastError();  // not sticky: keep it out of later launch checks
+            release();
             return fail(MKB_ERR_ALLOC, std::string("sequence parallel: allocating ") + what + ": " +
                                            cudaGetErrorString(e));
+        }
     }
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     ncclComm_t comm = nullptr;
     const ncclResult_t r = api->CommInitRank(&comm, world, uid, rank);
-    if (r != ncclSuccess)
+    if (r != ncclSuccess) {
+        release();
         return fail(MKB_ERR_CUDA, std::string("sequence parallel: ncclCommInitRank: ") + api->GetErrorString(r));
+    }
     sp_comm = comm;
     sp_world = world;
     sp_rank = rank;
@@ -366,8 +380,10 @@ mkb_status DitImpl::create(const mkb_dit_config& c)
         return fail(MKB_ERR_CUDA, "status word");
     auto alloc = [&](void** p, size_t bytes, const char* what) -> mkb_status {
         cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
-        if (e != cudaSuccess)
+        if (e != cudaSuccess) {
+            cudaGetLastError();  // not sticky: keep it out of later launch checks
             return fail(MKB_ERR_ALLOC, std::string("dit: allocating ") + what + ": " + cudaGetErrorString(e));
+        }
         return MKB_OK;
     };
 #define MKB_ALLOC(ptr, bytes)                                                                                          \

@@ -744,6 +744,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                     }
                     uint8_t* sa = smem + s * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+                    if (P.test_stall && it == 0 && blockIdx.x == 0)
+                        continue;  // the stage's bytes never arrive: full[0] cannot complete (failure-path test)
                     if constexpr (CONV) {
                         tma_load_4d(sa, &P.ta[p], &full[s], cw.c0, cw.x, cw.y, cw.b);
                         cw.next(args);
@@ -1148,14 +1150,10 @@ template <int BN, Epi EPI, bool CONV>
 cudaError_t launch_c(const GemmOp& op, cudaStream_t st)
 {
     constexpr int kSmem = Cfg<BN, epi_staging(EPI)>::kSmem;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e =
-            cudaFuncSetAttribute(k_gemm<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        if (e != cudaSuccess)
-            return e;
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_devs{0};
+    const cudaError_t e = smem_limit_once(attr_devs, k_gemm<BN, EPI, CONV>, kSmem);
+    if (e != cudaSuccess)
+        return e;
     launch_k(k_gemm<BN, EPI, CONV>, op.grid, kThreads, kSmem, st, op.p);
     count_launch();
     return cudaGetLastError();
@@ -1166,14 +1164,10 @@ cudaError_t launch_pair(const GemmOp& op, cudaStream_t st)
 {
     if constexpr (BN >= 128 && (BN / 2) % 16 == 0) {
         constexpr int kSmem = Cfg2<BN, epi_staging(EPI)>::kSmem;
-        static bool attr_set = false;
-        if (!attr_set) {
-            cudaError_t e = cudaFuncSetAttribute(k_gemm2<BN, EPI, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 kSmem);
-            if (e != cudaSuccess)
-                return e;
-            attr_set = true;
-        }
+        static std::atomic<uint64_t> attr_devs{0};
+        const cudaError_t e = smem_limit_once(attr_devs, k_gemm2<BN, EPI, CONV>, kSmem);
+        if (e != cudaSuccess)
+            return e;
         launch_k(k_gemm2<BN, EPI, CONV>, op.grid, kThreads, kSmem, st, op.p);
         count_launch();
         return cudaGetLastError();

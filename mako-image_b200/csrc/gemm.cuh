@@ -90,6 +90,9 @@ struct GemmParams {
     GemmArgs a[2];
     int nprob = 1;
     int tiles0 = 0;
+    // Failure-path testing only (mkb_selftest_stalled_gemm): the 1-CTA kernel's CTA 0 withholds the TMA load of its
+    // first stage, so the MMA warp's bounded wait on that stage runs out and the kernel takes its error exit.
+    int test_stall = 0;
 };
 
 // A prepared launch: tensor maps and arguments are built once (buffers are fixed), then launched any number of

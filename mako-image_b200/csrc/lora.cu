@@ -60,8 +60,10 @@ mkb_status lora_merge_rows(__nv_bfloat16* W, long ldw, long row0, long rows, lon
     float *dA = nullptr, *dB = nullptr;
     const size_t nA = size_t(rank) * cols, nB = size_t(rows) * rank;
     mkb_status s = MKB_OK;
-    if (cudaMalloc(&dA, nA * 4) != cudaSuccess || cudaMalloc(&dB, nB * 4) != cudaSuccess)
+    if (cudaMalloc(&dA, nA * 4) != cudaSuccess || cudaMalloc(&dB, nB * 4) != cudaSuccess) {
+        cudaGetLastError();  // not sticky: keep it out of later launch checks
         s = fail(MKB_ERR_ALLOC, "lora: device staging");
+    }
     if (s == MKB_OK && (cudaMemcpyAsync(dA, A, nA * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
                         cudaMemcpyAsync(dB, B, nB * 4, cudaMemcpyHostToDevice, st) != cudaSuccess))
         s = fail(MKB_ERR_CUDA, "lora: upload");

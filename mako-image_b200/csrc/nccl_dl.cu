@@ -2,7 +2,9 @@
 
 #include <dlfcn.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 namespace mkb {
 
@@ -13,12 +15,16 @@ const NcclApi* nccl_api(std::string* err)
     static bool ok = false;
     static std::once_flag once;
     std::call_once(once, [] {
-        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        // MKB_NCCL_LIB names another NCCL build to bind (a path or soname); by default the process's already
+        // loaded libnccl.so.2 (PyTorch's), else the system's.
+        const char* over = std::getenv("MKB_NCCL_LIB");
+        const std::string lib = over && over[0] ? over : "libnccl.so.2";
+        void* h = over && over[0] ? nullptr : dlopen(lib.c_str(), RTLD_NOW | RTLD_NOLOAD);
         if (!h)
-            h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+            h = dlopen(lib.c_str(), RTLD_NOW | RTLD_LOCAL);
         if (!h) {
             const char* e = dlerror();
-            load_error = std::string("libnccl.so.2 not loadable: ") + (e ? e : "?");
+            load_error = lib + " not loadable: " + (e ? e : "?");
             return;
         }
         auto bind = [&](auto& fn, const char* name) {
@@ -28,7 +34,7 @@ const NcclApi* nccl_api(std::string* err)
         if (!bind(api.GetUniqueId, "ncclGetUniqueId") || !bind(api.CommInitRank, "ncclCommInitRank") ||
             !bind(api.AllGather, "ncclAllGather") || !bind(api.CommDestroy, "ncclCommDestroy") ||
             !bind(api.GetErrorString, "ncclGetErrorString")) {
-            load_error = "libnccl.so.2 lacks an expected symbol";
+            load_error = lib + " lacks an expected symbol";
             return;
         }
         ok = true;
