@@ -522,21 +522,24 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
 
 namespace {
 
-// One-time set-up of a kernel instance: its shared memory size, and a check that the compiled launch register count
-// holds the warpgroups' register split (otherwise the softmax groups' increase could never be granted).
+// Set-up of a kernel instance: a one-time check that the compiled launch register count holds the warpgroups'
+// register split (otherwise the softmax groups' increase could never be granted), and its shared memory size on
+// each device it runs on.
 template <int HD>
 cudaError_t attn_setup()
 {
-    static cudaError_t status = [] {
+    static const cudaError_t regs = [] {
         cudaFuncAttributes fa{};
         cudaError_t e = cudaFuncGetAttributes(&fa, k_attn<HD>);
         if (e != cudaSuccess)
             return e;
-        if (fa.numRegs * kThreads < 128 * kRegsCtl + 256 * kRegsSoftmax)
-            return cudaErrorInvalidConfiguration;
-        return cudaFuncSetAttribute(k_attn<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem<HD>);
+        return fa.numRegs * kThreads < 128 * kRegsCtl + 256 * kRegsSoftmax ? cudaErrorInvalidConfiguration
+                                                                          : cudaSuccess;
     }();
-    return status;
+    if (regs != cudaSuccess)
+        return regs;
+    static std::atomic<uint64_t> attr_devs{0};
+    return smem_limit_once(attr_devs, k_attn<HD>, kSmem<HD>);
 }
 
 }  // namespace

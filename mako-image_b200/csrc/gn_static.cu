@@ -24,7 +24,10 @@ std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
 // The device address of g_gn_scratch on the current device, looked up once per device. In host code the symbol is a
-// host-side stand-in, not a device address, so it is never passed to a kernel itself.
+// host-side stand-in, not a device address, so it is never passed to a kernel itself. The cached address assumes the
+// device's primary context lives until the process exits: after cudaDeviceReset (or a release and re-creation of the
+// primary context) the module can load at another address, and this entry point must not be used again on that
+// device.
 mkb_status scratch_address(void** out)
 {
     int dev = 0;

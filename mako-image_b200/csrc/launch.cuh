@@ -13,6 +13,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <utility>
 
 namespace mkb {
@@ -40,6 +42,26 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device. cudaFuncSetAttribute acts on the
+// calling thread's current device only, so a launch site keeps one bit per device in `done` (devices 0..63) and a
+// process that launches on several devices sets the limit on each of them; threads that race both set it, which is
+// harmless. Devices beyond 63 set it on every call.
+template <typename... KArgs>
+inline cudaError_t smem_limit_once(std::atomic<uint64_t>& done, void (*kernel)(KArgs...), int bytes)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? uint64_t(1) << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit))
+        return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit)
+        done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
 }
 
 }  // namespace mkb

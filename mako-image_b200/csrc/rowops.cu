@@ -762,14 +762,13 @@ cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* 
     int blocks = (N + rows_per_block - 1) / rows_per_block;
     if (blocks > 148 * 8)
         blocks = 148 * 8;
-    static size_t smem_set[9] = {};
+    // Above 48 KB the limit is raised on every such launch: it belongs to the current device, and the sizes vary.
 #define MKB_GEMV(BB)                                                                                                   \
     case BB: {                                                                                                         \
-        if (smem > 48 * 1024 && smem > smem_set[BB]) {                                                                 \
+        if (smem > 48 * 1024) {                                                                                        \
             cudaError_t e = cudaFuncSetAttribute(k_gemv<BB>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
             if (e != cudaSuccess)                                                                                      \
                 return e;                                                                                              \
-            smem_set[BB] = smem;                                                                                       \
         }                                                                                                              \
         launch_k(k_gemv<BB>, blocks, 256, smem, st, W, x, ldx, bias, y, ldy, N, K, act);                               \
         break;                                                                                                         \
@@ -857,14 +856,10 @@ cudaError_t group_norm(const GnArgs& a, cudaStream_t st)
     const int px = gn_chunk_px(a.B, a.HW), nchunks = (a.HW + px - 1) / px;
     const int Q = a.C / 4, Rb = 256 / (Q < 256 ? Q : 256);
     const size_t smem = (size_t(2) * Rb * a.C + Rb) * sizeof(float);  // <= 48 KB + 4 B at C = 6144
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_gn_stats, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (2 * 6144 + 1) * int(sizeof(float)));
-        if (e != cudaSuccess)
-            return e;
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr_devs{0};
+    const cudaError_t e = smem_limit_once(attr_devs, k_gn_stats, (2 * 6144 + 1) * int(sizeof(float)));
+    if (e != cudaSuccess)
+        return e;
     launch_k(k_gn_stats, dim3(nchunks, a.B), 256, smem, st, a, px, nchunks);
     count_launch();
     launch_k(k_gn_finalize, dim3(a.groups, a.B), 256, 0, st, a, nchunks);
@@ -944,13 +939,11 @@ cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n
     const size_t smem = size_t(n) * 4;
     if (n % 4 == 0 && smem <= 96 * 1024 && !(reinterpret_cast<uintptr_t>(s) & 15) &&
         !(reinterpret_cast<uintptr_t>(p) & 7)) {
-        static size_t smem_set = 0;
-        if (smem > 48 * 1024 && smem > smem_set) {
-            const cudaError_t e =
-                cudaFuncSetAttribute(k_softmax_rows_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        static std::atomic<uint64_t> attr_devs{0};
+        if (smem > 48 * 1024) {
+            const cudaError_t e = smem_limit_once(attr_devs, k_softmax_rows_smem, 96 * 1024);
             if (e != cudaSuccess)
                 return e;
-            smem_set = 96 * 1024;
         }
         launch_k(k_softmax_rows_smem, dim3(unsigned(rows)), 512, smem, st, s, p, n, scale);
         count_launch();

@@ -358,9 +358,16 @@ std::unique_ptr<File> File::open(const std::string& path, std::string* err)
         t.dtype_name = dt->str;
         t.dtype = dt->str == "F32" ? DType::F32 : dt->str == "F16" ? DType::F16 : dt->str == "BF16" ? DType::BF16
                                                                                                     : DType::Other;
+        // The element count is checked as it is formed: a header whose dimensions overflow 64 bits (or exceed 2^48
+        // elements, far beyond any checkpoint) could otherwise wrap around to a product that matches its byte range.
+        int64_t elems = 1;
         for (const Json& d : shape->items) {
             if (d.kind != Json::kNumber || !d.num_is_int || d.num < 0) {
                 *err = "safetensors: entry " + name + " has a bad shape";
+                return nullptr;
+            }
+            if (__builtin_mul_overflow(elems, int64_t(d.num), &elems) || elems > (int64_t(1) << 48)) {
+                *err = "safetensors: entry " + name + " has a shape too large to address";
                 return nullptr;
             }
             t.shape.push_back(d.num);

@@ -56,7 +56,8 @@ def _raw(path, header, data=b"", hlen=None):
         f.write(data)
 
 
-@pytest.mark.parametrize("case", ["short", "hlen", "json", "offsets", "size", "shape", "dtype_read", "dup_ok"])
+@pytest.mark.parametrize("case", ["short", "hlen", "json", "offsets", "size", "shape", "overflow", "dtype_read",
+                                  "dup_ok"])
 def test_reader_rejects_malformed(tmp_path, case):
     import mkimage
 
@@ -75,6 +76,11 @@ def test_reader_rejects_malformed(tmp_path, case):
         _raw(p, {"t": {"dtype": "F32", "shape": [3], "data_offsets": [0, 8]}}, b"\0" * 8)
     elif case == "shape":
         _raw(p, {"t": {"dtype": "F32", "shape": [-2], "data_offsets": [0, 8]}}, b"\0" * 8)
+    elif case == "overflow":  # 2^32 x 2^32 elements: the 64-bit product wraps to 0, which would match [0, 0)
+        _raw(p, {"t": {"dtype": "F32", "shape": [1 << 32, 1 << 32], "data_offsets": [0, 0]}})
+        with pytest.raises(mkimage.MkbError, match="too large"):
+            mkimage.st_read(p)
+        return
     elif case == "dtype_read":
         _raw(p, {"t": {"dtype": "I64", "shape": [1], "data_offsets": [0, 8]}}, b"\0" * 8)
         with pytest.raises(mkimage.MkbError, match="unsupported dtype"):
