@@ -67,8 +67,9 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c);
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b);
 
 // 2^x for two lanes on the FMA pipe with packed f32x2 arithmetic: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f
-// by a degree-3 polynomial fitted here for least maximum relative error on that interval (7.5e-5, below bf16's
-// 3.9e-3), 2^n added to the exponent bits. Arguments below -126 flush to 0 like ex2.approx.ftz.
+// by the degree-3 polynomial of least maximum relative error on that interval (a minimax fit by the Remez exchange
+// algorithm, tests/ex2_fit.py; 7.5e-5, below bf16's 3.9e-3; tests/test_ex2_poly_cpu.py checks the bound), 2^n added
+// to the exponent bits. Arguments below -126 flush to 0 like ex2.approx.ftz.
 __device__ __forceinline__ float2 ex2_poly2(float2 x)
 {
     x.x = fmaxf(x.x, -126.0f);

@@ -52,6 +52,13 @@ def _check_block(got, want, what):
     assert err <= MAX_ABS and cos >= MIN_COS, f"{what}: max-abs {err:.3e}, cosine {cos:.6f}"
 
 
+def _check_delta(got_out, got_in, want_out, want_in, what):
+    """What a block adds to the residual stream (output minus input) on both sides: the residual it carries through
+    dominates its output, so this is the check that sees the block's own arithmetic."""
+    cos = _cos(got_out - got_in, want_out - want_in)
+    assert cos >= MIN_COS, f"{what}: contribution cosine {cos:.6f}"
+
+
 @pytest.mark.parametrize("h,w,S,B", [(16, 16, 40, 2), (10, 13, 7, 1)])
 def test_qwen1_blocks_and_velocity(cuda, h, w, S, B):
     """qwen1 at a reduced width (3 blocks): every block's text and image rows, then the velocity."""
@@ -71,10 +78,15 @@ def test_qwen1_blocks_and_velocity(cuda, h, w, S, B):
         want = {}
         v_ref = QD.step(cfg, W, lats[b], prompts[b], sigmas[b], h, w,
                         probe=lambda name, a: want.__setitem__(name, a))
+        prev = np.concatenate([got[("txt_in", -1)].reshape(B, S, D)[b], got[("img_in", -1)].reshape(B, N, D)[b]])
+        prev_want = np.concatenate([want["txt_in"], want["img_in"]])
         for i in range(NB):
             gt = got[("block.txt", i)].reshape(B, S, D)[b]
             gi = got[("block.img", i)].reshape(B, N, D)[b]
-            _check_block(np.concatenate([gt, gi]), want[f"block{i}"], f"sample {b} block {i}")
+            out = np.concatenate([gt, gi])
+            _check_block(out, want[f"block{i}"], f"sample {b} block {i}")
+            _check_delta(out, prev, want[f"block{i}"], prev_want, f"sample {b} block {i}")
+            prev, prev_want = out, want[f"block{i}"]
         _check_block(got[("temb", -1)].reshape(B, D)[b], want["temb"], "temb")
         v = vel[b]
         assert _rel(v, v_ref) < MAX_REL and _cos(v, v_ref) >= MIN_COS
@@ -103,8 +115,13 @@ def test_ref21_two_steps_with_text_cache(cuda):
             want = {}
             v_ref = QD.step(cfg, W, lats[b], prompts[b], sig, h, w, state=states[b],
                             probe=lambda name, a: want.__setitem__(name, a))
+            prev = got[("x_in", -1)].reshape(B, T, D)[b]
+            prev_want = np.concatenate([want["txt_in"], want["img_in"]]) if step_i == 0 else want["img_in"]
             for i in range(NB):
-                _check_block(got[("block", i)].reshape(B, T, D)[b], want[f"block{i}"], f"step {step_i} block {i}")
+                out = got[("block", i)].reshape(B, T, D)[b]
+                _check_block(out, want[f"block{i}"], f"step {step_i} block {i}")
+                _check_delta(out, prev, want[f"block{i}"], prev_want, f"step {step_i} block {i}")
+                prev, prev_want = out, want[f"block{i}"]
             assert _rel(vel[b], v_ref) < MAX_REL and _cos(vel[b], v_ref) >= MIN_COS
         lats = [l * 0.9 for l in lats]
 
@@ -126,9 +143,55 @@ def test_config1_block_full_width(cuda):
     d.set_probe(None)
     want = {}
     v_ref = QD.step(cfg, W, lats[0], prompts[0], 0.5, h, w, probe=lambda name, a: want.__setitem__(name, a))
-    _check_block(np.concatenate([got[("block.txt", 0)].reshape(S, D), got[("block.img", 0)].reshape(N, D)]),
-                 want["block0"], "config 1 block")
+    out = np.concatenate([got[("block.txt", 0)].reshape(S, D), got[("block.img", 0)].reshape(N, D)])
+    _check_block(out, want["block0"], "config 1 block")
+    _check_delta(out, np.concatenate([got[("txt_in", -1)].reshape(S, D), got[("img_in", -1)].reshape(N, D)]),
+                 want["block0"], np.concatenate([want["txt_in"], want["img_in"]]), "config 1 block")
     assert _rel(vel, v_ref) < MAX_REL and _cos(vel, v_ref) >= MIN_COS
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+def test_strong_modulation_block_contributions(cuda, variant):
+    """Weights whose modulation is of order one (the time MLP and modulation matrices scaled up, per-head norm
+    weights 1 + 0.5 N(0, 1)), the regime in which the inferred choices (tanh gates, per-row modulation, norm before
+    RoPE, interleaved RoPE pairs) change a block's contribution beyond tolerance (tests/test_semantics_cpu.py): every
+    block's contribution and the velocity against the oracle; for ref21 a second, cached-text step too."""
+    from tests.test_semantics_cpu import STRONG_MOD
+
+    D, H, F, NB, TD = 256, 2, 512, 2, 128
+    h, w, S = 6, 7, 9
+    N = h * w
+    d, cfg = _make(variant, D, H, F, NB, TD, 1, S, N, seed=13)
+    for i, (name, shape) in enumerate(d.weight_names()):
+        key = name.split(".", 1)[1] if name.startswith("blk") else name
+        if name.endswith(("norm_q", "norm_k")) or name == "txt_norm.w":
+            d.write_weight(name, 1.0 + 0.5 * rng.normal(rng.tensor_key(15, i), shape[0]))
+        elif key in STRONG_MOD:
+            d.write_weight(name, d.read_weight(name, shape) * STRONG_MOD[key])
+    W = d.weights()
+    prompts, lats = _inputs(1, S, N, TD, seed=16)
+    d.begin(prompts[0], h, w, slot=0)
+    state = {} if variant == 1 else None
+    for step_i, sig in enumerate([0.6, 0.45] if variant == 1 else [0.6]):
+        got = {}
+        d.set_probe(lambda name, layer, a: got.__setitem__((name, layer), a))
+        vel = d.step(lats[0], sig, slot=0)
+        d.set_probe(None)
+        want = {}
+        v_ref = QD.step(cfg, W, lats[0], prompts[0], sig, h, w, state=state,
+                        probe=lambda name, a: want.__setitem__(name, a))
+        if variant == 0:
+            prev = np.concatenate([got[("txt_in", -1)].reshape(S, D), got[("img_in", -1)].reshape(N, D)])
+            outs = [np.concatenate([got[("block.txt", i)].reshape(S, D), got[("block.img", i)].reshape(N, D)])
+                    for i in range(NB)]
+        else:
+            prev = got[("x_in", -1)].reshape(-1, D)
+            outs = [got[("block", i)].reshape(-1, D) for i in range(NB)]
+        prev_want = np.concatenate([want["txt_in"], want["img_in"]]) if step_i == 0 else want["img_in"]
+        for i in range(NB):
+            _check_delta(outs[i], prev, want[f"block{i}"], prev_want, f"step {step_i} block {i}")
+            prev, prev_want = outs[i], want[f"block{i}"]
+        assert _rel(vel, v_ref) < MAX_REL and _cos(vel, v_ref) >= MIN_COS, (_rel(vel, v_ref), _cos(vel, v_ref))
 
 
 def test_step_cfg_matches_two_steps(cuda):
