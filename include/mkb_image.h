@@ -415,8 +415,8 @@ int mkb_sdxl_timestep(float sigma);
 typedef struct mkb_vae_config {
     int channels[4]; /* block widths from the output side: 128, 256, 512, 512 (multiples of 128) */
     int layers;      /* 2: each up level has layers + 1 residual blocks */
-    int latent;      /* 4 latent channels */
-    float scale;     /* latents are tokens / scale (0.13025 for SDXL) */
+    int latent;      /* latent channels: 4 (SDXL) or 16 (the Qwen-Image-size token of 64 values) */
+    float scale;     /* by default latents are tokens / scale (0.13025 for SDXL); see mkb_vae_set_latent_stats */
     int max_gh, max_gw;
 } mkb_vae_config;
 
@@ -446,11 +446,18 @@ mkb_status mkb_unet_weight_lora_rows(mkb_unet* u, const char* name, long row0, l
 mkb_status mkb_unet_lora_merge(mkb_unet* u, const char* module, const float* A, const float* B, int rank,
                                int in_features, int out_features, float scale);
 mkb_status mkb_unet_load_lora(mkb_unet* u, const char* path, float scale, int* merged);
-/* Engine::decode: tokens [gh * gw][16] to RGBA [16 gh][16 gw][4] in [-1, 1] (alpha 1), host / device buffers. */
+/* Engine::decode: tokens [gh * gw][4 * latent] to RGBA [16 gh][16 gw][4] in [-1, 1] (alpha 1), host / device
+ * buffers. */
 mkb_status mkb_vae_decode(mkb_vae* v, const float* latents, int gh, int gw, float* rgba);
 mkb_status mkb_vae_decode_dev(mkb_vae* v, const float* latents_dev, int gh, int gw, float* rgba_dev, void* stream);
 mkb_status mkb_vae_set_probe(mkb_vae* v, mkb_probe_fn fn, void* user);
 double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw);
+/* The latent statistics the decoder undoes first: token value i (of 4 * latent: channel c, patch row py, column px
+ * at i = (c * 2 + py) * 2 + px) enters as v * std[i] + mean[i], the reference's per-value latents_mean /
+ * latents_std (Engine::decode, engine.cpp:890-898; a 16-channel VAE's config.json statistics repeated over the 2x2
+ * patch, or the batch-norm statistics of a packed-latent VAE). n = 4 * latent. Replaces the scale's default of
+ * mean 0, std 1 / scale. */
+mkb_status mkb_vae_set_latent_stats(mkb_vae* v, const float* mean, const float* std, int n);
 
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */

@@ -538,6 +538,28 @@ __global__ void k_unpack(const float* tok, __nv_bfloat16* img, int B, int gh, in
     }
 }
 
+// Tokens [gh*gw][4 z] of one image to its channels-last latent image [2gh][2gw][Cp] bf16: token value
+// i = (c * 2 + py) * 2 + px is channel c of pixel (2y + py, 2x + px), mapped to v * aff[i] + aff[4 z + i] (the
+// VAE's per-value latent statistics); channels z..Cp-1 are zero.
+__global__ void k_unpack_affine(const float* tok, __nv_bfloat16* img, int gh, int gw, int z, int Cp, const float* aff)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    const uint64_t total = uint64_t(4) * gh * gw * Cp;
+    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int c = int(i % Cp);
+        const uint64_t px = i / Cp;
+        const int x = int(px % (2 * gw)), y = int(px / (2 * gw));
+        float v = 0.f;
+        if (c < z) {
+            const int k = c * 4 + (y % 2) * 2 + x % 2;
+            v = tok[(uint64_t(y / 2) * gw + x / 2) * 4 * z + k] * aff[k] + aff[4 * z + k];
+        }
+        img[i] = __float2bfloat16_rn(v);
+    }
+}
+
 __global__ void k_pack(const float* img, int Cs, float* tok, int B, int gh, int gw)
 {
     grid_dep_wait();
@@ -907,6 +929,17 @@ cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, i
 {
     const uint64_t n = uint64_t(B) * 4 * gh * gw * Cp;
     launch_k(k_unpack, grid_for(n, 256), 256, 0, st, tokens, img, B, gh, gw, Cp, scale);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t unpack_tokens_affine_bf16(const float* tokens, __nv_bfloat16* img, int gh, int gw, int z, int Cp,
+                                      const float* affine, cudaStream_t st)
+{
+    if (z < 1 || z > Cp)
+        return cudaErrorInvalidValue;
+    const uint64_t n = uint64_t(4) * gh * gw * Cp;
+    launch_k(k_unpack_affine, grid_for(n, 256), 256, 0, st, tokens, img, gh, gw, z, Cp, affine);
     count_launch();
     return cudaGetLastError();
 }

@@ -99,6 +99,10 @@ cudaError_t unpack_tokens_bf16(const float* tokens, __nv_bfloat16* img, int B, i
                                cudaStream_t st);
 // The inverse for the first 4 of Cs channels of fp32 img [B][2gh][2gw][Cs] (sdxl.cpp:946-952).
 cudaError_t pack_tokens(const float* img, int Cs, float* tokens, int B, int gh, int gw, cudaStream_t st);
+// One image's tokens [gh*gw][4 z] (z latent channels in 2x2 patches) to its channels-last latent image
+// [2gh][2gw][Cp] bf16, value i of a token mapped to v * affine[i] + affine[4 z + i].
+cudaError_t unpack_tokens_affine_bf16(const float* tokens, __nv_bfloat16* img, int gh, int gw, int z, int Cp,
+                                      const float* affine, cudaStream_t st);
 // out[i] = silu(a[i] + b[i]).
 cudaError_t add_silu(const float* a, const float* b, float* out, uint64_t n, cudaStream_t st);
 // RGBA [B][H][W][4] = clamp(img[..][0:3], -1, 1), alpha 1, from fp32 img with Cs channels per pixel

@@ -976,6 +976,8 @@ struct VaeImpl {
     };
     std::vector<Op> ops;  // after conv_in
     int ctop = 0;
+    int z = 4;                    // latent channels; a token holds 4 z values (2x2 patches)
+    float* lat_aff = nullptr;     // per token value: [4 z] multipliers, then [4 z] offsets (latent statistics)
     PlanMap plans;
     float *tokens = nullptr, *rgba = nullptr;
     mkb_probe_fn probe = nullptr;
@@ -989,6 +991,8 @@ struct VaeImpl {
             cudaFree(tokens);
         if (rgba)
             cudaFree(rgba);
+        if (lat_aff)
+            cudaFree(lat_aff);
         if (stream)
             cudaStreamDestroy(stream);
     }
@@ -1003,8 +1007,9 @@ mkb_status VaeImpl::create(const mkb_vae_config& c)
     for (int l = 0; l < 4; ++l)
         if (c.channels[l] <= 0 || c.channels[l] % 128)
             return fail(MKB_ERR_INVALID, "vae: channels must be positive multiples of 128");
-    if (c.layers < 1 || c.latent != 4 || !(c.scale > 0) || c.max_gh < 1 || c.max_gw < 1)
-        return fail(MKB_ERR_INVALID, "vae: bad configuration (4 latent channels)");
+    if (c.layers < 1 || (c.latent != 4 && c.latent != 16) || !(c.scale > 0) || c.max_gh < 1 || c.max_gw < 1)
+        return fail(MKB_ERR_INVALID, "vae: bad configuration (4 or 16 latent channels)");
+    z = c.latent;
     ctop = c.channels[3];
     int ch = ctop;
     ops.push_back({Op::kRes, "mid.res0", ch, ch});
@@ -1019,9 +1024,9 @@ mkb_status VaeImpl::create(const mkb_vae_config& c)
         if (i < 3)
             ops.push_back({Op::kUp, "up" + std::to_string(i) + ".up", ch, ch});
     }
-    W.add("post_quant.w", WTable::kMat, 4, 4, 64, 64);
-    W.add("post_quant.b", WTable::kVec, 4, 0, 64);
-    W.add("conv_in.w", WTable::kConv3, ctop, 4, 0, 64);
+    W.add("post_quant.w", WTable::kMat, z, z, 64, 64);
+    W.add("post_quant.b", WTable::kVec, z, 0, 64);
+    W.add("conv_in.w", WTable::kConv3, ctop, z, 0, 64);
     W.add("conv_in.b", WTable::kVec, ctop);
     for (const Op& o : ops) {
         if (o.kind == Op::kRes) {
@@ -1056,15 +1061,20 @@ mkb_status VaeImpl::create(const mkb_vae_config& c)
     MKB_TRY_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
     status = device_status_word();
     MKB_TRY(W.alloc());
-    MKB_TRY_CUDA(cudaMalloc(&tokens, size_t(c.max_gh) * c.max_gw * 16 * 4), "vae");
+    MKB_TRY_CUDA(cudaMalloc(&tokens, size_t(c.max_gh) * c.max_gw * 4 * z * 4), "vae");
     MKB_TRY_CUDA(cudaMalloc(&rgba, size_t(c.max_gh) * c.max_gw * 256 * 4 * 4), "vae");
+    // Latent statistics: by default tokens / scale (mean 0, deviation 1 / scale for every value).
+    std::vector<float> aff(8 * z, 0.0f);
+    std::fill(aff.begin(), aff.begin() + 4 * z, 1.0f / c.scale);
+    MKB_TRY_CUDA(cudaMalloc(&lat_aff, aff.size() * 4), "vae");
+    MKB_TRY_CUDA(cudaMemcpy(lat_aff, aff.data(), aff.size() * 4, cudaMemcpyHostToDevice), "vae");
     return MKB_OK;
 }
 
 double VaeImpl::flops(int gh, int gw) const
 {
     double h = 2.0 * gh, w = 2.0 * gw;
-    double f = 2 * h * w * ctop * 9 * 4;
+    double f = 2 * h * w * ctop * 9 * z;
     for (const Op& o : ops) {
         const double P = h * w;
         if (o.kind == Op::kRes)
@@ -1127,10 +1137,12 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
     if (st != MKB_OK)
         return st;
     const WTable& w = W;
-    // Latents (tokens / scale, unpacked), post_quant 1x1 (4 -> 4, padded to 64 both ways), conv_in.
+    // Latents (tokens times the latent deviation plus the mean, unpacked), post_quant 1x1 (z -> z, padded to 64 both
+    // ways), conv_in.
     float* tok = tokens;
-    const float inv_scale = 1.0f / cfg.scale;
-    P.add([=](cudaStream_t s) { return unpack_tokens_bf16(tok, LAT, 1, gh, gw, 64, inv_scale, s); });
+    const float* aff = lat_aff;
+    const int zz = z;
+    P.add([=](cudaStream_t s) { return unpack_tokens_affine_bf16(tok, LAT, gh, gw, zz, 64, aff, s); });
     {
         GemmArgs a;
         a.M = n;
@@ -1647,7 +1659,7 @@ mkb_status mkb_vae_decode_dev(mkb_vae* v, const float* latents_dev, int gh, int 
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m.stream;
     Plan* plan = nullptr;
     MKB_TRY(m.build(gh, gw, &plan));
-    MKB_TRY_CUDA(cudaMemcpyAsync(m.tokens, latents_dev, size_t(gh) * gw * 16 * 4, cudaMemcpyDeviceToDevice, s),
+    MKB_TRY_CUDA(cudaMemcpyAsync(m.tokens, latents_dev, size_t(gh) * gw * 4 * m.z * 4, cudaMemcpyDeviceToDevice, s),
                  "latents");
     MKB_TRY(plan->run(s, m.probe, m.probe_user));
     MKB_TRY_CUDA(cudaMemcpyAsync(rgba_dev, m.rgba, size_t(gh) * gw * 256 * 4 * 4, cudaMemcpyDeviceToDevice, s),
@@ -1664,7 +1676,7 @@ mkb_status mkb_vae_decode(mkb_vae* v, const float* latents, int gh, int gw, floa
         return fail(MKB_ERR_INVALID, "vae_decode: grid out of range (2 * gw a multiple of 8)");
     Plan* plan = nullptr;
     MKB_TRY(m.build(gh, gw, &plan));
-    const size_t nt = size_t(gh) * gw * 16, no = size_t(gh) * gw * 256 * 4;
+    const size_t nt = size_t(gh) * gw * 4 * m.z, no = size_t(gh) * gw * 256 * 4;
     MKB_TRY_CUDA(cudaMemcpyAsync(m.tokens, latents, nt * 4, cudaMemcpyHostToDevice, m.stream), "latents upload");
     MKB_TRY(plan->run(m.stream, m.probe, m.probe_user));
     MKB_TRY_CUDA(cudaMemcpyAsync(rgba, m.rgba, no * 4, cudaMemcpyDeviceToHost, m.stream), "rgba download");
@@ -1688,5 +1700,24 @@ mkb_status mkb_vae_set_probe(mkb_vae* v, mkb_probe_fn fn, void* user)
 }
 
 double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw) { return v ? v->impl.flops(gh, gw) : 0.0; }
+
+mkb_status mkb_vae_set_latent_stats(mkb_vae* v, const float* mean, const float* std, int n)
+{
+    if (!v || !mean || !std)
+        return fail(MKB_ERR_INVALID, "vae_set_latent_stats: null argument");
+    VaeImpl& m = v->impl;
+    if (n != 4 * m.z)
+        return fail(MKB_ERR_INVALID, "vae_set_latent_stats: need one mean and deviation per token value (4 x latent)");
+    std::vector<float> aff(8 * m.z);
+    for (int i = 0; i < n; ++i) {
+        if (!(std[i] > 0) || !std::isfinite(mean[i]))
+            return fail(MKB_ERR_INVALID, "vae_set_latent_stats: deviations must be positive, means finite");
+        aff[i] = std[i];
+        aff[4 * m.z + i] = mean[i];
+    }
+    MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "sync");
+    MKB_TRY_CUDA(cudaMemcpy(m.lat_aff, aff.data(), aff.size() * 4, cudaMemcpyHostToDevice), "latent stats");
+    return MKB_OK;
+}
 
 }  // extern "C"

@@ -78,6 +78,7 @@ _SIGS = {
     "mkb_vae_decode_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "mkb_vae_set_probe": (_i, [_vp, _vp, _vp]),
     "mkb_vae_decode_flops": (ctypes.c_double, [_vp, _i, _i]),
+    "mkb_vae_set_latent_stats": (_i, [_vp, _vp, _vp, _i]),
     "mkb_sigmas": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp]),
     "mkb_top_sigma": (_f, [_vp, ctypes.c_uint32]),
     "mkb_guided_euler": (None, [_vp, _vp, _vp, _f, _f, _f, _l]),

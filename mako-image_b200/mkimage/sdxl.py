@@ -182,6 +182,12 @@ class Vae(_Weights):
     def decode_dev(self, latents_dev, gh, gw, out_dev, stream=None):
         check(lib.mkb_vae_decode_dev(self.h, ctypes.c_void_p(latents_dev), gh, gw, ctypes.c_void_p(out_dev), stream))
 
+    def set_latent_stats(self, mean, std):
+        """Per token value (4 x latent of them): latents enter the decoder as tokens * std + mean."""
+        m = np.ascontiguousarray(mean, np.float32)
+        s = np.ascontiguousarray(std, np.float32)
+        check(lib.mkb_vae_set_latent_stats(self.h, _fptr(m), _fptr(s), m.size))
+
     def decode_flops(self, gh, gw):
         return lib.mkb_vae_decode_flops(self.h, gh, gw)
 

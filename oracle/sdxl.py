@@ -143,11 +143,16 @@ def added_cond(pooled, gh, gw):
     return np.concatenate([np.asarray(pooled, np.float32)] + [sinusoid(v, 256) for v in (H, W, 0.0, 0.0, H, W)])
 
 
-def unpack(tokens, gh, gw, scale):
-    """Tokens [gh*gw][16] (channel, row, column of a 2x2 patch) to the channels-last image [2gh][2gw][4]
-    (sdxl.cpp:80-87)."""
-    t = np.asarray(tokens, np.float32).reshape(gh, gw, 4, 2, 2)
-    return (t.transpose(0, 3, 1, 4, 2).reshape(2 * gh, 2 * gw, 4) * np.float32(scale)).astype(np.float32)
+def unpack(tokens, gh, gw, scale, z=4, mean=None):
+    """Tokens [gh*gw][4 z] (channel, row, column of a 2x2 patch) to the channels-last image [2gh][2gw][z]
+    (sdxl.cpp:80-87), each value times `scale` (a number, or one per token value) plus `mean` (one per token value,
+    Engine::decode's latent statistics, engine.cpp:890-898)."""
+    t = np.asarray(tokens, np.float32).reshape(gh * gw, 4 * z)
+    t = t * np.asarray(scale, np.float32)
+    if mean is not None:
+        t = t + np.asarray(mean, np.float32)
+    t = t.astype(np.float32).reshape(gh, gw, z, 2, 2)
+    return t.transpose(0, 3, 1, 4, 2).reshape(2 * gh, 2 * gw, z).astype(np.float32)
 
 
 def pack(img, gh, gw):
@@ -310,11 +315,15 @@ def vae_weight_shapes(cfg):
     return s
 
 
-def vae_decode(cfg, W, tokens, gh, gw, probe=None):
-    """Engine::decode (engine.cpp:862-954), AutoencoderKL layout: tokens [gh*gw][16] (latents / scale) to RGBA
-    [16gh][16gw][4] in [-1, 1]."""
+def vae_decode(cfg, W, tokens, gh, gw, probe=None, stats=None):
+    """Engine::decode (engine.cpp:862-954), AutoencoderKL layout: tokens [gh*gw][4 latent] to RGBA [16gh][16gw][4] in
+    [-1, 1]. The latents are tokens / scale, or with stats = (mean, std) per token value tokens * std + mean."""
     pr = probe or (lambda name, a: None)
-    x = unpack(tokens, gh, gw, 1.0 / cfg["scale"])
+    z = cfg["latent"]
+    if stats is None:
+        x = unpack(tokens, gh, gw, 1.0 / cfg["scale"], z)
+    else:
+        x = unpack(tokens, gh, gw, stats[1], z, stats[0])
     h = _conv(W, "post_quant", x)
     for op in vae_structure(cfg)[1:]:
         kind = op[0]

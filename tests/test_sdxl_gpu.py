@@ -106,6 +106,25 @@ def test_vae_decode_reduced(cuda):
     assert _rel(img, ref) < 0.01, _rel(img, ref)
 
 
+def test_vae_decode_16_latent_channels(cuda):
+    """The decoder of a 16-channel latent (tokens of 64 values, the DiT's) with per-value latent statistics."""
+    import mkimage
+
+    cfg = dict(channels=(128, 128, 128, 256), layers=1, latent=16)
+    gh, gw = 4, 8
+    v = mkimage.Vae(mkimage.VaeConfig(max_gh=gh, max_gw=gw, **cfg))
+    v.init_random(29)
+    mean = (0.3 * rng.normal(rng.tensor_key(4, 5), 64)).astype(np.float32)
+    std = (1.0 + 0.5 * np.abs(rng.normal(rng.tensor_key(4, 6), 64))).astype(np.float32)
+    v.set_latent_stats(mean, std)
+    W = v.weights()
+    lat = rng.normal(rng.tensor_key(4, 7), gh * gw * 64).reshape(gh * gw, 64)
+    img = v.decode(lat, gh, gw)
+    ref = OS.vae_decode(OS.vae_default_cfg(**cfg), W, lat, gh, gw, stats=(mean, std))
+    assert img.shape == (16 * gh, 16 * gw, 4)
+    assert _rel(img, ref) < 0.01 and _cos(img, ref) >= 0.999, (_rel(img, ref), _cos(img, ref))
+
+
 def test_sdxl_schedule():
     import mkimage
 
