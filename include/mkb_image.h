@@ -459,6 +459,16 @@ double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw);
  * mean 0, std 1 / scale. */
 mkb_status mkb_vae_set_latent_stats(mkb_vae* v, const float* mean, const float* std, int n);
 
+/* Image output (host code, no device needed). mkb_to_rgba8: RGBA floats in [-1, 1] to 8-bit samples, x / 2 + 1/2
+ * clamped, times 255, rounded to nearest (the reference's to_rgba8, src/image/png.hpp:13-14, png.cpp:148-156).
+ * mkb_png_encode: a PNG of 8-bit RGBA [height][width][4] (colour type 6), or with rgb != 0 of its RGB samples (colour
+ * type 2), written with this library's own encoder (stored deflate blocks; the reference's encode_png,
+ * png.hpp:15-17, uses Apple's ImageIO). With out == NULL only *size is set; otherwise capacity must hold *size
+ * bytes. */
+mkb_status mkb_to_rgba8(const float* rgba, size_t count, uint8_t* out);
+mkb_status mkb_png_encode(const uint8_t* rgba8, uint32_t width, uint32_t height, int rgb, uint8_t* out,
+                          size_t capacity, size_t* size);
+
 /* The status word kernels write their error bits to (device memory owned by the library; 0 = no error). Reads and
  * clears it: returns MKB_OK, or MKB_ERR_KERNEL with the bits in *bits. Synchronises the device. */
 mkb_status mkb_check_kernels(uint32_t* bits);

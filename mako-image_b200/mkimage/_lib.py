@@ -79,6 +79,9 @@ _SIGS = {
     "mkb_vae_set_probe": (_i, [_vp, _vp, _vp]),
     "mkb_vae_decode_flops": (ctypes.c_double, [_vp, _i, _i]),
     "mkb_vae_set_latent_stats": (_i, [_vp, _vp, _vp, _i]),
+    "mkb_to_rgba8": (_i, [_vp, ctypes.c_size_t, _vp]),
+    "mkb_png_encode": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _i, _vp, ctypes.c_size_t,
+                            ctypes.POINTER(ctypes.c_size_t)]),
     "mkb_sigmas": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp]),
     "mkb_top_sigma": (_f, [_vp, ctypes.c_uint32]),
     "mkb_guided_euler": (None, [_vp, _vp, _vp, _f, _f, _f, _l]),
