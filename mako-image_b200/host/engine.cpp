@@ -67,7 +67,7 @@ std::vector<float> Engine::denoise(const Request& r)
     std::normal_distribution<float> nd;
     if (!r.noise.empty()) {
         if (r.noise.size() != x.size())
-            throw std::runtime_error("noise must be [h * w][64]");
+            throw std::runtime_error("noise must be [h * w][" + std::to_string(latent_width()) + "]");
         std::copy(r.noise.begin(), r.noise.end(), x.begin());
     } else {
         for (float& v : x)
@@ -75,6 +75,12 @@ std::vector<float> Engine::denoise(const Request& r)
     }
     const auto sig = sigmas(r.steps ? r.steps : default_steps(), N, r.terminal);
     const uint32_t steps = uint32_t(sig.size() - 1);
+    // A model that predicts the noise starts from noise at the top level's scale, sqrt(1 + sigma^2).
+    if (predicts_noise()) {
+        const float s0 = std::sqrt(1.0f + sig[0] * sig[0]);
+        for (float& v : x)
+            v *= s0;
+    }
     begin(r.prompt, r.h, r.w, 0);
     const float scale = r.guidance.value_or(default_guidance());
     const bool guided = scale != 1.0f && !r.negative.empty();
@@ -178,7 +184,7 @@ std::vector<float> QwenImage::denoise_device(const Request& r)
     std::normal_distribution<float> nd;
     if (!r.noise.empty()) {
         if (r.noise.size() != x.size())
-            throw std::runtime_error("noise must be [h * w][64]");
+            throw std::runtime_error("noise must be [h * w][" + std::to_string(latent_width()) + "]");
         std::copy(r.noise.begin(), r.noise.end(), x.begin());
     } else {
         for (float& v : x)
@@ -269,6 +275,99 @@ bool QwenImage::guided_step(std::vector<float>& x, float sigma, float sigma_next
         return false;
     check(mkb_dit_step_cfg(d_, x.data(), sigma, sigma_next, scale), "guided step");
     return true;
+}
+
+// ------------------------------------------------------------------------------------------------ SDXL
+
+Sdxl::Sdxl(const mkb_unet_config& cfg) : cfg_(cfg) { check(mkb_unet_create(&cfg, &u_), "create"); }
+
+Sdxl::~Sdxl() { mkb_unet_destroy(u_); }
+
+void Sdxl::init_random(uint64_t seed, float std) { check(mkb_unet_init_random(u_, seed, std), "init_random"); }
+
+void Sdxl::begin(std::span<const float> prompt, uint32_t h, uint32_t w, uint32_t slot)
+{
+    if (slot > 1)
+        throw std::runtime_error("slot must be 0 or 1");
+    if (prompt.empty())
+        throw std::runtime_error("prompt embeddings: no header");
+    const uint32_t S = uint32_t(prompt[0]);
+    if (!S || prompt.size() != 1 + uint64_t(S) * cfg_.context_dim + cfg_.pooled_dim)
+        throw std::runtime_error("prompt embeddings: sizes do not add up");
+    check(mkb_unet_begin(u_, prompt.data() + 1, int(S), prompt.data() + 1 + uint64_t(S) * cfg_.context_dim, int(h),
+                         int(w), int(slot)),
+          "begin");
+    gh_ = h;
+    gw_ = w;
+    ctx_rows_[slot] = S;
+}
+
+std::vector<float> Sdxl::step(std::span<const float> latents, float sigma, uint32_t slot)
+{
+    if (latents.size() != uint64_t(gh_) * gw_ * latent_width())
+        throw std::runtime_error("latents must be [h * w][16]");
+    std::vector<float> out(latents.size());
+    check(mkb_unet_step(u_, latents.data(), sigma, out.data(), int(slot)), "step");
+    return out;
+}
+
+std::vector<float> Sdxl::sigmas(uint32_t steps, uint32_t tokens, std::optional<float> terminal) const
+{
+    (void)tokens, (void)terminal;  // the discrete schedule depends on neither
+    std::vector<float> out(steps + 1);
+    check(mkb_sdxl_sigmas(steps, out.data()), "sigmas");
+    return out;
+}
+
+float Sdxl::top_sigma(uint32_t tokens) const { return sigmas(1, tokens)[0]; }
+
+bool Sdxl::guided_step(std::vector<float>& x, float sigma, float sigma_next, float scale)
+{
+    if (ctx_rows_[0] != ctx_rows_[1] || cfg_.max_batch < 2 || cfg_.slots < 2)
+        return false;
+    // Both slots in one batched pass, then the guided Euler update on the host.
+    const size_t n = x.size();
+    std::vector<float> in(2 * n), out(2 * n);
+    std::copy(x.begin(), x.end(), in.begin());
+    std::copy(x.begin(), x.end(), in.begin() + long(n));
+    const float s2[2] = {sigma, sigma};
+    check(mkb_unet_step_batch(u_, 2, 0, in.data(), s2, out.data()), "guided step");
+    mkb_guided_euler(x.data(), out.data(), out.data() + n, scale, sigma, sigma_next, long(n));
+    return true;
+}
+
+// ------------------------------------------------------------------------------------------------ VAE
+
+Vae::Vae(const mkb_vae_config& cfg) : cfg_(cfg) { check(mkb_vae_create(&cfg, &v_), "vae create"); }
+
+Vae::~Vae() { mkb_vae_destroy(v_); }
+
+std::vector<float> Vae::decode(std::span<const float> latents, uint32_t h, uint32_t w)
+{
+    if (latents.size() != uint64_t(h) * w * latent_width())
+        throw std::runtime_error("latents must be [h * w][" + std::to_string(latent_width()) + "]");
+    std::vector<float> img(uint64_t(16 * h) * (16 * w) * 4);
+    check(mkb_vae_decode(v_, latents.data(), int(h), int(w), img.data()), "decode");
+    return img;
+}
+
+void Vae::set_latent_stats(std::span<const float> mean, std::span<const float> std)
+{
+    if (mean.size() != std.size())
+        throw std::runtime_error("latent statistics: as many means as deviations");
+    check(mkb_vae_set_latent_stats(v_, mean.data(), std.data(), int(mean.size())), "latent statistics");
+}
+
+void Vae::init_random(uint64_t seed, float std) { check(mkb_vae_init_random(v_, seed, std), "vae init_random"); }
+
+int Vae::load(const std::vector<std::string>& files, bool strict)
+{
+    std::vector<const char*> p;
+    for (const auto& f : files)
+        p.push_back(f.c_str());
+    int n = 0;
+    check(mkb_vae_load_safetensors(v_, p.data(), int(p.size()), strict ? 1 : 0, &n), "vae load");
+    return n;
 }
 
 }  // namespace mkb::image

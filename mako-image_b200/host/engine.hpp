@@ -5,8 +5,10 @@
 //   Engine::begin / step            (engine.hpp:165-166)   -> mkb_dit_begin / mkb_dit_step
 //   Engine::sigmas / top_sigma      (engine.hpp:189-192)   -> mkb_sigmas / mkb_top_sigma
 //   Engine::generate's loop         (engine.cpp:367-508)   -> Engine::denoise: CFG, Euler, ER-SDE
+//   Engine::decode                  (engine.cpp:862-954)   -> Vae::decode (mkb_vae_decode)
+//   Sdxl::begin / step              (sdxl.cpp:672-953)     -> Sdxl (mkb_unet_begin / mkb_unet_step)
 //   Sampler, parse_sampler          (engine.hpp:49-53)
-// Left out (outside the hot path): text encoding (prompt embeddings are an input), the VAE, image I/O, LoRA files.
+// Left out (outside the hot path): text encoding (prompt embeddings are an input); image I/O is in png.hpp.
 #pragma once
 
 #include "../../include/mkb_image.h"
@@ -37,8 +39,8 @@ public:
     virtual float default_guidance() const = 0;
     virtual bool predicts_noise() const { return false; }
     virtual Sampler default_sampler() const { return Sampler::euler; }
-    // A token's latent values (64: 16 channels x a 2x2 patch).
-    uint32_t latent_width() const { return 64; }
+    // A token's latent values (Qwen-Image: 64, 16 channels x a 2x2 patch; SDXL: 16, 4 channels x 2x2).
+    virtual uint32_t latent_width() const { return 64; }
 
     virtual void begin(std::span<const float> prompt, uint32_t h, uint32_t w, uint32_t slot = 0) = 0;
     virtual std::vector<float> step(std::span<const float> latents, float sigma, uint32_t slot = 0) = 0;
@@ -48,15 +50,16 @@ public:
     virtual float top_sigma(uint32_t tokens) const;
 
     // Engine::generate's denoising loop (engine.cpp:453-507) from prompt embeddings to the final latents: noise
-    // from `noise` (or seeded), guidance with the negative prompt's embeddings when given and scale != 1, then
-    // Euler, Euler ancestral or ER-SDE steps. The reference then decodes with the VAE (not part of this path).
+    // from `noise` (or seeded; for a model that predicts the noise scaled to the top level's sqrt(1 + sigma^2),
+    // engine.cpp:453-458), guidance with the negative prompt's embeddings when given and scale != 1, then Euler,
+    // Euler ancestral or ER-SDE steps. Decoding is the VAE's (Vae::decode).
     struct Request {
-        std::span<const float> prompt, negative;  // [S][text_dim] each; negative empty: no guidance
+        std::span<const float> prompt, negative;  // the model's begin() layout; negative empty: no guidance
         uint32_t h = 64, w = 64;                   // latent grid (tokens)
         uint32_t steps = 0;                        // 0: default_steps()
         std::optional<float> guidance, terminal;
         std::optional<Sampler> sampler;
-        std::span<const float> noise;              // [h * w][64]; empty: from seed
+        std::span<const float> noise;              // [h * w][latent_width()]; empty: from seed
         uint64_t seed = 0;
         std::function<void(uint32_t, uint32_t)> progress;
     };
@@ -107,6 +110,64 @@ private:
     mkb_dit_config cfg_{};
     uint32_t gh_ = 0, gw_ = 0;
     uint32_t prompt_rows_[2] = {0, 0};
+};
+
+// The SDXL UNet on the B200 kernels (mkb_unet): an eps-predicting model with the discrete SDXL schedule.
+class Sdxl final : public Engine {
+public:
+    explicit Sdxl(const mkb_unet_config& cfg);
+    ~Sdxl() override;
+    Sdxl(const Sdxl&) = delete;
+    Sdxl& operator=(const Sdxl&) = delete;
+
+    const char* name() const override { return "SDXL (B200)"; }
+    uint32_t default_steps() const override { return 28; }
+    float default_guidance() const override { return 6.0f; }
+    bool predicts_noise() const override { return true; }
+    uint32_t latent_width() const override { return 16; }
+
+    // prompt: [S, then S x context_dim context rows, then pooled_dim pooled values], the reference's prompt
+    // embeddings layout (Sdxl::begin, sdxl.cpp:672-681).
+    void begin(std::span<const float> prompt, uint32_t h, uint32_t w, uint32_t slot = 0) override;
+    std::vector<float> step(std::span<const float> latents, float sigma, uint32_t slot = 0) override;
+    std::vector<float> sigmas(uint32_t steps, uint32_t tokens,
+                              std::optional<float> terminal = std::nullopt) const override;
+    float top_sigma(uint32_t tokens) const override;
+
+    void init_random(uint64_t seed, float std = 0.02f);
+    mkb_unet* handle() { return u_; }
+
+protected:
+    bool guided_step(std::vector<float>& x, float sigma, float sigma_next, float scale) override;
+
+private:
+    mkb_unet* u_ = nullptr;
+    mkb_unet_config cfg_{};
+    uint32_t gh_ = 0, gw_ = 0;
+    uint32_t ctx_rows_[2] = {0, 0};
+};
+
+// The VAE decoder (mkb_vae): Engine::decode's tokens-to-image pass.
+class Vae {
+public:
+    explicit Vae(const mkb_vae_config& cfg);
+    ~Vae();
+    Vae(const Vae&) = delete;
+    Vae& operator=(const Vae&) = delete;
+
+    // latents [h * w][4 * latent] to RGBA [16 h][16 w][4] in [-1, 1] (engine.cpp:862-954)
+    std::vector<float> decode(std::span<const float> latents, uint32_t h, uint32_t w);
+    // per token value: the decoder sees latents * std + mean (engine.cpp:890-898)
+    void set_latent_stats(std::span<const float> mean, std::span<const float> std);
+    void init_random(uint64_t seed, float std = 0.02f);
+    // Weights from checkpoint files by their own names (mkb_vae_load_safetensors); returns the count written.
+    int load(const std::vector<std::string>& files, bool strict = true);
+    uint32_t latent_width() const { return uint32_t(4 * cfg_.latent); }
+    mkb_vae* handle() { return v_; }
+
+private:
+    mkb_vae* v_ = nullptr;
+    mkb_vae_config cfg_{};
 };
 
 }  // namespace mkb::image

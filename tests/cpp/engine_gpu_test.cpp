@@ -1,11 +1,15 @@
 // The C++ Engine mirror on the B200 kernels: a small Qwen-Image-shape model (random weights), three guided Euler
 // steps through Engine::denoise (cond + uncond batched on the device, update fused) against the same steps as two
 // step() calls combined on the host, for both block variants; then the device loop (QwenImage::denoise_device)
-// against the host loop, and its ER-SDE run for reproducibility. Exit 0 on success.
+// against the host loop, and its ER-SDE run for reproducibility. Then the SDXL side through the C ABI: Sdxl::denoise
+// (noise at the top level's scale, cond + uncond batched) against unbatched step() calls, and Vae::decode of its
+// latents (mkb_vae_decode). Exit 0 on success.
 #include "../../mako-image_b200/host/engine.hpp"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <stdexcept>
 #include <vector>
 
 int main()
@@ -94,6 +98,94 @@ int main()
         std::printf("  %-4s variant %d: device ER-SDE reproducible (%d), finite (%d), differs from Euler by %.3e\n",
                     eok ? "ok" : "FAIL", variant, int(same), int(fin), diff);
         failures += !eok;
+    }
+    {
+        // SDXL: a reduced UNet (the full model's block structure) and VAE.
+        mkb_unet_config c{};
+        const int ch[3] = {64, 128, 256}, dep[3] = {0, 1, 1};
+        for (int k = 0; k < 3; ++k) {
+            c.channels[k] = ch[k];
+            c.depth[k] = dep[k];
+        }
+        c.layers = 2;
+        c.context_dim = 256;
+        c.pooled_dim = 128;
+        c.max_batch = 2;
+        c.max_gh = 8;
+        c.max_gw = 16;
+        c.max_context = 77;
+        c.slots = 2;
+        const uint32_t h = 8, w = 16, S = 20, N = h * w;
+        // The reference's prompt layout: [S, S x context_dim, pooled_dim].
+        auto embeds = [&](float f) {
+            std::vector<float> p = {float(S)};
+            for (uint32_t j = 0; j < S * 256 + 128; ++j)
+                p.push_back(std::sin(f * float(j) + 0.3f));
+            return p;
+        };
+        const auto prompt = embeds(0.11f), neg = embeds(0.05f);
+        std::vector<float> noise(N * 16);
+        for (size_t j = 0; j < noise.size(); ++j)
+            noise[j] = std::sin(0.41f * float(j) + 2.0f);
+        mkb::image::Sdxl a(c), b(c);
+        a.init_random(7);
+        b.init_random(7);
+        mkb::image::Engine::Request r;
+        r.prompt = prompt;
+        r.negative = neg;
+        r.h = h;
+        r.w = w;
+        r.steps = 3;
+        r.guidance = 5.0f;
+        r.noise = noise;
+        const auto got = a.denoise(r);
+        const auto sig = b.sigmas(3, N);
+        b.begin(prompt, h, w, 0);
+        b.begin(neg, h, w, 1);
+        std::vector<float> x(noise);
+        const float s0 = std::sqrt(1.0f + sig[0] * sig[0]);
+        for (float& v : x)
+            v *= s0;
+        for (int i = 0; i < 3; ++i) {
+            const auto v = b.step(x, sig[i], 0);
+            const auto u = b.step(x, sig[i], 1);
+            mkb_guided_euler(x.data(), v.data(), u.data(), 5.0f, sig[i], sig[i + 1], long(x.size()));
+        }
+        double err = 0, mx = 0;
+        bool finite = true;
+        for (size_t j = 0; j < x.size(); ++j) {
+            err = std::max(err, double(std::fabs(x[j] - got[j])));
+            mx = std::max(mx, double(std::fabs(x[j])));
+            finite &= std::isfinite(got[j]);
+        }
+        const bool ok = finite && err <= 1e-4 * std::max(1.0, mx);
+        std::printf("  %-4s sdxl: batched guided steps vs two step() calls, max-abs %.3e\n", ok ? "ok" : "FAIL", err);
+        failures += !ok;
+
+        mkb_vae_config vc{};
+        const int vch[4] = {128, 128, 128, 256};
+        for (int k = 0; k < 4; ++k)
+            vc.channels[k] = vch[k];
+        vc.layers = 1;
+        vc.latent = 4;
+        vc.scale = 0.13025f;
+        vc.max_gh = int(h);
+        vc.max_gw = int(w);
+        mkb::image::Vae vae(vc);
+        vae.init_random(9);
+        const auto img = vae.decode(got, h, w);
+        bool vok = img.size() == size_t(16 * h) * (16 * w) * 4;
+        for (size_t j = 0; vok && j < img.size(); ++j)
+            vok = std::isfinite(img[j]) && img[j] >= -1.0f && img[j] <= 1.0f && (j % 4 != 3 || img[j] == 1.0f);
+        bool threw = false;
+        try {
+            vae.decode(std::vector<float>(7), h, w);
+        } catch (const std::runtime_error&) {
+            threw = true;
+        }
+        vok = vok && threw;
+        std::printf("  %-4s sdxl: VAE decode to RGBA in [-1, 1], wrong latent size rejected\n", vok ? "ok" : "FAIL");
+        failures += !vok;
     }
     std::printf("%s\n", failures ? "FAILED" : "passed");
     return failures ? 1 : 0;

@@ -23,5 +23,6 @@ def test_engine_loop_cpu():
 
 @pytest.mark.gpu
 def test_engine_guided_steps_gpu(cuda):
-    """Engine::denoise's batched guided steps on the device against unbatched step() calls, both variants."""
+    """Engine::denoise's batched guided steps on the device against unbatched step() calls, both DiT variants and the
+    SDXL UNet, and the VAE decode, all through the C ABI."""
     _build_and_run("engine_gpu_test")
