@@ -209,6 +209,17 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def cfg_pair_group(dist, ws, rank):
+    """The process group of this rank's CFG pair when cond and uncond of one image sit on ranks 2i and 2i + 1.
+    new_group is collective, so every rank creates every pair's group and keeps its own."""
+    mine = None
+    for r0 in range(0, ws, 2):
+        grp = dist.new_group([r0, r0 + 1])
+        if rank // 2 == r0 // 2:
+            mine = grp
+    return mine
+
+
 def run_mkb(args, cfg):
     import numpy as np
     import torch
@@ -225,7 +236,17 @@ def run_mkb(args, cfg):
                                              device_id=dev)
     h, w, S, n_img = cfg["h"], cfg["w"], cfg["S"], cfg["images"]
     N = h * w
-    B = n_img * (2 if cfg["cfg"] else 1)
+    split_mode = args.split_samples and ws > 1
+    half_pair = False  # sample split with one sample (half a CFG pair) per rank
+    if split_mode:
+        # The job's images spread over the ranks, whole CFG pairs per rank while there are enough (strong scaling:
+        # the total work is fixed); with twice as many ranks as images, cond and uncond of one image sit on two
+        # neighbouring ranks, which exchange their predictions for the guided update.
+        if not cfg["cfg"] or (n_img % ws and ws != 2 * n_img):
+            raise SystemExit(f"--split-samples: {n_img} CFG pairs do not divide over {ws} ranks")
+        half_pair = ws == 2 * n_img
+        n_img = 1 if half_pair else n_img // ws
+    B = 1 if half_pair else n_img * (2 if cfg["cfg"] else 1)
     d = mkimage.Dit(mkimage.DitConfig(variant=mkimage.QWEN1, hidden=D, heads=H, ffn=F, blocks=cfg["blocks"],
                                       text_dim=TD, max_batch=B, max_text_tokens=S, max_image_tokens=N, slots=B))
     d.init_random(seed=1234)
@@ -236,10 +257,12 @@ def run_mkb(args, cfg):
         torch.distributed.broadcast_object_list(obj, src=0)
         d.set_sequence_parallel(obj[0], rank, ws)
     for s in range(B):
-        prompt = rng.normal(rng.tensor_key(99, s), S * TD).reshape(S, TD)
+        prompt = rng.normal(rng.tensor_key(99, (rank % 2) if half_pair else s), S * TD).reshape(S, TD)
         d.begin(prompt, h, w, slot=s)
-    # Replicas step their own images; a sequence-parallel group steps the same images on every rank.
-    lat_host = rng.normal(rng.tensor_key(98, 0 if sp_mode else rank), n_img * N * 64).reshape(n_img, N, 64)
+    # Replicas step their own images; a sequence-parallel group steps the same images on every rank; split samples
+    # step their share of the job's images (both ranks of a split pair the same latents).
+    lat_key = 0 if sp_mode else (rank // 2 if half_pair else rank)
+    lat_host = rng.normal(rng.tensor_key(98, lat_key), n_img * N * 64).reshape(n_img, N, 64)
     lat = torch.from_numpy(lat_host).to(dev)
     sig = mkimage.sigmas(40, N)
     i0 = int(np.argmin(np.abs(sig[:-1] - 0.5)))
@@ -249,8 +272,23 @@ def run_mkb(args, cfg):
     torch.cuda.set_stream(stream)
     sp = mkimage.stream_ptr(stream)
 
+    pair_group = None
+    if half_pair:
+        pair_group = cfg_pair_group(torch.distributed, ws, rank)
+        vel = torch.empty(N * 64, device=dev)
+        both = torch.empty(2, N * 64, device=dev)
+        guided = torch.empty(N * 64, device=dev)
+
     def one_step():
-        if cfg["cfg"]:
+        if half_pair:
+            # This rank's prediction, the partner's by an all-gather of the pair, then the same guided Euler update
+            # on both ranks (rank 2i holds the prompt, 2i + 1 the negative).
+            d.step_batch_dev([0], lat.data_ptr(), [sigma], vel.data_ptr(), sp)
+            torch.distributed.all_gather_into_tensor(both, vel, group=pair_group)
+            mkimage.check(mkimage.lib.mkb_cfg_combine_dev(guided.data_ptr(), both[0].data_ptr(), both[1].data_ptr(),
+                                                          4.0, N * 64, sp))
+            mkimage.check(mkimage.lib.mkb_axpy_dev(lat.data_ptr(), guided.data_ptr(), sigma_next - sigma, N * 64, sp))
+        elif cfg["cfg"]:
             d.step_cfg_dev(n_img, lat.data_ptr(), sigma, sigma_next, 4.0, sp)
         else:
             out = torch.empty_like(lat)
@@ -280,12 +318,13 @@ def run_mkb(args, cfg):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
         torch.distributed.barrier()
-    value = n_img * (1 if sp_mode else ws) * 1e3 / ms
+    job_images = cfg["images"] if (sp_mode or split_mode) else n_img * ws
+    value = job_images * 1e3 / ms
     flops_step = d.step_flops(B) / (ws if sp_mode else 1)  # this rank's share of the step
 
     # End to end through the public host-buffer API: pinned latents in, updated latents out, every step.
     e2e = None
-    if cfg["cfg"] and n_img == 1:
+    if cfg["cfg"] and n_img == 1 and not half_pair:
         pinned = torch.from_numpy(lat_host[0].copy()).pin_memory()
         guided = d.step_cfg_inplace(pinned.numpy())  # H2D from and D2H into the pinned buffer every step
         for _ in range(2):
@@ -300,29 +339,20 @@ def run_mkb(args, cfg):
             t = torch.tensor([t_e2e], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             t_e2e = t.item()
-        e2e = {"value": n_img * ws / t_e2e, "unit": UNIT, "h2d_bytes_per_step": N * 64 * 4,
+        e2e = {"value": job_images / t_e2e, "unit": UNIT, "h2d_bytes_per_step": N * 64 * 4,
                "d2h_bytes_per_step": N * 64 * 4}
 
-    # Roofline of the dominant kernel: the tcgen05 GEMM at the step's FFN-up shape (the largest GEMM, GELU
-    # epilogue), timed alone on the same stream with CUDA events.
+    # Roofline: each of the block's hot kernels timed alone on the same stream with CUDA events at the step's
+    # shapes; the dominant one (the FFN-up GEMM) is the line's `kernel`, the table gives all five and the
+    # time-weighted fraction of one block's set.
     peak_tf, peak_hbm, peak_kind = _peaks()
-    M_img = B * N
-    xa = torch.randn(M_img, D, device=dev).to(torch.bfloat16)
-    wa = (torch.randn(F, D, device=dev) * 0.02).to(torch.bfloat16)
-    ba = torch.zeros(F, device=dev)
-    ya = torch.empty(M_img, F, device=dev, dtype=torch.bfloat16)
-    for _ in range(3):
-        mkimage.ops.proj(xa, wa, ba, act=mkimage.ops.ACT_GELU_TANH, out=ya)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    g0.record(stream)
-    for _ in range(reps):
-        mkimage.ops.proj(xa, wa, ba, act=mkimage.ops.ACT_GELU_TANH, out=ya)
-    g1.record(stream)
-    torch.cuda.synchronize()
-    gemm_ms = g0.elapsed_time(g1) / reps
-    gemm_flops = 2.0 * M_img * F * D
-    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    table = {}
+    for name, (fn, work) in hot_kernels(dev, cfg).items():
+        kms = time_kernel(fn, stream)
+        table[name] = {"ms": kms, "achieved": work / (kms * 1e-3) / 1e12, "frac": work / (kms * 1e-3) / 1e12 / peak_tf,
+                       "gflop": work / 1e9}
+    mkimage.ops.check_kernels()
+    achieved = table["ffn_up"]["achieved"]
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "gemm_ffn_up_config2.md")) as f:
@@ -331,10 +361,14 @@ def run_mkb(args, cfg):
                     traffic = float(ln.split(":")[1])
     except Exception:
         pass
+    block_work = sum(t["gflop"] for t in table.values()) * 1e9
+    block_ms = sum(t["ms"] for t in table.values())
     roofline = {"bound": "tensor", "kernel": "k_gemm2 (tcgen05 CTA pair, 256x256 tiles, FFN-up 8192x12288x3072, "
                                               "GELU epilogue)",
                 "achieved": achieved, "peak": peak_tf, "peak_kind": peak_kind, "unit": "TFLOP/s",
                 "frac": achieved / peak_tf, "traffic": traffic,
+                "kernels": table,
+                "block_time_weighted_frac": block_work / (block_ms * 1e-3) / 1e12 / peak_tf,
                 **_step_fracs(flops_step / (ms * 1e-3) / 1e12)}
 
     cpu = None
@@ -345,12 +379,17 @@ def run_mkb(args, cfg):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "strong" if sp_mode else "weak",
+                "scaling": "strong" if (sp_mode or split_mode) else "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": cfg["workload"], "hidden": D, "heads": H, "ffn": F, "blocks": cfg["blocks"],
                            "image_tokens": N, "text_tokens": S, "samples_per_gpu": B,
                            "parallelism": (f"sequence parallel x{ws} (each rank 1/{ws} of every sample's joint rows, "
                                            f"K/V all-gathered per block over NCCL)") if sp_mode else
+                                          (f"sample split x{ws} ({cfg['images']} images, "
+                                           + ("cond / uncond of an image on neighbouring ranks, predictions "
+                                              "all-gathered per step)" if half_pair else
+                                              f"{n_img} whole CFG pairs per rank, no collective)"))
+                                          if split_mode else
                                           f"replicas x{ws} (images per GPU as configured, CFG pair batched)",
                            "l2": "inputs larger than L2 (40.8 GB of weights streamed per step)",
                            "step_tflop": flops_step / 1e12},
@@ -579,56 +618,94 @@ def run_sdxl(args, which):
         torch.distributed.destroy_process_group()
 
 
-def run_kernel(args, cfg):
-    """One hot kernel alone at the config's shape, for profiling: 3 warm-up launches then 3 timed ones (CUDA
-    events). gemm: the FFN-up projection (GELU epilogue); attention: the joint flash attention of one block;
-    oproj: the image rows' O-projection with the gated residual (TMA reduce-add into the fp32 residual stream)."""
+def hot_kernels(dev, cfg, names=None):
+    """The block's hot kernels at the config's image-row shapes (CFG batch rows together), each as (launch, FLOPs):
+    qkv (the fused QKV projection with per-head RMSNorm + RoPE into the attention layout), attention (joint, all
+    L = S + N keys), oproj (the O-projection with the gated residual reduce-added by TMA), ffn_up (GELU epilogue),
+    ffn_down (gated residual). Synthetic inputs of the right shapes; weights N(0, 0.02)."""
     import torch
     import mkimage
 
-    dev = torch.device("cuda", 0)
     h, w, S, n_img = cfg["h"], cfg["w"], cfg["S"], cfg["images"]
     N = h * w
     B = n_img * (2 if cfg["cfg"] else 1)
     L = S + N
+    M = B * N
     g = torch.Generator(device=dev).manual_seed(0)
-    if args.kernel == "gemm":
-        x = torch.randn(B * N, D, device=dev, generator=g).to(torch.bfloat16)
-        wt = (torch.randn(F, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        b = torch.zeros(F, device=dev)
-        y = torch.empty(B * N, F, device=dev, dtype=torch.bfloat16)
-        fn = lambda: mkimage.ops.proj(x, wt, b, act=mkimage.ops.ACT_GELU_TANH, out=y)  # noqa: E731
-        work, unit = 2.0 * B * N * F * D, "TFLOP/s"
-    elif args.kernel == "oproj":
-        x = torch.randn(B * N, D, device=dev, generator=g).to(torch.bfloat16)
-        wt = (torch.randn(D, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        b = torch.zeros(D, device=dev)
-        resid = torch.randn(B * N, D, device=dev, generator=g)
-        gate = torch.randn(B, D, device=dev, generator=g) * 0.1
-        fn = lambda: mkimage.ops.proj_gate_add(x, wt, resid, gate, bias=b, rows_per_sample=N)  # noqa: E731
-        work, unit = 2.0 * B * N * D * D, "TFLOP/s"
-    elif args.kernel == "attention":
+    out = {}
+    names = names or ["qkv", "attention", "oproj", "ffn_up", "ffn_down"]
+
+    def mat(r, c, sd=1.0):
+        return (torch.randn(r, c, device=dev, generator=g) * sd).to(torch.bfloat16)
+
+    if "qkv" in names:
+        x, wq = mat(M, D), mat(3 * D, D, 0.02)
+        bq = torch.zeros(3 * D, device=dev)
+        nq, nk = torch.ones(128, device=dev), torch.ones(128, device=dev)
+        rope = torch.zeros(L, 64, 2, device=dev)
+        rope[..., 0] = 1.0
+        qh = torch.empty(B, H, L, 128, device=dev, dtype=torch.bfloat16)
+        kh, vh = torch.empty_like(qh), torch.empty_like(qh)
+        out["qkv"] = (lambda: mkimage.ops.proj_qkv_heads(x, wq, bq, nq, nk, rope, qh, kh, vh, N, S),
+                      2.0 * M * 3 * D * D)
+    if "attention" in names:
         q = torch.randn(B, H, L, 128, device=dev, generator=g).to(torch.bfloat16)
         k, v = torch.randn_like(q), torch.randn_like(q)
         o0 = torch.empty(B * S, D, device=dev, dtype=torch.bfloat16)
         o1 = torch.empty(B * N, D, device=dev, dtype=torch.bfloat16)
-        fn = lambda: mkimage.ops.attention(q, k, v, o0, o1, split=S)  # noqa: E731
-        work, unit = 4.0 * B * L * L * D, "TFLOP/s"
-    else:
-        raise SystemExit(f"unknown kernel {args.kernel}")
-    for _ in range(3):
+        out["attention"] = (lambda: mkimage.ops.attention(q, k, v, o0, o1, split=S), 4.0 * B * L * L * D)
+    if "oproj" in names or "ffn_down" in names:
+        resid = torch.randn(M, D, device=dev, generator=g)
+        gate = torch.randn(B, D, device=dev, generator=g) * 0.1
+        bd = torch.zeros(D, device=dev)
+        if "oproj" in names:
+            xo, wo = mat(M, D), mat(D, D, 0.02)
+            out["oproj"] = (lambda: mkimage.ops.proj_gate_add(xo, wo, resid, gate, bias=bd, rows_per_sample=N),
+                            2.0 * M * D * D)
+        if "ffn_down" in names:
+            xf, wf = mat(M, F), mat(D, F, 0.02)
+            out["ffn_down"] = (lambda: mkimage.ops.proj_gate_add(xf, wf, resid, gate, bias=bd, rows_per_sample=N),
+                               2.0 * M * D * F)
+    if "ffn_up" in names:
+        xu, wu = mat(M, D), mat(F, D, 0.02)
+        bu = torch.zeros(F, device=dev)
+        yu = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+        out["ffn_up"] = (lambda: mkimage.ops.proj(xu, wu, bu, act=mkimage.ops.ACT_GELU_TANH, out=yu),
+                         2.0 * M * F * D)
+    return out
+
+
+def time_kernel(fn, stream, reps=20, warmup=3):
+    """Mean milliseconds per launch over `reps` back-to-back launches, CUDA events on the launching stream."""
+    import torch
+
+    for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(3):
+    e0.record(stream)
+    for _ in range(reps):
         fn()
-    e1.record()
+    e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / 3
+    return e0.elapsed_time(e1) / reps
+
+
+def run_kernel(args, cfg):
+    """One hot kernel alone at the config's shape, for profiling (see hot_kernels): 3 warm-up launches then 3 timed
+    ones (CUDA events)."""
+    import torch
+    import mkimage
+
+    dev = torch.device("cuda", 0)
+    name = {"gemm": "ffn_up"}.get(args.kernel, args.kernel)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    fn, work = hot_kernels(dev, cfg, [name])[name]
+    ms = time_kernel(fn, stream, reps=3)
     mkimage.ops.check_kernels()
-    print(json.dumps({"kernel": args.kernel, "config": cfg["workload"], "ms": ms,
-                      "achieved": work / (ms * 1e-3) / 1e12, "unit": unit}), flush=True)
+    print(json.dumps({"kernel": name, "config": cfg["workload"], "ms": ms, "achieved": work / (ms * 1e-3) / 1e12,
+                      "unit": "TFLOP/s"}), flush=True)
 
 
 def main():
@@ -639,9 +716,11 @@ def main():
     ap.add_argument("--impl", choices=["mkb", "reference"], default="mkb")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split-samples", action="store_true",
+                    help="DiT configs under torchrun: the config's images spread over the ranks (strong scaling)")
     ap.add_argument("--sp", action="store_true",
                     help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
-    ap.add_argument("--kernel", choices=["gemm", "oproj", "attention"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]

@@ -90,6 +90,7 @@ _SIGS = {
     "mkb_er_sde_sigma": (_f, [_vp, _i]),
     "mkb_er_sde_step": (_i, [_vp, _i, _vp, _vp, _vp, _l, _f]),
     "mkb_cfg_combine_dev": (_i, [_vp, _vp, _vp, _f, _l, _vp]),
+    "mkb_axpy_dev": (_i, [_vp, _vp, _f, _l, _vp]),
     "mkb_euler_ancestral_dev": (_i, [_vp, _vp, _f, _f, _u64, _u64, _l, _vp]),
     "mkb_er_sde_step_dev": (_i, [_vp, _i, _vp, _vp, _vp, _u64, _u64, _l, _f, _vp]),
     "mkb_dit_guided_velocity_dev": (_i, [_vp, _i, _vp, _f, _f, _vp, _vp]),
