@@ -256,6 +256,8 @@ def run_mkb(args, cfg):
         obj = [mkimage.nccl_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
         d.set_sequence_parallel(obj[0], rank, ws)
+        if args.sp_exchange == "peer":
+            d.set_peer_exchange(True)
     for s in range(B):
         prompt = rng.normal(rng.tensor_key(99, (rank % 2) if half_pair else s), S * TD).reshape(S, TD)
         d.begin(prompt, h, w, slot=s)
@@ -384,7 +386,9 @@ def run_mkb(args, cfg):
                 "config": {"workload": cfg["workload"], "hidden": D, "heads": H, "ffn": F, "blocks": cfg["blocks"],
                            "image_tokens": N, "text_tokens": S, "samples_per_gpu": B,
                            "parallelism": (f"sequence parallel x{ws} (each rank 1/{ws} of every sample's joint rows, "
-                                           f"K/V all-gathered per block over NCCL)") if sp_mode else
+                                           + ("K/V shards pushed into the peers' memory by copy engines during the "
+                                              "attention)" if args.sp_exchange == "peer" else
+                                              "K/V all-gathered per block over NCCL)")) if sp_mode else
                                           (f"sample split x{ws} ({cfg['images']} images, "
                                            + ("cond / uncond of an image on neighbouring ranks, predictions "
                                               "all-gathered per step)" if half_pair else
@@ -720,6 +724,9 @@ def main():
                     help="DiT configs under torchrun: the config's images spread over the ranks (strong scaling)")
     ap.add_argument("--sp", action="store_true",
                     help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
+    ap.add_argument("--sp-exchange", choices=["peer", "nccl"], default="peer",
+                    help="--sp: K/V shards pushed into the peers' memory by copy engines during the attention "
+                         "(peer) or all-gathered by NCCL before it (nccl)")
     ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()

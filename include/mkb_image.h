@@ -144,9 +144,11 @@ enum { MKB_MASK_NONE = 0, MKB_MASK_COND_CAUSAL = 1 };
 
 /* Flash attention, head dim d = 64 or 128: out = softmax(q k^T / sqrt(d)) v per (sample, head). q is
  * [B][H][Lq_rows][d], k and v [B][H][Lk_rows][d] (bf16, head-major, as mkb_proj_qkv_heads / mkb_proj_heads write
- * them); the first Lq query rows and Lk keys are used. Query row i sits at joint position q_pos0 + i; keys at positions 0..Lk-1. MKB_MASK_COND_CAUSAL: a
- * query at position < cond_len sees keys < cond_len only (the reference's text rows, which is what lets it cache the
- * text K/V; qwen_image.cpp:251-271). Output rows are bf16 [.][H*128]: position p < split goes to row
+ * them); the first Lq query rows and Lk keys are used. Query row i sits at joint position q_pos0 + i; keys at
+ * positions 0..Lk-1. MKB_MASK_COND_CAUSAL (the runtime's `block` argument, qwen_image.cpp:271 and sdxl.cpp:501): a
+ * query at position p < cond_len sees keys 0..p only, causal and never a later row (the reference's text rows, which
+ * is what lets it cache the text K/V, qwen_image.cpp:251-262); queries at p >= cond_len see every key. cond_len >= Lk
+ * is plain causal attention (the CLIP encoders' block = UINT32_MAX). Output rows are bf16 [.][H*128]: position p < split goes to row
  * (b * rows0 + p) of out0, otherwise row (b * rows1 + p - split) of out1 (the text and image streams' inputs of the
  * output projection; columns [h * d, h * d + d)). Replaces TransformerRuntime::attention() (qwen_image.cpp:271) and the
  * hd-64 flash_attn_coop_64_32 the SDXL UNet calls (sdxl.cpp:450-457). */
@@ -162,6 +164,20 @@ mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const voi
                                    int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
                                    int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
                                    int kv_shard_rows, int kv_plane_stride, void* stream);
+
+/* The same over shards that other ranks copy into this GPU's memory while the kernel runs (the sequence-parallel
+ * peer exchange; no counterpart in the reference, which runs on one device). Shard own_shard is complete at launch;
+ * before reading any other shard g the kernel waits until the 64-bit device flag shard_ready[g] >= *shard_expect
+ * (both device pointers; an acquire load at system scope). Every CTA starts at its own shard's keys and wraps round,
+ * so only the online softmax's rounding differs from mkb_attention_kv_shards. A flag that does not reach the value
+ * within 2 s ends the launch; mkb_check_kernels then reports MKB_ERR_KERNEL with bit 0x100. mask must be
+ * MKB_MASK_NONE. */
+mkb_status mkb_attention_kv_arriving(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk,
+                                     int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
+                                     int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
+                                     int kv_shard_rows, int kv_plane_stride, int own_shard,
+                                     const unsigned long long* shard_ready, const unsigned long long* shard_expect,
+                                     void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * The denoiser (image::Engine's model interface, src/image/engine.hpp:158-166, on the Qwen-Image-style MMDiT).
@@ -294,6 +310,16 @@ mkb_status mkb_dit_set_probe(mkb_dit* d, mkb_probe_fn fn, void* user);
 #define MKB_NCCL_ID_BYTES 128
 mkb_status mkb_nccl_unique_id(void* out, size_t bytes);
 mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int rank, int world);
+/* Moves the per-block K/V exchange of a sequence-parallel handle from the NCCL all-gather to peer memory (enable 1)
+ * or back (0); collective, every rank with the same value, after mkb_dit_set_sequence_parallel. No counterpart in the
+ * reference. Every rank exports a K/V region over CUDA IPC (the ranks must share a node, each GPU able to reach the
+ * others) and maps the others'; after each block's QKV projection a copy engine pushes the rank's shard into every
+ * peer's region and then raises the rank's ready flag there, and the attention starts on its own shard and waits
+ * (bounded, 2 s; MKB_ERR_KERNEL on timeout) for each other shard's flag, so the transfers overlap the attention
+ * instead of preceding it. The key order differs per rank, so results match the one-GPU step to rounding, no longer
+ * bit for bit; all ranks still end with identical latents. Fails with MKB_ERR_CUDA on every rank if any rank cannot
+ * allocate, export or map, leaving the all-gather in place. */
+mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable);
 /* The rows rank `rank` of `world` owns for S text and N image tokens per sample: text_rows (S on rank 0, else 0),
  * image_rows starting at image token image_row0, and shard_rows = (S + N) / world joint rows. Host arithmetic only. */
 mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,

@@ -333,6 +333,18 @@ mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const voi
                                    int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
                                    int kv_shard_rows, int kv_plane_stride, void* stream)
 {
+    return mkb_attention_kv_arriving(q, Lq, Lq_rows, k, v, Lk, Lk_rows, B, H, head_dim, q_pos0, mask, cond_len, split,
+                                     out0, ld0, rows0, out1, ld1, rows1, kv_shard_rows, kv_plane_stride, -1, nullptr,
+                                     nullptr, stream);
+}
+
+mkb_status mkb_attention_kv_arriving(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk,
+                                     int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
+                                     int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
+                                     int kv_shard_rows, int kv_plane_stride, int own_shard,
+                                     const unsigned long long* shard_ready, const unsigned long long* shard_expect,
+                                     void* stream)
+{
     if (!q || !k || !v)
         return fail(MKB_ERR_INVALID, "attention: null q/k/v");
     if (mask != MKB_MASK_NONE && mask != MKB_MASK_COND_CAUSAL)
@@ -356,6 +368,9 @@ mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const voi
     a.rows1 = rows1;
     a.kv_shard_rows = kv_shard_rows;
     a.kv_plane_stride = kv_plane_stride;
+    a.own_shard = own_shard < 0 ? -1 : own_shard;
+    a.shard_ready = shard_ready;
+    a.shard_expect = shard_expect;
     a.status = device_status_word();
     AttnOp op;
     const char* err = nullptr;

@@ -63,9 +63,6 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c);
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b);
-
 // 2^x for two lanes on the FMA pipe with packed f32x2 arithmetic: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f
 // by the degree-3 polynomial of least maximum relative error on that interval (a minimax fit by the Remez exchange
 // algorithm, tests/ex2_fit.py; 7.5e-5, below bf16's 3.9e-3; tests/test_ex2_poly_cpu.py checks the bound), 2^n added
@@ -90,22 +87,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c)
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
-}
-
-// Packed two-lane fp32 arithmetic: one instruction for both lanes.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
-{
-    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b),
-             rc = *reinterpret_cast<uint64_t*>(&c), rd;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
-    return *reinterpret_cast<float2*>(&rd);
-}
-
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
-{
-    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b), rd;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
-    return *reinterpret_cast<float2*>(&rd);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
@@ -148,14 +129,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q0 = blockIdx.x * 2 * kTile, h = blockIdx.y, b = blockIdx.z;
     const int bh = b * a.H + h;
 
-    // Keys this CTA needs: query rows that are all text (condition-causal) stop at the text boundary.
+    // Keys this CTA needs: when its query rows are all condition rows (causal among themselves), keys up to the
+    // last row's position.
     int n_keys = a.Lk;
     if (a.mask == kMaskCondCausal) {
         const int last_pos = a.q_pos0 + min(q0 + 2 * kTile, a.Lq) - 1;
         if (last_pos < a.cond_len)
-            n_keys = min(a.Lk, a.cond_len);
+            n_keys = min(a.Lk, last_pos + 1);
     }
     const int nkv = (n_keys + kTile - 1) / kTile;
+    // Key tile taken at step j: j0 + j, wrapping round (j0 = 0 unless other ranks' shards arrive during the launch).
+    const int j0 = a.own_shard >= 0 ? a.own_shard * (a.kv_shard_rows / kTile) : 0;
+    const auto key_tile = [&](int j) { return j + j0 < nkv ? j + j0 : j + j0 - nkv; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -195,6 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
             bool ok = true;
+            int arrived = a.own_shard;  // the shard whose arrival was last confirmed
+            const unsigned long long want = a.own_shard >= 0 ? *a.shard_expect : 0;
             mbar_arrive_expect_tx(q_full, 2 * TB);
             for (int t = 0; t < 2; ++t)
                 for (int pn = 0; pn < HD / 64; ++pn)
@@ -206,12 +193,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                // Row and plane of key tile j (shards never split a tile: kv_shard_rows is a multiple of 128).
-                int krow = j * kTile, kplane = bh;
+                // Row and plane of the key tile (shards never split a tile: kv_shard_rows is a multiple of 128).
+                int krow = key_tile(j) * kTile, kplane = bh;
                 if (a.kv_shard_rows > 0) {
                     const int g = krow / a.kv_shard_rows;
                     krow -= g * a.kv_shard_rows;
                     kplane = g * a.kv_plane_stride + bh;
+                    if (a.own_shard >= 0 && g != arrived) {  // another rank's shard: once its copy has landed
+                        if (!wait_flag_ge(a.shard_ready + g, want, a.status, kErrShardWait, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        arrived = g;
+                    }
                 }
                 mbar_arrive_expect_tx(&k_full[st], TB);
                 for (int pn = 0; pn < HD / 64; ++pn)
@@ -309,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qrow = q0 + t * kTile + r;
         const int qpos = a.q_pos0 + qrow;
         const bool text_query = a.mask == kMaskCondCausal && qpos < a.cond_len;
-        const int key_limit = text_query ? min(a.Lk, a.cond_len) : a.Lk;
+        const int key_limit = text_query ? min(a.Lk, qpos + 1) : a.Lk;  // a condition row: keys up to its own
         const float sc = a.scale_log2;
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
@@ -325,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(t_lane + col_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
             tmem_ld32(t_lane + col_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
             tmem_wait_ld();
-            const int valid = min(kTile, key_limit - j * kTile);  // keys [0, valid) of this tile are visible
+            const int valid = min(kTile, key_limit - key_tile(j) * kTile);  // keys [0, valid) of the tile are visible
             if (valid < kTile) {
 #pragma unroll
                 for (int i = 0; i < 128; ++i)
@@ -511,6 +505,12 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         const int shards = (args.Lk + args.kv_shard_rows - 1) / args.kv_shard_rows;
         kv_rows = args.kv_shard_rows;
         kv_planes = (shards - 1) * args.kv_plane_stride + bh;
+    }
+    if (args.own_shard >= 0 &&
+        (args.kv_shard_rows <= 0 || args.mask != kMaskNone || !args.shard_ready || !args.shard_expect ||
+         long(args.own_shard) * args.kv_shard_rows >= args.Lk || (reinterpret_cast<uintptr_t>(args.shard_ready) & 7))) {
+        *err = "attention: arriving shards need K/V shards, no mask, 8-byte aligned flags and own_shard inside Lk";
+        return false;
     }
     if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) || !make_heads_map(&op.tk, k, kv_rows, kv_planes, hd, err) ||
         !make_heads_map(&op.tv, v, kv_rows, kv_planes, hd, err))

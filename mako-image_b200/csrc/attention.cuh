@@ -13,7 +13,9 @@ namespace mkb {
 
 enum AttnMask : int {
     kMaskNone = 0,      // every query sees every key (Qwen-Image-1 joint attention)
-    kMaskCondCausal = 1 // queries at joint positions < cond_len see only keys < cond_len (the reference's text rows)
+    kMaskCondCausal = 1 // a query at joint position p < cond_len sees keys 0..p (the condition rows are causal, and
+                        // never see a later row); queries at p >= cond_len see every key. cond_len = S: the reference's
+                        // text rows; cond_len >= Lk: plain causal attention (its CLIP text encoders)
 };
 
 struct AttnArgs {
@@ -40,6 +42,14 @@ struct AttnArgs {
     // of the k / v maps. This is the layout a sequence-parallel all-gather leaves (one shard per rank).
     int kv_shard_rows = 0;
     int kv_plane_stride = 0;
+    // Shards that other ranks copy in while the kernel runs (the peer-memory K/V exchange). own_shard >= 0 makes
+    // every CTA take its key tiles starting with shard own_shard (written on this GPU before the launch) and
+    // wrapping round, and wait before the first tile of any other shard g until shard_ready[g] >= *shard_expect
+    // (an acquire load at system scope, bounded by kWaitNs; on timeout the kErrShardWait bit). Needs
+    // kv_shard_rows > 0 and kMaskNone. The key order only changes the online softmax's rounding.
+    int own_shard = -1;
+    const unsigned long long* shard_ready = nullptr;
+    const unsigned long long* shard_expect = nullptr;
     uint32_t* status = nullptr;
 };
 

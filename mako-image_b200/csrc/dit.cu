@@ -8,6 +8,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "lora.cuh"
 #include "nccl_dl.cuh"
 #include "rowops.cuh"
@@ -26,6 +27,7 @@ namespace {
 
 constexpr int kHeadDim = 128, kLatent = 64, kTimeDim = 256;
 constexpr float kEps = 1e-6f;
+constexpr size_t kSpFlagBytes = 512;  // the peer exchange's ready flags: one 64-bit word per rank, up to 64 ranks
 constexpr int kSwigluBlock = 128;  // gate/up interleave of the SwiGLU GEMM (one 256-wide tile = 128 gate + 128 up)
 
 uint64_t splitmix64_host(uint64_t x)
@@ -130,6 +132,7 @@ struct DitImpl {
     struct Plan {
         std::vector<GemmOp> ops;  // indexed by the builder
         AttnOp att;
+        AttnOp att_odd;  // odd blocks' attention under the peer exchange (the second K/V buffer)
         std::vector<GemmOp> per_sample;  // ref21 txt_in2 / img_in per sample
     };
     std::map<std::tuple<int, int, int, int>, std::unique_ptr<Plan>> plans;
@@ -152,6 +155,27 @@ struct DitImpl {
     __nv_bfloat16* kv_all = nullptr;  // [world][2 (K, V)][B][H][Lg][128] for the step's B and Lg
     float* vel_x = nullptr;           // [world][B][Lg][64]: velocity exchange
     float* vel_full = nullptr;        // [Bmax][Nmax][64]: all image rows' velocities after the exchange
+    // Peer-memory exchange of the K/V shards (replaces the per-block all-gather): the QKV epilogue writes this rank's
+    // shard into its slot of this GPU's exchange region; a copy stream pushes the slot into every peer's region, peer
+    // r-1 first, then r-2 and so on (the order in which the peers' attention reaches shard r, each starting at its
+    // own), raising this rank's ready flag there after each copy; the attention waits on the flags. Blocks alternate
+    // between two K/V buffers, so no push lands in a buffer a peer still reads: this rank pushes block i + 2 after
+    // its attention of block i + 1, which waited for the peer's block-(i + 1) shard, which the peer pushes only after
+    // its own attention of block i. The copies run on copy engines, not SMs, so they overlap the attention.
+    bool sp_p2p = false;
+    uint8_t* sp_region = nullptr;          // [ready flags, kSpFlagBytes][K/V, even blocks][K/V, odd blocks]
+    size_t sp_kv_bytes = 0;                // one K/V buffer: [world][2][Bmax][H][sp_lg_max][128] bf16
+    std::vector<uint8_t*> sp_peer;         // every rank's region as mapped in this process (own region at sp_rank)
+    unsigned long long* sp_seq = nullptr;  // [0] steps run, [1 + i] the ready value of block i in the current step
+    cudaStream_t sp_side = nullptr;        // the pushes
+    cudaEvent_t sp_ev[3] = {};             // fork; pushes of even / odd blocks done
+    __nv_bfloat16* kv_buf(int parity) const
+    {
+        return reinterpret_cast<__nv_bfloat16*>(sp_region + kSpFlagBytes + parity * sp_kv_bytes);
+    }
+    mkb_status sp_set_peer(bool on);
+    void sp_release_peer();
+    mkb_status sp_push(int B, int Lg, int block, cudaStream_t s);
     SpRows rows_of(int S, int N) const
     {
         SpRows r;
@@ -208,6 +232,7 @@ DitImpl::~DitImpl()
     for (auto& g : graphs)
         if (g.second.exec)
             cudaGraphExecDestroy(g.second.exec);
+    sp_release_peer();
     if (sp_comm) {
         if (const NcclApi* api = nccl_api(nullptr))
             api->CommDestroy(sp_comm);
@@ -273,6 +298,140 @@ mkb_status DitImpl::set_sp(const void* id, int rank, int world)
             cudaGraphExecDestroy(g.second.exec);
     graphs.clear();
     plans.clear();
+    return MKB_OK;
+}
+
+void DitImpl::sp_release_peer()
+{
+    if (sp_side)
+        cudaStreamSynchronize(sp_side);
+    for (int g = 0; g < int(sp_peer.size()); ++g)
+        if (sp_peer[g] && g != sp_rank)
+            cudaIpcCloseMemHandle(sp_peer[g]);
+    sp_peer.clear();
+    for (cudaEvent_t& e : sp_ev) {
+        if (e)
+            cudaEventDestroy(e);
+        e = nullptr;
+    }
+    if (sp_side)
+        cudaStreamDestroy(sp_side);
+    sp_side = nullptr;
+    if (sp_region)
+        cudaFree(sp_region);
+    if (sp_seq)
+        cudaFree(sp_seq);
+    sp_region = nullptr;
+    sp_seq = nullptr;
+    sp_p2p = false;
+    cudaGetLastError();  // a failed set-up step is reported by the caller, not by later launches
+}
+
+// Switches the K/V exchange between the NCCL all-gather and peer memory. Collective over the group: every rank
+// calls it with the same `on`. Each rank exports its exchange region over CUDA IPC, the handles go round by an
+// all-gather, and every rank maps the others'; a second all-gather makes every rank fail together if any could not.
+mkb_status DitImpl::sp_set_peer(bool on)
+{
+    if (sp_world < 2 || !sp_comm)
+        return fail(MKB_ERR_STATE, "peer exchange: set sequence parallelism first");
+    if (on == sp_p2p)
+        return MKB_OK;
+    MKB_TRY_CUDA(cudaStreamSynchronize(stream), "peer exchange: sync");
+    for (auto& g : graphs)  // plans and graphs hold the K/V buffers of the other mode
+        if (g.second.exec)
+            cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+    plans.clear();
+    if (!on) {
+        sp_release_peer();
+        return MKB_OK;
+    }
+    const NcclApi* api = nccl_api(nullptr);
+    // Round 1: allocate, export, gather the handles (with a success word each).
+    struct Entry {
+        cudaIpcMemHandle_t h;
+        int ok;
+        int pad[15];
+    };
+    sp_kv_bytes = (size_t(sp_world) * 2 * Bmax * H * sp_lg_max * kHeadDim * 2 + 255) / 256 * 256;
+    std::string why;
+    Entry mine{};
+    auto step = [&](cudaError_t e, const char* what) {
+        if (e != cudaSuccess && why.empty())
+            why = std::string(what) + ": " + cudaGetErrorString(e);
+        return e == cudaSuccess;
+    };
+    bool ok = step(cudaMalloc(&sp_region, kSpFlagBytes + 2 * sp_kv_bytes), "allocating the exchange region") &&
+              step(cudaMemsetAsync(sp_region, 0, kSpFlagBytes + 2 * sp_kv_bytes, stream), "clearing it") &&
+              step(cudaMalloc(&sp_seq, (1 + size_t(NB)) * 8), "allocating the block counters") &&
+              step(cudaMemsetAsync(sp_seq, 0, (1 + size_t(NB)) * 8, stream), "clearing them") &&
+              step(cudaIpcGetMemHandle(&mine.h, sp_region), "cudaIpcGetMemHandle") &&
+              step(cudaStreamCreateWithFlags(&sp_side, cudaStreamNonBlocking), "copy stream");
+    for (cudaEvent_t& e : sp_ev)
+        ok = ok && step(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "events");
+    mine.ok = ok;
+    std::vector<Entry> all(sp_world);
+    auto gather = [&](const Entry& e) -> bool {
+        Entry* buf = reinterpret_cast<Entry*>(vel_x);  // the velocity exchange buffer, idle between steps
+        if (cudaMemcpyAsync(buf + sp_rank, &e, sizeof(Entry), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+            return false;
+        if (api->AllGather(buf + sp_rank, buf, sizeof(Entry), ncclUint8, sp_comm, stream) != ncclSuccess)
+            return false;
+        return cudaMemcpyAsync(all.data(), buf, sizeof(Entry) * sp_world, cudaMemcpyDeviceToHost, stream) ==
+                   cudaSuccess &&
+               cudaStreamSynchronize(stream) == cudaSuccess;
+    };
+    auto all_ok = [&] {
+        for (const Entry& e : all)
+            if (!e.ok)
+                return false;
+        return true;
+    };
+    bool agreed = gather(mine) && all_ok();
+    if (agreed) {
+        // Round 2: map every peer's region.
+        sp_peer.assign(sp_world, nullptr);
+        sp_peer[sp_rank] = sp_region;
+        const std::vector<Entry> handles = all;
+        bool opened = true;
+        for (int g = 0; g < sp_world && opened; ++g) {
+            if (g == sp_rank)
+                continue;
+            void* p = nullptr;
+            opened = step(cudaIpcOpenMemHandle(&p, handles[g].h, cudaIpcMemLazyEnablePeerAccess),
+                          "cudaIpcOpenMemHandle");
+            sp_peer[g] = static_cast<uint8_t*>(p);
+        }
+        Entry e2{};
+        e2.ok = opened;
+        agreed = gather(e2) && all_ok();
+    }
+    if (!agreed) {
+        sp_release_peer();
+        return fail(MKB_ERR_CUDA, "peer exchange: " + (why.empty() ? std::string("another rank failed") : why));
+    }
+    sp_p2p = true;
+    return MKB_OK;
+}
+
+// The pushes of block `block`'s K/V shard (this rank's slot of its buffer) into every peer's region, each followed by
+// the 8-byte copy of the block's ready value into the peer's flag of this rank, on the copy stream (forked from s
+// after the QKV projection that wrote the shard).
+mkb_status DitImpl::sp_push(int B, int Lg, int block, cudaStream_t s)
+{
+    const size_t shard = size_t(2) * B * H * Lg * kHeadDim * 2;
+    const size_t off = kSpFlagBytes + size_t(block & 1) * sp_kv_bytes + size_t(sp_rank) * shard;
+    MKB_TRY_CUDA(cudaEventRecord(sp_ev[0], s), "push fork");
+    MKB_TRY_CUDA(cudaStreamWaitEvent(sp_side, sp_ev[0], 0), "push fork");
+    for (int k = 1; k < sp_world; ++k) {
+        const int q = (sp_rank - k + sp_world) % sp_world;
+        MKB_TRY_CUDA(cudaMemcpyAsync(sp_peer[q] + off, sp_region + off, shard, cudaMemcpyDeviceToDevice, sp_side),
+                     "K/V push");
+        MKB_TRY_CUDA(cudaMemcpyAsync(sp_peer[q] + size_t(sp_rank) * 8, sp_seq + 1 + block, 8,
+                                     cudaMemcpyDeviceToDevice, sp_side),
+                     "ready flag");
+    }
+    MKB_TRY_CUDA(cudaEventRecord(sp_ev[1 + (block & 1)], sp_side), "push done");
     return MKB_OK;
 }
 
@@ -529,10 +688,10 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         const int M_s[2] = {Mt, Mi}, rps[2] = {S, Nl}, off[2] = {0, St};
         // RoPE row of head-layout row p: the joint position, p + rank * Lh.
         const float* rope_s[2] = {rope, rope + size_t(sp ? sp_rank : 0) * Lh * kHeadDim};
-        // K and V of this rank go straight into its slot of the all-gather buffer.
+        // K and V of this rank go straight into its slot of the all-gather buffer, or of the block's K/V buffer of
+        // the peer exchange.
         const size_t kv_shard = size_t(B) * H * Lh * kHeadDim;
-        __nv_bfloat16* k_dst = sp ? kv_all + size_t(sp_rank) * 2 * kv_shard : kh;
-        __nv_bfloat16* v_dst = sp ? k_dst + kv_shard : vh;
+        auto kv_base = [&](int block) { return sp_p2p ? kv_buf(block & 1) : kv_all; };
         const char* nm[2] = {"txt", "img"};
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
         // its tail, all on 256 x 256 CTA-pair tiles (QKV: two heads per CTA): the pair halves each SM's W traffic
@@ -559,8 +718,8 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 a.K = D;
                 a.bias = V(p + "qkv.b");
                 a.qh = qh;
-                a.kh = k_dst;
-                a.vh = v_dst;
+                a.kh = sp ? kv_base(i) + size_t(sp_rank) * 2 * kv_shard : kh;
+                a.vh = sp ? a.kh + kv_shard : vh;
                 a.norm_q = V(p + "norm_q");
                 a.norm_k = V(p + "norm_k");
                 a.rope = rope_s[s];
@@ -650,7 +809,14 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
             at.kv_plane_stride = 2 * B * H;
         }
         at.status = status;
-        if (!attn_prepare(plan->att, qh, Lh, sp ? kv_all : kh, sp ? kv_all + kv_shard : vh, L, at, &err))
+        if (sp_p2p) {  // shards arrive during the launch; the expected flag value is set per block at launch
+            at.own_shard = sp_rank;
+            at.shard_ready = reinterpret_cast<const unsigned long long*>(sp_region);
+            at.shard_expect = sp_seq + 1;
+            if (!attn_prepare(plan->att_odd, qh, Lh, kv_buf(1), kv_buf(1) + kv_shard, L, at, &err))
+                return fail(MKB_ERR_INVALID, err);
+        }
+        if (!attn_prepare(plan->att, qh, Lh, sp ? kv_base(0) : kh, sp ? kv_base(0) + kv_shard : vh, L, at, &err))
             return fail(MKB_ERR_INVALID, err);
     } else {
         const int T = first ? L : N, split = first ? S : 0, Mr = B * T;
@@ -772,6 +938,18 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
     return MKB_OK;
 }
 
+// The peer exchange's per-step ready values: seq[0] counts steps; block i of step e is announced as e * blocks + i + 1,
+// which grows across blocks and steps, so a flag at or above it means that block's shard of this step has landed.
+__global__ void k_sp_step(unsigned long long* seq, int blocks)
+{
+    grid_dep_wait();
+    const unsigned long long e = seq[0] + 1;
+    seq[0] = e;
+    for (int i = 0; i < blocks; ++i)
+        seq[1 + i] = e * blocks + i + 1;
+    grid_dep_launch();
+}
+
 #define MKB_K(expr, what) MKB_TRY_CUDA((expr), what)
 
 // Runs one step for B samples whose latents are in `lat` (device, [B][N][64]) with host noise levels `sigmas`.
@@ -864,6 +1042,10 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     const int St = q1 ? rw.text : S, Nl = q1 ? rw.image : N;
     GemmOp* g = plan->ops.data() + size_t(NB) * per;
     const int R = q1 ? B : 2 * B;
+    if (sp_p2p) {
+        MKB_K(launch_k(k_sp_step, dim3(1), dim3(1), 0, s, sp_seq, NB), "step counter");
+        count_launch();
+    }
     // Time path: sinusoid -> lin1 -> silu -> lin2 (temb) -> silu -> modulations (qwen_image.cpp:179-205).
     MKB_K(timestep_sinusoid(sig, tp, R, s), "sinusoid");
     MKB_K(gemv(M("time.lin1.w"), tp, kTimeDim, V("time.lin1.b"), h1, D, R, D, kTimeDim, kActSilu, s), "time lin1");
@@ -936,8 +1118,15 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
                 return ln_modulate2(la[0], la[1], s);
             };
             MKB_K(ln(1, 0), "ln_modulate 1");
+            if (sp_p2p && i >= 2)  // block i - 2's pushes read the buffer this QKV writes
+                MKB_K(cudaStreamWaitEvent(s, sp_ev[1 + (i & 1)], 0), "push join");
             MKB_K(gemm_launch(o[0], s), "qkv");
-            if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
+            if (sp_p2p) {
+                MKB_TRY(sp_push(B, rw.shard, i, s));
+                AttnOp at = i & 1 ? plan->att_odd : plan->att;
+                at.args.shard_expect = sp_seq + 1 + i;
+                MKB_K(attn_launch(at, s), "attention");
+            } else if (sp_world > 1) {  // every rank's K and V shards to every rank, in place
                 const size_t count = size_t(2) * B * H * rw.shard * kHeadDim;
                 const ncclResult_t r = nccl_api(nullptr)->AllGather(kv_all + size_t(sp_rank) * count, kv_all, count,
                                                                    ncclBfloat16, sp_comm, s);
@@ -945,7 +1134,8 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
                     return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
                                                   nccl_api(nullptr)->GetErrorString(r));
             }
-            MKB_K(attn_launch(plan->att, s), "attention");
+            if (!sp_p2p)
+                MKB_K(attn_launch(plan->att, s), "attention");
             MKB_K(gemm_launch(o[1], s), "o proj");
             MKB_K(ln(4, 3), "ln_modulate 2");
             MKB_K(gemm_launch(o[2], s), "ff1");
@@ -990,6 +1180,10 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
             MKB_TRY(emit("block", i, x_img, long(Mr) * D, s));
         }
     }
+
+    if (sp_p2p)  // the last two blocks' pushes
+        for (int p = 0; p < 2 && p < NB; ++p)
+            MKB_K(cudaStreamWaitEvent(s, sp_ev[1 + p], 0), "push join");
 
     // norm_out + proj_out (qwen_image.cpp:285-288).
     LnModArgs la{};
@@ -1437,6 +1631,12 @@ mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int ra
 {
     MKB_TRY(check_handle(d));
     return d->impl.set_sp(nccl_id, rank, world);
+}
+
+mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable)
+{
+    MKB_TRY(check_handle(d));
+    return d->impl.sp_set_peer(enable != 0);
 }
 
 mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,

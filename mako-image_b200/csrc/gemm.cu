@@ -492,6 +492,73 @@ __device__ __forceinline__ void epi_drain_resid(EpiTma& e, uint32_t* status)
             mbar_wait(&e.rbar[b], (e.rphase >> b) & 1, status, kErrWaitDrain, nullptr);
 }
 
+// GroupNorm statistics of one warp's 32 rows (pixels) of a 32-column chunk of a convolution's output, for the
+// 32 / CPG channel groups in the chunk. Each lane sums its row's values of every group, shifted by lane 0's first
+// value of the group (shifted sums keep the variance exact to fp32 rounding for these 32 x CPG values); the lanes
+// then reduce-scatter the 2 x (32 / CPG) sums in halving steps (lane bit 4 decides first, so the lane holding a
+// group's shifted sum of squares is lane ^ 16 of the one holding its shifted sum) and one lane per group writes
+// (count, mean, M2). Rows outside the image count nothing.
+template <int CPG>
+__device__ __forceinline__ void gn_warp_stats(const GemmArgs& a, const float (&v)[32], bool row_ok, int col0,
+                                              int img, int chunk)
+{
+    constexpr int NG = 32 / CPG, V = 2 * NG, kSteps = NG == 8 ? 4 : NG == 4 ? 3 : 2;
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    float x[V], sh[NG];
+    const float keep_row = row_ok ? 1.f : 0.f;
+#pragma unroll
+    for (int k = 0; k < NG; ++k) {
+        sh[k] = __shfl_sync(full, v[k * CPG], 0);
+        // Two channels per packed instruction: d = x keep - shift keep (x - shift, or 0 outside the image), then the
+        // sums of d and d^2.
+        const float2 kr = make_float2(keep_row, keep_row), nsk = make_float2(-sh[k] * keep_row, -sh[k] * keep_row);
+        float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < CPG; i += 2) {
+            const float2 d = ffma2(make_float2(v[k * CPG + i], v[k * CPG + i + 1]), kr, nsk);
+            s1 = fadd2(s1, d);
+            s2 = ffma2(d, d, s2);
+        }
+        x[k] = s1.x + s1.y;
+        x[NG + k] = s2.x + s2.y;
+    }
+#pragma unroll
+    for (int step = 0; step < 5; ++step) {
+        const int o = 16 >> step;
+        const int half = V >> (step + 1);
+        if (half >= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+                const float send = upper ? x[i] : x[i + half];
+                const float keep = upper ? x[i + half] : x[i];
+                x[i] = keep + __shfl_xor_sync(full, send, o);
+            }
+        } else {
+            x[0] += __shfl_xor_sync(full, x[0], o);
+        }
+    }
+    const float s2 = __shfl_xor_sync(full, x[0], 16);
+    const float n = float(__popc(__ballot_sync(full, row_ok)) * CPG);
+    constexpr int kLow = (1 << (5 - kSteps)) - 1;  // lane bits the final butterfly summed over
+    if ((lane & 16) || (lane & kLow))
+        return;
+    int k = 0;
+#pragma unroll
+    for (int st = 1; st < kSteps; ++st)
+        k += ((lane >> (4 - st)) & 1) * (V >> (st + 1));
+    float shk = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < NG; ++kk)
+        shk = kk == k ? sh[kk] : shk;
+    const float s1 = x[0];
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n > 0.f)
+        o = make_float4(n, shk + s1 / n, fmaxf(s2 - s1 * (s1 / n), 0.f), 0.f);
+    a.gn_part[(long(img) * (a.N / CPG) + col0 / CPG + k) * a.gn_chunks + chunk] = o;
+}
+
 // The fp32 epilogues through TMA. Per 32-column chunk the 128 epilogue threads (one row each, r = row within the
 // tile) write their row of a staging box, then one thread stores it (out_mode 1, 3) or reduce-adds it into the
 // output (out_mode 2: the output is the residual). kAdd writes acc + bias + addvec (+ the residual box, out_mode 3);
@@ -639,6 +706,17 @@ __device__ __forceinline__ void epilogue_tma(const GemmArgs& a, const CUtensorMa
             for (int j = 0; j < 8; ++j)
                 *box_chunk(box, r, j) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             fence_proxy_async_smem();
+            if constexpr (EPI == Epi::kAdd && CONV) {
+                if (a.gn_part) {  // c1, c2, c3 = x0, y0, image of the pixel tile
+                    const int chunk = ((c2 / a.conv_th) * (a.conv_wo / a.conv_tw) + c1 / a.conv_tw) * 4 + (r >> 5);
+                    if (a.gn_cpg == 4)
+                        gn_warp_stats<4>(a, v, row_ok, col0, c3, chunk);
+                    else if (a.gn_cpg == 8)
+                        gn_warp_stats<8>(a, v, row_ok, col0, c3, chunk);
+                    else
+                        gn_warp_stats<16>(a, v, row_ok, col0, c3, chunk);
+                }
+            }
         }
         named_barrier_sync<1, 128>();
         if (e.issuer && active) {
@@ -1472,6 +1550,20 @@ bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long l
     return true;
 }
 
+int conv_tile_w(int Wo)
+{
+    int tw = 128;
+    while (tw > 1 && Wo % tw)
+        tw >>= 1;
+    return tw;
+}
+
+int conv_gn_chunks(int Ho, int Wo)
+{
+    const int tw = conv_tile_w(Wo), th = 128 / tw;
+    return (Wo / tw) * ((Ho + th - 1) / th) * 4;
+}
+
 bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int C, const void* W, int Cout,
                   int taps, int stride, const GemmArgs& args_in, int bn, const char** err)
 {
@@ -1488,9 +1580,7 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     GemmArgs a = args_in;
     const int Ho = taps == 9 ? (Hi + 2 - 3) / stride + 1 : Hi, Wo = taps == 9 ? (Wi + 2 - 3) / stride + 1 : Wi;
     // Tile: tw columns x (128 / tw) rows of output pixels, tw the widest power of two <= 128 dividing Wo.
-    int tw = 128;
-    while (tw > 1 && Wo % tw)
-        tw >>= 1;
+    const int tw = conv_tile_w(Wo);
     if (tw < 8) {
         *err = "conv: the output width must be a multiple of 8";
         return false;
@@ -1511,6 +1601,15 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     a.K = taps * C;
     if (a.seg_rows == (1 << 30))
         a.seg_rows = Ho * Wo;  // per-sample vectors index by image
+    if (a.gn_part) {
+        if (epi != Epi::kAdd || !a.out_f32 || (a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16) ||
+            (reinterpret_cast<uintptr_t>(a.gn_part) & 15)) {
+            *err = "conv: GroupNorm statistics need the fp32 add epilogue, 4, 8 or 16 channels a group, 16-byte "
+                   "aligned partials";
+            return false;
+        }
+        a.gn_chunks = conv_gn_chunks(Ho, Wo);
+    }
     if (!check_epilogue(epi, a, bn, err))
         return false;
     auto fn = encode_fn();
@@ -1543,6 +1642,10 @@ bool conv_prepare(GemmOp& op, Epi epi, const void* X, int B, int Hi, int Wi, int
     op.p.a[0] = a;
     if (epi_tma(epi) && !prepare_out_boxes(op.p, 0, epi, bn, true, err))
         return false;
+    if (a.gn_part && !op.p.a[0].out_mode) {
+        *err = "conv: GroupNorm statistics need the output boxes of the TMA epilogue";
+        return false;
+    }
     op.p.nprob = 1;
     op.epi = epi;
     op.bn = bn;

@@ -77,6 +77,13 @@ struct GemmArgs {
     // conv_th x conv_tw pixels (128 rows), and K = conv_taps * conv_c runs tap by tap.
     int conv_hi = 0, conv_wi = 0, conv_c = 0, conv_ho = 0, conv_wo = 0;
     int conv_stride = 1, conv_taps = 0, conv_pad = 0, conv_tw = 16, conv_th = 8, conv_b = 0;
+    // A convolution's kAdd epilogue with fp32 boxes can also leave the GroupNorm statistics of its output (the
+    // values it stores, after bias and residual): per image, group of gn_cpg channels (4, 8 or 16) and 32 pixels,
+    // float4 (count, mean, M2, 0) at gn_part[(image * (N / gn_cpg) + group) * gn_chunks + chunk], where chunk =
+    // (the tile's index within its image) * 4 + the tile's 32-pixel quarter. conv_prepare sets gn_chunks.
+    float4* gn_part = nullptr;
+    int gn_cpg = 0;
+    int gn_chunks = 0;
     uint32_t* status = nullptr;     // error bits (kErr*), may be null
 };
 
@@ -130,6 +137,9 @@ int gemm_pick_bn(long M, int N, bool pairs = false);
 bool gemm_add_problem(GemmOp& op, const void* X, long ldx, const void* W, long ldw, const GemmArgs& args,
                       const char** err);
 cudaError_t gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+// Chunks per image of a convolution's GroupNorm statistics (GemmArgs::gn_part) at output size Ho x Wo.
+int conv_gn_chunks(int Ho, int Wo);
 
 // Builds a convolution as an implicit GEMM: X is the channels-last bf16 input [B][Hi][Wi][C] (C a multiple of 64),
 // W the weights [Cout][taps][C] (taps 9 = 3x3 with padding 1, or 1), stride 1 or 2. args.M / N / K are filled in;

@@ -301,6 +301,8 @@ __host__ __device__ inline int gn_chunk_px(int B, int HW)
     return int(want < 16 ? 16 : want);
 }
 
+constexpr int kGnSegments = 32;  // segments per group of the statistics a convolution left (k_gn_finalize_parts)
+
 // Chan et al.'s pairwise combination of (count, mean, M2).
 __device__ __forceinline__ void chan_combine(float& n, float& mean, float& m2, float nb, float meanb, float m2b)
 {
@@ -412,19 +414,82 @@ __global__ void __launch_bounds__(256) k_gn_finalize(const GnArgs a, int nchunks
     }
 }
 
-// y = x * scale_c + shift_c (then SiLU) as bf16, scale_c = rstd_g gamma_c, shift_c = beta_c - mean_g scale_c; each
-// thread keeps its quad's four (scale, shift) in registers. Block (x, b) covers pixels [x * px, (x + 1) * px).
-__global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a, int nchunks, int px)
+// The statistics a convolution's epilogue left, float4 (count, mean, M2, 0) per [B][groups][nchunks] (a group's
+// chunks contiguous, read coalesced), combined per segment of the chunks: block (g, b, s) writes segment s of group
+// g as float4 (count, mean, M2, 0) at a.ws[((b * groups + g) * gridDim.z + s) * 4]. k_gn_apply combines the
+// segments (a few per group) when it starts, so no single block walks all of a group's chunks.
+__global__ void __launch_bounds__(256) k_gn_finalize_parts(const GnArgs a, const float4* parts, int nchunks)
 {
     grid_dep_wait();
     grid_dep_launch();
+    __shared__ float sn[256], sm[256], sq[256];
+    const int g = blockIdx.x, b = blockIdx.y, segs = gridDim.z;
+    const int k0 = int(long(nchunks) * blockIdx.z / segs), k1 = int(long(nchunks) * (blockIdx.z + 1) / segs);
+    const float4* p = parts + (long(b) * a.groups + g) * nchunks;
+    float n = 0.f, mean = 0.f, m2 = 0.f;
+    for (int k = k0 + threadIdx.x; k < k1; k += blockDim.x) {
+        const float4 o = p[k];
+        chan_combine(n, mean, m2, o.x, o.y, o.z);
+    }
+    sn[threadIdx.x] = n;
+    sm[threadIdx.x] = mean;
+    sq[threadIdx.x] = m2;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            float nn = sn[threadIdx.x], mm = sm[threadIdx.x], qq = sq[threadIdx.x];
+            chan_combine(nn, mm, qq, sn[threadIdx.x + w], sm[threadIdx.x + w], sq[threadIdx.x + w]);
+            sn[threadIdx.x] = nn;
+            sm[threadIdx.x] = mm;
+            sq[threadIdx.x] = qq;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        reinterpret_cast<float4*>(a.ws)[(long(b) * a.groups + g) * segs + blockIdx.z] = make_float4(sn[0], sm[0], sq[0], 0.f);
+}
+
+// y = x * scale_c + shift_c (then SiLU) as bf16, scale_c = rstd_g gamma_c, shift_c = beta_c - mean_g scale_c; each
+// thread keeps its quad's four (scale, shift) in registers. Block (x, b) covers pixels [x * px, (x + 1) * px).
+// segs > 0: the statistics are k_gn_finalize_parts' segments, combined here per group into shared memory first.
+__global__ void __launch_bounds__(256) k_gn_apply(const GnArgs a, int nchunks, int px, int segs)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float sfin[2 * 256];
     const int b = blockIdx.y;
+    const float* fin = a.ws + long(a.B) * nchunks * a.groups * 3 + long(b) * a.groups * 2;
+    if (segs > 0) {
+        // Eight lanes per group, each combining every eighth segment, then the lanes' results by shuffles.
+        for (int base = 0; base < a.groups * 8; base += blockDim.x) {
+            const int idx = base + threadIdx.x, g = idx >> 3, l = idx & 7;
+            float n = 0.f, mean = 0.f, m2 = 0.f;
+            if (g < a.groups) {
+                const float4* s = reinterpret_cast<const float4*>(a.ws) + (long(b) * a.groups + g) * segs;
+                for (int k = l; k < segs; k += 8) {
+                    const float4 o = s[k];
+                    chan_combine(n, mean, m2, o.x, o.y, o.z);
+                }
+            }
+#pragma unroll
+            for (int off = 4; off > 0; off >>= 1) {
+                const float n2 = __shfl_xor_sync(0xffffffffu, n, off), mean2 = __shfl_xor_sync(0xffffffffu, mean, off),
+                            m22 = __shfl_xor_sync(0xffffffffu, m2, off);
+                chan_combine(n, mean, m2, n2, mean2, m22);
+            }
+            if (g < a.groups && l == 0) {
+                sfin[2 * g] = mean;
+                sfin[2 * g + 1] = rsqrtf(m2 / fmaxf(n, 1.f) + a.eps);
+            }
+        }
+        __syncthreads();
+        fin = sfin;
+    }
     const int Q = a.C / 4, Qb = Q < 256 ? Q : 256, Rb = 256 / Qb;
     const int t = threadIdx.x, r = t / Qb, q0 = t % Qb;
     if (r >= Rb)
         return;
     const int p0 = blockIdx.x * px, np = min(px, a.HW - p0);
-    const float* fin = a.ws + long(a.B) * nchunks * a.groups * 3 + long(b) * a.groups * 2;
     const int cpg = a.C / a.groups;
     const float4* xb = reinterpret_cast<const float4*>(a.x + (long(b) * a.HW + p0) * a.C);
     uint2* yb = reinterpret_cast<uint2*>(a.y + (long(b) * a.HW + p0) * a.C);
@@ -888,7 +953,21 @@ cudaError_t group_norm(const GnArgs& a, cudaStream_t st)
     count_launch();
     // Apply: about eight blocks per SM over the batch.
     const int apx = int(std::max<long>(16, (long(a.B) * a.HW + 8 * 148 - 1) / (8 * 148)));
-    launch_k(k_gn_apply, dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st, a, nchunks, apx);
+    launch_k(k_gn_apply, dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st, a, nchunks, apx, 0);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t group_norm_from_parts(const GnArgs& a, const float4* parts, int nchunks, cudaStream_t st)
+{
+    if (a.B <= 0 || a.HW <= 0 || a.groups <= 0 || a.groups > 256 || a.C % a.groups || a.C % 4 || !a.ws ||
+        (reinterpret_cast<uintptr_t>(a.ws) & 15) || !a.gamma || !parts || nchunks <= 0)
+        return cudaErrorInvalidValue;
+    const int segs = std::min(kGnSegments, nchunks);
+    launch_k(k_gn_finalize_parts, dim3(a.groups, a.B, segs), 256, 0, st, a, parts, nchunks);
+    count_launch();
+    const int apx = int(std::max<long>(16, (long(a.B) * a.HW + 8 * 148 - 1) / (8 * 148)));
+    launch_k(k_gn_apply, dim3((a.HW + apx - 1) / apx, a.B), 256, 0, st, a, 0, apx, segs);
     count_launch();
     return cudaGetLastError();
 }

@@ -80,6 +80,9 @@ struct GnArgs {
 };
 size_t group_norm_workspace(int B, int HW, int C, int groups);
 cudaError_t group_norm(const GnArgs& a, cudaStream_t st);
+// The same with the statistics pass already done by the convolution that wrote x (GemmArgs::gn_part): parts holds
+// float4 (count, mean, M2, 0) per [B][groups][nchunks]; a.ws (16-byte aligned) needs B * groups * 128 floats.
+cudaError_t group_norm_from_parts(const GnArgs& a, const float4* parts, int nchunks, cudaStream_t st);
 
 // Nearest 2x upsampling of channels-last fp32 x [B][H][W][C] into bf16 y [B][2H][2W][C] (the upsample2x kernel,
 // src/kernels/image.metal:77-84), ready as a convolution input.

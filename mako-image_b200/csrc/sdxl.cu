@@ -13,6 +13,7 @@
 #include "rowops.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <deque>
 #include <functional>
 #include <map>
@@ -24,6 +25,19 @@
 namespace mkb {
 
 namespace {
+
+// Whether the VAE's convolutions leave the GroupNorm statistics of their outputs (MKB_GN_FUSED=0: the three-pass
+// GroupNorm everywhere, for comparison; the statistics need the TMA epilogue, so MKB_TMA_EPI=0 turns them off too).
+bool gn_fused_enabled()
+{
+    static const bool on = [] {
+        const char* f = std::getenv("MKB_GN_FUSED");
+        const char* t = std::getenv("MKB_TMA_EPI");
+        return !(f && f[0] == '0') && !(t && t[0] == '0');
+    }();
+    return on;
+}
+
 
 constexpr int kHead = 64, kTime = 256, kAdded6 = 6 * 256;
 constexpr int kGluBlock = 128;
@@ -332,13 +346,18 @@ struct Builder {
     }
     // 3x3 (taps 9) or 1x1 convolution of bf16 x [B][H][W][Cin] into y (fp32 or bf16, row stride ldy) with bias,
     // per-image addvec and fp32 residual.
+    // With gn_part the convolution also leaves its output's GroupNorm statistics (32 groups) there, for gn_from().
     void conv(const __nv_bfloat16* x, int B, int H, int W, int Cin, const __nv_bfloat16* w, int Cout, int taps,
               int stride, const float* bias, const float* addvec, long addvec_stride, const float* resid, void* y,
-              long ldy, bool out_f32)
+              long ldy, bool out_f32, float4* gn_part = nullptr)
     {
         if (!ok())
             return;
         GemmArgs a;
+        if (gn_part) {
+            a.gn_part = gn_part;
+            a.gn_cpg = Cout / 32;
+        }
         a.bias = bias;
         a.addvec = addvec;
         a.addvec_stride = addvec_stride;
@@ -381,6 +400,15 @@ struct Builder {
             return;
         GnArgs a{x, y, g, b, B, HW, C, 32, eps, silu ? 1 : 0, P.gn_ws};
         P.add([a](cudaStream_t s) { return group_norm(a, s); });
+    }
+    // GroupNorm of x whose statistics the convolution that wrote it left in parts (nchunks per image and group).
+    void gn_from(const float* x, const float4* parts, int nchunks, __nv_bfloat16* y, const float* g, const float* b,
+                 int B, int HW, int C, float eps, bool silu)
+    {
+        if (!ok())
+            return;
+        GnArgs a{x, y, g, b, B, HW, C, 32, eps, silu ? 1 : 0, P.gn_ws};
+        P.add([a, parts, nchunks](cudaStream_t s) { return group_norm_from_parts(a, parts, nchunks, s); });
     }
     void attn(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v, int B, int H, int Lq, int Lk,
               __nv_bfloat16* out, int hd = kHead)
@@ -1133,7 +1161,20 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
     float* SC = P.buf<float>(size_t(qn) * n, &st);
     __nv_bfloat16* PR = P.buf<__nv_bfloat16>(size_t(qn) * n, &st);
     __nv_bfloat16* AT = P.buf<__nv_bfloat16>(size_t(n) * ca, &st);
-    P.gn_ws = P.buf<float>(gnmost / 4 + 16, &st);
+    P.gn_ws = P.buf<float>(std::max(gnmost / 4, size_t(32) * 128) + 16, &st);  // also the fused path's segments
+    // GroupNorm statistics left by the convolutions (where every channel count of the decoder gives groups of 4, 8
+    // or 16): GA for the residual stream (conv_in, each block's conv2, the upsampling convolutions), GB for conv1.
+    const bool fuse = gn_fused_enabled();
+    size_t parts_most = 0;
+    {
+        int hh = H0, ww = W0;
+        for (const Op& o : ops)
+            if (o.kind == Op::kUp)
+                hh *= 2, ww *= 2;
+        parts_most = size_t(conv_gn_chunks(hh, ww)) * 32;
+    }
+    float4* GA = fuse ? P.buf<float4>(parts_most, &st) : nullptr;
+    float4* GB = fuse ? P.buf<float4>(parts_most, &st) : nullptr;
     if (st != MKB_OK)
         return st;
     const WTable& w = W;
@@ -1155,9 +1196,20 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
         bd.gemm(Epi::kAdd, LAT, 64, w.M("post_quant.w"), 64, a, 64);
     }
     float* cur = F[0];
-    bd.conv(PQ, 1, H0, W0, 64, w.M("conv_in.w"), ctop, 9, 1, w.V("conv_in.b"), nullptr, 0, nullptr, cur, ctop, true);
+    // Whether cur's statistics are in GA (it came from a convolution whose channels split into groups of 4..16).
+    auto can_fuse = [&](int C) { return fuse && C % 32 == 0 && (C / 32 == 4 || C / 32 == 8 || C / 32 == 16); };
+    bool cur_parts = can_fuse(ctop);
+    bd.conv(PQ, 1, H0, W0, 64, w.M("conv_in.w"), ctop, 9, 1, w.V("conv_in.b"), nullptr, 0, nullptr, cur, ctop, true,
+            cur_parts ? GA : nullptr);
     P.probe("conv_in", -1, cur, long(n) * ctop);
     int h = H0, wd = W0, c = ctop;
+    // GroupNorm of cur (or of conv1's output U, from GB), from the statistics when there are some.
+    auto norm = [&](const float* X, bool parts, const float4* G, const std::string& wn, int C, bool silu) {
+        if (parts)
+            bd.gn_from(X, G, conv_gn_chunks(h, wd), T, w.V(wn + ".w"), w.V(wn + ".b"), 1, h * wd, C, 1e-6f, silu);
+        else
+            bd.gn(X, T, w.V(wn + ".w"), w.V(wn + ".b"), 1, h * wd, C, 1e-6f, silu);
+    };
     auto pick = [&](const float* x) {
         for (float* f : F)
             if (f != x)
@@ -1172,10 +1224,11 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
             // engine.cpp:732-746 (GroupNorm eps 1e-6 in the AutoencoderKL layout)
             const float* X = cur;
             float* Y = pick(X);
-            bd.gn(X, T, w.V(o.name + ".gn1.w"), w.V(o.name + ".gn1.b"), 1, HW, o.cin, 1e-6f, true);
+            norm(X, cur_parts, GA, o.name + ".gn1", o.cin, true);
+            const bool u_parts = can_fuse(o.cout);
             bd.conv(T, 1, h, wd, o.cin, w.M(o.name + ".conv1.w"), o.cout, 9, 1, w.V(o.name + ".conv1.b"), nullptr, 0,
-                    nullptr, U, o.cout, true);
-            bd.gn(U, T, w.V(o.name + ".gn2.w"), w.V(o.name + ".gn2.b"), 1, HW, o.cout, 1e-6f, true);
+                    nullptr, U, o.cout, true, u_parts ? GB : nullptr);
+            norm(U, u_parts, GB, o.name + ".gn2", o.cout, true);
             const float* R = X;
             if (o.cin != o.cout) {
                 const size_t cnt = size_t(HW) * o.cin;
@@ -1191,15 +1244,16 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
                 bd.gemm(Epi::kAdd, T2, o.cin, w.M(o.name + ".skip.w"), o.cin, a);
                 R = SK;
             }
+            cur_parts = can_fuse(o.cout);
             bd.conv(T, 1, h, wd, o.cout, w.M(o.name + ".conv2.w"), o.cout, 9, 1, w.V(o.name + ".conv2.b"), nullptr,
-                    0, R, Y, o.cout, true);
+                    0, R, Y, o.cout, true, cur_parts ? GA : nullptr);
             cur = Y;
             c = o.cout;
         } else if (o.kind == Op::kAttn) {
             // engine.cpp:748-778: GroupNorm, qkv 1x1, scores per query chunk, row softmax, P V, proj + residual.
             const float* X = cur;
             float* Y = pick(X);
-            bd.gn(X, T, w.V("mid.attn.gn.w"), w.V("mid.attn.gn.b"), 1, HW, c, 1e-6f, false);
+            norm(X, cur_parts, GA, "mid.attn.gn", c, false);
             GemmArgs q;
             q.M = HW;
             q.N = 3 * c;
@@ -1243,21 +1297,23 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
             pr.out_f32 = 1;
             bd.gemm(Epi::kAdd, AT, c, w.M("mid.attn.proj.w"), c, pr);
             cur = Y;
+            cur_parts = false;  // a plain GEMM wrote it
         } else {
             const float* X = cur;
             float* Y = pick(X);
             const int hh = h, ww2 = wd, cc = o.cin;
             P.add([=](cudaStream_t s) { return upsample2x_bf16(X, T, 1, hh, ww2, cc, s); });
             h *= 2, wd *= 2;
+            cur_parts = can_fuse(o.cin);
             bd.conv(T, 1, h, wd, o.cin, w.M(o.name + ".w"), o.cin, 9, 1, w.V(o.name + ".b"), nullptr, 0, nullptr, Y,
-                    o.cin, true);
+                    o.cin, true, cur_parts ? GA : nullptr);
             cur = Y;
         }
         P.probe(o.name, -1, cur, long(h) * wd * c);
     }
     if (!bd.ok())
         return bd.st;
-    bd.gn(cur, T, w.V("out.gn.w"), w.V("out.gn.b"), 1, h * wd, c, 1e-6f, true);
+    norm(cur, cur_parts, GA, "out.gn", c, true);
     float* O = pick(cur);
     bd.conv(T, 1, h, wd, c, w.M("out.conv.w"), 32, 9, 1, w.V("out.conv.b"), nullptr, 0, nullptr, O, 32, true);
     float* rg = rgba;

@@ -20,6 +20,7 @@ enum : uint32_t {
     kErrAttnWait = 1u << 5,      // attention pipeline wait timed out
     kErrShape = 1u << 6,         // a kernel was launched with a shape it does not support
     kErrWaitEpiLoad = 1u << 7,   // GEMM epilogue gave up waiting for its residual box
+    kErrShardWait = 1u << 8,     // attention gave up waiting for another rank's K/V shard to arrive
 };
 
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far above any legitimate stage wait
@@ -34,6 +35,49 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Packed two-lane fp32 arithmetic: one instruction for both lanes.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b),
+             rc = *reinterpret_cast<uint64_t*>(&c), rd;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+    return *reinterpret_cast<float2*>(&rd);
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
+{
+    uint64_t ra = *reinterpret_cast<uint64_t*>(&a), rb = *reinterpret_cast<uint64_t*>(&b), rd;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    return *reinterpret_cast<float2*>(&rd);
+}
+
+// Waits until the 64-bit flag in global memory (written by another GPU's copy engine) reaches `want`: an acquire
+// load at system scope, then a proxy fence so that TMA loads issued after the return see the data written before
+// the flag. Gives up after kWaitNs (sets `err_bit` and *abort), at once when *abort is set by another role of the
+// CTA, and when `err_bit` is already set in *status (another CTA gave up on the same flag).
+__device__ __forceinline__ bool wait_flag_ge(const unsigned long long* flag, unsigned long long want,
+                                             uint32_t* status, uint32_t err_bit, volatile int* abort)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+        if (v >= want) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            return true;
+        }
+        const bool others = status && (*reinterpret_cast<volatile uint32_t*>(status) & err_bit);
+        if ((abort && *abort) || others || globaltimer_ns() - t0 > kWaitNs) {
+            if (status && !others)
+                atomicOr(status, err_bit);
+            if (abort)
+                *abort = 1;
+            return false;
+        }
+        __nanosleep(128);
+    }
 }
 
 // ---------------------------------------------------------------- mbarrier

@@ -177,6 +177,11 @@ class Dit:
         buf = ctypes.create_string_buffer(bytes(nccl_id), NCCL_ID_BYTES)
         check(lib.mkb_dit_set_sequence_parallel(self.h, buf, rank, world))
 
+    def set_peer_exchange(self, enable: bool = True):
+        """Moves the per-block K/V exchange from the NCCL all-gather to copy-engine pushes into the peers' memory
+        (collective; see mkb_dit_sp_peer_exchange)."""
+        check(lib.mkb_dit_sp_peer_exchange(self.h, int(bool(enable))))
+
 
 NCCL_ID_BYTES = 128
 

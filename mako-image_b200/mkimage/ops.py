@@ -98,6 +98,20 @@ def attention_kv_shards(q, k, v, out0, out1, split, Lk, kv_shard_rows, kv_plane_
                                       out1.stride(0), rows1, kv_shard_rows, kv_plane_stride, stream_ptr()))
 
 
+def attention_kv_arriving(q, k, v, out0, out1, split, Lk, kv_shard_rows, kv_plane_stride, own_shard, shard_ready,
+                          shard_expect, Lq=None, q_pos0=0):
+    """attention_kv_shards() where shard own_shard is complete and every other shard g is read only once the int64
+    device flag shard_ready[g] >= shard_expect[0] (see mkb_attention_kv_arriving)."""
+    B, H, Lq_rows, hd = q.shape
+    Lq = Lq or Lq_rows
+    rows0 = out0.shape[0] // B if out0 is not None else 0
+    rows1 = out1.shape[0] // B
+    check(lib.mkb_attention_kv_arriving(_p(q), Lq, Lq_rows, _p(k), _p(v), Lk, Lk, B, H, hd, q_pos0, MASK_NONE, 0,
+                                        split, _p(out0), out0.stride(0) if out0 is not None else 0, rows0, _p(out1),
+                                        out1.stride(0), rows1, kv_shard_rows, kv_plane_stride, own_shard,
+                                        _p(shard_ready), _p(shard_expect), stream_ptr()))
+
+
 def proj_add(x, w, bias=None, addvec=None, rows_per_sample=None, resid=None, out=None, out_f32=True):
     """y = x @ w.T + bias + addvec[row // rows_per_sample] + resid (fp32 or bf16 out; resid may be out)."""
     import torch

@@ -8,8 +8,10 @@ Two variants, selected by `cfg["variant"]`:
 * "ref21": the reference's own math (src/image/qwen_image.cpp:144-293): one weight set for text and image rows; one
   shared modulation Linear D -> 4D applied to silu(temb) of two timesteps (row 0: sigma, the image; row 1: t = 0, the
   text; :196-205, :222); LayerNorm x (1 + scale) without shift (src/kernels/image.metal:33-53); tanh-squashed gates
-  (:56-65); SwiGLU FFN (:277-280); condition-causal attention (text rows attend to text keys only, so the text K/V
-  is cached after the first step, :251-262); RoPE positions text (t, t, t), image (S, y - ceil(h/2), x - ceil(w/2))
+  (:56-65); SwiGLU FFN (:277-280); condition-causal attention (the runtime's `block = S`, :271: a text row at
+  position p attends to keys 0..p, causal among the text and never to an image key, so the text K/V is cached after
+  the first step, :251-262; the same argument is UINT32_MAX for the CLIP encoders, sdxl.cpp:501, which
+  docs/architecture.md:92 calls causal, and 0 for unmasked attention, sdxl.cpp:773); RoPE positions text (t, t, t), image (S, y - ceil(h/2), x - ceil(w/2))
   (:134-141); no biases.
 * "qwen1": the Qwen-Image(-1) shape BASELINE.json names: separate text and image weights with biases; per-block
   AdaLN Linear D -> 6D per stream ([shift1, scale1, gate1, shift2, scale2, gate2]); x (1 + scale) + shift; plain
@@ -167,7 +169,8 @@ def block_ref21(cfg, W, i, x, split, mod, rope, kv_cache=None):
             kv_cache["k"], kv_cache["v"] = k[:, :S].copy(), v[:, :S].copy()
     Lk = k.shape[1]
     qpos = np.arange(Lk - T, Lk)
-    mask = (qpos[:, None] >= S) | (np.arange(Lk)[None, :] < S)  # text queries see text keys only
+    # Condition-causal: a text query at position p sees keys 0..p (never an image key); image queries see all.
+    mask = (qpos[:, None] >= S) | (np.arange(Lk)[None, :] <= qpos[:, None])
     att = _unheads(O.attention(q, k, v, mask))
     x = x + np.tanh(rowmod[:, D:2 * D]) * O.linear(att, W[f"blk{i}.o.w"])
     xn = O.ln_modulate(x, rowmod[:, 2 * D:3 * D], None, EPS)

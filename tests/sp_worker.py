@@ -1,8 +1,9 @@
 """One rank of the two-GPU sequence-parallel test (test_sp_gpu.py), run as its own process.
 
 Rank 0 makes the NCCL id and hands it to the other ranks through a file in the shared temporary folder. Every rank
-runs the same steps on a sequence-parallel handle; rank 0 also runs them on an unsplit handle as the reference.
-Results go to rank<r>.npy / ref.npy in that folder."""
+runs the same steps on a sequence-parallel handle, its K/V exchanged by the NCCL all-gather or (argument "peer") by
+pushes into the peers' memory; rank 0 also runs them on an unsplit handle as the reference. Results go to
+rank<r>.npy / ref.npy in that folder."""
 
 import os
 import sys
@@ -34,6 +35,7 @@ def run_steps(d, lat):
 
 def main():
     rank, world, tmp = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3]
+    exchange = sys.argv[4] if len(sys.argv) > 4 else "nccl"
     import torch
     import mkimage
 
@@ -63,6 +65,8 @@ def main():
         d.init_random(seed=5)
         if sp:
             d.set_sequence_parallel(nid, rank, world)
+            if exchange == "peer":
+                d.set_peer_exchange(True)
         for slot in range(4):
             d.begin(prompts[slot], GH, GW, slot)
         return d

@@ -38,7 +38,7 @@ def _run(cuda, B, H, S, N, mask, later=False):
     pos = np.arange(L)
     m = None
     if mask == mkimage.ops.MASK_COND_CAUSAL:
-        m = (pos[:, None] >= S) | (pos[None, :] < S)
+        m = (pos[:, None] >= S) | (pos[None, :] <= pos[:, None])  # text rows causal, image rows see all
     for b in range(B):
         ref = O.attention(qn[b], kn[b], vn[b], m)  # [H][L][128]
         ref = ref.transpose(1, 0, 2).reshape(L, H * 128)
@@ -112,3 +112,81 @@ def test_attention_kv_shards_bit_exact(cuda, hd, G, B, H, S, N):
     assert mkimage.ops.check_kernels() == 0
     for b in range(B):
         assert torch.equal(outr[b * Lg:(b + 1) * Lg], ref1[b * N + r * Lg - S:b * N + (r + 1) * Lg - S])
+
+
+@pytest.mark.parametrize("hd,G,B,H,S,N", [(128, 2, 2, 3, 100, 412), (128, 4, 1, 2, 64, 960)])
+def test_attention_kv_arriving(cuda, hd, G, B, H, S, N):
+    """Shards that other ranks copy in during the launch (mkb_attention_kv_arriving): with every ready flag at the
+    expected value, each shard's queries (a rank's rows, own_shard = that rank) read the keys starting at their own
+    shard and wrapping round. Only the online softmax's rounding differs from the in-order call: outputs within the
+    oracle tolerance of it (max-abs 2e-2, cosine 0.9999), and against the oracle itself."""
+    import torch
+    import mkimage
+
+    L = S + N
+    Lg = L // G
+    q = _heads((B, H, L, hd), 21, cuda)
+    k = _heads((B, H, L, hd), 22, cuda)
+    v = _heads((B, H, L, hd), 23, cuda)
+    kv = torch.empty(G, 2, B * H, Lg, hd, dtype=torch.bfloat16, device=cuda)
+    for g in range(G):
+        kv[g, 0] = k.reshape(B * H, L, hd)[:, g * Lg:(g + 1) * Lg]
+        kv[g, 1] = v.reshape(B * H, L, hd)[:, g * Lg:(g + 1) * Lg]
+    ready = torch.full((G,), 7, dtype=torch.int64, device=cuda)
+    expect = torch.tensor([7], dtype=torch.int64, device=cuda)
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    for r in range(G):
+        qr = q[:, :, r * Lg:(r + 1) * Lg].contiguous()
+        want = torch.zeros(B * Lg, H * hd, dtype=torch.bfloat16, device=cuda)
+        got = torch.zeros_like(want)
+        mkimage.ops.attention_kv_shards(qr, kv[0, 0], kv[0, 1], None, want, split=r * Lg, Lk=L, kv_shard_rows=Lg,
+                                        kv_plane_stride=2 * B * H, q_pos0=r * Lg)
+        mkimage.ops.attention_kv_arriving(qr, kv[0, 0], kv[0, 1], None, got, split=r * Lg, Lk=L,
+                                          kv_shard_rows=Lg, kv_plane_stride=2 * B * H, own_shard=r,
+                                          shard_ready=ready, shard_expect=expect, q_pos0=r * Lg)
+        assert mkimage.ops.check_kernels() == 0
+        a, w = got.float().cpu().numpy(), want.float().cpu().numpy()
+        assert np.abs(a - w).max() < 2e-2
+        assert (a * w).sum() / np.sqrt((a * a).sum() * (w * w).sum()) > 0.9999
+        for b in range(B):
+            ref = O.attention(qn[b, :, r * Lg:(r + 1) * Lg], kn[b], vn[b], None)
+            ref = ref.transpose(1, 0, 2).reshape(Lg, H * hd)
+            assert np.abs(a[b * Lg:(b + 1) * Lg] - ref).max() < 2e-2
+
+
+def test_attention_kv_arriving_flag_never_set(cuda):
+    """A shard whose ready flag nobody raises: every CTA gives up after the bounded wait (2 s for the first, at once
+    for the others once the status bit is set), the launch reports MKB_ERR_KERNEL with the shard-wait bit (0x100),
+    and the same context then runs the call correctly once the flag is raised."""
+    import ctypes
+    import time
+
+    import torch
+    import mkimage
+
+    G, B, H, Lg, hd = 2, 1, 2, 256, 128
+    L = G * Lg
+    q = _heads((B, H, Lg, hd), 31, cuda)
+    kv = _heads((G, 2, B * H, Lg, hd), 32, cuda)
+    ready = torch.tensor([5, 4], dtype=torch.int64, device=cuda)  # shard 1 short of the expected 5
+    expect = torch.tensor([5], dtype=torch.int64, device=cuda)
+    out = torch.zeros(B * Lg, H * hd, dtype=torch.bfloat16, device=cuda)
+    assert mkimage.ops.check_kernels() == 0
+    t0 = time.time()
+    mkimage.ops.attention_kv_arriving(q, kv[0, 0], kv[0, 1], None, out, split=0, Lk=L, kv_shard_rows=Lg,
+                                      kv_plane_stride=2 * B * H, own_shard=0, shard_ready=ready, shard_expect=expect)
+    bits = ctypes.c_uint32()
+    code = mkimage.lib.mkb_check_kernels(ctypes.byref(bits))
+    elapsed = time.time() - t0
+    assert code == 4, (code, mkimage.lib.mkb_last_error())  # MKB_ERR_KERNEL
+    assert bits.value & 0x100, hex(bits.value)
+    assert 1.5 < elapsed < 60, elapsed
+    assert mkimage.ops.check_kernels() == 0
+    ready[1] = 5
+    mkimage.ops.attention_kv_arriving(q, kv[0, 0], kv[0, 1], None, out, split=0, Lk=L, kv_shard_rows=Lg,
+                                      kv_plane_stride=2 * B * H, own_shard=0, shard_ready=ready, shard_expect=expect)
+    assert mkimage.ops.check_kernels() == 0
+    want = torch.zeros_like(out)
+    mkimage.ops.attention_kv_shards(q, kv[0, 0], kv[0, 1], None, want, split=0, Lk=L, kv_shard_rows=Lg,
+                                    kv_plane_stride=2 * B * H)
+    assert (out.float() - want.float()).abs().max().item() < 2e-2

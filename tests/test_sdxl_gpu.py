@@ -86,6 +86,11 @@ def test_unet_geglu_bias_order(cuda):
 
 
 def test_vae_decode_reduced(cuda):
+    _vae_reduced_check()
+
+
+def _vae_reduced_check():
+    """The decoder at channels 128/128/256/256 (GroupNorm groups of 4 and 8 channels), one layer, an 8 x 8 latent."""
     import mkimage
 
     cfg = dict(channels=(128, 128, 256, 256), layers=1)
@@ -104,6 +109,29 @@ def test_vae_decode_reduced(cuda):
         assert _cos(got[name], want[name].ravel()) >= 0.999, name
     assert img.shape == (128, 128, 4) and np.all(img[..., 3] == 1.0)
     assert _rel(img, ref) < 0.01, _rel(img, ref)
+
+
+_THREE_PASS_CHILD = r"""
+import sys
+sys.path[:0] = [{root!r}, {pkg!r}]
+from tests.test_sdxl_gpu import _vae_reduced_check
+_vae_reduced_check()
+print("THREE_PASS_OK")
+"""
+
+
+def test_vae_decode_three_pass_group_norm(cuda):
+    """The decode above with every GroupNorm taking its statistics in a pass of its own (MKB_GN_FUSED=0) instead of
+    from the convolution that wrote its input. The switch is read once per process, so this runs in a child."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = _THREE_PASS_CHILD.format(root=root, pkg=os.path.join(root, "mako-image_b200"))
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, MKB_GN_FUSED="0"), capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "THREE_PASS_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-4000:])
 
 
 def test_vae_decode_16_latent_channels(cuda):

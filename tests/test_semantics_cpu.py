@@ -2,8 +2,9 @@
 
 The reference's GEMM, attention and per-head norm kernels live in its absent runtime, so a few of the oracle's
 choices are inferred from call sites rather than read from code: per-head RMSNorm before RoPE, RoPE on interleaved
-pairs (mode 2), SwiGLU as silu(first half) x second half, the condition-causal mask of the reference variant, the
-text rows' modulation row (t = 0) and its tanh-squashed gates. The device kernels implement the same choices, so
+pairs (mode 2), SwiGLU as silu(first half) x second half, the condition-causal mask of the reference variant (text
+rows causal among themselves, never seeing an image key), the text rows' modulation row (t = 0) and its
+tanh-squashed gates. The device kernels implement the same choices, so
 the GPU parity tests cannot tell whether a choice is right; what they can do is notice a kernel that made the other
 choice. Each test here flips one choice in the oracle alone and checks that what the first block adds to the
 residual stream (its output minus its input) moves beyond the tolerance the GPU tests hold that contribution to
@@ -128,6 +129,21 @@ def test_ref21_fully_joint_mask(monkeypatch):
     """The reference variant with text rows attending to image keys too (no condition-causal mask)."""
     att = O.attention
     _flipped(monkeypatch, "ref21", O, "attention", lambda q, k, v, mask=None: att(q, k, v, None))
+
+
+def test_ref21_text_rows_see_every_text_key(monkeypatch):
+    """The reference variant with its text rows attending to all text keys (the runtime's `block` argument cutting
+    off only the image keys) instead of causally to keys 0..p."""
+    att = O.attention
+
+    def all_text(q, k, v, mask=None):
+        if mask is not None:
+            text = ~mask.all(axis=1)  # the text rows: the only rows that do not see every key
+            mask = mask.copy()
+            mask[np.ix_(text, np.arange(int(text.sum())))] = True
+        return att(q, k, v, mask)
+
+    _flipped(monkeypatch, "ref21", O, "attention", all_text)
 
 
 def test_ref21_text_rows_take_the_image_modulation(monkeypatch):

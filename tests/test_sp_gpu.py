@@ -1,10 +1,12 @@
 """Sequence-parallel DiT step (mkb_dit_set_sequence_parallel) on two GPUs against the one-GPU step.
 
-Each rank runs every GEMM, norm and RoPE on its own joint rows and the ranks all-gather K and V per block, so every
+Each rank runs every GEMM, norm and RoPE on its own joint rows. With the NCCL all-gather of K and V per block every
 output row goes through the same arithmetic in the same order as on one GPU: the bar is bit-for-bit equality of the
 velocities and updated latents, on every rank, through the host, guided and device-buffer calls (the guided call
-three times: eager, captured into a CUDA graph with the collectives inside, replayed). NVLS is off for these
-processes. Skipped with fewer than two GPUs."""
+three times: eager, captured into a CUDA graph with the collectives inside, replayed). With the peer-memory exchange
+(mkb_dit_sp_peer_exchange) each rank's attention starts at its own shard's keys, so the bar is the ranks' equality
+with each other and a relative L2 error below 5e-3 against the one-GPU step. NVLS is off for these processes.
+Skipped with fewer than two GPUs."""
 
 import os
 import subprocess
@@ -18,13 +20,15 @@ pytestmark = pytest.mark.gpu
 WORKER = os.path.join(os.path.dirname(os.path.abspath(__file__)), "sp_worker.py")
 
 
-def test_sequence_parallel_two_gpus_bit_exact(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_sequence_parallel_two_gpus(tmp_path, exchange):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, WORKER, str(r), "2", str(tmp_path)], env=env) for r in range(2)]
+    procs = [subprocess.Popen([sys.executable, WORKER, str(r), "2", str(tmp_path), exchange], env=env)
+             for r in range(2)]
     try:
         codes = [p.wait(timeout=300) for p in procs]
     finally:
@@ -35,7 +39,13 @@ def test_sequence_parallel_two_gpus_bit_exact(tmp_path):
     assert codes == [0, 0], codes
     ref = np.load(tmp_path / "ref.npy")
     assert np.isfinite(ref).all() and np.abs(ref).max() > 0
+    got = [np.load(tmp_path / f"rank{r}.npy") for r in range(2)]
+    assert np.array_equal(got[0], got[1])  # every rank applies the same update to the gathered velocities
     for r in range(2):
-        got = np.load(tmp_path / f"rank{r}.npy")
-        assert got.shape == ref.shape
-        assert np.array_equal(got, ref), (r, np.abs(got - ref).max())
+        assert got[r].shape == ref.shape
+        if exchange == "nccl":
+            assert np.array_equal(got[r], ref), (r, np.abs(got[r] - ref).max())
+        else:  # each rank reads the keys from its own shard round: the softmax's rounding differs
+            for a, w in zip(got[r], ref):
+                rel = np.sqrt(((a - w) ** 2).sum() / (w ** 2).sum())
+                assert rel < 5e-3, (r, rel)
