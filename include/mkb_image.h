@@ -38,8 +38,9 @@ const char* mkb_last_error(void);
 /* Kernel launches this library has made in this process (all threads, all devices). */
 uint64_t mkb_kernel_launches(void);
 
-/* Activations a projection epilogue can apply. */
-enum { MKB_ACT_NONE = 0, MKB_ACT_GELU_TANH = 1, MKB_ACT_SILU = 2 };
+/* Activations a projection epilogue can apply (quick GELU x sigmoid(1.702 x) and the erf GELU: the CLIP text
+ * encoders' fc1, src/image/sdxl.cpp:508). */
+enum { MKB_ACT_NONE = 0, MKB_ACT_GELU_TANH = 1, MKB_ACT_SILU = 2, MKB_ACT_QUICK_GELU = 3, MKB_ACT_GELU_ERF = 4 };
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Runtime operations (device pointers). bf16 matrices are row-major with the given leading dimension in elements.
@@ -484,6 +485,52 @@ double mkb_vae_decode_flops(const mkb_vae* v, int gh, int gw);
  * patch, or the batch-norm statistics of a packed-latent VAE). n = 4 * latent. Replaces the scale's default of
  * mean 0, std 1 / scale. */
 mkb_status mkb_vae_set_latent_stats(mkb_vae* v, const float* mean, const float* std, int n);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * SDXL's text encoders: the text side of Sdxl (src/image/sdxl.hpp:46 encode_clip, and :30 prompt_embeddings, the
+ * override of engine.hpp:161). The tokenizer (image::ClipTokenizer) stays with the caller: these take its token ids.
+ * ------------------------------------------------------------------------------------------------------------- */
+
+typedef struct mkb_clip_config {
+    int which;      /* 0: CLIP ViT-L (quick GELU; the output is its second to last layer's states); 1: OpenCLIP bigG
+                       (erf GELU; also the pooled state: the final state at the first end token, ln_final, times the
+                       1280-wide text projection) */
+    int width;      /* E: 768 / 1280, a multiple of 128, heads of 64 */
+    int heads;      /* E / 64 */
+    int layers;     /* 12 / 32 */
+    int ffn;        /* 3072 / 5120 */
+    int vocab;      /* 49408 */
+    int max_chunks; /* 77-token chunks one encode call takes */
+} mkb_clip_config;
+
+typedef struct mkb_clip mkb_clip;
+mkb_status mkb_clip_create(const mkb_clip_config* cfg, mkb_clip** out);
+void mkb_clip_destroy(mkb_clip* c);
+mkb_status mkb_clip_init_random(mkb_clip* c, uint64_t seed, float std);
+/* The weight table: "tok" [vocab][E] and "pos" [77][E] (fp32: the checkpoint's F16 embeddings kept exactly),
+ * per layer "lN.ln1.w/b", "lN.qkv.w" [3E][E] (q, k, v rows), "lN.qkv.b", "lN.o.w/b", "lN.ln2.w/b", "lN.fc1.w"
+ * [F][E], "lN.fc1.b", "lN.fc2.w" [E][F], "lN.fc2.b"; bigG also "lnf.w/b" and "proj" [E][1280] as stored. */
+int mkb_clip_weight_count(const mkb_clip* c);
+mkb_status mkb_clip_weight_info(const mkb_clip* c, int i, const char** name, long* dims, int* ndim);
+mkb_status mkb_clip_weight_read(mkb_clip* c, const char* name, float* host);
+mkb_status mkb_clip_weight_write(mkb_clip* c, const char* name, const float* host);
+/* Weights from an SDXL checkpoint (Sdxl::load_clip, sdxl.cpp:154-237): ViT-L under
+ * "conditioner.embedders.0.transformer.text_model." (HF CLIPTextModel names, q / k / v stacked), bigG under
+ * "conditioner.embedders.1.model." (OpenCLIP names: in_proj, c_fc, c_proj, ln_final, text_projection); the prefixes
+ * may also be absent. strict and loaded as for mkb_vae_load_safetensors. */
+mkb_status mkb_clip_load_safetensors(mkb_clip* c, const char* const* paths, int n_paths, int strict, int* loaded);
+mkb_status mkb_clip_set_probe(mkb_clip* c, mkb_probe_fn fn, void* user);
+/* Sdxl::encode_clip (sdxl.cpp:459-546) for `chunks` chunks of 77 token ids (host [chunks][77]): hidden (host,
+ * [chunks * 77][E]) the second to last layer's states; pooled (host [chunks][1280], bigG only, may be NULL) each
+ * chunk's pooled state (a bigG chunk must hold the end token 49407). Causal attention in heads of 64; projections
+ * take their inputs split into bf16 parts as the reference's do. Ids out of range are MKB_ERR_INVALID. */
+mkb_status mkb_clip_encode(mkb_clip* c, const int32_t* ids, int chunks, float* hidden, float* pooled);
+/* Sdxl::prompt_embeddings after tokenization (sdxl.cpp:599-639): chunks of ids for each encoder (ViT-L padded with
+ * the end token, bigG with 0, as Sdxl::chunks pads them) and per-token weights (host [chunks][77], NULL = all 1) to
+ * context (host [chunks * 77][E_L + E_G], ViT-L's then bigG's states per token; a token of weight w != 1 gets
+ * (z - e) w + e with e the empty prompt's states at its position) and pooled (host [1280], the first chunk's). */
+mkb_status mkb_sdxl_prompt_embeddings(mkb_clip* l, mkb_clip* g, const int32_t* ids_l, const int32_t* ids_g,
+                                      const float* weights, int chunks, float* context, float* pooled);
 
 /* Image output (host code, no device needed). mkb_to_rgba8: RGBA floats in [-1, 1] to 8-bit samples, x / 2 + 1/2
  * clamped, times 255, rounded to nearest (the reference's to_rgba8, src/image/png.hpp:13-14, png.cpp:148-156).

@@ -105,7 +105,7 @@ uint64_t mkb_kernel_launches(void) { return g_launches.load(std::memory_order_re
 mkb_status mkb_proj(const void* x, long ldx, const void* w, long ldw, const float* bias, void* y, long ldy, int M,
                     int N, int K, int act, int out_f32, void* stream)
 {
-    if (act < MKB_ACT_NONE || act > MKB_ACT_SILU)
+    if (act < MKB_ACT_NONE || act > MKB_ACT_GELU_ERF)
         return fail(MKB_ERR_INVALID, "proj: unknown activation");
     GemmArgs a;
     a.M = M;

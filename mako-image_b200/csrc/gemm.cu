@@ -98,6 +98,10 @@ __device__ __forceinline__ float gelu_tanh(float x)
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+__device__ __forceinline__ float quick_gelu(float x) { return x / (1.0f + __expf(-1.702f * x)); }
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
+
 // The activation over a 32-column chunk. The switch sits outside the loop so the 32 independent chains interleave
 // (a per-element branch serializes each SFU round trip).
 __device__ __forceinline__ void apply_act32(float (&v)[32], int act)
@@ -110,6 +114,14 @@ __device__ __forceinline__ void apply_act32(float (&v)[32], int act)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
             v[j] = silu(v[j]);
+    } else if (act == kActQuickGelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = quick_gelu(v[j]);
+    } else if (act == kActGeluErf) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            v[j] = gelu_erf(v[j]);
     }
 }
 
@@ -184,8 +196,6 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
 }
 
 // The epilogue of one tile for one thread (one row). t_row: TMEM address of this row's accumulator, column 0.
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
-
 template <int BN, Epi EPI>
 __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int row, bool row_ok, int n0,
                                          const float* sb)

@@ -27,7 +27,9 @@ enum class Epi : int {
 // gate half).
 enum Glu : int { kGluSilu = 0, kGluGelu = 1 };
 
-enum Act : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };
+// Epilogue activations: GELU (tanh form), SiLU, quick GELU x sigmoid(1.702 x) and the erf GELU (the CLIP text
+// encoders' fc1, sdxl.cpp:508).
+enum Act : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2, kActQuickGelu = 3, kActGeluErf = 4 };
 
 struct GemmArgs {
     int M = 0, N = 0, K = 0;

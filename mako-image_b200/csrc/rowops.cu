@@ -774,6 +774,112 @@ __global__ void k_transpose(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloa
     }
 }
 
+// ---------------------------------------------------------------- SDXL text encoders (sdxl.cpp:459-546)
+
+// x[m][e] = tok[ids[m]][e] + pos[m % T][e]: a token's embedding row plus its position's. One block per row.
+__global__ void __launch_bounds__(256) k_clip_embed(const int* ids, const float* tok, const float* pos, float* x,
+                                                   int T, int E)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    const int m = blockIdx.x;
+    const float* t = tok + long(ids[m]) * E;
+    const float* p = pos + long(m % T) * E;
+    float* y = x + long(m) * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+        y[e] = t[e] + p[e];
+}
+
+// The bf16 rounding of v and of what it left out, packed as y[col] and y[N + col] of a row of 2N.
+__device__ __forceinline__ void split_store(__nv_bfloat16* y, int N, int col, float v)
+{
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    y[col] = hi;
+    y[N + col] = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
+// LayerNorm of fp32 rows (two passes over the row for mean and variance), the result split into bf16 parts. One
+// warp per row.
+__global__ void __launch_bounds__(256) k_ln_split(const float* x, const float* g, const float* b, __nv_bfloat16* y,
+                                                 int M, int E, float eps)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    const int m = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (m >= M)
+        return;
+    const float* r = x + long(m) * E;
+    float s = 0.f;
+    for (int e = lane; e < E; e += 32)
+        s += r[e];
+    const float mean = warp_sum(s) / E;
+    float q = 0.f;
+    for (int e = lane; e < E; e += 32) {
+        const float d = r[e] - mean;
+        q = fmaf(d, d, q);
+    }
+    const float inv = rsqrtf(warp_sum(q) / E + eps);
+    __nv_bfloat16* o = y + long(m) * 2 * E;
+    for (int e = lane; e < E; e += 32)
+        split_store(o, E, e, (r[e] - mean) * inv * g[e] + b[e]);
+}
+
+__global__ void __launch_bounds__(256) k_split_bf16(const float* x, __nv_bfloat16* y, long M, int N)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    const long n = M * N;
+    for (long i = blockIdx.x * long(blockDim.x) + threadIdx.x; i < n; i += long(gridDim.x) * blockDim.x) {
+        const long m = i / N;
+        split_store(y + m * 2 * N, N, int(i - m * N), x[i]);
+    }
+}
+
+// bigG's pooled state per chunk b: LayerNorm of row eos[b] of chunk b, times proj [E][P] as stored. One block per
+// chunk; the normed row in shared memory, each thread a strided set of output columns (coalesced proj rows).
+__global__ void __launch_bounds__(256) k_clip_pooled(const float* x, const int* eos, const float* g, const float* b,
+                                                    const float* proj, float* out, int T, int E, int P, float eps)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float row[2048];
+    __shared__ float red[8];
+    const int c = blockIdx.x, t = threadIdx.x;
+    const float* r = x + (long(c) * T + eos[c]) * E;
+    auto block_sum = [&](float v) {
+        v = warp_sum(v);
+        if (t % 32 == 0)
+            red[t / 32] = v;
+        __syncthreads();
+        float s = 0.f;
+        for (int w = 0; w < 8; ++w)
+            s += red[w];
+        __syncthreads();
+        return s;
+    };
+    float s = 0.f;
+    for (int e = t; e < E; e += 256) {
+        row[e] = r[e];
+        s += row[e];
+    }
+    const float mean = block_sum(s) / E;
+    float q = 0.f;
+    for (int e = t; e < E; e += 256) {
+        const float d = row[e] - mean;
+        q = fmaf(d, d, q);
+    }
+    const float inv = rsqrtf(block_sum(q) / E + eps);
+    for (int e = t; e < E; e += 256)
+        row[e] = (row[e] - mean) * inv * g[e] + b[e];
+    __syncthreads();
+    for (int j = t; j < P; j += 256) {
+        float acc = 0.f;
+        for (int i = 0; i < E; ++i)
+            acc = fmaf(row[i], proj[long(i) * P + j], acc);
+        out[long(c) * P + j] = acc;
+    }
+}
+
 int grid_for(uint64_t n, int threads)
 {
     uint64_t g = (n + threads - 1) / threads;
@@ -1071,6 +1177,45 @@ cudaError_t transpose_bf16(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat
 {
     dim3 grid(unsigned((rows + 31) / 32), unsigned((cols + 31) / 32));
     launch_k(k_transpose, grid, dim3(32, 8), 0, st, x, ldx, c0, y, rows, cols);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t clip_embed(const int* ids, const float* tok, const float* pos, float* x, int M, int T, int E,
+                       cudaStream_t st)
+{
+    if (M <= 0 || T <= 0 || E <= 0)
+        return cudaErrorInvalidValue;
+    launch_k(k_clip_embed, dim3(M), 256, 0, st, ids, tok, pos, x, T, E);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t ln_split_bf16(const float* x, const float* g, const float* b, __nv_bfloat16* y, int M, int E, float eps,
+                          cudaStream_t st)
+{
+    if (M <= 0 || E <= 0)
+        return cudaErrorInvalidValue;
+    launch_k(k_ln_split, dim3((M + 7) / 8), 256, 0, st, x, g, b, y, M, E, eps);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t split_bf16(const float* x, __nv_bfloat16* y, long M, int N, cudaStream_t st)
+{
+    if (M <= 0 || N <= 0)
+        return cudaErrorInvalidValue;
+    launch_k(k_split_bf16, grid_for(uint64_t(M) * N, 256), 256, 0, st, x, y, M, N);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t clip_pooled(const float* x, const int* eos, const float* g, const float* b, const float* proj, float* out,
+                        int B, int T, int E, int P, float eps, cudaStream_t st)
+{
+    if (B <= 0 || E <= 0 || E > 2048 || P <= 0)
+        return cudaErrorInvalidValue;
+    launch_k(k_clip_pooled, dim3(B), 256, 0, st, x, eos, g, b, proj, out, T, E, P, eps);
     count_launch();
     return cudaGetLastError();
 }

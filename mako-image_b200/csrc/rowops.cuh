@@ -118,6 +118,21 @@ cudaError_t softmax_rows_bf16(const float* s, __nv_bfloat16* p, long rows, int n
 cudaError_t transpose_bf16(const __nv_bfloat16* x, long ldx, int c0, __nv_bfloat16* y, long rows, int cols,
                            cudaStream_t st);
 
+// SDXL's text encoders (Sdxl::encode_clip, sdxl.cpp:459-546).
+// x [M][E] fp32 = tok[ids[m]] + pos[m % T]: token plus position embeddings (ids checked by the caller).
+cudaError_t clip_embed(const int* ids, const float* tok, const float* pos, float* x, int M, int T, int E,
+                       cudaStream_t st);
+// LayerNorm (gamma g, beta b) of fp32 rows x [M][E] into y [M][2E] bf16: y[m][e] the bf16 rounding of the normed value
+// v, y[m][E + e] the bf16 rounding of v minus it. A GEMM over K = 2E against weights duplicated along K then
+// multiplies v to within ~2^-16: the split the reference's text-encoder GEMMs use (docs/architecture.md:9-11).
+cudaError_t ln_split_bf16(const float* x, const float* g, const float* b, __nv_bfloat16* y, int M, int E, float eps,
+                          cudaStream_t st);
+// The same split of fp32 x [M][N] into y [M][2N] bf16.
+cudaError_t split_bf16(const float* x, __nv_bfloat16* y, long M, int N, cudaStream_t st);
+// out [B][P] = LayerNorm(x row (b * T + eos[b])) times proj [E][P] (bigG's pooled state, sdxl.cpp:521-541); E <= 2048.
+cudaError_t clip_pooled(const float* x, const int* eos, const float* g, const float* b, const float* proj, float* out,
+                        int B, int T, int E, int P, float eps, cudaStream_t st);
+
 // x[i] += dt * (v_u[i] + g * (v_c[i] - v_u[i])) (classifier-free guidance then an Euler step, engine.cpp:476-480,
 // :500-503); with v_u null: x += dt * v_c.
 cudaError_t cfg_euler(float* x, const float* v_c, const float* v_u, float g, float dt, uint64_t n, cudaStream_t st);

@@ -12,6 +12,7 @@
 #include "lora.cuh"
 #include "rowops.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <deque>
@@ -58,9 +59,12 @@ uint64_t mix64(uint64_t x)
 //   conv3  bf16 [r][3][3][c] -> [rp][9][cp]      (3x3 convolution, tap-major, input channels padded)
 //   glu    bf16 [r][c], r = 2F (first half / second half) -> rows interleaved in blocks of 128 for the GLU epilogue
 //   gluvec fp32 [r], the bias of a glu matrix, interleaved the same way (the GLU epilogue reads bias by device column)
+//   matdup bf16 [r][c] -> [r][2c], the matrix twice along K: against an input split into a bf16 part and the bf16
+//          rounding of its remainder ([hi | lo], K = 2c), one GEMM multiplies the fp32 input
+//   tab    fp32 [r][c] (embedding tables and other fp32 matrices)
 struct WTable {
-    enum Kind { kVec, kMat, kConv3, kGlu, kGluVec };
-    static bool is_vec(Kind k) { return k == kVec || k == kGluVec; }
+    enum Kind { kVec, kMat, kConv3, kGlu, kGluVec, kMatDup, kTab };
+    static bool is_vec(Kind k) { return k == kVec || k == kGluVec || k == kTab; }
     struct W {
         std::string name;
         Kind kind;
@@ -69,8 +73,13 @@ struct WTable {
         bool norm;
         size_t dev_count() const
         {
+            if (kind == kTab)
+                return size_t(r) * c;
+            if (kind == kMatDup)
+                return size_t(rp) * 2 * cp;
             return is_vec(kind) ? size_t(rp) : kind == kConv3 ? size_t(rp) * 9 * cp : size_t(rp) * cp;
         }
+        long dev_cols() const { return kind == kMatDup ? 2 * cp : cp; }  // row stride of a matrix on the device
     };
     std::vector<W> ws;
     std::map<std::string, int> idx;
@@ -82,9 +91,10 @@ struct WTable {
     {
         W w{name, k, r, c, rp ? rp : r, cp ? cp : c, 0, norm};
         if (is_vec(k)) {
-            w.rp = (w.rp + 3) & ~3L;
+            if (k != kTab)
+                w.rp = (w.rp + 3) & ~3L;
             w.off = nvec;
-            nvec += w.dev_count();
+            nvec += (w.dev_count() + 3) & ~size_t(3);
         } else {
             w.off = nmat;
             nmat += (w.dev_count() + 7) & ~size_t(7);  // 16-byte aligned starts
@@ -139,11 +149,19 @@ struct WTable {
             const uint64_t key = mix64(seed * 0x100000001B3ull + i);
             const float sd = w.norm ? 0.1f : std, mean = w.norm ? 1.0f : 0.0f;
             if (is_vec(w.kind)) {
-                MKB_TRY_CUDA(fill_normal(vec + w.off, false, w.r, key, 0, sd, mean, s), "init");
+                MKB_TRY_CUDA(fill_normal(vec + w.off, false, w.kind == kTab ? w.dev_count() : size_t(w.r), key, 0, sd,
+                                         mean, s),
+                             "init");
                 continue;
             }
             __nv_bfloat16* p = mat + w.off;
             MKB_TRY_CUDA(fill_normal(p, true, w.dev_count(), key, 0, sd, mean, s), "init");
+            if (w.kind == kMatDup) {  // the second copy along K equals the first
+                MKB_TRY_CUDA(cudaMemcpy2DAsync(p + w.cp, size_t(w.cp) * 4, p, size_t(w.cp) * 4, size_t(w.cp) * 2,
+                                               size_t(w.rp), cudaMemcpyDeviceToDevice, s),
+                             "init copy");
+                continue;
+            }
             // padding stays zero
             const long taps = w.kind == kConv3 ? 9 : 1;
             if (w.cp > w.c)
@@ -163,8 +181,10 @@ struct WTable {
         const W* w = find(name);
         if (!w || !host)
             return fail(MKB_ERR_INVALID, "weight_read: unknown weight " + name);
-        if (w->kind == kVec) {
-            MKB_TRY_CUDA(cudaMemcpy(host, vec + w->off, w->r * 4, cudaMemcpyDeviceToHost), "weight read");
+        if (w->kind == kVec || w->kind == kTab) {
+            MKB_TRY_CUDA(cudaMemcpy(host, vec + w->off, (w->kind == kTab ? w->dev_count() : size_t(w->r)) * 4,
+                                    cudaMemcpyDeviceToHost),
+                         "weight read");
             return MKB_OK;
         }
         if (w->kind == kGluVec) {
@@ -176,12 +196,12 @@ struct WTable {
         }
         std::vector<__nv_bfloat16> t(w->dev_count());
         MKB_TRY_CUDA(cudaMemcpy(t.data(), mat + w->off, t.size() * 2, cudaMemcpyDeviceToHost), "weight read");
-        const long taps = w->kind == kConv3 ? 9 : 1;
+        const long taps = w->kind == kConv3 ? 9 : 1, ld = w->dev_cols();
         for (long i = 0; i < w->r; ++i) {
             const long di = w->kind == kGlu ? glu_row(i, w->r) : i;
             for (long k = 0; k < taps; ++k)
                 for (long j = 0; j < w->c; ++j)
-                    host[(i * taps + k) * w->c + j] = __bfloat162float(t[(size_t(di) * taps + k) * w->cp + j]);
+                    host[(i * taps + k) * w->c + j] = __bfloat162float(t[(size_t(di) * taps + k) * ld + j]);
         }
         return MKB_OK;
     }
@@ -190,8 +210,10 @@ struct WTable {
         const W* w = find(name);
         if (!w || !host)
             return fail(MKB_ERR_INVALID, "weight_write: unknown weight " + name);
-        if (w->kind == kVec) {
-            MKB_TRY_CUDA(cudaMemcpy(vec + w->off, host, w->r * 4, cudaMemcpyHostToDevice), "weight write");
+        if (w->kind == kVec || w->kind == kTab) {
+            MKB_TRY_CUDA(cudaMemcpy(vec + w->off, host, (w->kind == kTab ? w->dev_count() : size_t(w->r)) * 4,
+                                    cudaMemcpyHostToDevice),
+                         "weight write");
             return MKB_OK;
         }
         if (w->kind == kGluVec) {
@@ -202,12 +224,16 @@ struct WTable {
             return MKB_OK;
         }
         std::vector<__nv_bfloat16> t(w->dev_count(), __float2bfloat16_rn(0.f));
-        const long taps = w->kind == kConv3 ? 9 : 1;
+        const long taps = w->kind == kConv3 ? 9 : 1, ld = w->dev_cols();
         for (long i = 0; i < w->r; ++i) {
             const long di = w->kind == kGlu ? glu_row(i, w->r) : i;
             for (long k = 0; k < taps; ++k)
-                for (long j = 0; j < w->c; ++j)
-                    t[(size_t(di) * taps + k) * w->cp + j] = __float2bfloat16_rn(host[(i * taps + k) * w->c + j]);
+                for (long j = 0; j < w->c; ++j) {
+                    const __nv_bfloat16 v = __float2bfloat16_rn(host[(i * taps + k) * w->c + j]);
+                    t[(size_t(di) * taps + k) * ld + j] = v;
+                    if (w->kind == kMatDup)
+                        t[size_t(di) * ld + w->cp + j] = v;
+                }
         }
         MKB_TRY_CUDA(cudaMemcpy(mat + w->off, t.data(), t.size() * 2, cudaMemcpyHostToDevice), "weight write");
         return MKB_OK;
@@ -221,7 +247,10 @@ struct WTable {
             *name = w.name.c_str();
         int n = 0;
         long d[4] = {w.r, 0, 0, 0};
-        if (is_vec(w.kind))
+        if (w.kind == kTab) {
+            d[1] = w.c;
+            n = 2;
+        } else if (is_vec(w.kind))
             n = 1;
         else if (w.kind == kConv3) {
             d[1] = 3, d[2] = 3, d[3] = w.c;
@@ -1326,6 +1355,239 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
     return MKB_OK;
 }
 
+// ------------------------------------------------------------------------------------------------ text encoders
+
+constexpr int kClipTokens = 77, kClipPooled = 1280, kClipEnd = 49407;
+constexpr float kClipEps = 1e-5f;
+
+// One of SDXL's text encoders (Sdxl::encode_clip, sdxl.cpp:459-546): CLIP ViT-L (which 0: quick GELU, its output the
+// second to last layer's states) or OpenCLIP bigG (which 1: erf GELU, also the pooled state). Each layer: LayerNorm,
+// q | k | v projection into heads of 64, causal attention over the 77 tokens, output projection added to the
+// residual, LayerNorm, fc1 with the activation, fc2 added to the residual. Every projection whose input the reference
+// splits into bf16 parts (docs/architecture.md:9-11) takes it as [hi | lo] against its weights held twice along K:
+// the LayerNorm outputs and fc1's output. The attention output feeds the output projection as bf16.
+struct ClipImpl {
+    mkb_clip_config cfg{};
+    WTable W;
+    cudaStream_t stream = nullptr;
+    uint32_t* status = nullptr;
+    PlanMap plans;
+    int* ids = nullptr;       // [max_chunks * 77]
+    int* eos = nullptr;       // [max_chunks]: each chunk's first end token
+    float* hidden = nullptr;  // [max_chunks * 77][E]
+    float* pooled = nullptr;  // [max_chunks][1280]
+    mkb_probe_fn probe = nullptr;
+    void* probe_user = nullptr;
+    std::vector<float> empty_hidden;  // the empty prompt's hidden states (computed on first need)
+
+    ~ClipImpl()
+    {
+        plans.clear();
+        W.release();
+        for (void* p : {static_cast<void*>(ids), static_cast<void*>(eos), static_cast<void*>(hidden),
+                        static_cast<void*>(pooled)})
+            if (p)
+                cudaFree(p);
+        if (stream)
+            cudaStreamDestroy(stream);
+    }
+    int run_layers() const { return cfg.which == 1 ? cfg.layers : cfg.layers - 1; }
+    mkb_status create(const mkb_clip_config& c);
+    mkb_status build(int B, Plan** out);
+    mkb_status encode(const int32_t* host_ids, int B, float* hidden_out, float* pooled_out);
+};
+
+mkb_status ClipImpl::create(const mkb_clip_config& c)
+{
+    cfg = c;
+    if ((c.which != 0 && c.which != 1) || c.width <= 0 || c.width % 128 || c.width > 2048 || c.heads * kHead != c.width ||
+        c.layers < 2 || c.ffn <= 0 || c.ffn % 128 || c.vocab <= kClipEnd || c.max_chunks < 1)
+        return fail(MKB_ERR_INVALID, "clip: bad configuration (width a multiple of 128 up to 2048 in heads of 64, "
+                                     "ffn a multiple of 128, at least 2 layers, the CLIP vocabulary)");
+    const long E = c.width, F = c.ffn;
+    W.add("tok", WTable::kTab, c.vocab, E);
+    W.add("pos", WTable::kTab, kClipTokens, E);
+    for (int i = 0; i < c.layers; ++i) {
+        const std::string p = "l" + std::to_string(i) + ".";
+        W.add(p + "ln1.w", WTable::kVec, E, 0, 0, 0, true);
+        W.add(p + "ln1.b", WTable::kVec, E);
+        W.add(p + "qkv.w", WTable::kMatDup, 3 * E, E);
+        W.add(p + "qkv.b", WTable::kVec, 3 * E);
+        W.add(p + "o.w", WTable::kMat, E, E);
+        W.add(p + "o.b", WTable::kVec, E);
+        W.add(p + "ln2.w", WTable::kVec, E, 0, 0, 0, true);
+        W.add(p + "ln2.b", WTable::kVec, E);
+        W.add(p + "fc1.w", WTable::kMatDup, F, E);
+        W.add(p + "fc1.b", WTable::kVec, F);
+        W.add(p + "fc2.w", WTable::kMatDup, E, F);
+        W.add(p + "fc2.b", WTable::kVec, E);
+    }
+    if (c.which == 1) {
+        W.add("lnf.w", WTable::kVec, E, 0, 0, 0, true);
+        W.add("lnf.b", WTable::kVec, E);
+        W.add("proj", WTable::kTab, E, kClipPooled);
+    }
+    MKB_TRY_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    status = device_status_word();
+    const size_t rows = size_t(c.max_chunks) * kClipTokens;
+    MKB_TRY(W.alloc());
+    MKB_TRY_CUDA(cudaMalloc(&ids, rows * 4), "clip buffers");
+    MKB_TRY_CUDA(cudaMalloc(&eos, size_t(c.max_chunks) * 4), "clip buffers");
+    MKB_TRY_CUDA(cudaMalloc(&hidden, rows * E * 4), "clip buffers");
+    MKB_TRY_CUDA(cudaMalloc(&pooled, size_t(c.max_chunks) * kClipPooled * 4), "clip buffers");
+    return MKB_OK;
+}
+
+mkb_status ClipImpl::build(int B, Plan** out)
+{
+    const std::vector<int> key = {B};
+    auto it = plans.find(key);
+    if (it != plans.end()) {
+        *out = it->second.get();
+        return MKB_OK;
+    }
+    auto plan = std::make_unique<Plan>();
+    Plan& P = *plan;
+    mkb_status st = MKB_OK;
+    Builder bd{P, status};
+    const int E = cfg.width, F = cfg.ffn, H = cfg.heads, T = kClipTokens, M = B * T;
+    float* X = P.buf<float>(size_t(M) * E, &st);
+    __nv_bfloat16* XS = P.buf<__nv_bfloat16>(size_t(M) * 2 * E, &st);
+    __nv_bfloat16* QH = P.buf<__nv_bfloat16>(size_t(M) * E, &st);
+    __nv_bfloat16* KH = P.buf<__nv_bfloat16>(size_t(M) * E, &st);
+    __nv_bfloat16* VH = P.buf<__nv_bfloat16>(size_t(M) * E, &st);
+    __nv_bfloat16* AT = P.buf<__nv_bfloat16>(size_t(M) * E, &st);
+    float* HF = P.buf<float>(size_t(M) * F, &st);
+    __nv_bfloat16* HS = P.buf<__nv_bfloat16>(size_t(M) * 2 * F, &st);
+    if (st != MKB_OK)
+        return st;
+    const WTable& w = W;
+    const int* id = ids;
+    const float *tok = w.V("tok"), *pos = w.V("pos");
+    P.add([=](cudaStream_t s) { return clip_embed(id, tok, pos, X, M, T, E, s); });
+    AttnArgs at;  // causal over each chunk's 77 tokens: the condition-causal mask with every row a condition row
+    at.B = B;
+    at.H = H;
+    at.Lq = T;
+    at.Lk = T;
+    at.mask = kMaskCondCausal;
+    at.cond_len = T;
+    at.head_dim = kHead;
+    at.scale_log2 = 1.4426950408889634f / std::sqrt(float(kHead));
+    at.split = 0;
+    at.out1 = AT;
+    at.ld1 = E;
+    at.rows1 = T;
+    at.status = status;
+    AttnOp aop;
+    const char* err = nullptr;
+    if (!attn_prepare(aop, QH, T, KH, VH, T, at, &err))
+        return fail(MKB_ERR_INVALID, std::string("clip plan: ") + (err ? err : "attention"));
+    const int act = cfg.which == 0 ? kActQuickGelu : kActGeluErf;
+    for (int i = 0; i < run_layers() && bd.ok(); ++i) {
+        const std::string p = "l" + std::to_string(i) + ".";
+        const float *g1 = w.V(p + "ln1.w"), *b1 = w.V(p + "ln1.b"), *g2 = w.V(p + "ln2.w"), *b2 = w.V(p + "ln2.b");
+        P.add([=](cudaStream_t s) { return ln_split_bf16(X, g1, b1, XS, M, E, kClipEps, s); });
+        GemmArgs q;
+        q.M = M;
+        q.N = 3 * E;
+        q.K = 2 * E;
+        q.bias = w.V(p + "qkv.b");
+        q.qh = QH;
+        q.kh = KH;
+        q.vh = VH;
+        q.D = E;
+        q.head_dim = kHead;
+        q.L = T;
+        q.seg_rows = T;
+        bd.gemm(Epi::kHeads, XS, 2 * E, w.M(p + "qkv.w"), 2 * E, q);
+        P.add([aop](cudaStream_t s) { return attn_launch(aop, s); });
+        GemmArgs o;
+        o.M = M;
+        o.N = E;
+        o.K = E;
+        o.bias = w.V(p + "o.b");
+        o.add_resid = X;
+        o.ld_add_resid = E;
+        o.out = X;
+        o.ldo = E;
+        o.out_f32 = 1;
+        bd.gemm(Epi::kAdd, AT, E, w.M(p + "o.w"), E, o);
+        P.add([=](cudaStream_t s) { return ln_split_bf16(X, g2, b2, XS, M, E, kClipEps, s); });
+        GemmArgs f1;
+        f1.M = M;
+        f1.N = F;
+        f1.K = 2 * E;
+        f1.bias = w.V(p + "fc1.b");
+        f1.act = act;
+        f1.out = HF;
+        f1.ldo = F;
+        bd.gemm(Epi::kF32, XS, 2 * E, w.M(p + "fc1.w"), 2 * E, f1);
+        P.add([=](cudaStream_t s) { return split_bf16(HF, HS, M, F, s); });
+        GemmArgs f2 = o;
+        f2.K = 2 * F;
+        f2.bias = w.V(p + "fc2.b");
+        bd.gemm(Epi::kAdd, HS, 2 * F, w.M(p + "fc2.w"), 2 * F, f2);
+        P.probe("layer", i, X, long(M) * E);
+        if (i + 2 == cfg.layers) {
+            float* hid = hidden;
+            P.add([=](cudaStream_t s) {
+                return cudaMemcpyAsync(hid, X, size_t(M) * E * 4, cudaMemcpyDeviceToDevice, s);
+            });
+        }
+    }
+    if (!bd.ok())
+        return bd.st;
+    if (cfg.which == 1) {
+        const float *g = w.V("lnf.w"), *b = w.V("lnf.b"), *pr = w.V("proj");
+        const int* e = eos;
+        float* po = pooled;
+        P.add([=](cudaStream_t s) { return clip_pooled(X, e, g, b, pr, po, B, T, E, kClipPooled, kClipEps, s); });
+    }
+    *out = plan.get();
+    plans[key] = std::move(plan);
+    return MKB_OK;
+}
+
+// Chunks of 77 ids on the host -> hidden states [B * 77][E] and (bigG) pooled states [B][1280] on the host.
+mkb_status ClipImpl::encode(const int32_t* host_ids, int B, float* hidden_out, float* pooled_out)
+{
+    if (!host_ids || !hidden_out || B < 1 || B > cfg.max_chunks)
+        return fail(MKB_ERR_INVALID, "clip_encode: null argument or chunk count out of range");
+    std::vector<int> e(B, -1);
+    for (int b = 0; b < B; ++b)
+        for (int t = 0; t < kClipTokens; ++t) {
+            const int32_t v = host_ids[size_t(b) * kClipTokens + t];
+            if (v < 0 || v >= cfg.vocab)
+                return fail(MKB_ERR_INVALID, "clip_encode: token out of range");
+            if (v == kClipEnd && e[b] < 0)
+                e[b] = t;
+        }
+    if (cfg.which == 1)
+        for (int b = 0; b < B; ++b)
+            if (e[b] < 0)
+                return fail(MKB_ERR_INVALID, "clip_encode: a chunk without its end token");
+    Plan* plan = nullptr;
+    MKB_TRY(build(B, &plan));
+    const size_t rows = size_t(B) * kClipTokens;
+    MKB_TRY_CUDA(cudaMemcpyAsync(ids, host_ids, rows * 4, cudaMemcpyHostToDevice, stream), "ids upload");
+    MKB_TRY_CUDA(cudaMemcpyAsync(eos, e.data(), size_t(B) * 4, cudaMemcpyHostToDevice, stream), "ids upload");
+    MKB_TRY(plan->run(stream, probe, probe_user));
+    MKB_TRY_CUDA(cudaMemcpyAsync(hidden_out, hidden, rows * cfg.width * 4, cudaMemcpyDeviceToHost, stream),
+                 "hidden download");
+    if (pooled_out && cfg.which == 1)
+        MKB_TRY_CUDA(cudaMemcpyAsync(pooled_out, pooled, size_t(B) * kClipPooled * 4, cudaMemcpyDeviceToHost, stream),
+                     "pooled download");
+    MKB_TRY_CUDA(cudaStreamSynchronize(stream), "encode sync");
+    uint32_t bits = 0;
+    MKB_TRY_CUDA(cudaMemcpy(&bits, status, 4, cudaMemcpyDeviceToHost), "status");
+    if (bits) {
+        cudaMemset(status, 0, 4);
+        return fail(MKB_ERR_KERNEL, "clip_encode: kernel status " + std::to_string(bits));
+    }
+    return MKB_OK;
+}
+
 namespace {
 
 // Sdxl's discrete schedule and its timestep pick (sdxl.cpp:130-139, 643-651, 653-670).
@@ -1379,6 +1641,10 @@ struct mkb_unet {
 };
 struct mkb_vae {
     mkb::VaeImpl impl;
+};
+
+struct mkb_clip {
+    mkb::ClipImpl impl;
 };
 
 using namespace mkb;
@@ -1773,6 +2039,124 @@ mkb_status mkb_vae_set_latent_stats(mkb_vae* v, const float* mean, const float* 
     }
     MKB_TRY_CUDA(cudaStreamSynchronize(m.stream), "sync");
     MKB_TRY_CUDA(cudaMemcpy(m.lat_aff, aff.data(), aff.size() * 4, cudaMemcpyHostToDevice), "latent stats");
+    return MKB_OK;
+}
+
+mkb_status mkb_clip_create(const mkb_clip_config* cfg, mkb_clip** out)
+{
+    if (!cfg || !out)
+        return fail(MKB_ERR_INVALID, "clip_create: null argument");
+    auto* c = new (std::nothrow) mkb_clip;
+    if (!c)
+        return fail(MKB_ERR_ALLOC, "clip_create: host allocation");
+    mkb_status s = c->impl.create(*cfg);
+    if (s != MKB_OK) {
+        delete c;
+        return s;
+    }
+    *out = c;
+    return MKB_OK;
+}
+
+void mkb_clip_destroy(mkb_clip* c)
+{
+    if (c) {
+        cudaStreamSynchronize(c->impl.stream);
+        delete c;
+    }
+}
+
+mkb_status mkb_clip_init_random(mkb_clip* c, uint64_t seed, float std)
+{
+    if (!c)
+        return fail(MKB_ERR_INVALID, "clip: null handle");
+    return c->impl.W.init_random(seed, std, c->impl.stream);
+}
+
+int mkb_clip_weight_count(const mkb_clip* c) { return c ? int(c->impl.W.ws.size()) : 0; }
+
+mkb_status mkb_clip_weight_info(const mkb_clip* c, int i, const char** name, long* dims, int* ndim)
+{
+    if (!c)
+        return fail(MKB_ERR_INVALID, "clip: null handle");
+    return c->impl.W.info(i, name, dims, ndim);
+}
+
+mkb_status mkb_clip_weight_read(mkb_clip* c, const char* name, float* host)
+{
+    if (!c || !name)
+        return fail(MKB_ERR_INVALID, "clip: null argument");
+    MKB_TRY_CUDA(cudaStreamSynchronize(c->impl.stream), "sync");
+    return c->impl.W.read(name, host);
+}
+
+mkb_status mkb_clip_weight_write(mkb_clip* c, const char* name, const float* host)
+{
+    if (!c || !name)
+        return fail(MKB_ERR_INVALID, "clip: null argument");
+    MKB_TRY_CUDA(cudaStreamSynchronize(c->impl.stream), "sync");
+    return c->impl.W.write(name, host);
+}
+
+mkb_status mkb_clip_set_probe(mkb_clip* c, mkb_probe_fn fn, void* user)
+{
+    if (!c)
+        return fail(MKB_ERR_INVALID, "clip: null handle");
+    c->impl.probe = fn;
+    c->impl.probe_user = user;
+    return MKB_OK;
+}
+
+mkb_status mkb_clip_encode(mkb_clip* c, const int32_t* ids, int chunks, float* hidden, float* pooled)
+{
+    if (!c)
+        return fail(MKB_ERR_INVALID, "clip: null handle");
+    return c->impl.encode(ids, chunks, hidden, pooled);
+}
+
+mkb_status mkb_sdxl_prompt_embeddings(mkb_clip* l, mkb_clip* g, const int32_t* ids_l, const int32_t* ids_g,
+                                      const float* weights, int chunks, float* context, float* pooled)
+{
+    if (!l || !g || !ids_l || !ids_g || !context || !pooled)
+        return fail(MKB_ERR_INVALID, "prompt_embeddings: null argument");
+    ClipImpl &L = l->impl, &G = g->impl;
+    if (L.cfg.which != 0 || G.cfg.which != 1)
+        return fail(MKB_ERR_INVALID, "prompt_embeddings: need the ViT-L handle (which 0) and the bigG one (which 1)");
+    if (chunks < 1 || chunks > L.cfg.max_chunks || chunks > G.cfg.max_chunks)
+        return fail(MKB_ERR_INVALID, "prompt_embeddings: chunk count out of range");
+    const int EL = L.cfg.width, EG = G.cfg.width, T = kClipTokens;
+    const size_t rows = size_t(chunks) * T;
+    std::vector<float> zl(rows * EL), zg(rows * EG), pg(size_t(chunks) * kClipPooled);
+    MKB_TRY(L.encode(ids_l, chunks, zl.data(), nullptr));
+    MKB_TRY(G.encode(ids_g, chunks, zg.data(), pg.data()));
+    bool weighted = false;
+    for (size_t i = 0; weights && i < rows; ++i)
+        weighted = weighted || weights[i] != 1.0f;
+    std::vector<float> el, eg;
+    if (weighted) {  // a weighted token's states move away from the empty prompt's by its weight (sdxl.cpp:618-631)
+        std::vector<int32_t> e(T, kClipEnd);
+        e[0] = kClipEnd - 1;
+        el.resize(size_t(T) * EL);
+        MKB_TRY(L.encode(e.data(), 1, el.data(), nullptr));
+        std::fill(e.begin() + 2, e.end(), 0);
+        eg.resize(size_t(T) * EG);
+        std::vector<float> unused(kClipPooled);
+        MKB_TRY(G.encode(e.data(), 1, eg.data(), unused.data()));
+    }
+    for (size_t r = 0; r < rows; ++r) {
+        float* row = context + r * (EL + EG);
+        const float w = weights ? weights[r] : 1.0f;
+        const size_t t = r % T;
+        for (int i = 0; i < EL; ++i) {
+            const float z = zl[r * EL + i];
+            row[i] = w != 1.0f ? (z - el[t * EL + i]) * w + el[t * EL + i] : z;
+        }
+        for (int i = 0; i < EG; ++i) {
+            const float z = zg[r * EG + i];
+            row[EL + i] = w != 1.0f ? (z - eg[t * EG + i]) * w + eg[t * EG + i] : z;
+        }
+    }
+    std::copy(pg.begin(), pg.begin() + kClipPooled, pooled);  // the first chunk's pooled state
     return MKB_OK;
 }
 

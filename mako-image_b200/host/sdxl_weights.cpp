@@ -239,6 +239,59 @@ bool vae_sources(const std::string& w, Alts* alts)
     return false;
 }
 
+// The text encoders' weights (Sdxl::load_clip, src/image/sdxl.cpp:154-237): ViT-L in the HF CLIPTextModel names
+// (q, k, v projections stacked into qkv), bigG in the OpenCLIP names (in_proj already stacked).
+bool clip_sources(int which, const std::string& w, Alts* alts)
+{
+    if (w == "tok" || w == "pos") {
+        const bool t = w == "tok";
+        *alts = {{which == 0 ? (t ? "embeddings.token_embedding.weight" : "embeddings.position_embedding.weight")
+                             : (t ? "token_embedding.weight" : "positional_embedding")}};
+        return true;
+    }
+    if (which == 1 && (w == "lnf.w" || w == "lnf.b" || w == "proj")) {
+        *alts = {{w == "proj" ? "text_projection" : w == "lnf.w" ? "ln_final.weight" : "ln_final.bias"}};
+        return true;
+    }
+    unsigned i = 0;
+    int used = 0;
+    if (std::sscanf(w.c_str(), "l%u.%n", &i, &used) != 1 || used <= 0)
+        return false;
+    std::string stem, suf;
+    if (!split_wb(w.substr(size_t(used)), &stem, &suf))
+        return false;
+    const std::string n = std::to_string(i);
+    if (which == 0) {
+        const std::string l = "encoder.layers." + n + ".";
+        if (stem == "qkv") {
+            *alts = {{l + "self_attn.q_proj" + suf, l + "self_attn.k_proj" + suf, l + "self_attn.v_proj" + suf}};
+            return true;
+        }
+        const std::pair<const char*, const char*> m[] = {{"ln1", "layer_norm1"}, {"o", "self_attn.out_proj"},
+                                                         {"ln2", "layer_norm2"}, {"fc1", "mlp.fc1"},
+                                                         {"fc2", "mlp.fc2"}};
+        for (auto& [ours, theirs] : m)
+            if (stem == ours) {
+                *alts = {{l + theirs + suf}};
+                return true;
+            }
+        return false;
+    }
+    const std::string l = "transformer.resblocks." + n + ".";
+    if (stem == "qkv") {
+        *alts = {{l + (suf == ".weight" ? "attn.in_proj_weight" : "attn.in_proj_bias")}};
+        return true;
+    }
+    const std::pair<const char*, const char*> m[] = {{"ln1", "ln_1"}, {"o", "attn.out_proj"}, {"ln2", "ln_2"},
+                                                     {"fc1", "mlp.c_fc"}, {"fc2", "mlp.c_proj"}};
+    for (auto& [ours, theirs] : m)
+        if (stem == ours) {
+            *alts = {{l + theirs + suf}};
+            return true;
+        }
+    return false;
+}
+
 }  // namespace
 
 namespace {
@@ -360,6 +413,26 @@ mkb_status mkb_unet_load_safetensors(mkb_unet* u, const char* const* paths, int 
             unet_sources,
             {"model.diffusion_model.", ""},
             "unet"};
+    return load(m, paths, n_paths, strict, loaded);
+}
+
+mkb_status mkb_clip_load_safetensors(mkb_clip* c, const char* const* paths, int n_paths, int strict, int* loaded)
+{
+    if (!c)
+        return fail(MKB_ERR_INVALID, "clip: null handle");
+    int which = 0;
+    for (int i = 0; i < mkb_clip_weight_count(c); ++i) {  // bigG's table alone has the text projection
+        const char* n = nullptr;
+        if (mkb_clip_weight_info(c, i, &n, nullptr, nullptr) == MKB_OK && std::strcmp(n, "proj") == 0)
+            which = 1;
+    }
+    Model m{[c] { return mkb_clip_weight_count(c); },
+            [c](int i, const char** n, long* d, int* nd) { return mkb_clip_weight_info(c, i, n, d, nd); },
+            [c](const char* n, const float* h) { return mkb_clip_weight_write(c, n, h); },
+            [which](const std::string& w, Alts* a) { return clip_sources(which, w, a); },
+            which == 0 ? std::vector<std::string>{"conditioner.embedders.0.transformer.text_model.", "text_model.", ""}
+                       : std::vector<std::string>{"conditioner.embedders.1.model.", ""},
+            "clip"};
     return load(m, paths, n_paths, strict, loaded);
 }
 

@@ -6,5 +6,5 @@ buffers are passed as raw pointers (for example ``tensor.data_ptr()`` of a torch
 from ._lib import lib, MkbError, check, LIB_PATH, stream_ptr  # noqa: F401
 from . import ops  # noqa: F401
 from .dit import Dit, DitConfig, QWEN1, REF21, nccl_unique_id, sp_rows, NCCL_ID_BYTES, st_read  # noqa: F401
-from .sdxl import Unet, UnetConfig, Vae, VaeConfig, sdxl_sigmas, sdxl_timestep  # noqa: F401
+from .sdxl import Unet, UnetConfig, Vae, VaeConfig, Clip, ClipConfig, prompt_embeddings, sdxl_sigmas, sdxl_timestep  # noqa: F401,E501
 from .sampler import Schedule, sigmas, top_sigma, guided_euler, ErSde, cfg_combine_dev, euler_ancestral_dev  # noqa: F401,E501

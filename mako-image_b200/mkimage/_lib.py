@@ -79,6 +79,17 @@ _SIGS = {
     "mkb_vae_set_probe": (_i, [_vp, _vp, _vp]),
     "mkb_vae_decode_flops": (ctypes.c_double, [_vp, _i, _i]),
     "mkb_vae_set_latent_stats": (_i, [_vp, _vp, _vp, _i]),
+    "mkb_clip_create": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "mkb_clip_destroy": (None, [_vp]),
+    "mkb_clip_init_random": (_i, [_vp, _u64, _f]),
+    "mkb_clip_weight_count": (_i, [_vp]),
+    "mkb_clip_weight_info": (_i, [_vp, _i, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_l), ctypes.POINTER(_i)]),
+    "mkb_clip_weight_read": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_clip_weight_write": (_i, [_vp, ctypes.c_char_p, _vp]),
+    "mkb_clip_load_safetensors": (_i, [_vp, ctypes.POINTER(ctypes.c_char_p), _i, _i, ctypes.POINTER(_i)]),
+    "mkb_clip_set_probe": (_i, [_vp, _vp, _vp]),
+    "mkb_clip_encode": (_i, [_vp, _vp, _i, _vp, _vp]),
+    "mkb_sdxl_prompt_embeddings": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "mkb_to_rgba8": (_i, [_vp, ctypes.c_size_t, _vp]),
     "mkb_png_encode": (_i, [_vp, ctypes.c_uint32, ctypes.c_uint32, _i, _vp, ctypes.c_size_t,
                             ctypes.POINTER(ctypes.c_size_t)]),

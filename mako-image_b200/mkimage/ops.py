@@ -4,7 +4,7 @@ import ctypes
 
 from ._lib import lib, check, stream_ptr
 
-ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
+ACT_NONE, ACT_GELU_TANH, ACT_SILU, ACT_QUICK_GELU, ACT_GELU_ERF = 0, 1, 2, 3, 4
 
 
 def _p(t):

@@ -1,6 +1,7 @@
 """The SDXL UNet and VAE decoder handles (include/mkb_image.h part 3) as Python objects."""
 
 import ctypes
+import dataclasses
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -190,6 +191,65 @@ class Vae(_Weights):
 
     def decode_flops(self, gh, gw):
         return lib.mkb_vae_decode_flops(self.h, gh, gw)
+
+
+@dataclass
+class ClipConfig:
+    """which 0: CLIP ViT-L (768 wide, 12 layers); 1: OpenCLIP bigG (1280, 32 layers, pooled state)."""
+    which: int = 0
+    width: int = 768
+    heads: int = 12
+    layers: int = 12
+    ffn: int = 3072
+    vocab: int = 49408
+    max_chunks: int = 4
+
+    @staticmethod
+    def sdxl(which, **over):
+        c = ClipConfig() if which == 0 else ClipConfig(which=1, width=1280, heads=20, layers=32, ffn=5120)
+        return dataclasses.replace(c, **over)
+
+
+class _CClip(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("which", "width", "heads", "layers", "ffn", "vocab", "max_chunks")]
+
+
+class Clip(_Weights):
+    """One of SDXL's text encoders (mkb_clip_*)."""
+
+    _prefix = "clip"
+
+    def __init__(self, cfg: ClipConfig):
+        self.cfg = cfg
+        c = _CClip(*(getattr(cfg, n) for n, _ in _CClip._fields_))
+        h = ctypes.c_void_p()
+        check(lib.mkb_clip_create(ctypes.byref(c), ctypes.byref(h)))
+        self.h = h
+        self._probe = None
+
+    def encode(self, ids):
+        """ids [chunks][77] -> (hidden [chunks * 77][E], pooled [chunks][1280] for bigG else None)."""
+        ids = np.ascontiguousarray(np.asarray(ids, np.int32).reshape(-1, 77))
+        n = ids.shape[0]
+        hidden = np.empty((n * 77, self.cfg.width), np.float32)
+        pooled = np.empty((n, 1280), np.float32) if self.cfg.which == 1 else None
+        check(lib.mkb_clip_encode(self.h, ids.ctypes.data_as(ctypes.c_void_p), n, _fptr(hidden),
+                                  _fptr(pooled) if pooled is not None else None))
+        return hidden, pooled
+
+
+def prompt_embeddings(clip_l, clip_g, ids_l, ids_g, weights=None):
+    """mkb_sdxl_prompt_embeddings: ([chunks * 77][E_L + E_G] context, [1280] pooled)."""
+    ids_l = np.ascontiguousarray(np.asarray(ids_l, np.int32).reshape(-1, 77))
+    ids_g = np.ascontiguousarray(np.asarray(ids_g, np.int32).reshape(-1, 77))
+    n = ids_l.shape[0]
+    w = None if weights is None else np.ascontiguousarray(np.asarray(weights, np.float32).reshape(n, 77))
+    ctx = np.empty((n * 77, clip_l.cfg.width + clip_g.cfg.width), np.float32)
+    pooled = np.empty(1280, np.float32)
+    check(lib.mkb_sdxl_prompt_embeddings(clip_l.h, clip_g.h, ids_l.ctypes.data_as(ctypes.c_void_p),
+                                         ids_g.ctypes.data_as(ctypes.c_void_p), _fptr(w) if w is not None else None,
+                                         n, _fptr(ctx), _fptr(pooled)))
+    return ctx, pooled
 
 
 def sdxl_sigmas(steps):
