@@ -7,7 +7,9 @@
 * The prompt embeddings of weighted chunks (two chunks, weights 0.7 and 1.3 on some tokens), side by side.
 * The checkpoint names of both encoders (Sdxl::load_clip, sdxl.cpp:154-237) and rejected inputs.
 
-Random weights N(0, 0.02) with the token and position tables at N(0, 1) scale, so the residual stream is O(1)."""
+Random weights N(0, 0.02) with the token and position tables at N(0, 0.5) scale, so the residual stream is O(1).
+The reference's own bar on the encoders' states, the weighted conditioning and the pooled state is rel-RMS < 0.01
+(tests/sdxl_ref_test.cpp:203-218); these hold half of it."""
 
 import os
 import sys
