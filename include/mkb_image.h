@@ -166,6 +166,13 @@ mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const voi
                                    int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,
                                    int kv_shard_rows, int kv_plane_stride, void* stream);
 
+/* Single-head attention at head dim d = 256 or 512: the VAE decoder's mid-block attention over every pixel of the
+ * latent image (Engine::vae_attention, src/image/engine.cpp:748-778, which runs it as a score GEMM, a row softmax and
+ * a P V GEMM; here one flash kernel). q, k and v of n rows sit side by side in one bf16 buffer (rows of ld elements,
+ * at columns q_col, k_col and v_col, multiples of 64); out (bf16, rows ldo apart) = softmax(q k^T / sqrt(d)) v. */
+mkb_status mkb_attention_wide(const void* qkv, long ld, int n, int d, int q_col, int k_col, int v_col, void* out,
+                              long ldo, void* stream);
+
 /* The same over shards that other ranks copy into this GPU's memory while the kernel runs (the sequence-parallel
  * peer exchange; no counterpart in the reference, which runs on one device). Shard own_shard is complete at launch;
  * before reading any other shard g the kernel waits until the 64-bit device flag shard_ready[g] >= *shard_expect

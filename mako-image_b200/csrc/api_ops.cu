@@ -328,6 +328,28 @@ mkb_status mkb_attention(const void* q, int Lq, int Lq_rows, const void* k, cons
                                    out0, ld0, rows0, out1, ld1, rows1, 0, 0, stream);
 }
 
+mkb_status mkb_attention_wide(const void* qkv, long ld, int n, int d, int q_col, int k_col, int v_col, void* out,
+                              long ldo, void* stream)
+{
+    if (!qkv || !out)
+        return fail(MKB_ERR_INVALID, "attention_wide: null buffer");
+    AttnWideArgs a;
+    a.n = n;
+    a.d = d;
+    a.q_col = q_col;
+    a.k_col = k_col;
+    a.v_col = v_col;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.ldo = ldo;
+    a.scale_log2 = 1.4426950408889634f / sqrtf(float(d));
+    a.status = device_status_word();
+    AttnWideOp op;
+    const char* err = nullptr;
+    if (!attn_wide_prepare(op, qkv, ld, a, &err))
+        return fail(MKB_ERR_INVALID, err ? err : "attention_wide: unsupported arguments");
+    return cuda_status(attn_wide_launch(op, static_cast<cudaStream_t>(stream)), "attention_wide launch");
+}
+
 mkb_status mkb_attention_kv_shards(const void* q, int Lq, int Lq_rows, const void* k, const void* v, int Lk,
                                    int Lk_rows, int B, int H, int head_dim, int q_pos0, int mask, int cond_len,
                                    int split, void* out0, long ld0, int rows0, void* out1, long ld1, int rows1,

@@ -60,6 +60,28 @@ struct AttnOp {
     bool ready = false;
 };
 
+// Single-head attention at head dim d = 256 or 512 over n rows whose q, k and v sit side by side in one bf16 buffer
+// (rows of ld elements; q, k, v at columns q_col, k_col, v_col): out[row][0, d) = softmax(q k^T / sqrt(d)) v, bf16,
+// rows ldo apart (the VAE decoder's mid-block attention, Engine::vae_attention, src/image/engine.cpp:748-778).
+struct AttnWideArgs {
+    int n = 0, d = 0;
+    int q_col = 0, k_col = 0, v_col = 0;
+    __nv_bfloat16* out = nullptr;
+    long ldo = 0;
+    float scale_log2 = 0.f;  // softmax scale * log2(e)
+    uint32_t* status = nullptr;
+};
+
+struct AttnWideOp {
+    CUtensorMap tm;
+    AttnWideArgs args;
+    dim3 grid;
+    bool ready = false;
+};
+
+bool attn_wide_prepare(AttnWideOp& op, const void* qkv, long ld, const AttnWideArgs& args, const char** err);
+cudaError_t attn_wide_launch(const AttnWideOp& op, cudaStream_t stream);
+
 // q: [B][H][Lq_rows][d], k/v: [B][H][Lk_rows][d] (bf16, contiguous); Lq_rows >= args.Lq, Lk_rows >= args.Lk.
 bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const void* v, int Lk_rows,
                   const AttnArgs& args, const char** err);

@@ -29,6 +29,15 @@ namespace {
 
 // Whether the VAE's convolutions leave the GroupNorm statistics of their outputs (MKB_GN_FUSED=0: the three-pass
 // GroupNorm everywhere, for comparison; the statistics need the TMA epilogue, so MKB_TMA_EPI=0 turns them off too).
+bool vae_flash_enabled()  // MKB_VAE_FLASH=0: the mid attention as score GEMMs, row softmax and P V GEMMs
+{
+    static const bool on = [] {
+        const char* f = std::getenv("MKB_VAE_FLASH");
+        return !(f && f[0] == '0');
+    }();
+    return on;
+}
+
 bool gn_fused_enabled()
 {
     static const bool on = [] {
@@ -1183,12 +1192,14 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
     __nv_bfloat16* LAT = P.buf<__nv_bfloat16>(size_t(H0) * W0 * 64, &st);
     __nv_bfloat16* PQ = P.buf<__nv_bfloat16>(size_t(H0) * W0 * 64, &st);
     const int n = H0 * W0, ca = ctop;
-    // mid attention: q/k/v rows, V^T, and the score chunk (queries per pass so scores stay near 256 MB)
+    // mid attention: q/k/v rows; one flash kernel at 256 / 512 channels, else V^T and the score chunk (queries per
+    // pass so scores stay near 256 MB) for score GEMMs, a row softmax and P V GEMMs
+    const bool flash = vae_flash_enabled() && (ca == 256 || ca == 512);
     const int qn = std::min(n, std::max(128, int((size_t(64) << 20) / size_t(n)) / 128 * 128));
     __nv_bfloat16* QKV = P.buf<__nv_bfloat16>(size_t(n) * 3 * ca, &st);
-    __nv_bfloat16* VT = P.buf<__nv_bfloat16>(size_t(n) * ca, &st);
-    float* SC = P.buf<float>(size_t(qn) * n, &st);
-    __nv_bfloat16* PR = P.buf<__nv_bfloat16>(size_t(qn) * n, &st);
+    __nv_bfloat16* VT = flash ? nullptr : P.buf<__nv_bfloat16>(size_t(n) * ca, &st);
+    float* SC = flash ? nullptr : P.buf<float>(size_t(qn) * n, &st);
+    __nv_bfloat16* PR = flash ? nullptr : P.buf<__nv_bfloat16>(size_t(qn) * n, &st);
     __nv_bfloat16* AT = P.buf<__nv_bfloat16>(size_t(n) * ca, &st);
     P.gn_ws = P.buf<float>(std::max(gnmost / 4, size_t(32) * 128) + 16, &st);  // also the fused path's segments
     // GroupNorm statistics left by the convolutions (where every channel count of the decoder gives groups of 4, 8
@@ -1293,9 +1304,27 @@ mkb_status VaeImpl::build(int gh, int gw, Plan** out)
             q.out_f32 = 0;
             bd.gemm(Epi::kAdd, T, c, w.M("mid.attn.qkv.w"), c, q);
             const int cc = c;
-            P.add([=](cudaStream_t s) { return transpose_bf16(QKV, 3L * cc, 2 * cc, VT, HW, cc, s); });
             const float sc = 1.0f / std::sqrt(float(c));
-            for (int q0 = 0; q0 < HW && bd.ok(); q0 += qn) {
+            if (flash) {
+                AttnWideArgs wa;
+                wa.n = HW;
+                wa.d = c;
+                wa.q_col = 0;
+                wa.k_col = c;
+                wa.v_col = 2 * c;
+                wa.out = AT;
+                wa.ldo = c;
+                wa.scale_log2 = 1.4426950408889634f * sc;
+                wa.status = status;
+                AttnWideOp aop;
+                const char* aerr = nullptr;
+                if (!attn_wide_prepare(aop, QKV, 3L * c, wa, &aerr))
+                    return fail(MKB_ERR_INVALID, std::string("vae plan: ") + (aerr ? aerr : "mid attention"));
+                P.add([aop](cudaStream_t s) { return attn_wide_launch(aop, s); });
+            } else {
+                P.add([=](cudaStream_t s) { return transpose_bf16(QKV, 3L * cc, 2 * cc, VT, HW, cc, s); });
+            }
+            for (int q0 = 0; q0 < HW && bd.ok() && !flash; q0 += qn) {
                 const int m = std::min(qn, HW - q0);
                 GemmArgs sa;
                 sa.M = m;

@@ -112,6 +112,21 @@ def attention_kv_arriving(q, k, v, out0, out1, split, Lk, kv_shard_rows, kv_plan
                                         _p(shard_ready), _p(shard_expect), stream_ptr()))
 
 
+def attention_wide(qkv, d, n=None, q_col=0, k_col=None, v_col=None, out=None):
+    """Single-head attention at head dim 256 / 512 over rows of qkv [n][ld] holding q, k, v side by side (see
+    mkb_attention_wide); returns out [n][d] bf16."""
+    import torch
+
+    n = n or qkv.shape[0]
+    k_col = d if k_col is None else k_col
+    v_col = 2 * d if v_col is None else v_col
+    if out is None:
+        out = torch.empty(n, d, device=qkv.device, dtype=torch.bfloat16)
+    check(lib.mkb_attention_wide(_p(qkv), qkv.stride(0), n, d, q_col, k_col, v_col, _p(out), out.stride(0),
+                                 stream_ptr()))
+    return out
+
+
 def proj_add(x, w, bias=None, addvec=None, rows_per_sample=None, resid=None, out=None, out_f32=True):
     """y = x @ w.T + bias + addvec[row // rows_per_sample] + resid (fp32 or bf16 out; resid may be out)."""
     import torch

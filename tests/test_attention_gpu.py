@@ -190,3 +190,22 @@ def test_attention_kv_arriving_flag_never_set(cuda):
     mkimage.ops.attention_kv_shards(q, kv[0, 0], kv[0, 1], None, want, split=0, Lk=L, kv_shard_rows=Lg,
                                     kv_plane_stride=2 * B * H)
     assert (out.float() - want.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("d,n", [(512, 300), (512, 1024), (256, 77), (256, 640)])
+def test_attention_wide_single_head(cuda, d, n):
+    """mkb_attention_wide (the VAE mid block's single-head attention at 256 / 512 channels) against the oracle: q, k
+    and v side by side in rows of 3d, ragged n (keys past the last full tile masked), both output halves."""
+    import torch
+    import mkimage
+
+    qkv = _heads((n, 3 * d), 41 + d, cuda)
+    out = mkimage.ops.attention_wide(qkv, d)
+    assert mkimage.ops.check_kernels() == 0
+    x = qkv.float().cpu().numpy()
+    q, k, v = x[:, :d], x[:, d:2 * d], x[:, 2 * d:]
+    ref = O.attention(q[None], k[None], v[None], None)[0]
+    got = out.float().cpu().numpy()
+    err = np.abs(got - ref).max()
+    cos = (got * ref).sum() / np.sqrt((got ** 2).sum() * (ref ** 2).sum())
+    assert err < 2e-2 and cos > 0.999, (err, cos)
