@@ -63,32 +63,6 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-// 2^x for two lanes on the FMA pipe with packed f32x2 arithmetic: x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f
-// by the degree-3 polynomial of least maximum relative error on that interval (a minimax fit by the Remez exchange
-// algorithm, tests/ex2_fit.py; 7.5e-5, below bf16's 3.9e-3; tests/test_ex2_poly_cpu.py checks the bound), 2^n added
-// to the exponent bits. Arguments below -126 flush to 0 like ex2.approx.ftz.
-__device__ __forceinline__ float2 ex2_poly2(float2 x)
-{
-    x.x = fmaxf(x.x, -126.0f);
-    x.y = fmaxf(x.y, -126.0f);
-    const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
-    const float2 n = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
-    const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
-    float2 p = ffma2(make_float2(0.055171459913253784f, 0.055171459913253784f), f,
-                     make_float2(0.2426108568906784f, 0.2426108568906784f));
-    p = ffma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-    p = ffma2(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
-    return make_float2(__int_as_float(__float_as_int(p.x) + ((__float_as_int(t.x) - 0x4B400000) << 23)),
-                       __int_as_float(__float_as_int(p.y) + ((__float_as_int(t.y) - 0x4B400000) << 23)));
-}
-
-__device__ __forceinline__ float fmax3(float a, float b, float c)
-{
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
 {
     uint32_t a[16], b[16];

@@ -31,13 +31,16 @@ namespace mkb {
 namespace {
 
 constexpr int kWThreads = 256;
-constexpr int kWStages = 5;
 constexpr int kWTile = 128;                  // query rows per CTA, keys per key tile
 constexpr int kWPanel = kWTile * 64 * 2;     // 128 rows x 64 bf16 with the 128-byte swizzle: 16 KB
 constexpr uint32_t kWTmemCols = 512;
 constexpr float kWRescale = 8.0f;            // log2 units
+// K / V panels in flight: as many as fit beside the resident Q tile in 227 KB.
 template <int D>
-constexpr int kWSmem = 1024 + (D / 64) * kWPanel + kWStages * kWPanel + 256;
+constexpr int kWStages = D == 512 ? 6 : 8;
+template <int D>
+constexpr int kWSmem = 1024 + (D / 64) * kWPanel + kWStages<D> * kWPanel + 256;
+static_assert(kWSmem<512> <= 227 * 1024 && kWSmem<256> <= 227 * 1024, "shared memory over the per-CTA limit");
 
 __device__ __forceinline__ float wex2(float x)
 {
@@ -52,15 +55,16 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
     constexpr int NQ = D / 64;   // Q / K panels: the contraction in 64-wide steps
     constexpr int NV = D / 128;  // V panels of this CTA's output half
     constexpr int DH = D / 2;
+    constexpr int kWS = kWStages<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* ring = smem + NQ * kWPanel;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kWStages * kWPanel);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kWS * kWPanel);
     uint64_t* q_full = bars;
-    uint64_t* full = bars + 1;                // [kWStages]
-    uint64_t* empty = full + kWStages;        // [kWStages]
-    uint64_t* s_full = empty + kWStages;      // [2] by key-tile parity
+    uint64_t* full = bars + 1;            // [kWS]
+    uint64_t* empty = full + kWS;         // [kWS]
+    uint64_t* s_full = empty + kWS;       // [2] by key-tile parity
     uint64_t* p_full = s_full + 2;            // [2]
     uint64_t* o_done = p_full + 2;            // [2]
     uint64_t* drain = o_done + 2;
@@ -73,7 +77,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < kWStages; ++i) {
+        for (int i = 0; i < kWS; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
             for (int c = 0; c < NQ; ++c)
                 tma_load_2d(sQ + c * kWPanel, &tm, q_full, a.q_col + 64 * c, q0);
             auto put = [&](int col, int row) {
-                const uint32_t s = it % kWStages, ph = (it / kWStages) & 1;
+                const uint32_t s = it % kWS, ph = (it / kWS) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, a.status, kErrAttnWait, abort_flag))
                     return false;
                 mbar_arrive_expect_tx(&full[s], kWPanel);
@@ -133,8 +137,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
             }
             if (!ok) {  // let the loads already issued land before the CTA can exit
                 mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
-                for (uint32_t j = it > uint32_t(kWStages) ? it - kWStages : 0; j < it; ++j)
-                    mbar_wait(&full[j % kWStages], (j / kWStages) & 1, a.status, kErrWaitDrain, nullptr);
+                for (uint32_t j = it > uint32_t(kWS) ? it - kWS : 0; j < it; ++j)
+                    mbar_wait(&full[j % kWS], (j / kWS) & 1, a.status, kErrWaitDrain, nullptr);
             }
         }
     } else if (warp == 1) {
@@ -145,7 +149,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
             uint32_t it = 0;
             bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
             auto take = [&](uint32_t& addr) {
-                const uint32_t s = it % kWStages, ph = (it / kWStages) & 1;
+                const uint32_t s = it % kWS, ph = (it / kWS) & 1;
                 if (!mbar_wait(&full[s], ph, a.status, kErrAttnWait, abort_flag))
                     return false;
                 tc_fence_after();
@@ -153,7 +157,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
                 return true;
             };
             auto give = [&] {  // the stage is free once the MMAs issued on it have read it
-                mma_commit(&empty[it % kWStages]);
+                mma_commit(&empty[it % kWS]);
                 ++it;
             };
             auto issue_s = [&](int j) {
@@ -229,10 +233,17 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
                     if (i >= valid)
                         s[i] = __float_as_uint(-INFINITY);
             }
-            float mx = __uint_as_float(s[0]);
+            // Row max as 8 independent chains of 3-input max.
+            float mc[8];
 #pragma unroll
-            for (int i = 1; i < 128; ++i)
-                mx = fmaxf(mx, __uint_as_float(s[i]));
+            for (int u = 0; u < 8; ++u)
+                mc[u] = fmaxf(__uint_as_float(s[2 * u]), __uint_as_float(s[2 * u + 1]));
+#pragma unroll
+            for (int i = 16; i < 128; i += 16)
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    mc[u] = fmax3(mc[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+            float mx = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
             mx *= sc;
             const bool need = mx > m_used + kWRescale;
             if (__any_sync(0xffffffffu, need)) {
@@ -265,24 +276,34 @@ __global__ void __launch_bounds__(kWThreads, 1) k_attn_wide(const __grid_constan
                 }
                 m_used = m_new;
             }
-            float ls = 0.0f;
+            // x = s * scale - m two scores per packed FMA; every eighth pair's 2^x on the FMA pipe (a polynomial) to
+            // offload the SFU; the row sum in 4 packed accumulators.
+            const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m_used, -m_used);
+            float2 ls[4] = {};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t p[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int k = c * 32 + 2 * i;
-                    const float e0 = wex2(fmaf(__uint_as_float(s[k]), sc, -m_used));
-                    const float e1 = wex2(fmaf(__uint_as_float(s[k + 1]), sc, -m_used));
-                    ls += e0 + e1;
-                    p[i] = pack_bf16x2(e0, e1);
+                    const float2 x = ffma2(make_float2(__uint_as_float(s[k]), __uint_as_float(s[k + 1])), sc2, nm2);
+                    float2 e;
+                    if (i % 8 == 7) {
+                        e = ex2_poly2(x);
+                    } else {
+                        e.x = wex2(x.x);
+                        e.y = wex2(x.y);
+                    }
+                    ls[i & 3] = fadd2(ls[i & 3], e);
+                    p[i] = pack_bf16x2(e.x, e.y);
                 }
                 tmem_st16(t_lane + col_s + c * 16, p);
             }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[j & 1]);
-            l += ls;
+            const float2 l01 = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
+            l += l01.x + l01.y;
         }
         const int jl = nkv - 1;
         if (ok && nkv > 0 && mbar_wait(&o_done[jl & 1], (jl >> 1) & 1, a.status, kErrAttnWait, abort_flag)) {
