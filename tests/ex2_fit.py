@@ -1,4 +1,4 @@
-"""The fit behind the attention kernel's FMA-pipe 2^x (ex2_poly2 in mako-image_b200/csrc/attention.cu).
+"""The fit behind the attention kernel's FMA-pipe 2^x (ex2_poly2 in mako-image_b200/csrc/sm100.cuh).
 
 2^x = 2^n * 2^f with n = round(x) and f in [-1/2, 1/2]; 2^f is a degree-3 polynomial whose coefficients minimise
 the maximum RELATIVE error on that interval (a minimax fit, found with the Remez exchange algorithm: alternate

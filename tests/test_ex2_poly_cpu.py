@@ -1,4 +1,4 @@
-"""The attention kernel's FMA-pipe 2^x (ex2_poly2, mako-image_b200/csrc/attention.cu): its constants are the
+"""The attention kernel's FMA-pipe 2^x (ex2_poly2, mako-image_b200/csrc/sm100.cuh): its constants are the
 minimax-relative-error fit of tests/ex2_fit.py, and evaluated the kernel's way in fp32 they stay within the stated
 7.5e-5 relative error (below bf16's 3.9e-3 rounding of P) over the exponents the softmax produces: x = s - m with
 m the running row maximum, so x <= 8 (the lazy-rescaling threshold) and anything below -126 flushes to zero."""
@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _coeffs():
-    with open(os.path.join(ROOT, "mako-image_b200", "csrc", "attention.cu")) as f:
+    with open(os.path.join(ROOT, "mako-image_b200", "csrc", "sm100.cuh")) as f:
         return kernel_coefficients(f.read())
 
 
