@@ -156,9 +156,9 @@ struct DitImpl {
     float* vel_x = nullptr;           // [world][B][Lg][64]: velocity exchange
     float* vel_full = nullptr;        // [Bmax][Nmax][64]: all image rows' velocities after the exchange
     // Peer-memory exchange of the K/V shards (replaces the per-block all-gather): the QKV epilogue writes this rank's
-    // shard into its slot of this GPU's exchange region; a copy stream pushes the slot into every peer's region, peer
-    // r-1 first, then r-2 and so on (the order in which the peers' attention reaches shard r, each starting at its
-    // own), raising this rank's ready flag there after each copy; the attention waits on the flags. Blocks alternate
+    // shard into its slot of this GPU's exchange region; one copy stream per peer pushes the slot into that peer's
+    // region (the copies run side by side on the copy engines: one at a time would move ~1/7 of the link bandwidth at
+    // eight ranks) and then raises this rank's ready flag there; the attention waits on the flags. Blocks alternate
     // between two K/V buffers, so no push lands in a buffer a peer still reads: this rank pushes block i + 2 after
     // its attention of block i + 1, which waited for the peer's block-(i + 1) shard, which the peer pushes only after
     // its own attention of block i. The copies run on copy engines, not SMs, so they overlap the attention.
@@ -167,8 +167,9 @@ struct DitImpl {
     size_t sp_kv_bytes = 0;                // one K/V buffer: [world][2][Bmax][H][sp_lg_max][128] bf16
     std::vector<uint8_t*> sp_peer;         // every rank's region as mapped in this process (own region at sp_rank)
     unsigned long long* sp_seq = nullptr;  // [0] steps run, [1 + i] the ready value of block i in the current step
-    cudaStream_t sp_side = nullptr;        // the pushes
-    cudaEvent_t sp_ev[3] = {};             // fork; pushes of even / odd blocks done
+    std::vector<cudaStream_t> sp_side;     // the pushes, one stream per peer
+    cudaEvent_t sp_fork = nullptr;
+    std::vector<cudaEvent_t> sp_done[2];   // per block parity, per copy stream: the pushes done
     __nv_bfloat16* kv_buf(int parity) const
     {
         return reinterpret_cast<__nv_bfloat16*>(sp_region + kSpFlagBytes + parity * sp_kv_bytes);
@@ -303,20 +304,26 @@ mkb_status DitImpl::set_sp(const void* id, int rank, int world)
 
 void DitImpl::sp_release_peer()
 {
-    if (sp_side)
-        cudaStreamSynchronize(sp_side);
+    for (cudaStream_t x : sp_side)
+        if (x)
+            cudaStreamSynchronize(x);
     for (int g = 0; g < int(sp_peer.size()); ++g)
         if (sp_peer[g] && g != sp_rank)
             cudaIpcCloseMemHandle(sp_peer[g]);
     sp_peer.clear();
-    for (cudaEvent_t& e : sp_ev) {
-        if (e)
-            cudaEventDestroy(e);
-        e = nullptr;
+    for (auto& v : sp_done) {
+        for (cudaEvent_t e : v)
+            if (e)
+                cudaEventDestroy(e);
+        v.clear();
     }
-    if (sp_side)
-        cudaStreamDestroy(sp_side);
-    sp_side = nullptr;
+    if (sp_fork)
+        cudaEventDestroy(sp_fork);
+    sp_fork = nullptr;
+    for (cudaStream_t x : sp_side)
+        if (x)
+            cudaStreamDestroy(x);
+    sp_side.clear();
     if (sp_region)
         cudaFree(sp_region);
     if (sp_seq)
@@ -366,9 +373,15 @@ mkb_status DitImpl::sp_set_peer(bool on)
               step(cudaMalloc(&sp_seq, (1 + size_t(NB)) * 8), "allocating the block counters") &&
               step(cudaMemsetAsync(sp_seq, 0, (1 + size_t(NB)) * 8, stream), "clearing them") &&
               step(cudaIpcGetMemHandle(&mine.h, sp_region), "cudaIpcGetMemHandle") &&
-              step(cudaStreamCreateWithFlags(&sp_side, cudaStreamNonBlocking), "copy stream");
-    for (cudaEvent_t& e : sp_ev)
-        ok = ok && step(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "events");
+              step(cudaEventCreateWithFlags(&sp_fork, cudaEventDisableTiming), "events");
+    sp_side.assign(sp_world - 1, nullptr);
+    for (auto& v : sp_done)
+        v.assign(sp_world - 1, nullptr);
+    for (int k = 0; k < sp_world - 1; ++k) {
+        ok = ok && step(cudaStreamCreateWithFlags(&sp_side[k], cudaStreamNonBlocking), "copy streams");
+        for (auto& v : sp_done)
+            ok = ok && step(cudaEventCreateWithFlags(&v[k], cudaEventDisableTiming), "events");
+    }
     mine.ok = ok;
     std::vector<Entry> all(sp_world);
     auto gather = [&](const Entry& e) -> bool {
@@ -421,17 +434,18 @@ mkb_status DitImpl::sp_push(int B, int Lg, int block, cudaStream_t s)
 {
     const size_t shard = size_t(2) * B * H * Lg * kHeadDim * 2;
     const size_t off = kSpFlagBytes + size_t(block & 1) * sp_kv_bytes + size_t(sp_rank) * shard;
-    MKB_TRY_CUDA(cudaEventRecord(sp_ev[0], s), "push fork");
-    MKB_TRY_CUDA(cudaStreamWaitEvent(sp_side, sp_ev[0], 0), "push fork");
+    MKB_TRY_CUDA(cudaEventRecord(sp_fork, s), "push fork");
     for (int k = 1; k < sp_world; ++k) {
         const int q = (sp_rank - k + sp_world) % sp_world;
-        MKB_TRY_CUDA(cudaMemcpyAsync(sp_peer[q] + off, sp_region + off, shard, cudaMemcpyDeviceToDevice, sp_side),
+        cudaStream_t x = sp_side[k - 1];
+        MKB_TRY_CUDA(cudaStreamWaitEvent(x, sp_fork, 0), "push fork");
+        MKB_TRY_CUDA(cudaMemcpyAsync(sp_peer[q] + off, sp_region + off, shard, cudaMemcpyDeviceToDevice, x),
                      "K/V push");
         MKB_TRY_CUDA(cudaMemcpyAsync(sp_peer[q] + size_t(sp_rank) * 8, sp_seq + 1 + block, 8,
-                                     cudaMemcpyDeviceToDevice, sp_side),
+                                     cudaMemcpyDeviceToDevice, x),
                      "ready flag");
+        MKB_TRY_CUDA(cudaEventRecord(sp_done[block & 1][k - 1], x), "push done");
     }
-    MKB_TRY_CUDA(cudaEventRecord(sp_ev[1 + (block & 1)], sp_side), "push done");
     return MKB_OK;
 }
 
@@ -1119,7 +1133,8 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
             };
             MKB_K(ln(1, 0), "ln_modulate 1");
             if (sp_p2p && i >= 2)  // block i - 2's pushes read the buffer this QKV writes
-                MKB_K(cudaStreamWaitEvent(s, sp_ev[1 + (i & 1)], 0), "push join");
+                for (cudaEvent_t e : sp_done[i & 1])
+                    MKB_K(cudaStreamWaitEvent(s, e, 0), "push join");
             MKB_K(gemm_launch(o[0], s), "qkv");
             if (sp_p2p) {
                 MKB_TRY(sp_push(B, rw.shard, i, s));
@@ -1183,7 +1198,8 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
 
     if (sp_p2p)  // the last two blocks' pushes
         for (int p = 0; p < 2 && p < NB; ++p)
-            MKB_K(cudaStreamWaitEvent(s, sp_ev[1 + p], 0), "push join");
+            for (cudaEvent_t e : sp_done[p])
+                MKB_K(cudaStreamWaitEvent(s, e, 0), "push join");
 
     // norm_out + proj_out (qwen_image.cpp:285-288).
     LnModArgs la{};
