@@ -679,6 +679,29 @@ def hot_kernels(dev, cfg, names=None):
     return out
 
 
+def vae_kernel(dev, name):
+    """The VAE decoder's hot kernels at config 4's shapes (1024^2 output, 128^2 latent), as (launch, FLOPs):
+    vae_attention, the mid block's single-head attention over the 128^2 latent pixels at 512 channels (q | k | v rows
+    side by side, as the VAE's QKV projection writes them); vae_conv128, a 3x3 convolution 128 -> 128 at 1024^2 with
+    bias and residual (the last level's conv2)."""
+    import torch
+    import mkimage
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    if name == "vae_attention":
+        n, d = 128 * 128, 512
+        qkv = torch.randn(n, 3 * d, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(n, d, device=dev, dtype=torch.bfloat16)
+        return (lambda: mkimage.ops.attention_wide(qkv, d, out=out)), 4.0 * n * n * d
+    hw, c = 1024, 128
+    x = torch.randn(1, hw, hw, c, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(c, 9 * c, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.zeros(c, device=dev)
+    res = torch.randn(1, hw, hw, c, device=dev, generator=g)
+    out = torch.empty(1, hw, hw, c, device=dev)
+    return (lambda: mkimage.ops.conv2d(x, w, bias=b, resid=res, out=out)), 2.0 * hw * hw * c * 9 * c
+
+
 def time_kernel(fn, stream, reps=20, warmup=3):
     """Mean milliseconds per launch over `reps` back-to-back launches, CUDA events on the launching stream."""
     import torch
@@ -705,7 +728,10 @@ def run_kernel(args, cfg):
     name = {"gemm": "ffn_up"}.get(args.kernel, args.kernel)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
-    fn, work = hot_kernels(dev, cfg, [name])[name]
+    if name.startswith("vae_"):
+        fn, work = vae_kernel(dev, name)
+    else:
+        fn, work = hot_kernels(dev, cfg, [name])[name]
     ms = time_kernel(fn, stream, reps=3)
     mkimage.ops.check_kernels()
     print(json.dumps({"kernel": name, "config": cfg["workload"], "ms": ms, "achieved": work / (ms * 1e-3) / 1e12,
@@ -727,7 +753,8 @@ def main():
     ap.add_argument("--sp-exchange", choices=["peer", "nccl"], default="peer",
                     help="--sp: K/V shards pushed into the peers' memory by copy engines during the attention "
                          "(peer) or all-gathered by NCCL before it (nccl)")
-    ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down", "vae_attention",
+                                         "vae_conv128"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
