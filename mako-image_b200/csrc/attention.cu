@@ -21,6 +21,7 @@
 
 #include <cudaTypedefs.h>
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 namespace mkb {
@@ -75,11 +76,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
     tmem_st16(taddr + 16, b);
 }
 
-template <int HD>
+// PAIR (head dim 128, MKB_ATTN_PAIR=1): CTAs run as clusters of two over the same (sample, head), each with its own two
+// query tiles, and the leader issues every MMA for both as 256-row cta_group::2 MMAs: each CTA loads half of every key
+// tile (64 keys, by rows) and half of every V tile (64 of the 128 columns), so per SM the K and V tiles cross shared
+// memory at half the bytes. The follower's softmax signals P on the leader's barrier; the leader's commits reach both
+// CTAs. Measured at the config-2 shape it is slower than one CTA per tile pair (832 against 1093 TFLOP/s; 920 with a
+// quarter of the exponentials on the FMA pipe): the two CTAs' softmax phases now gate every MMA of both, and the
+// exponentials, not shared memory, set the pace. It stays as an option, tested for parity.
+template <int HD, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     k_attn(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
            const __grid_constant__ CUtensorMap tv, const AttnArgs a)
 {
+    static_assert(!PAIR || HD == 128, "CTA pairs split V by 64-column panels: head dim 128 only");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int TB = kTileBytes<HD>;
@@ -102,12 +111,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int q0 = blockIdx.x * 2 * kTile, h = blockIdx.y, b = blockIdx.z;
     const int bh = b * a.H + h;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+    const bool leader = rank == 0;
 
-    // Keys this CTA needs: when its query rows are all condition rows (causal among themselves), keys up to the
-    // last row's position.
+    // Keys this CTA (pair) needs: when its query rows are all condition rows (causal among themselves), keys up to
+    // the last row's position.
     int n_keys = a.Lk;
     if (a.mask == kMaskCondCausal) {
-        const int last_pos = a.q_pos0 + min(q0 + 2 * kTile, a.Lq) - 1;
+        const int q_end = PAIR ? ((blockIdx.x | 1) + 1) * 2 * kTile : q0 + 2 * kTile;
+        const int last_pos = a.q_pos0 + min(q_end, a.Lq) - 1;
         if (last_pos < a.cond_len)
             n_keys = min(a.Lk, last_pos + 1);
     }
@@ -124,8 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[2 * i], 128);
-            mbar_init(&p_full[2 * i + 1], 128);
+            mbar_init(&p_full[2 * i], PAIR ? 256 : 128);  // (pairs: the leader's, both CTAs' softmax threads)
+            mbar_init(&p_full[2 * i + 1], PAIR ? 256 : 128);
             mbar_init(&o_done[i], 1);
         }
         mbar_init(drain, 1);
@@ -139,11 +151,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     grid_dep_wait();  // before TMEM allocation and the first global access
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
     tc_fence_after();
     grid_dep_launch();
     const uint32_t tmem = *tmem_slot;
@@ -156,10 +175,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int arrived = a.own_shard;  // the shard whose arrival was last confirmed
             const unsigned long long want = a.own_shard >= 0 ? *a.shard_expect : 0;
-            mbar_arrive_expect_tx(q_full, 2 * TB);
-            for (int t = 0; t < 2; ++t)
-                for (int pn = 0; pn < HD / 64; ++pn)
-                    tma_load_3d(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile, bh);
+            if constexpr (PAIR) {
+                if (leader)
+                    mbar_arrive_expect_tx(q_full, 4 * TB);  // both CTAs' two tiles
+                for (int t = 0; t < 2; ++t)
+                    for (int pn = 0; pn < HD / 64; ++pn)
+                        tma_load_3d_pair(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile,
+                                         bh);
+            } else {
+                mbar_arrive_expect_tx(q_full, 2 * TB);
+                for (int t = 0; t < 2; ++t)
+                    for (int pn = 0; pn < HD / 64; ++pn)
+                        tma_load_3d(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile, bh);
+            }
             for (int j = 0; j < nkv && ok; ++j) {
                 const int st = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
@@ -181,20 +209,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                         arrived = g;
                     }
                 }
-                mbar_arrive_expect_tx(&k_full[st], TB);
-                for (int pn = 0; pn < HD / 64; ++pn)
-                    tma_load_3d(sK + st * TB + pn * kPanel, &tk, &k_full[st], pn * 64, krow, kplane);
+                if constexpr (PAIR) {  // this CTA's 64 keys of the tile; the leader's barrier counts both halves
+                    if (leader)
+                        mbar_arrive_expect_tx(&k_full[st], TB);
+                    for (int pn = 0; pn < HD / 64; ++pn)
+                        tma_load_3d_pair(sK + st * TB + pn * (kPanel / 2), &tk, &k_full[st], pn * 64,
+                                         krow + 64 * int(rank), kplane);
+                } else {
+                    mbar_arrive_expect_tx(&k_full[st], TB);
+                    for (int pn = 0; pn < HD / 64; ++pn)
+                        tma_load_3d(sK + st * TB + pn * kPanel, &tk, &k_full[st], pn * 64, krow, kplane);
+                }
                 ++issued_k;
                 if (!mbar_wait(&v_empty[st], ph ^ 1, a.status, kErrAttnWait, abort_flag)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&v_full[st], TB);
-                for (int pn = 0; pn < HD / 64; ++pn)
-                    tma_load_3d(sV + st * TB + pn * kPanel, &tv, &v_full[st], pn * 64, krow, kplane);
+                if constexpr (PAIR) {  // this CTA's 64 columns of V
+                    if (leader)
+                        mbar_arrive_expect_tx(&v_full[st], TB);
+                    tma_load_3d_pair(sV + st * TB, &tv, &v_full[st], 64 * int(rank), krow, kplane);
+                } else {
+                    mbar_arrive_expect_tx(&v_full[st], TB);
+                    for (int pn = 0; pn < HD / 64; ++pn)
+                        tma_load_3d(sV + st * TB + pn * kPanel, &tv, &v_full[st], pn * 64, krow, kplane);
+                }
                 ++issued_v;
             }
-            if (!ok) {  // let the loads already issued land before the CTA can exit
+            // Let the loads already issued land before the CTA can exit (a pair's loads complete on the leader's
+            // barriers, which only the leader can wait on: the cluster barrier at the end keeps both CTAs alive).
+            if (!ok && !PAIR) {
                 mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
                 for (int j = issued_k > 2 ? issued_k - 2 : 0; j < issued_k; ++j)
                     mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status, kErrWaitDrain, nullptr);
@@ -203,9 +247,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, 0, 0);
-            constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, 0, 1);  // V is MN-major (head dim contiguous)
+        if (lane == 0 && leader) {
+            constexpr int kM = PAIR ? 256 : 128;  // a pair's MMAs cover both CTAs' 128 rows
+            constexpr uint32_t idesc_s = idesc_bf16_f32(kM, 128, 0, 0);
+            constexpr uint32_t idesc_o = idesc_bf16_f32(kM, HD, 0, 1);  // V is MN-major (head dim contiguous)
+            const auto commit = [](uint64_t* bar) {
+                if constexpr (PAIR)
+                    mma_commit_pair(bar);
+                else
+                    mma_commit(bar);
+            };
             const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
             // Issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1). Each tile's next S follows its own
             // P V directly, so tile A's softmax overlaps tile B's two MMAs and the other way round. S_t(j+1)
@@ -216,10 +267,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k) {
                     const uint32_t off = (k >> 2) * kPanel + (k & 3) * 32;
-                    mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
-                                desc_kmajor_sw128(k_addr + st * TB + off), idesc_s, k > 0);
+                    if constexpr (PAIR)  // each CTA's K half: 64-row panels
+                        mma_bf16_ss_pair(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
+                                         desc_kmajor_sw128(k_addr + st * TB + (k >> 2) * (kPanel / 2) + (k & 3) * 32),
+                                         idesc_s, k > 0);
+                    else
+                        mma_bf16_ss(tmem + t * 128, desc_kmajor_sw128(q_addr + t * TB + off),
+                                    desc_kmajor_sw128(k_addr + st * TB + off), idesc_s, k > 0);
                 }
-                mma_commit(&s_full[t]);
+                commit(&s_full[t]);
             };
             bool ok = mbar_wait(q_full, 0, a.status, kErrAttnWait, abort_flag);
             if (ok && nkv > 0) {
@@ -228,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     issue_s(0, 0);
                     issue_s(1, 0);
-                    mma_commit(&k_empty[0]);
+                    commit(&k_empty[0]);
                 }
             }
             for (int j = 0; j < nkv && ok; ++j) {
@@ -247,24 +303,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_after();
                         // 16 keys per step: P columns 8k.., V rows 16k.. (two 8-row atoms).
 #pragma unroll
-                        for (int k = kSplitP<HD> ? 4 * half : 0; k < 4 * half + 4; ++k)
-                            mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
-                                        desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
-                                        (j > 0) || (k > 0));
+                        for (int k = kSplitP<HD> ? 4 * half : 0; k < 4 * half + 4; ++k) {
+                            if constexpr (PAIR)  // each CTA's 64 columns of V: one panel
+                                mma_bf16_ts_pair(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
+                                                 desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024),
+                                                 idesc_o, (j > 0) || (k > 0));
+                            else
+                                mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + 8 * k,
+                                            desc_mnmajor_sw128(v_addr + st * TB + k * 2048, kPanel, 1024), idesc_o,
+                                            (j > 0) || (k > 0));
+                        }
                     }
                     if (!ok)
                         break;
-                    mma_commit(&o_done[t]);
+                    commit(&o_done[t]);
                     if (next)
                         issue_s(t, st1);
                 }
                 if (!ok)
                     break;
-                mma_commit(&v_empty[st]);
+                commit(&v_empty[st]);
                 if (next)
-                    mma_commit(&k_empty[st1]);
+                    commit(&k_empty[st1]);
             }
-            mma_commit(drain);  // arrives once every MMA issued above has completed
+            commit(drain);  // arrives once every MMA issued above has completed
             mbar_wait(drain, 0, a.status, kErrWaitDrain, nullptr);
         }
     } else if (warp >= 4) {
@@ -356,7 +418,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (c == 3 || (kSplitP<HD> && c == 1)) {  // keys up to 64 (c + 1) / 2 published
                     tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(&p_full[2 * t + c / 2]);
+                    if (PAIR && !leader)  // the leader's barrier counts both CTAs' rows
+                        mbar_arrive_cluster(map_to_cta(smem_u32(&p_full[2 * t + c / 2]), 0));
+                    else
+                        mbar_arrive(&p_full[2 * t + c / 2]);
                 }
             }
             const float2 l01 = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
@@ -392,10 +457,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync_all();  // the leader's MMAs read this CTA's shared memory and tensor memory until here
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem, kTmemCols);
+        else
+            tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+bool attn_pairs_enabled()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("MKB_ATTN_PAIR");
+        return v && v[0] == '1';
+    }();
+    return on;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
@@ -413,9 +492,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-// Head-major [BH][rows][128] bf16 as a 3-D map, box 64 x 128 x 1 with the 128-byte swizzle; rows past `rows` of a
-// head read as zeros.
-bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, int hd, const char** err)
+// Head-major [BH][rows][128] bf16 as a 3-D map, box 64 x box_rows x 1 with the 128-byte swizzle; rows past `rows` of
+// a head read as zeros.
+bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, int hd, const char** err, int box_rows = 128)
 {
     auto fn = encode_fn();
     if (!fn) {
@@ -428,7 +507,7 @@ bool make_heads_map(CUtensorMap* m, const void* p, int rows, int bh, int hd, con
     }
     cuuint64_t dims[3] = {cuuint64_t(hd), cuuint64_t(rows), cuuint64_t(bh)};
     cuuint64_t strides[2] = {cuuint64_t(hd) * 2, cuuint64_t(rows) * hd * 2};
-    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t box[3] = {64, cuuint32_t(box_rows), 1};
     cuuint32_t es[3] = {1, 1, 1};
     if (fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(p), dims, strides, box, es,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -486,11 +565,15 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         *err = "attention: arriving shards need K/V shards, no mask, 8-byte aligned flags and own_shard inside Lk";
         return false;
     }
-    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) || !make_heads_map(&op.tk, k, kv_rows, kv_planes, hd, err) ||
+    // CTA pairs for head dim 128 (MKB_ATTN_PAIR=0: one CTA per pair of query tiles throughout).
+    op.pair = hd == 128 && attn_pairs_enabled();
+    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) ||
+        !make_heads_map(&op.tk, k, kv_rows, kv_planes, hd, err, op.pair ? 64 : 128) ||
         !make_heads_map(&op.tv, v, kv_rows, kv_planes, hd, err))
         return false;
     op.args = args;
-    op.grid = dim3((args.Lq + 2 * kTile - 1) / (2 * kTile), args.H, args.B);
+    const int blocks = (args.Lq + 2 * kTile - 1) / (2 * kTile);
+    op.grid = dim3(op.pair ? (blocks + 1) / 2 * 2 : blocks, args.H, args.B);
     op.ready = true;
     return true;
 }
@@ -500,12 +583,12 @@ namespace {
 // Set-up of a kernel instance: a one-time check that the compiled launch register count holds the warpgroups'
 // register split (otherwise the softmax groups' increase could never be granted), and its shared memory size on
 // each device it runs on.
-template <int HD>
+template <int HD, bool PAIR>
 cudaError_t attn_setup()
 {
     static const cudaError_t regs = [] {
         cudaFuncAttributes fa{};
-        cudaError_t e = cudaFuncGetAttributes(&fa, k_attn<HD>);
+        cudaError_t e = cudaFuncGetAttributes(&fa, k_attn<HD, PAIR>);
         if (e != cudaSuccess)
             return e;
         return fa.numRegs * kThreads < 128 * kRegsCtl + 256 * kRegsSoftmax ? cudaErrorInvalidConfiguration
@@ -514,7 +597,7 @@ cudaError_t attn_setup()
     if (regs != cudaSuccess)
         return regs;
     static std::atomic<uint64_t> attr_devs{0};
-    return smem_limit_once(attr_devs, k_attn<HD>, kSmem<HD>);
+    return smem_limit_once(attr_devs, k_attn<HD, PAIR>, kSmem<HD>);
 }
 
 }  // namespace
@@ -524,15 +607,18 @@ cudaError_t attn_launch(const AttnOp& op, cudaStream_t st)
     if (!op.ready)
         return cudaErrorInvalidValue;
     if (op.args.head_dim == 64) {
-        cudaError_t e = attn_setup<64>();
+        cudaError_t e = attn_setup<64, false>();
         if (e != cudaSuccess)
             return e;
-        launch_k(k_attn<64>, op.grid, kThreads, kSmem<64>, st, op.tq, op.tk, op.tv, op.args);
+        launch_k(k_attn<64, false>, op.grid, kThreads, kSmem<64>, st, op.tq, op.tk, op.tv, op.args);
     } else {
-        cudaError_t e = attn_setup<128>();
+        cudaError_t e = op.pair ? attn_setup<128, true>() : attn_setup<128, false>();
         if (e != cudaSuccess)
             return e;
-        launch_k(k_attn<128>, op.grid, kThreads, kSmem<128>, st, op.tq, op.tk, op.tv, op.args);
+        if (op.pair)
+            launch_k_pairs(k_attn<128, true>, op.grid, kThreads, kSmem<128>, st, op.tq, op.tk, op.tv, op.args);
+        else
+            launch_k(k_attn<128, false>, op.grid, kThreads, kSmem<128>, st, op.tq, op.tk, op.tv, op.args);
     }
     count_launch();
     return cudaGetLastError();

@@ -57,6 +57,7 @@ struct AttnOp {
     CUtensorMap tq, tk, tv;
     AttnArgs args;
     dim3 grid;
+    bool pair = false;  // CTA pairs (head dim 128): K read in 64-row halves, grid.x even
     bool ready = false;
 };
 

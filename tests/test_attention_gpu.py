@@ -209,3 +209,33 @@ def test_attention_wide_single_head(cuda, d, n):
     err = np.abs(got - ref).max()
     cos = (got * ref).sum() / np.sqrt((got ** 2).sum() * (ref ** 2).sum())
     assert err < 2e-2 and cos > 0.999, (err, cos)
+
+
+_PAIR_CHILD = r"""
+import sys
+sys.path[:0] = [{root!r}, {pkg!r}]
+import torch
+import tests.test_attention_gpu as t
+cuda = torch.device("cuda", 0)
+t._run(cuda, 2, 3, 44, 256, 0)
+t._run(cuda, 1, 2, 77, 1000, 0)
+t._run(cuda, 2, 3, 44, 256, 1)
+t._run(cuda, 2, 2, 130, 260, 1, later=True)
+t.test_attention_kv_shards_bit_exact(cuda, 128, 4, 1, 2, 64, 960)
+t.test_attention_kv_arriving(cuda, 128, 2, 2, 3, 100, 412)
+print("PAIR_OK")
+"""
+
+
+def test_attention_cta_pairs(cuda):
+    """The CTA-pair form of the head-dim-128 kernel (MKB_ATTN_PAIR=1, read once per process, so in a child): joint,
+    condition-causal and cached-text masks, key shards and arriving shards, against the oracle as above."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = _PAIR_CHILD.format(root=root, pkg=os.path.join(root, "mako-image_b200"))
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, MKB_ATTN_PAIR="1"), capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "PAIR_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-4000:])
