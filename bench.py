@@ -258,6 +258,10 @@ def run_mkb(args, cfg):
         d.set_sequence_parallel(obj[0], rank, ws)
         if args.sp_exchange == "peer":
             d.set_peer_exchange(True)
+        elif args.sp_exchange == "heads":
+            d.set_head_exchange(1)
+        elif args.sp_exchange == "heads_peer":
+            d.set_head_exchange(2)
     for s in range(B):
         prompt = rng.normal(rng.tensor_key(99, (rank % 2) if half_pair else s), S * TD).reshape(S, TD)
         d.begin(prompt, h, w, slot=s)
@@ -388,6 +392,11 @@ def run_mkb(args, cfg):
                            "parallelism": (f"sequence parallel x{ws} (each rank 1/{ws} of every sample's joint rows, "
                                            + ("K/V shards pushed into the peers' memory by copy engines during the "
                                               "attention)" if args.sp_exchange == "peer" else
+                                              f"q/k/v all-to-all to {H // ws} heads per rank and outputs back, per "
+                                              "block over NCCL)" if args.sp_exchange == "heads" else
+                                              f"q/k/v of {H // ws} heads per rank and the outputs stored into the "
+                                              "peers' memory by the QKV and attention epilogues)"
+                                              if args.sp_exchange == "heads_peer" else
                                               "K/V all-gathered per block over NCCL)")) if sp_mode else
                                           (f"sample split x{ws} ({cfg['images']} images, "
                                            + ("cond / uncond of an image on neighbouring ranks, predictions "
@@ -750,9 +759,11 @@ def main():
                     help="DiT configs under torchrun: the config's images spread over the ranks (strong scaling)")
     ap.add_argument("--sp", action="store_true",
                     help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
-    ap.add_argument("--sp-exchange", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--sp-exchange", choices=["peer", "nccl", "heads", "heads_peer"], default="peer",
                     help="--sp: K/V shards pushed into the peers' memory by copy engines during the attention "
-                         "(peer) or all-gathered by NCCL before it (nccl)")
+                         "(peer), all-gathered by NCCL before it (nccl), or q/k/v exchanged all-to-all so that "
+                         "each rank attends over whole sequences of heads / ranks heads (heads), the same with the "
+                         "QKV and attention epilogues storing into the peers' memory (heads_peer)")
     ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down", "vae_attention",
                                          "vae_conv128"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")

@@ -328,6 +328,21 @@ mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int ra
  * bit for bit; all ranks still end with identical latents. Fails with MKB_ERR_CUDA on every rank if any rank cannot
  * allocate, export or map, leaving the all-gather in place. */
 mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable);
+/* Replaces the per-block K/V all-gather of a sequence-parallel handle by a head-parallel exchange (mode 1: NCCL,
+ * mode 2: peer memory) or goes back to it (mode 0); collective, every rank with the same mode, after
+ * mkb_dit_set_sequence_parallel. No counterpart in the reference. Rank r attends over all joint rows of heads
+ * [r * H / world, (r + 1) * H / world): after each block's QKV projection every rank's rows of those heads reach rank
+ * r, and after the attention its outputs return to the ranks that own the rows, before the output projection. A rank
+ * receives 4 (world - 1) / world^2 of one step-wide activation per block against the all-gather's
+ * 2 (world - 1) / world (a quarter at eight ranks). Mode 1 moves the rows by two NCCL all-to-alls per block. Mode 2
+ * has the QKV and attention epilogues store them straight into the peers' memory (CUDA IPC regions; the ranks must
+ * share a node, each GPU able to reach the others): each rank raises a flag in every peer after its stores, the
+ * attention waits (bounded, 2 s; MKB_ERR_KERNEL on timeout) for a peer's flag before its first tile of that peer's
+ * rows, and the output projection for every peer's attention. Every row sees its keys in the one-GPU order, so
+ * both modes equal the one-GPU step bit for bit. Needs the head count divisible by world (MKB_ERR_INVALID
+ * otherwise); turns the peer K/V exchange off; MKB_ERR_ALLOC / MKB_ERR_CUDA on every rank if any rank cannot
+ * allocate, export or map, leaving the all-gather in place. */
+mkb_status mkb_dit_sp_head_exchange(mkb_dit* d, int mode);
 /* The rows rank `rank` of `world` owns for S text and N image tokens per sample: text_rows (S on rank 0, else 0),
  * image_rows starting at image token image_row0, and shard_rows = (S + N) / world joint rows. Host arithmetic only. */
 mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,

@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int nkv = (n_keys + kTile - 1) / kTile;
     // Key tile taken at step j: j0 + j, wrapping round (j0 = 0 unless other ranks' shards arrive during the launch).
-    const int j0 = a.own_shard >= 0 ? a.own_shard * (a.kv_shard_rows / kTile) : 0;
+    const int j0 = a.own_shard >= 0 && a.rotate ? a.own_shard * (a.kv_shard_rows / kTile) : 0;
     const auto key_tile = [&](int j) { return j + j0 < nkv ? j + j0 : j + j0 - nkv; };
 
     if (threadIdx.x == 0) {
@@ -172,21 +172,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
-            bool ok = true;
+            bool ok = true, q_issued = PAIR;
             int arrived = a.own_shard;  // the shard whose arrival was last confirmed
             const unsigned long long want = a.own_shard >= 0 ? *a.shard_expect : 0;
+            // Row and plane of query tile t (shards never split a tile: q_shard_rows is a multiple of 128).
+            const auto q_at = [&](int t, int* plane) {
+                int row = a.q_row0 + q0 + t * kTile;
+                *plane = bh;
+                if (a.q_shard_rows > 0) {
+                    const int g = row / a.q_shard_rows;
+                    row -= g * a.q_shard_rows;
+                    *plane = g * a.q_plane_stride + bh;
+                }
+                return row;
+            };
             if constexpr (PAIR) {
                 if (leader)
                     mbar_arrive_expect_tx(q_full, 4 * TB);  // both CTAs' two tiles
-                for (int t = 0; t < 2; ++t)
+                for (int t = 0; t < 2; ++t) {
+                    int plane;
+                    const int row = q_at(t, &plane);
                     for (int pn = 0; pn < HD / 64; ++pn)
-                        tma_load_3d_pair(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile,
-                                         bh);
+                        tma_load_3d_pair(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, row, plane);
+                }
             } else {
-                mbar_arrive_expect_tx(q_full, 2 * TB);
-                for (int t = 0; t < 2; ++t)
-                    for (int pn = 0; pn < HD / 64; ++pn)
-                        tma_load_3d(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, a.q_row0 + q0 + t * kTile, bh);
+                // Query rows stored by other ranks during the launch: each tile's shard once its flag is up.
+                if (a.own_shard >= 0 && a.q_shard_rows > 0)
+                    for (int t = 0; t < 2 && ok; ++t) {
+                        const int gq = (a.q_row0 + q0 + t * kTile) / a.q_shard_rows;
+                        if (gq != a.own_shard && q0 + t * kTile < a.Lq)
+                            ok = wait_flag_ge(a.shard_ready + gq, want, a.status, kErrShardWait, abort_flag);
+                    }
+                if (ok) {
+                    mbar_arrive_expect_tx(q_full, 2 * TB);
+                    for (int t = 0; t < 2; ++t) {
+                        int plane;
+                        const int row = q_at(t, &plane);
+                        for (int pn = 0; pn < HD / 64; ++pn)
+                            tma_load_3d(sQ + t * TB + pn * kPanel, &tq, q_full, pn * 64, row, plane);
+                    }
+                    q_issued = true;
+                }
             }
             for (int j = 0; j < nkv && ok; ++j) {
                 const int st = j & 1;
@@ -201,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int g = krow / a.kv_shard_rows;
                     krow -= g * a.kv_shard_rows;
                     kplane = g * a.kv_plane_stride + bh;
-                    if (a.own_shard >= 0 && g != arrived) {  // another rank's shard: once its copy has landed
+                    if (a.own_shard >= 0 && g != arrived && g != a.own_shard) {  // another rank's: once landed
                         if (!wait_flag_ge(a.shard_ready + g, want, a.status, kErrShardWait, abort_flag)) {
                             ok = false;
                             break;
@@ -239,7 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Let the loads already issued land before the CTA can exit (a pair's loads complete on the leader's
             // barriers, which only the leader can wait on: the cluster barrier at the end keeps both CTAs alive).
             if (!ok && !PAIR) {
-                mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
+                if (q_issued)
+                    mbar_wait(q_full, 0, a.status, kErrWaitDrain, nullptr);
                 for (int j = issued_k > 2 ? issued_k - 2 : 0; j < issued_k; ++j)
                     mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status, kErrWaitDrain, nullptr);
                 for (int j = issued_v > 2 ? issued_v - 2 : 0; j < issued_v; ++j)
@@ -433,8 +460,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool row_ok = qrow < a.Lq;
             __nv_bfloat16* dst = nullptr;
             if (row_ok) {
-                dst = qpos < a.split ? a.out0 + (long(b) * a.rows0 + qpos) * a.ld0
-                                     : a.out1 + (long(b) * a.rows1 + (qpos - a.split)) * a.ld1;
+                if (a.out_shard_rows > 0) {
+                    const int g = qpos / a.out_shard_rows, i = qpos - g * a.out_shard_rows;
+                    const AttnOutShard& e = a.out_shards[g];
+                    dst = i < e.text_rows ? e.txt + (long(b) * e.text_rows + i) * a.ld0
+                                          : e.img + (long(b) * (a.out_shard_rows - e.text_rows) + i - e.text_rows) * a.ld0;
+                } else {
+                    dst = qpos < a.split ? a.out0 + (long(b) * a.rows0 + qpos) * a.ld0
+                                         : a.out1 + (long(b) * a.rows1 + (qpos - a.split)) * a.ld1;
+                }
                 dst += h * HD;
             }
 #pragma unroll 1
@@ -525,19 +559,26 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
 {
     op.ready = false;
     if (args.B <= 0 || args.H <= 0 || args.Lq <= 0 || args.Lk <= 0 || args.q_row0 < 0 ||
-        Lq_rows < args.q_row0 + args.Lq || Lk_rows < args.Lk) {
+        (args.q_shard_rows <= 0 && Lq_rows < args.q_row0 + args.Lq) || Lk_rows < args.Lk) {
         *err = "attention: bad sizes";
         return false;
     }
-    const bool text_rows = args.q_pos0 < args.split;  // some query rows route to out0
-    if (!args.out1 || (text_rows && !args.out0) || (args.ld0 & 7) || (args.ld1 & 7)) {
-        *err = "attention: outputs missing or leading dimensions not multiples of 8";
-        return false;
-    }
-    if ((text_rows && args.rows0 < args.split) || args.q_pos0 < 0 ||
-        args.q_pos0 + args.Lq - args.split > args.rows1) {
-        *err = "attention: output rows do not cover the query positions";
-        return false;
+    if (args.out_shard_rows > 0) {
+        if (!args.out_shards || (args.ld0 & 7) || args.q_pos0 < 0 || args.ld0 < long(args.H) * args.head_dim) {
+            *err = "attention: output shards need their table and ld0 a multiple of 8 covering the heads";
+            return false;
+        }
+    } else {
+        const bool text_rows = args.q_pos0 < args.split;  // some query rows route to out0
+        if (!args.out1 || (text_rows && !args.out0) || (args.ld0 & 7) || (args.ld1 & 7)) {
+            *err = "attention: outputs missing or leading dimensions not multiples of 8";
+            return false;
+        }
+        if ((text_rows && args.rows0 < args.split) || args.q_pos0 < 0 ||
+            args.q_pos0 + args.Lq - args.split > args.rows1) {
+            *err = "attention: output rows do not cover the query positions";
+            return false;
+        }
     }
     if (args.mask == kMaskCondCausal && args.cond_len <= 0) {
         *err = "attention: condition-causal mask needs cond_len > 0";
@@ -565,9 +606,20 @@ bool attn_prepare(AttnOp& op, const void* q, int Lq_rows, const void* k, const v
         *err = "attention: arriving shards need K/V shards, no mask, 8-byte aligned flags and own_shard inside Lk";
         return false;
     }
-    // CTA pairs for head dim 128 (MKB_ATTN_PAIR=0: one CTA per pair of query tiles throughout).
-    op.pair = hd == 128 && attn_pairs_enabled();
-    if (!make_heads_map(&op.tq, q, Lq_rows, bh, hd, err) ||
+    int q_rows = Lq_rows, q_planes = bh;
+    if (args.q_shard_rows > 0) {
+        if (args.q_shard_rows % 128 || args.q_plane_stride < bh || args.q_row0 != 0 || Lq_rows < args.q_shard_rows) {
+            *err = "attention: query shards need a multiple of 128 rows, q_row0 0 and a plane stride >= B * H";
+            return false;
+        }
+        const int shards = (args.Lq + args.q_shard_rows - 1) / args.q_shard_rows;
+        q_rows = args.q_shard_rows;
+        q_planes = (shards - 1) * args.q_plane_stride + bh;
+    }
+    // CTA pairs for head dim 128 (MKB_ATTN_PAIR=0: one CTA per pair of query tiles throughout); not with query
+    // tiles that arrive during the launch.
+    op.pair = hd == 128 && attn_pairs_enabled() && !(args.own_shard >= 0 && args.q_shard_rows > 0);
+    if (!make_heads_map(&op.tq, q, q_rows, q_planes, hd, err) ||
         !make_heads_map(&op.tk, k, kv_rows, kv_planes, hd, err, op.pair ? 64 : 128) ||
         !make_heads_map(&op.tv, v, kv_rows, kv_planes, hd, err))
         return false;

@@ -18,6 +18,13 @@ enum AttnMask : int {
                         // text rows; cond_len >= Lk: plain causal attention (its CLIP text encoders)
 };
 
+struct AttnOutShard {
+    __nv_bfloat16* txt = nullptr;
+    __nv_bfloat16* img = nullptr;
+    int text_rows = 0;
+    int pad = 0;
+};
+
 struct AttnArgs {
     int B = 0, H = 0;
     int Lq = 0;          // query rows per (sample, head) in q
@@ -42,12 +49,27 @@ struct AttnArgs {
     // of the k / v maps. This is the layout a sequence-parallel all-gather leaves (one shard per rank).
     int kv_shard_rows = 0;
     int kv_plane_stride = 0;
+    // Queries split the same way (q_shard_rows a multiple of 128, 0 = unsplit; needs q_row0 = 0): query row r of
+    // head bh is row r % q_shard_rows of plane (r / q_shard_rows) * q_plane_stride + bh of the q map.
+    int q_shard_rows = 0;
+    int q_plane_stride = 0;
+    // Outputs by shards of out_shard_rows joint positions (0 = the split routing above): position p of sample b
+    // is local row i = p % out_shard_rows of shard g = p / out_shard_rows and goes through out_shards[g] (a device
+    // array, one entry per shard): i < text_rows to row (b * text_rows + i) of txt, else to row
+    // (b * (out_shard_rows - text_rows) + i - text_rows) of img; rows ld0 apart, columns [h * head_dim, ...). The
+    // head-parallel exchange's destinations, one per owning rank (its send span, or its rows on that GPU).
+    int out_shard_rows = 0;
+    const AttnOutShard* out_shards = nullptr;
     // Shards that other ranks copy in while the kernel runs (the peer-memory K/V exchange). own_shard >= 0 makes
     // every CTA take its key tiles starting with shard own_shard (written on this GPU before the launch) and
     // wrapping round, and wait before the first tile of any other shard g until shard_ready[g] >= *shard_expect
     // (an acquire load at system scope, bounded by kWaitNs; on timeout the kErrShardWait bit). Needs
-    // kv_shard_rows > 0 and kMaskNone. The key order only changes the online softmax's rounding.
+    // kv_shard_rows > 0 and kMaskNone. The key order only changes the online softmax's rounding. rotate = 0 keeps
+    // the keys in order (shard 0 first: the one-GPU rounding), with the same waits before every shard other than
+    // the last one confirmed; query tiles of a shard other than own_shard (q_shard_rows > 0) wait the same way
+    // before they are loaded. The head-parallel exchange over peer memory, whose peers store q, k and v here.
     int own_shard = -1;
+    int rotate = 1;
     const unsigned long long* shard_ready = nullptr;
     const unsigned long long* shard_expect = nullptr;
     uint32_t* status = nullptr;

@@ -12,8 +12,10 @@
 #include "lora.cuh"
 #include "nccl_dl.cuh"
 #include "rowops.cuh"
+#include "sm100.cuh"
 
 #include <cmath>
+#include <cstddef>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -28,6 +30,7 @@ namespace {
 constexpr int kHeadDim = 128, kLatent = 64, kTimeDim = 256;
 constexpr float kEps = 1e-6f;
 constexpr size_t kSpFlagBytes = 512;  // the peer exchange's ready flags: one 64-bit word per rank, up to 64 ranks
+constexpr size_t kHxFlagBytes = 1024; // the head exchange's: q|k|v stored [64], attention outputs stored [64]
 constexpr int kSwigluBlock = 128;  // gate/up interleave of the SwiGLU GEMM (one 256-wide tile = 128 gate + 128 up)
 
 uint64_t splitmix64_host(uint64_t x)
@@ -94,6 +97,16 @@ const char* sp_partition(int S, int N, int world, int rank, SpRows* out)
 
 }  // namespace
 
+// The head-parallel exchange's per-rank destinations (a device table per plan, up to 64 ranks): where the QKV
+// epilogue stores each rank's heads, where the attention stores each rank's rows, and (peer-memory mode) the flags
+// this rank raises in every peer's region.
+struct HxTables {
+    __nv_bfloat16* group_dst[64];
+    AttnOutShard out[64];
+    unsigned long long* sig_qkv[64];
+    unsigned long long* sig_att[64];
+};
+
 struct DitImpl {
     mkb_dit_config cfg{};
     int D = 0, H = 0, F = 0, NB = 0, TD = 0;
@@ -134,6 +147,12 @@ struct DitImpl {
         AttnOp att;
         AttnOp att_odd;  // odd blocks' attention under the peer exchange (the second K/V buffer)
         std::vector<GemmOp> per_sample;  // ref21 txt_in2 / img_in per sample
+        HxTables* tab = nullptr;  // device copy: the head exchange's destinations for this geometry
+        ~Plan()
+        {
+            if (tab)
+                cudaFree(tab);
+        }
     };
     std::map<std::tuple<int, int, int, int>, std::unique_ptr<Plan>> plans;
 
@@ -177,6 +196,33 @@ struct DitImpl {
     mkb_status sp_set_peer(bool on);
     void sp_release_peer();
     mkb_status sp_push(int B, int Lg, int block, cudaStream_t s);
+    // Head-parallel exchange (replaces the K/V all-gather; H divisible by the ranks): after each block's QKV
+    // projection an all-to-all gives every rank all joint rows of its H / world heads (the QKV epilogue writes the
+    // rows of rank g's heads into span g of the send buffer, its own heads straight into the receive buffer), the
+    // attention runs over whole sequences for those heads, and a second all-to-all returns each rank's rows of
+    // every head. Per block a rank receives 4 (world - 1) / world^2 of one step-wide activation instead of the
+    // all-gather's 2 (world - 1) / world, and every row sees its keys in the one-GPU order.
+    // Mode 1 moves the spans with NCCL (send and receive buffers in sp_hx, outputs gathered into the O projection's
+    // rows by a copy kernel); mode 2 stores them straight into the peers' memory from the QKV and attention
+    // epilogues (every rank's IPC region holds [flags][q|k|v receive][the O projection's input rows], the
+    // attention waits for each peer's q|k|v flag before its first tile of that peer's rows, and the O projection
+    // waits for every peer's attention-done flag).
+    int sp_heads = 0;
+    __nv_bfloat16* sp_hx = nullptr;  // mode 1: [q|k|v send][q|k|v receive][output send][output receive]
+    size_t sp_hx_qkv = 0;            // elements of one q|k|v buffer: [world][3][B][H / world][Lg][128]
+    size_t sp_hx_o = 0;              // elements of one output buffer: [world][B][Lg][H / world * 128]
+    __nv_bfloat16* hx_region_qkv(int g) const  // mode 2: rank g's q|k|v receive buffer, as mapped here
+    {
+        return reinterpret_cast<__nv_bfloat16*>(sp_peer[g] + kHxFlagBytes);
+    }
+    __nv_bfloat16* hx_region_rows(int g) const  // mode 2: rank g's O projection input rows
+    {
+        return hx_region_qkv(g) + sp_hx_qkv;
+    }
+    bool sp_open_region(size_t bytes, bool ok, std::string* why);
+    mkb_status sp_set_heads(int mode);
+    mkb_status sp_all_to_all(const __nv_bfloat16* send, __nv_bfloat16* recv, size_t count, cudaStream_t s);
+    bool sp_agree(bool ok);
     SpRows rows_of(int S, int N) const
     {
         SpRows r;
@@ -215,7 +261,7 @@ struct DitImpl {
 DitImpl::~DitImpl()
 {
     void* bufs[] = {wmat, wvec, x_txt, x_img, vel, lat, xn, qh, kh, vh, attn, hid, lat_bf, txt_bf, txt_mid,
-                    tp, h1, temb, st, mod, omod, sig, rope, cfg_lat, kv_all, vel_x, vel_full};
+                    tp, h1, temb, st, mod, omod, sig, rope, cfg_lat, kv_all, vel_x, vel_full, sp_hx};
     if (stream)
         cudaStreamSynchronize(stream);
     for (void* p : bufs)
@@ -334,54 +380,28 @@ void DitImpl::sp_release_peer()
     cudaGetLastError();  // a failed set-up step is reported by the caller, not by later launches
 }
 
-// Switches the K/V exchange between the NCCL all-gather and peer memory. Collective over the group: every rank
-// calls it with the same `on`. Each rank exports its exchange region over CUDA IPC, the handles go round by an
-// all-gather, and every rank maps the others'; a second all-gather makes every rank fail together if any could not.
-mkb_status DitImpl::sp_set_peer(bool on)
+// Allocates this rank's exchange region (`bytes`, zeroed), exports it over CUDA IPC, gathers every rank's handle
+// (an NCCL all-gather through the idle velocity buffer) and maps the peers' regions into sp_peer (own region at
+// sp_rank). `ok` carries this rank's earlier set-up into the first agreement; a second one follows the mapping.
+// Every rank returns the same answer; on false *why holds this rank's reason (empty: another rank failed), and the
+// caller releases what was made.
+bool DitImpl::sp_open_region(size_t bytes, bool ok, std::string* why)
 {
-    if (sp_world < 2 || !sp_comm)
-        return fail(MKB_ERR_STATE, "peer exchange: set sequence parallelism first");
-    if (on == sp_p2p)
-        return MKB_OK;
-    MKB_TRY_CUDA(cudaStreamSynchronize(stream), "peer exchange: sync");
-    for (auto& g : graphs)  // plans and graphs hold the K/V buffers of the other mode
-        if (g.second.exec)
-            cudaGraphExecDestroy(g.second.exec);
-    graphs.clear();
-    plans.clear();
-    if (!on) {
-        sp_release_peer();
-        return MKB_OK;
-    }
     const NcclApi* api = nccl_api(nullptr);
-    // Round 1: allocate, export, gather the handles (with a success word each).
     struct Entry {
         cudaIpcMemHandle_t h;
         int ok;
         int pad[15];
     };
-    sp_kv_bytes = (size_t(sp_world) * 2 * Bmax * H * sp_lg_max * kHeadDim * 2 + 255) / 256 * 256;
-    std::string why;
-    Entry mine{};
     auto step = [&](cudaError_t e, const char* what) {
-        if (e != cudaSuccess && why.empty())
-            why = std::string(what) + ": " + cudaGetErrorString(e);
+        if (e != cudaSuccess && why->empty())
+            *why = std::string(what) + ": " + cudaGetErrorString(e);
         return e == cudaSuccess;
     };
-    bool ok = step(cudaMalloc(&sp_region, kSpFlagBytes + 2 * sp_kv_bytes), "allocating the exchange region") &&
-              step(cudaMemsetAsync(sp_region, 0, kSpFlagBytes + 2 * sp_kv_bytes, stream), "clearing it") &&
-              step(cudaMalloc(&sp_seq, (1 + size_t(NB)) * 8), "allocating the block counters") &&
-              step(cudaMemsetAsync(sp_seq, 0, (1 + size_t(NB)) * 8, stream), "clearing them") &&
-              step(cudaIpcGetMemHandle(&mine.h, sp_region), "cudaIpcGetMemHandle") &&
-              step(cudaEventCreateWithFlags(&sp_fork, cudaEventDisableTiming), "events");
-    sp_side.assign(sp_world - 1, nullptr);
-    for (auto& v : sp_done)
-        v.assign(sp_world - 1, nullptr);
-    for (int k = 0; k < sp_world - 1; ++k) {
-        ok = ok && step(cudaStreamCreateWithFlags(&sp_side[k], cudaStreamNonBlocking), "copy streams");
-        for (auto& v : sp_done)
-            ok = ok && step(cudaEventCreateWithFlags(&v[k], cudaEventDisableTiming), "events");
-    }
+    Entry mine{};
+    ok = ok && step(cudaMalloc(&sp_region, bytes), "allocating the exchange region") &&
+         step(cudaMemsetAsync(sp_region, 0, bytes, stream), "clearing it") &&
+         step(cudaIpcGetMemHandle(&mine.h, sp_region), "cudaIpcGetMemHandle");
     mine.ok = ok;
     std::vector<Entry> all(sp_world);
     auto gather = [&](const Entry& e) -> bool {
@@ -400,26 +420,64 @@ mkb_status DitImpl::sp_set_peer(bool on)
                 return false;
         return true;
     };
-    bool agreed = gather(mine) && all_ok();
-    if (agreed) {
-        // Round 2: map every peer's region.
-        sp_peer.assign(sp_world, nullptr);
-        sp_peer[sp_rank] = sp_region;
-        const std::vector<Entry> handles = all;
-        bool opened = true;
-        for (int g = 0; g < sp_world && opened; ++g) {
-            if (g == sp_rank)
-                continue;
-            void* p = nullptr;
-            opened = step(cudaIpcOpenMemHandle(&p, handles[g].h, cudaIpcMemLazyEnablePeerAccess),
-                          "cudaIpcOpenMemHandle");
-            sp_peer[g] = static_cast<uint8_t*>(p);
-        }
-        Entry e2{};
-        e2.ok = opened;
-        agreed = gather(e2) && all_ok();
+    if (!gather(mine) || !all_ok())
+        return false;
+    sp_peer.assign(sp_world, nullptr);
+    sp_peer[sp_rank] = sp_region;
+    const std::vector<Entry> handles = all;
+    bool opened = true;
+    for (int g = 0; g < sp_world && opened; ++g) {
+        if (g == sp_rank)
+            continue;
+        void* p = nullptr;
+        opened = step(cudaIpcOpenMemHandle(&p, handles[g].h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        sp_peer[g] = static_cast<uint8_t*>(p);
     }
-    if (!agreed) {
+    Entry e2{};
+    e2.ok = opened;
+    return gather(e2) && all_ok();
+}
+
+// Switches the K/V exchange between the NCCL all-gather and peer memory. Collective over the group: every rank
+// calls it with the same `on`. Each rank exports its exchange region over CUDA IPC, the handles go round by an
+// all-gather, and every rank maps the others'; a second all-gather makes every rank fail together if any could not.
+mkb_status DitImpl::sp_set_peer(bool on)
+{
+    if (sp_world < 2 || !sp_comm)
+        return fail(MKB_ERR_STATE, "peer exchange: set sequence parallelism first");
+    if (on == sp_p2p)
+        return MKB_OK;
+    if (on && sp_heads)
+        MKB_TRY(sp_set_heads(0));
+    MKB_TRY_CUDA(cudaStreamSynchronize(stream), "peer exchange: sync");
+    for (auto& g : graphs)  // plans and graphs hold the K/V buffers of the other mode
+        if (g.second.exec)
+            cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+    plans.clear();
+    if (!on) {
+        sp_release_peer();
+        return MKB_OK;
+    }
+    sp_kv_bytes = (size_t(sp_world) * 2 * Bmax * H * sp_lg_max * kHeadDim * 2 + 255) / 256 * 256;
+    std::string why;
+    auto step = [&](cudaError_t e, const char* what) {
+        if (e != cudaSuccess && why.empty())
+            why = std::string(what) + ": " + cudaGetErrorString(e);
+        return e == cudaSuccess;
+    };
+    bool ok = step(cudaMalloc(&sp_seq, (1 + size_t(NB)) * 8), "allocating the block counters") &&
+              step(cudaMemsetAsync(sp_seq, 0, (1 + size_t(NB)) * 8, stream), "clearing them") &&
+              step(cudaEventCreateWithFlags(&sp_fork, cudaEventDisableTiming), "events");
+    sp_side.assign(sp_world - 1, nullptr);
+    for (auto& v : sp_done)
+        v.assign(sp_world - 1, nullptr);
+    for (int k = 0; k < sp_world - 1; ++k) {
+        ok = ok && step(cudaStreamCreateWithFlags(&sp_side[k], cudaStreamNonBlocking), "copy streams");
+        for (auto& v : sp_done)
+            ok = ok && step(cudaEventCreateWithFlags(&v[k], cudaEventDisableTiming), "events");
+    }
+    if (!sp_open_region(kSpFlagBytes + 2 * sp_kv_bytes, ok, &why)) {
         sp_release_peer();
         return fail(MKB_ERR_CUDA, "peer exchange: " + (why.empty() ? std::string("another rank failed") : why));
     }
@@ -446,6 +504,103 @@ mkb_status DitImpl::sp_push(int B, int Lg, int block, cudaStream_t s)
                      "ready flag");
         MKB_TRY_CUDA(cudaEventRecord(sp_done[block & 1][k - 1], x), "push done");
     }
+    return MKB_OK;
+}
+
+// True on every rank when every rank passes ok: a one-word all-gather through the velocity exchange buffer.
+bool DitImpl::sp_agree(bool ok)
+{
+    const NcclApi* api = nccl_api(nullptr);
+    int* buf = reinterpret_cast<int*>(vel_x);  // idle between steps
+    std::vector<int> all(sp_world, 0);
+    const int mine = ok ? 1 : 0;
+    if (cudaMemcpyAsync(buf + sp_rank, &mine, sizeof(int), cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        api->AllGather(buf + sp_rank, buf, 1, ncclInt32, sp_comm, stream) != ncclSuccess ||
+        cudaMemcpyAsync(all.data(), buf, sizeof(int) * sp_world, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+        return false;
+    for (int v : all)
+        if (!v)
+            return false;
+    return true;
+}
+
+// Switches to the head-parallel exchange (mode 1: NCCL all-to-all, 2: stores into the peers' memory) or back to the
+// K/V all-gather (0). Collective: every rank with the same mode.
+mkb_status DitImpl::sp_set_heads(int mode)
+{
+    if (sp_world < 2 || !sp_comm)
+        return fail(MKB_ERR_STATE, "head exchange: set sequence parallelism first");
+    if (mode < 0 || mode > 2)
+        return fail(MKB_ERR_INVALID, "head exchange: mode must be 0, 1 or 2");
+    if (mode == sp_heads)
+        return MKB_OK;
+    if (mode && H % sp_world)
+        return fail(MKB_ERR_INVALID, "head exchange: the heads must divide evenly over the ranks");
+    if (sp_p2p)
+        MKB_TRY(sp_set_peer(false));
+    MKB_TRY_CUDA(cudaStreamSynchronize(stream), "head exchange: sync");
+    for (auto& g : graphs)  // plans and graphs hold the buffers of the other mode
+        if (g.second.exec)
+            cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+    plans.clear();
+    if (sp_hx)
+        cudaFree(sp_hx);
+    sp_hx = nullptr;
+    sp_release_peer();
+    sp_heads = 0;
+    if (!mode)
+        return MKB_OK;
+    sp_hx_qkv = size_t(3) * Bmax * H * sp_lg_max * kHeadDim;
+    sp_hx_o = size_t(Bmax) * sp_lg_max * H * kHeadDim;
+    if (mode == 1) {
+        const cudaError_t e = cudaMalloc(&sp_hx, (2 * sp_hx_qkv + 2 * sp_hx_o) * sizeof(__nv_bfloat16));
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            sp_hx = nullptr;
+        }
+        if (!sp_agree(e == cudaSuccess)) {
+            if (sp_hx)
+                cudaFree(sp_hx);
+            sp_hx = nullptr;
+            return fail(e == cudaSuccess ? MKB_ERR_CUDA : MKB_ERR_ALLOC,
+                        e == cudaSuccess ? std::string("head exchange: another rank failed")
+                                         : std::string("head exchange: allocating: ") + cudaGetErrorString(e));
+        }
+    } else {
+        std::string why;
+        const bool ok = cudaMalloc(&sp_seq, (1 + size_t(NB)) * 8) == cudaSuccess &&
+                        cudaMemsetAsync(sp_seq, 0, (1 + size_t(NB)) * 8, stream) == cudaSuccess;
+        if (!ok)
+            why = "allocating the block counters";
+        if (!sp_open_region(kHxFlagBytes + (sp_hx_qkv + sp_hx_o) * sizeof(__nv_bfloat16), ok, &why)) {
+            cudaGetLastError();
+            sp_release_peer();
+            return fail(MKB_ERR_CUDA, "head exchange: " + (why.empty() ? std::string("another rank failed") : why));
+        }
+    }
+    sp_heads = mode;
+    return MKB_OK;
+}
+
+// All-to-all of `count` elements per rank pair: span g of `send` to rank g, rank g's span into span g of `recv`.
+// This rank's own span is written in place by the producer and not copied.
+mkb_status DitImpl::sp_all_to_all(const __nv_bfloat16* send, __nv_bfloat16* recv, size_t count, cudaStream_t s)
+{
+    const NcclApi* api = nccl_api(nullptr);
+    ncclResult_t r = api->GroupStart();
+    for (int k = 1; k < sp_world && r == ncclSuccess; ++k) {
+        const int to = (sp_rank + k) % sp_world, from = (sp_rank - k + sp_world) % sp_world;
+        r = api->Send(send + size_t(to) * count, count, ncclBfloat16, to, sp_comm, s);
+        if (r == ncclSuccess)
+            r = api->Recv(recv + size_t(from) * count, count, ncclBfloat16, from, sp_comm, s);
+    }
+    const ncclResult_t r2 = api->GroupEnd();
+    if (r == ncclSuccess)
+        r = r2;
+    if (r != ncclSuccess)
+        return fail(MKB_ERR_CUDA, std::string("dit: head exchange all-to-all: ") + api->GetErrorString(r));
     return MKB_OK;
 }
 
@@ -696,7 +851,9 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         const int Mt = B * St, Mi = B * Nl;
         const long mstride = long(NB) * 12 * D;  // per-sample stride of the stacked modulation
         __nv_bfloat16* xn_s[2] = {xn, xn + size_t(Mt) * D};
-        __nv_bfloat16* at_s[2] = {attn, attn + size_t(Mt) * D};
+        // The O projection's input rows: this GPU's exchange region when peers store into them.
+        __nv_bfloat16* const rows_in = sp && sp_heads == 2 ? hx_region_rows(sp_rank) : attn;
+        __nv_bfloat16* at_s[2] = {rows_in, rows_in + size_t(Mt) * D};
         __nv_bfloat16* hd_s[2] = {hid, hid + size_t(Mt) * F};
         float* x_s[2] = {x_txt, x_img};
         const int M_s[2] = {Mt, Mi}, rps[2] = {S, Nl}, off[2] = {0, St};
@@ -706,6 +863,41 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
         // the peer exchange.
         const size_t kv_shard = size_t(B) * H * Lh * kHeadDim;
         auto kv_base = [&](int block) { return sp_p2p ? kv_buf(block & 1) : kv_all; };
+        // Head-parallel exchange: Hr heads per rank; span g of the q|k|v buffers holds q, k, v of rank g's heads
+        // (hx_chunk elements each), [3][B][Hr][Lh][128].
+        const int hx = sp ? sp_heads : 0;
+        const int Hr = hx ? H / sp_world : H;
+        const size_t hx_chunk = size_t(B) * Hr * Lh * kHeadDim;
+        __nv_bfloat16* const hx_recv = hx == 1 ? sp_hx + sp_hx_qkv : hx == 2 ? hx_region_qkv(sp_rank) : nullptr;
+        if (hx) {
+            HxTables t{};
+            const size_t och = size_t(B) * Lh * Hr * kHeadDim;  // mode 1: one output span
+            __nv_bfloat16* const o_send = hx == 1 ? hx_recv + sp_hx_qkv : nullptr;
+            for (int g = 0; g < sp_world; ++g) {
+                const int st_g = g == 0 ? S : 0;  // rank g's text rows
+                if (hx == 1) {  // spans to send, this rank's own straight into the receive buffers
+                    t.group_dst[g] = (g == sp_rank ? hx_recv : sp_hx) + size_t(g) * 3 * hx_chunk;
+                    t.out[g].img = (g == sp_rank ? o_send + sp_hx_o : o_send) + size_t(g) * och;
+                } else {  // rank g's receive buffer and input rows, columns of this rank's heads
+                    t.group_dst[g] = hx_region_qkv(g) + size_t(sp_rank) * 3 * hx_chunk;
+                    __nv_bfloat16* rows = hx_region_rows(g) + size_t(sp_rank) * Hr * kHeadDim;
+                    t.out[g].txt = st_g ? rows : nullptr;
+                    t.out[g].text_rows = st_g;
+                    t.out[g].img = rows + size_t(B) * st_g * D;
+                    if (g != sp_rank) {
+                        t.sig_qkv[g] = reinterpret_cast<unsigned long long*>(sp_peer[g]) + sp_rank;
+                        t.sig_att[g] = reinterpret_cast<unsigned long long*>(sp_peer[g]) + 64 + sp_rank;
+                    }
+                }
+            }
+            if (cudaMalloc(&plan->tab, sizeof(HxTables)) != cudaSuccess) {
+                cudaGetLastError();
+                plan->tab = nullptr;
+                return fail(MKB_ERR_ALLOC, "dit: head exchange tables");
+            }
+            MKB_TRY_CUDA(cudaMemcpy(plan->tab, &t, sizeof(HxTables), cudaMemcpyHostToDevice), "head exchange tables");
+        }
+        HxTables* const tab = plan->tab;
         const char* nm[2] = {"txt", "img"};
         // Per block four launches, each the image rows' GEMM (problem 0) with the text rows' (problem 1) filling
         // its tail, all on 256 x 256 CTA-pair tiles (QKV: two heads per CTA): the pair halves each SM's W traffic
@@ -734,6 +926,12 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
                 a.qh = qh;
                 a.kh = sp ? kv_base(i) + size_t(sp_rank) * 2 * kv_shard : kh;
                 a.vh = sp ? a.kh + kv_shard : vh;
+                if (hx) {
+                    a.head_group = Hr;
+                    a.group_chunk = long(hx_chunk);
+                    a.group_dst = reinterpret_cast<__nv_bfloat16* const*>(reinterpret_cast<char*>(tab) +
+                                                                          offsetof(HxTables, group_dst));
+                }
                 a.norm_q = V(p + "norm_q");
                 a.norm_k = V(p + "norm_k");
                 a.rope = rope_s[s];
@@ -830,7 +1028,26 @@ mkb_status DitImpl::build_plan(int B, int S, int N, int first, Plan** out)
             if (!attn_prepare(plan->att_odd, qh, Lh, kv_buf(1), kv_buf(1) + kv_shard, L, at, &err))
                 return fail(MKB_ERR_INVALID, err);
         }
-        if (!attn_prepare(plan->att, qh, Lh, sp ? kv_base(0) : kh, sp ? kv_base(0) + kv_shard : vh, L, at, &err))
+        if (hx) {  // Hr heads over all L rows, queries and keys in rank shards; outputs to their rows' owners
+            at.H = Hr;
+            at.Lq = L;
+            at.q_pos0 = 0;
+            at.q_shard_rows = Lh;
+            at.q_plane_stride = 3 * B * Hr;
+            at.kv_plane_stride = 3 * B * Hr;
+            at.out_shard_rows = Lh;
+            at.out_shards = reinterpret_cast<const AttnOutShard*>(reinterpret_cast<char*>(tab) + offsetof(HxTables, out));
+            at.ld0 = hx == 1 ? long(Hr) * kHeadDim : D;
+            if (hx == 2) {  // peers' rows arrive during the launch; keys in order (the one-GPU rounding)
+                at.own_shard = sp_rank;
+                at.rotate = 0;
+                at.shard_ready = reinterpret_cast<const unsigned long long*>(sp_region);
+                at.shard_expect = sp_seq + 1;
+            }
+            if (!attn_prepare(plan->att, hx_recv, Lh, hx_recv + hx_chunk, hx_recv + 2 * hx_chunk, L, at, &err))
+                return fail(MKB_ERR_INVALID, err);
+        } else if (!attn_prepare(plan->att, qh, Lh, sp ? kv_base(0) : kh, sp ? kv_base(0) + kv_shard : vh, L, at,
+                                 &err))
             return fail(MKB_ERR_INVALID, err);
     } else {
         const int T = first ? L : N, split = first ? S : 0, Mr = B * T;
@@ -964,6 +1181,52 @@ __global__ void k_sp_step(unsigned long long* seq, int blocks)
     grid_dep_launch();
 }
 
+// The head-parallel exchange's returned outputs, src [rank g][sample][shard row][w8 x 8 columns of g's heads], into
+// the output projection's input rows (every sample's text rows first, then the image rows), columns g * 8 w8...:
+// one 16-byte vector per thread.
+__global__ void k_sp_heads_gather(const uint4* __restrict__ src, __nv_bfloat16* __restrict__ attn, int B, int Lh,
+                                  int St, int w8, int D, int n)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    const long Mt = long(B) * St;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+        const int c = e % w8, rest = e / w8;
+        const int i = rest % Lh, gb = rest / Lh;
+        const int b = gb % B, g = gb / B;
+        const long row = i < St ? long(b) * St + i : Mt + long(b) * (Lh - St) + (i - St);
+        reinterpret_cast<uint4*>(attn + row * D + long(g) * w8 * 8)[c] = src[e];
+    }
+}
+
+// The head exchange over peer memory: raises this rank's flag of the current block (the value at `value`) in every
+// peer's region, after everything the kernels before it stored (into the peers' memory too) is complete: the
+// dependent-launch wait returns once they are, then a system-scope fence and one release store per peer.
+__global__ void k_sp_signal(unsigned long long* const* flags, const unsigned long long* value, int n)
+{
+    grid_dep_wait();
+    const int g = threadIdx.x;
+    if (g < n && flags[g]) {
+        const unsigned long long v = *value;
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flags[g]), "l"(v) : "memory");
+    }
+    grid_dep_launch();
+}
+
+// Waits (each lane one peer, bounded like every wait: kErrShardWait on timeout) until every peer's flag in this
+// rank's region has reached the current block's value: the peers' attention outputs are in this GPU's rows.
+__global__ void k_sp_wait(const unsigned long long* flags, int n, int self, const unsigned long long* value,
+                          uint32_t* status)
+{
+    grid_dep_wait();
+    const int g = threadIdx.x;
+    if (g < n && g != self)
+        wait_flag_ge(flags + g, *value, status, kErrShardWait, nullptr);
+    __syncthreads();
+    grid_dep_launch();
+}
+
 #define MKB_K(expr, what) MKB_TRY_CUDA((expr), what)
 
 // Runs one step for B samples whose latents are in `lat` (device, [B][N][64]) with host noise levels `sigmas`.
@@ -1056,7 +1319,7 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     const int St = q1 ? rw.text : S, Nl = q1 ? rw.image : N;
     GemmOp* g = plan->ops.data() + size_t(NB) * per;
     const int R = q1 ? B : 2 * B;
-    if (sp_p2p) {
+    if (sp_p2p || sp_heads == 2) {
         MKB_K(launch_k(k_sp_step, dim3(1), dim3(1), 0, s, sp_seq, NB), "step counter");
         count_launch();
     }
@@ -1136,7 +1399,42 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
                 for (cudaEvent_t e : sp_done[i & 1])
                     MKB_K(cudaStreamWaitEvent(s, e, 0), "push join");
             MKB_K(gemm_launch(o[0], s), "qkv");
-            if (sp_p2p) {
+            if (sp_heads == 2) {  // the epilogues store into the peers' memory; flags order the steps
+                HxTables* const tab = plan->tab;
+                const auto table = [&](size_t off) {
+                    return reinterpret_cast<unsigned long long* const*>(reinterpret_cast<char*>(tab) + off);
+                };
+                const unsigned long long* value = sp_seq + 1 + i;
+                MKB_K(launch_k(k_sp_signal, dim3(1), dim3(64), 0, s, table(offsetof(HxTables, sig_qkv)), value,
+                               sp_world),
+                      "q|k|v stored");
+                AttnOp at = plan->att;
+                at.args.shard_expect = value;
+                MKB_K(attn_launch(at, s), "attention");
+                MKB_K(launch_k(k_sp_signal, dim3(1), dim3(64), 0, s, table(offsetof(HxTables, sig_att)), value,
+                               sp_world),
+                      "outputs stored");
+                MKB_K(launch_k(k_sp_wait, dim3(1), dim3(64), 0, s,
+                               reinterpret_cast<const unsigned long long*>(sp_region) + 64, sp_world, sp_rank, value,
+                               status),
+                      "outputs wait");
+                count_launch();
+                count_launch();
+                count_launch();
+            } else if (sp_heads) {
+                const int Hr = H / sp_world, w8 = Hr * kHeadDim / 8;
+                __nv_bfloat16* recv = sp_hx + sp_hx_qkv;
+                __nv_bfloat16* o_send = recv + sp_hx_qkv;
+                __nv_bfloat16* o_recv = o_send + sp_hx_o;
+                MKB_TRY(sp_all_to_all(sp_hx, recv, size_t(3) * B * Hr * rw.shard * kHeadDim, s));
+                MKB_K(attn_launch(plan->att, s), "attention");
+                MKB_TRY(sp_all_to_all(o_send, o_recv, size_t(B) * rw.shard * Hr * kHeadDim, s));
+                const int n = sp_world * B * rw.shard * w8;
+                MKB_K(launch_k(k_sp_heads_gather, dim3(std::min((n + 255) / 256, 148 * 8)), dim3(256), 0, s,
+                               reinterpret_cast<const uint4*>(o_recv), attn, B, rw.shard, St, w8, D, n),
+                      "head gather");
+                count_launch();
+            } else if (sp_p2p) {
                 MKB_TRY(sp_push(B, rw.shard, i, s));
                 AttnOp at = i & 1 ? plan->att_odd : plan->att;
                 at.args.shard_expect = sp_seq + 1 + i;
@@ -1149,7 +1447,7 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
                     return fail(MKB_ERR_CUDA, std::string("dit: K/V all-gather: ") +
                                                   nccl_api(nullptr)->GetErrorString(r));
             }
-            if (!sp_p2p)
+            if (!sp_p2p && !sp_heads)
                 MKB_K(attn_launch(plan->att, s), "attention");
             MKB_K(gemm_launch(o[1], s), "o proj");
             MKB_K(ln(4, 3), "ln_modulate 2");
@@ -1653,6 +1951,12 @@ mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable)
 {
     MKB_TRY(check_handle(d));
     return d->impl.sp_set_peer(enable != 0);
+}
+
+mkb_status mkb_dit_sp_head_exchange(mkb_dit* d, int mode)
+{
+    MKB_TRY(check_handle(d));
+    return d->impl.sp_set_heads(mode);
 }
 
 mkb_status mkb_dit_sp_rows(int S, int N, int world, int rank, int* text_rows, int* image_rows, int* image_row0,

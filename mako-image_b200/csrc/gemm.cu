@@ -359,6 +359,11 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
             }
             __nv_bfloat16* base = which == 0 ? a.qh : which == 1 ? a.kh : a.vh;
             __nv_bfloat16* dst = base + ((long(bsample) * heads + head) * a.L + pos) * 128;
+            if (a.head_group > 0) {
+                const int grp = head / a.head_group;
+                dst = a.group_dst[grp] + which * a.group_chunk +
+                      ((long(bsample) * a.head_group + head - grp * a.head_group) * a.L + pos) * 128;
+            }
             const float* w = which == 0 ? a.norm_q : a.norm_k;
 #pragma unroll 1
             for (int c = 0; c < 128; c += 32) {
@@ -1466,6 +1471,11 @@ bool check_epilogue(Epi epi, const GemmArgs& args, int bn, const char** err)
     }
     if (epi == Epi::kQkv && (bn < 128 || args.D % bn || args.N != 3 * args.D || !args.qh || !args.kh || !args.vh)) {
         *err = "gemm: qkv epilogue needs N = 3 D, D a multiple of the tile width, and q/k/v outputs";
+        return false;
+    }
+    if (epi == Epi::kQkv && args.head_group > 0 &&
+        ((args.D / 128) % args.head_group || args.group_chunk <= 0 || !args.group_dst)) {
+        *err = "gemm: qkv head groups must divide the heads and have a positive chunk and a destination table";
         return false;
     }
     if (epi == Epi::kSwiGLU && (bn != 256 || args.N % bn)) {

@@ -58,6 +58,13 @@ struct GemmArgs {
     const float* rope = nullptr;    // [L][64][2] (cos, sin) per joint position, or null for no rotation
     int D = 0;                      // width of each of q, k, v (heads * head_dim)
     int L = 0;                      // joint sequence length of the head layout
+    // kQkv: heads in groups of head_group (0: one group, the layout above). Head h of group g = h / head_group goes
+    // to group_dst[g] + which * group_chunk + ((sample * head_group + h % head_group) * L + position) * 128 (which:
+    // 0 q, 1 k, 2 v); group_dst is a device array of one base per group: the spans of the head-parallel exchange,
+    // in this GPU's memory or mapped from the peer that attends over those heads.
+    int head_group = 0;
+    long group_chunk = 0;
+    __nv_bfloat16* const* group_dst = nullptr;
     float eps = 1e-6f;
     int head_dim = 128;             // kHeads: 64 or 128
     int part0 = 0;                  // kHeads: the first column block goes to q (0), k (1) or v (2)

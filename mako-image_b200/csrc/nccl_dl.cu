@@ -32,7 +32,9 @@ const NcclApi* nccl_api(std::string* err)
             return fn != nullptr;
         };
         if (!bind(api.GetUniqueId, "ncclGetUniqueId") || !bind(api.CommInitRank, "ncclCommInitRank") ||
-            !bind(api.AllGather, "ncclAllGather") || !bind(api.CommDestroy, "ncclCommDestroy") ||
+            !bind(api.AllGather, "ncclAllGather") || !bind(api.Send, "ncclSend") || !bind(api.Recv, "ncclRecv") ||
+            !bind(api.GroupStart, "ncclGroupStart") || !bind(api.GroupEnd, "ncclGroupEnd") ||
+            !bind(api.CommDestroy, "ncclCommDestroy") ||
             !bind(api.GetErrorString, "ncclGetErrorString")) {
             load_error = lib + " lacks an expected symbol";
             return;

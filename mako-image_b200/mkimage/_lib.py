@@ -111,6 +111,7 @@ _SIGS = {
     "mkb_attention_kv_arriving": (_i, [_vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _l, _i, _vp,
                                        _l, _i, _i, _i, _i, _vp, _vp, _vp]),
     "mkb_dit_sp_peer_exchange": (_i, [_vp, _i]),
+    "mkb_dit_sp_head_exchange": (_i, [_vp, _i]),
     "mkb_attention_wide": (_i, [_vp, _l, _i, _i, _i, _i, _i, _vp, _l, _vp]),
     "mkb_nccl_unique_id": (_i, [_vp, ctypes.c_size_t]),
     "mkb_dit_variant": (_i, [_vp]),

@@ -182,6 +182,12 @@ class Dit:
         (collective; see mkb_dit_sp_peer_exchange)."""
         check(lib.mkb_dit_sp_peer_exchange(self.h, int(bool(enable))))
 
+    def set_head_exchange(self, mode: int = 1):
+        """Replaces the per-block K/V all-gather by the head-parallel exchange: each rank attends over all rows of
+        heads / world heads, the rows reaching it by NCCL all-to-alls (mode 1) or by stores into the peers' memory
+        from the QKV and attention epilogues (mode 2); 0 goes back (collective; see mkb_dit_sp_head_exchange)."""
+        check(lib.mkb_dit_sp_head_exchange(self.h, int(mode)))
+
 
 NCCL_ID_BYTES = 128
 

@@ -1,8 +1,9 @@
 """One rank of the two-GPU sequence-parallel test (test_sp_gpu.py), run as its own process.
 
 Rank 0 makes the NCCL id and hands it to the other ranks through a file in the shared temporary folder. Every rank
-runs the same steps on a sequence-parallel handle, its K/V exchanged by the NCCL all-gather or (argument "peer") by
-pushes into the peers' memory; rank 0 also runs them on an unsplit handle as the reference. Results go to
+runs the same steps on a sequence-parallel handle, its K/V exchanged by the NCCL all-gather, (argument "peer") by
+pushes into the peers' memory, or by the head-parallel exchange over NCCL (argument "heads") or over peer memory
+("heads_peer"); rank 0 also runs them on an unsplit handle as the reference. Results go to
 rank<r>.npy / ref.npy in that folder."""
 
 import os
@@ -67,6 +68,10 @@ def main():
             d.set_sequence_parallel(nid, rank, world)
             if exchange == "peer":
                 d.set_peer_exchange(True)
+            elif exchange == "heads":
+                d.set_head_exchange(1)
+            elif exchange == "heads_peer":
+                d.set_head_exchange(2)
         for slot in range(4):
             d.begin(prompts[slot], GH, GW, slot)
         return d

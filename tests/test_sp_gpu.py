@@ -3,7 +3,9 @@
 Each rank runs every GEMM, norm and RoPE on its own joint rows. With the NCCL all-gather of K and V per block every
 output row goes through the same arithmetic in the same order as on one GPU: the bar is bit-for-bit equality of the
 velocities and updated latents, on every rank, through the host, guided and device-buffer calls (the guided call
-three times: eager, captured into a CUDA graph with the collectives inside, replayed). With the peer-memory exchange
+three times: eager, captured into a CUDA graph with the collectives inside, replayed); the same holds for the
+head-parallel exchange (mkb_dit_sp_head_exchange) over NCCL and over peer memory, where each rank attends over all
+rows of half the heads with the keys in the one-GPU order. With the peer-memory exchange
 (mkb_dit_sp_peer_exchange) each rank's attention starts at its own shard's keys, so the bar is the ranks' equality
 with each other and a relative L2 error below 5e-3 against the one-GPU step. NVLS is off for these processes.
 Skipped with fewer than two GPUs."""
@@ -20,7 +22,7 @@ pytestmark = pytest.mark.gpu
 WORKER = os.path.join(os.path.dirname(os.path.abspath(__file__)), "sp_worker.py")
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("exchange", ["nccl", "peer", "heads", "heads_peer"])
 def test_sequence_parallel_two_gpus(tmp_path, exchange):
     import torch
 
@@ -43,7 +45,7 @@ def test_sequence_parallel_two_gpus(tmp_path, exchange):
     assert np.array_equal(got[0], got[1])  # every rank applies the same update to the gathered velocities
     for r in range(2):
         assert got[r].shape == ref.shape
-        if exchange == "nccl":
+        if exchange in ("nccl", "heads", "heads_peer"):
             assert np.array_equal(got[r], ref), (r, np.abs(got[r] - ref).max())
         else:  # each rank reads the keys from its own shard round: the softmax's rounding differs
             for a, w in zip(got[r], ref):
