@@ -46,3 +46,25 @@ def test_errors_are_codes_not_crashes():
     assert mkimage.lib.mkb_dit_create(None, None) != 0
     assert "null" in mkimage.lib.mkb_last_error().decode()
     assert mkimage.lib.mkb_er_sde_create(None, 1, 0, 0.0, None) != 0
+
+
+def test_nccl_binding_takes_every_entry_point(tmp_path):
+    """The run-time NCCL binding (the sequence-parallel exchanges' all-gather, send / receive and group calls) binds
+    all nine entry points from the library MKB_NCCL_LIB names: with the stand-in the failure tests use, making a
+    communicator id succeeds, and a library lacking one of them is refused with a message. No GPU involved."""
+    so = tmp_path / "libfake_nccl.so"
+    src = os.path.join(ROOT, "tests", "fake_nccl", "fake_nccl.c")
+    subprocess.run(["gcc", "-shared", "-fPIC", "-O1", "-o", str(so), src], check=True)
+    short = tmp_path / "libshort_nccl.so"
+    subprocess.run(["gcc", "-shared", "-fPIC", "-O1", "-DFAKE_NCCL_NO_P2P", "-o", str(short), src], check=True)
+    code = ("import ctypes, sys; sys.path.insert(0, {pkg!r}); import mkimage; "
+            "buf = ctypes.create_string_buffer(128); "
+            "r = mkimage.lib.mkb_nccl_unique_id(buf, 128); print(r, mkimage.lib.mkb_last_error().decode())")
+    code = code.format(pkg=os.path.join(ROOT, "mako-image_b200"))
+    for lib, want in ((so, "0 "), (short, "2 ")):  # MKB_OK, MKB_ERR_CUDA
+        r = subprocess.run(["python", "-c", code], env=dict(os.environ, MKB_NCCL_LIB=str(lib)), capture_output=True,
+                           text=True, timeout=120)
+        assert r.returncode == 0, r.stderr
+        assert r.stdout.startswith(want), r.stdout
+        if want == "2 ":
+            assert "lacks an expected symbol" in r.stdout, r.stdout
