@@ -30,7 +30,14 @@ constexpr int kThreads = 192;
 constexpr int kEpiBox = 128 * 32 * 4;
 constexpr int kBiasBytes = 256 * 4;
 constexpr bool epi_tma(Epi e) { return e == Epi::kAdd || e == Epi::kResid || e == Epi::kBF16; }
-constexpr int epi_staging(Epi e) { return epi_tma(e) ? 2 * kEpiBox + kBiasBytes : 0; }
+// The QKV epilogue's staging: per epilogue warp one head of its 32 rows (32 x 256 bytes), so that the rows leave as
+// whole 256-byte rows (coalesced; into another GPU's memory under the head-parallel exchange) rather than as
+// 16-byte pieces 256 bytes apart.
+constexpr int kQkvStage = 32 * 128 * 2;
+constexpr int epi_staging(Epi e)
+{
+    return epi_tma(e) ? 2 * kEpiBox + kBiasBytes : e == Epi::kQkv ? 4 * kQkvStage : 0;
+}
 
 // Stages: up to 8 within 200 KB, fewer where the epilogue's staging would not fit beside them in 227 KB.
 constexpr int stages_for(int stage_bytes, int staging)
@@ -198,7 +205,7 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
 // The epilogue of one tile for one thread (one row). t_row: TMEM address of this row's accumulator, column 0.
 template <int BN, Epi EPI>
 __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int row, bool row_ok, int n0,
-                                         const float* sb)
+                                         const float* sb, uint8_t* stg = nullptr)
 {
     if constexpr (EPI == Epi::kBF16 || EPI == Epi::kF32 || EPI == Epi::kResid || EPI == Epi::kAdd) {
 #pragma unroll 1
@@ -364,6 +371,9 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
                 dst = a.group_dst[grp] + which * a.group_chunk +
                       ((long(bsample) * a.head_group + head - grp * a.head_group) * a.L + pos) * 128;
             }
+            if (!row_ok)
+                dst = nullptr;
+            const int lane = threadIdx.x & 31;
             const float* w = which == 0 ? a.norm_q : a.norm_k;
 #pragma unroll 1
             for (int c = 0; c < 128; c += 32) {
@@ -400,8 +410,28 @@ __device__ __forceinline__ void epilogue(const GemmArgs& a, uint32_t t_row, int 
                         }
                     }
                 }
-                store_bf16x32(dst + c, v);
+                // This row's 64 bytes at 16-byte chunks c / 8 .. c / 8 + 3 of its 256-byte staging row, chunk j
+                // placed at j ^ (row & 15) so that a warp's writes and the copy-out's reads spread over the banks.
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int j = c / 8 + k;
+                    *reinterpret_cast<uint4*>(stg + lane * 256 + ((j ^ (lane & 15)) << 4)) =
+                        make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                   pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+                }
             }
+            __syncwarp();
+            // The warp's 32 rows of this head leave as whole rows: half a warp per 256-byte row.
+#pragma unroll 4
+            for (int k = 0; k < 16; ++k) {
+                const int idx = k * 32 + lane, rr = idx >> 4, j = idx & 15;
+                __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), rr));
+                if (d)
+                    *reinterpret_cast<uint4*>(d + j * 8) =
+                        *reinterpret_cast<const uint4*>(stg + rr * 256 + ((j ^ (rr & 15)) << 4));
+            }
+            __syncwarp();
         }
     }
 }
@@ -954,14 +984,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
                     epilogue_tma<BN, EPI, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
                                            nb * BN, x0, y0, b, sb, et, status, abort_flag);
                 else
-                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb);
+                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb, staging + q * kQkvStage);
             } else {
                 const int row0 = mb * kBM, row = row0 + r;
                 if (epi_tma(EPI) && args.out_mode)
                     epilogue_tma<BN, EPI, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
                                             nb * BN, row0, 0, 0, sb, et, status, abort_flag);
                 else
-                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
+                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb, staging + q * kQkvStage);
             }
             if (has_next) {
                 // The TMA boxes' last barrier already follows every read of the current copy; a per-thread tile
@@ -1187,14 +1217,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) k_gemm2
                     epilogue_tma<BN, EPI, true>(args, &P.to[p], &P.tr[p], t_row, r, row, row_ok, b < args.conv_b,
                                            nb * BN, x0, y0, b, sb, et, status, abort_flag);
                 else
-                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb);
+                    epilogue<BN, EPI>(args, t_row, row, row_ok, nb * BN, sb, staging + q * kQkvStage);
             } else {
                 const int row0 = mb * kPM + int(rank) * kBM, row = row0 + r;
                 if (epi_tma(EPI) && args.out_mode)
                     epilogue_tma<BN, EPI, false>(args, &P.to[p], &P.tr[p], t_row, r, row, row < args.M, row0 < args.M,
                                             nb * BN, row0, 0, 0, sb, et, status, abort_flag);
                 else
-                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb);
+                    epilogue<BN, EPI>(args, t_row, row, row < args.M, nb * BN, sb, staging + q * kQkvStage);
             }
             if (has_next) {
                 // The TMA boxes' last barrier already follows every read of the current copy; a per-thread tile
