@@ -256,6 +256,8 @@ def run_mkb(args, cfg):
         obj = [mkimage.nccl_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(obj, src=0)
         d.set_sequence_parallel(obj[0], rank, ws)
+        if args.sp_exchange.startswith("heads") and H % ws:
+            args.sp_exchange = "peer"  # the head split needs the heads to divide over the ranks
         if args.sp_exchange == "peer":
             d.set_peer_exchange(True)
         elif args.sp_exchange == "heads":
@@ -759,11 +761,12 @@ def main():
                     help="DiT configs under torchrun: the config's images spread over the ranks (strong scaling)")
     ap.add_argument("--sp", action="store_true",
                     help="DiT configs under torchrun: one sequence-parallel group over all ranks instead of replicas")
-    ap.add_argument("--sp-exchange", choices=["peer", "nccl", "heads", "heads_peer"], default="peer",
+    ap.add_argument("--sp-exchange", choices=["peer", "nccl", "heads", "heads_peer"], default="heads_peer",
                     help="--sp: K/V shards pushed into the peers' memory by copy engines during the attention "
                          "(peer), all-gathered by NCCL before it (nccl), or q/k/v exchanged all-to-all so that "
                          "each rank attends over whole sequences of heads / ranks heads (heads), the same with the "
-                         "QKV and attention epilogues storing into the peers' memory (heads_peer)")
+                         "QKV and attention epilogues storing into the peers' memory (heads_peer, the default; "
+                         "peer when the heads do not divide over the ranks)")
     ap.add_argument("--kernel", choices=["gemm", "qkv", "attention", "oproj", "ffn_up", "ffn_down", "vae_attention",
                                          "vae_conv128"], default=None,
                     help="run one hot kernel alone at the config's shape (profiling)")
