@@ -113,6 +113,11 @@ struct DitImpl {
     int Bmax = 0, Smax = 0, Nmax = 0, Lmax = 0;
     cudaStream_t stream = nullptr;
     uint32_t* status = nullptr;
+    // qwen1: block i's modulation GEMV (i >= 1) runs on a side stream beside the blocks before it (its blocks use no
+    // shared memory, so they fit on SMs beside the GEMMs' CTAs), joined before block i; block 0's on the step's stream.
+    cudaStream_t mod_side = nullptr;
+    cudaEvent_t mod_fork = nullptr;
+    std::vector<cudaEvent_t> mod_ready;
 
     std::vector<Weight> weights;
     std::map<std::string, int> windex;
@@ -284,6 +289,15 @@ DitImpl::~DitImpl()
         if (const NcclApi* api = nccl_api(nullptr))
             api->CommDestroy(sp_comm);
     }
+    if (mod_side)
+        cudaStreamSynchronize(mod_side);
+    for (cudaEvent_t e : mod_ready)
+        if (e)
+            cudaEventDestroy(e);
+    if (mod_fork)
+        cudaEventDestroy(mod_fork);
+    if (mod_side)
+        cudaStreamDestroy(mod_side);
     if (stream)
         cudaStreamDestroy(stream);
 }
@@ -703,6 +717,13 @@ mkb_status DitImpl::create(const mkb_dit_config& c)
     }
 
     MKB_TRY_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    if (q1) {
+        MKB_TRY_CUDA(cudaStreamCreateWithFlags(&mod_side, cudaStreamNonBlocking), "modulation stream");
+        MKB_TRY_CUDA(cudaEventCreateWithFlags(&mod_fork, cudaEventDisableTiming), "modulation events");
+        mod_ready.assign(NB, nullptr);
+        for (auto& e : mod_ready)
+            MKB_TRY_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "modulation events");
+    }
     status = device_status_word();
     if (!status)
         return fail(MKB_ERR_CUDA, "status word");
@@ -1330,8 +1351,17 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     MKB_TRY(emit("temb", -1, temb, long(R) * D, s));
     MKB_K(silu_f32(temb, st, size_t(R) * D, s), "silu");
     if (q1) {
+        // Block 0's modulation on the step's stream, the others on the side stream (joined before their blocks).
         const int Nm = NB * 12 * D;
-        MKB_K(gemv(wmat, st, D, wvec, mod, Nm, B, Nm, D, kActNone, s), "modulation");
+        MKB_K(gemv(wmat, st, D, wvec, mod, Nm, B, 12 * D, D, kActNone, s), "modulation");
+        MKB_K(cudaEventRecord(mod_fork, s), "modulation fork");
+        MKB_K(cudaStreamWaitEvent(mod_side, mod_fork, 0), "modulation fork");
+        for (int i = 1; i < NB; ++i) {
+            const size_t r0 = size_t(i) * 12 * D;
+            MKB_K(gemv(wmat + r0 * D, st, D, wvec + r0, mod + r0, Nm, B, 12 * D, D, kActNone, mod_side, true),
+                  "modulation");
+            MKB_K(cudaEventRecord(mod_ready[i], mod_side), "modulation ready");
+        }
         MKB_K(gemv(M("norm_out.w"), st, D, V("norm_out.b"), omod, 2 * D, B, 2 * D, D, kActNone, s), "norm_out mod");
     } else {
         MKB_K(gemv(M("mod.w"), st, D, nullptr, mod, 4 * D, R, 4 * D, D, kActNone, s), "modulation");
@@ -1373,6 +1403,8 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
     for (int i = 0; i < NB; ++i) {
         GemmOp* o = plan->ops.data() + size_t(i) * per;
         if (q1) {
+            if (i > 0)
+                MKB_K(cudaStreamWaitEvent(s, mod_ready[i], 0), "modulation join");
             const int Mt = B * St, Mi = B * Nl;
             const long mstride = long(NB) * 12 * D;
             // The text and image rows' modulated LayerNorms, one launch for both streams.

@@ -127,10 +127,12 @@ __global__ void __launch_bounds__(256) k_rms(const RmsArgs a)
         }
 }
 
-// GEMV: x staged in shared memory; each warp takes 4 weight rows at a time, lanes stride the row in 16-byte chunks.
+// GEMV: x staged in shared memory (XS) or read through L1 (no shared memory, so that its blocks fit beside a
+// GEMM's on an SM); each warp takes 4 weight rows at a time, lanes stride the row in 16-byte chunks. Both forms do
+// the same arithmetic in the same order.
 constexpr int kGemvRows = 4;
 
-template <int B>
+template <int B, bool XS>
 __global__ void __launch_bounds__(256) k_gemv(const __nv_bfloat16* __restrict__ W, const float* __restrict__ x,
                                               long ldx, const float* __restrict__ bias, float* __restrict__ y,
                                               long ldy, int N, int K, int act)
@@ -138,9 +140,11 @@ __global__ void __launch_bounds__(256) k_gemv(const __nv_bfloat16* __restrict__ 
     grid_dep_wait();
     grid_dep_launch();
     extern __shared__ float xs[];  // [B][K]
-    for (int i = threadIdx.x; i < B * K; i += blockDim.x)
-        xs[i] = x[long(i / K) * ldx + i % K];
-    __syncthreads();
+    if constexpr (XS) {
+        for (int i = threadIdx.x; i < B * K; i += blockDim.x)
+            xs[i] = x[long(i / K) * ldx + i % K];
+        __syncthreads();
+    }
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = K >> 3;
@@ -159,8 +163,10 @@ __global__ void __launch_bounds__(256) k_gemv(const __nv_bfloat16* __restrict__ 
                                   : make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-                const float4 xa = *reinterpret_cast<const float4*>(xs + b * K + c * 8);
-                const float4 xb = *reinterpret_cast<const float4*>(xs + b * K + c * 8 + 4);
+                const float4 xa = XS ? *reinterpret_cast<const float4*>(xs + b * K + c * 8)
+                                     : __ldg(reinterpret_cast<const float4*>(x + b * ldx + c * 8));
+                const float4 xb = XS ? *reinterpret_cast<const float4*>(xs + b * K + c * 8 + 4)
+                                     : __ldg(reinterpret_cast<const float4*>(x + b * ldx + c * 8 + 4));
 #pragma unroll
                 for (int r = 0; r < kGemvRows; ++r) {
                     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w[r]);
@@ -946,11 +952,12 @@ cudaError_t rms_norm_rows(const RmsArgs& a, cudaStream_t st)
 }
 
 cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* bias, float* y, long ldy, int B,
-                 int N, int K, int act, cudaStream_t st)
+                 int N, int K, int act, cudaStream_t st, bool no_smem)
 {
-    if (B < 1 || B > 8 || K % 8 || N <= 0 || (reinterpret_cast<uintptr_t>(W) & 15))
+    if (B < 1 || B > 8 || K % 8 || N <= 0 || (reinterpret_cast<uintptr_t>(W) & 15) ||
+        (no_smem && ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 3))))
         return cudaErrorInvalidValue;
-    const size_t smem = size_t(B) * K * sizeof(float);
+    const size_t smem = no_smem ? 0 : size_t(B) * K * sizeof(float);
     const int rows_per_block = 8 * kGemvRows;
     int blocks = (N + rows_per_block - 1) / rows_per_block;
     if (blocks > 148 * 8)
@@ -958,12 +965,17 @@ cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* 
     // Above 48 KB the limit is raised on every such launch: it belongs to the current device, and the sizes vary.
 #define MKB_GEMV(BB)                                                                                                   \
     case BB: {                                                                                                         \
+        if (no_smem) {                                                                                                 \
+            launch_k(k_gemv<BB, false>, blocks, 256, 0, st, W, x, ldx, bias, y, ldy, N, K, act);                       \
+            break;                                                                                                     \
+        }                                                                                                              \
         if (smem > 48 * 1024) {                                                                                        \
-            cudaError_t e = cudaFuncSetAttribute(k_gemv<BB>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+            cudaError_t e =                                                                                            \
+                cudaFuncSetAttribute(k_gemv<BB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));       \
             if (e != cudaSuccess)                                                                                      \
                 return e;                                                                                              \
         }                                                                                                              \
-        launch_k(k_gemv<BB>, blocks, 256, smem, st, W, x, ldx, bias, y, ldy, N, K, act);                               \
+        launch_k(k_gemv<BB, true>, blocks, 256, smem, st, W, x, ldx, bias, y, ldy, N, K, act);                         \
         break;                                                                                                         \
     }
     switch (B) {

@@ -40,9 +40,11 @@ struct RmsArgs {
 cudaError_t rms_norm_rows(const RmsArgs& a, cudaStream_t st);
 
 // y[b][n] = act(W[n] . x[b] + bias[n]) for b < B (B <= 8): bf16 weights [N][K], fp32 activations [B][K] (rows ldx
-// apart), fp32 out (rows ldy apart). act: 0 none, 2 silu (GemmArgs's Act values).
+// apart), fp32 out (rows ldy apart). act: 0 none, 2 silu (GemmArgs's Act values). no_smem: x read through L1 (x and
+// ldx 16-byte aligned) instead of staged in shared memory, so that the blocks can share SMs with a GEMM's; the same
+// results.
 cudaError_t gemv(const __nv_bfloat16* W, const float* x, long ldx, const float* bias, float* y, long ldy, int B,
-                 int N, int K, int act, cudaStream_t st);
+                 int N, int K, int act, cudaStream_t st, bool no_smem = false);
 
 // tp[r][0:128] = cos(1000 t_r f_i), tp[r][128:256] = sin(1000 t_r f_i), f_i = exp(-ln(10000) i / 128), for the rows'
 // noise levels t (qwen_image.cpp:179-187).
