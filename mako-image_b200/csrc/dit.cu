@@ -1354,8 +1354,10 @@ mkb_status DitImpl::body(int B, const int* slot_ids, int S, int N, int first, Pl
         // Block 0's modulation on the step's stream, the others on the side stream (joined before their blocks).
         const int Nm = NB * 12 * D;
         MKB_K(gemv(wmat, st, D, wvec, mod, Nm, B, 12 * D, D, kActNone, s), "modulation");
-        MKB_K(cudaEventRecord(mod_fork, s), "modulation fork");
-        MKB_K(cudaStreamWaitEvent(mod_side, mod_fork, 0), "modulation fork");
+        if (NB > 1) {  // (a fork with no work on the side would leave the step's graph capture unjoined)
+            MKB_K(cudaEventRecord(mod_fork, s), "modulation fork");
+            MKB_K(cudaStreamWaitEvent(mod_side, mod_fork, 0), "modulation fork");
+        }
         for (int i = 1; i < NB; ++i) {
             const size_t r0 = size_t(i) * 12 * D;
             MKB_K(gemv(wmat + r0 * D, st, D, wvec + r0, mod + r0, Nm, B, 12 * D, D, kActNone, mod_side, true),

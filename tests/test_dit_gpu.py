@@ -214,9 +214,10 @@ def test_step_cfg_matches_two_steps(cuda):
 
 def test_graph_replay_matches_eager(cuda):
     """The step body runs eagerly on a geometry's first call, is captured as a CUDA graph on the second and replayed
-    after. Alternating latents make a replay that did no work visible (it would return the previous call's result)."""
-    for variant in (0, 1):
-        d, cfg = _make(variant, 512, 4, 1024, 2, 256, 2, 20, 64, seed=21)
+    after. Alternating latents make a replay that did no work visible (it would return the previous call's result).
+    qwen1 also with one block: its modulation then has no side-stream part, which the capture must not fork."""
+    for variant, blocks in ((0, 2), (0, 1), (1, 2)):
+        d, cfg = _make(variant, 512, 4, 1024, blocks, 256, 2, 20, 64, seed=21)
         prompts, lats = _inputs(2, 20, 64, 256, seed=8)
         a = np.stack(lats)
         b = a[::-1].copy() * 0.5
