@@ -325,8 +325,8 @@ mkb_status mkb_dit_set_sequence_parallel(mkb_dit* d, const void* nccl_id, int ra
  * peer's region and then raises the rank's ready flag there, and the attention starts on its own shard and waits
  * (bounded, 2 s; MKB_ERR_KERNEL on timeout) for each other shard's flag, so the transfers overlap the attention
  * instead of preceding it. The key order differs per rank, so results match the one-GPU step to rounding, no longer
- * bit for bit; all ranks still end with identical latents. Fails with MKB_ERR_CUDA on every rank if any rank cannot
- * allocate, export or map, leaving the all-gather in place. */
+ * bit for bit; all ranks still end with identical latents. Turns the head exchange (below) off. Fails with
+ * MKB_ERR_CUDA on every rank if any rank cannot allocate, export or map, leaving the all-gather in place. */
 mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable);
 /* Replaces the per-block K/V all-gather of a sequence-parallel handle by a head-parallel exchange (mode 1: NCCL,
  * mode 2: peer memory) or goes back to it (mode 0); collective, every rank with the same mode, after
