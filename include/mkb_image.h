@@ -579,6 +579,14 @@ mkb_status mkb_check_kernels(uint32_t* bits);
 mkb_status mkb_selftest_stalled_gemm(const void* x, long ldx, const void* w, long ldw, float* y, long ldy, int M,
                                      int N, int K, void* stream);
 
+/* Failure-path self-test of the head exchange's wait for its peers (mkb_dit_sp_head_exchange mode 2; no counterpart
+ * in the reference): launches the wait that holds a rank's output projection until every flag in `flags` (n device
+ * words, the rank's own at index `self` skipped) has reached *value (a device word). A flag that stays below runs
+ * out the bounded 2 s wait; mkb_check_kernels then returns MKB_ERR_KERNEL with bit 0x100 and the context stays
+ * usable. For tests of error detection; nothing else calls it. */
+mkb_status mkb_selftest_peer_wait(const unsigned long long* flags, int n, int self, const unsigned long long* value,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

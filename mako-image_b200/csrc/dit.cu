@@ -1987,6 +1987,19 @@ mkb_status mkb_dit_sp_peer_exchange(mkb_dit* d, int enable)
     return d->impl.sp_set_peer(enable != 0);
 }
 
+mkb_status mkb_selftest_peer_wait(const unsigned long long* flags, int n, int self, const unsigned long long* value,
+                                  void* stream)
+{
+    if (!flags || !value || n < 1 || n > 64 || (reinterpret_cast<uintptr_t>(flags) & 7) ||
+        (reinterpret_cast<uintptr_t>(value) & 7))
+        return fail(MKB_ERR_INVALID, "selftest: need 1-64 8-byte aligned flags and an 8-byte aligned value");
+    MKB_TRY_CUDA(launch_k(k_sp_wait, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, n, self, value,
+                          device_status_word()),
+                 "selftest launch");
+    count_launch();
+    return MKB_OK;
+}
+
 mkb_status mkb_dit_sp_head_exchange(mkb_dit* d, int mode)
 {
     MKB_TRY(check_handle(d));

@@ -26,6 +26,7 @@ _SIGS = {
     "mkb_swiglu_interleave": (_i, []),
     "mkb_check_kernels": (_i, [_u32p]),
     "mkb_selftest_stalled_gemm": (_i, [_vp, _l, _vp, _l, _vp, _l, _i, _i, _i, _vp]),
+    "mkb_selftest_peer_wait": (_i, [_vp, _i, _i, _vp, _vp]),
     "mkb_proj_add": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _vp, _l, _vp, _l, _i, _i, _i, _i, _vp]),
     "mkb_proj_heads": (_i, [_vp, _l, _vp, _l, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "mkb_proj_geglu": (_i, [_vp, _l, _vp, _l, _vp, _vp, _l, _i, _i, _i, _vp]),

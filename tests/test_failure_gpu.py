@@ -2,6 +2,9 @@
 
 * On the device: a GEMM whose first CTA never receives its first stage (mkb_selftest_stalled_gemm) must end on its
   own through the bounded waits, report MKB_ERR_KERNEL through mkb_check_kernels, and leave the context usable.
+* On the device, the head exchange's wait for its peers (mkb_selftest_peer_wait): a peer flag that nothing raises
+  runs out the bounded wait, is reported as MKB_ERR_KERNEL with the shard-wait bit, and the same wait passes at once
+  when every flag is up.
 * On the host: an allocation that cannot succeed in mkb_dit_create returns MKB_ERR_ALLOC and leaks nothing; an
   NCCL communicator that cannot be made (a stand-in libnccl bound through MKB_NCCL_LIB whose ncclCommInitRank
   returns an error) makes mkb_dit_set_sequence_parallel fail cleanly, and the handle keeps working on one GPU."""
@@ -134,3 +137,25 @@ def test_sequence_parallel_nccl_failure_leaves_handle_usable(cuda, tmp_path):
     code = _SP_FAIL_CHILD.format(root=ROOT, pkg=os.path.join(ROOT, "mako-image_b200"))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "SP_FAIL_OK" in r.stdout, (r.stdout[-2000:], r.stderr[-4000:])
+
+
+def test_peer_wait_times_out_and_context_survives(cuda):
+    import torch
+    import mkimage
+
+    flags = torch.tensor([7, 6, 7, 0], dtype=torch.int64, device=cuda)  # rank 1's flag short; 3 is this rank's own
+    value = torch.tensor([7], dtype=torch.int64, device=cuda)
+    assert mkimage.ops.check_kernels() == 0
+    t0 = time.time()
+    mkimage.check(mkimage.lib.mkb_selftest_peer_wait(_p(flags), 4, 3, _p(value), None))
+    bits = ctypes.c_uint32()
+    code = mkimage.lib.mkb_check_kernels(ctypes.byref(bits))
+    elapsed = time.time() - t0
+    assert code == 4, (code, mkimage.lib.mkb_last_error())  # MKB_ERR_KERNEL
+    assert bits.value == 0x100, hex(bits.value)  # the shard-wait bit
+    assert 1.5 < elapsed < 30, elapsed
+    flags[1] = 8  # every peer's flag up (at or above the value): no wait, no error
+    t0 = time.time()
+    mkimage.check(mkimage.lib.mkb_selftest_peer_wait(_p(flags), 4, 3, _p(value), None))
+    assert mkimage.ops.check_kernels() == 0
+    assert time.time() - t0 < 1.5
