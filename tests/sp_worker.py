@@ -37,12 +37,19 @@ def run_steps(d, lat):
 def main():
     rank, world, tmp = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3]
     exchange = sys.argv[4] if len(sys.argv) > 4 else "nccl"
+    wide = len(sys.argv) > 5 and sys.argv[5] == "wide"  # Qwen-Image's widths, 2 blocks, 1024^2 (L = 4352)
     import torch
     import mkimage
 
     torch.cuda.set_device(rank)
-    cfg = mkimage.DitConfig(variant=mkimage.QWEN1, hidden=256, heads=2, ffn=512, blocks=2, text_dim=TD,
-                            max_batch=4, max_text_tokens=S, max_image_tokens=GH * GW, slots=4)
+    global S, GH, GW, TD
+    if wide:
+        S, GH, GW, TD = 256, 64, 64, 3584
+        cfg = mkimage.DitConfig(variant=mkimage.QWEN1, hidden=3072, heads=24, ffn=12288, blocks=2, text_dim=TD,
+                                max_batch=4, max_text_tokens=S, max_image_tokens=GH * GW, slots=4)
+    else:
+        cfg = mkimage.DitConfig(variant=mkimage.QWEN1, hidden=256, heads=2, ffn=512, blocks=2, text_dim=TD,
+                                max_batch=4, max_text_tokens=S, max_image_tokens=GH * GW, slots=4)
     idf = os.path.join(tmp, "nccl_id")
     if rank == 0:
         nid = mkimage.nccl_unique_id()

@@ -51,3 +51,30 @@ def test_sequence_parallel_two_gpus(tmp_path, exchange):
             for a, w in zip(got[r], ref):
                 rel = np.sqrt(((a - w) ** 2).sum() / (w ** 2).sum())
                 assert rel < 5e-3, (r, rel)
+
+
+@pytest.mark.parametrize("exchange", ["heads_peer", "nccl"])
+def test_sequence_parallel_two_gpus_full_width(tmp_path, exchange):
+    """The same bar at Qwen-Image's widths (hidden 3072, 24 heads, FFN 12288, text 3584) on a 1024^2 image (4352
+    joint rows, 2176 per rank), two blocks: the head split over peer memory and the K/V all-gather both equal the
+    one-GPU step bit for bit."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, WORKER, str(r), "2", str(tmp_path), exchange, "wide"], env=env)
+             for r in range(2)]
+    try:
+        codes = [p.wait(timeout=600) for p in procs]
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+                p.wait()
+    assert codes == [0, 0], codes
+    ref = np.load(tmp_path / "ref.npy")
+    assert np.isfinite(ref).all() and np.abs(ref).max() > 0
+    for r in range(2):
+        got = np.load(tmp_path / f"rank{r}.npy")
+        assert np.array_equal(got, ref), (r, np.abs(got - ref).max())
