@@ -159,3 +159,22 @@ def test_peer_wait_times_out_and_context_survives(cuda):
     mkimage.check(mkimage.lib.mkb_selftest_peer_wait(_p(flags), 4, 3, _p(value), None))
     assert mkimage.ops.check_kernels() == 0
     assert time.time() - t0 < 1.5
+
+
+def test_exchange_switches_need_sequence_parallelism(cuda):
+    """The exchange switches are refused (MKB_ERR_STATE) on a handle without sequence parallelism, which then steps
+    normally."""
+    import mkimage
+
+    d = mkimage.Dit(_small_cfg(mkimage))
+    try:
+        d.init_random(5)
+        for call, code in ((lambda: mkimage.lib.mkb_dit_sp_head_exchange(d.h, 2), 3),
+                           (lambda: mkimage.lib.mkb_dit_sp_head_exchange(d.h, 1), 3),
+                           (lambda: mkimage.lib.mkb_dit_sp_peer_exchange(d.h, 1), 3)):
+            assert call() == code, mkimage.lib.mkb_last_error()
+            assert b"sequence parallelism" in mkimage.lib.mkb_last_error()
+        _small_step(mkimage, d)
+        assert mkimage.ops.check_kernels() == 0
+    finally:
+        d.close()
